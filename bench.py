@@ -1,0 +1,342 @@
+"""Benchmark of the int4 Llama hot path on B200 (one process per GPU; torchrun for N > 1).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemv|decode] [--impl ours|reference]
+
+Prints ONE JSON line (rank 0). Workloads:
+  gemv    BASELINE config 1: int4 GEMV y[5120] = dequant(W)[5120, 3072] . x[3072], group 128, fp16 x/y.
+          One step = 32 back-to-back calls over 32 distinct weight copies (260 MB > 126 MB L2), each
+          a separate kernel launch captured in one CUDA graph (programmatic dependent launch lets a
+          call's weight stream start while the previous call finishes). value = weight+scale+x+y
+          bytes moved per second, summed over ranks (replicas: the GEMV does not shard).
+--impl reference times the CPU restatement of the reference path (oracle port) on the host cores of
+rank 0; other ranks exit without work.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "iree-adreno-genai-tuner_b200"))
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tests" / "golden"))
+
+GEMV_N, GEMV_K, GEMV_G = 5120, 3072, 128
+GEMV_BYTES = GEMV_N * GEMV_K // 2 + GEMV_N * (GEMV_K // GEMV_G) * 2 + GEMV_K * 2 + GEMV_N * 2  # 8,126,464
+GEMV_COPIES = 32
+METRIC_GEMV = "int4 GEMV HBM GB/s (5120x3072)"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profile_traffic(name):
+    """dram bytes per launch recorded from an ncu capture in profiles/<name>.txt ("traffic_bytes_per_launch: N")."""
+    p = ROOT / "profiles" / f"{name}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (median SM clock, throttle reasons seen)."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                mx = float(f[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+def init_dist(world, local):
+    import torch
+    import torch.distributed as dist
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return dist if world > 1 else None
+
+
+def max_over_ranks(v, dist_mod):
+    import torch
+    if dist_mod is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist_mod.all_reduce(t, op=dist_mod.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(v, dist_mod):
+    import torch
+    if dist_mod is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist_mod.all_reduce(t)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline (oracle port of the reference's QLinear dequant + linear, scripts/llm/llama_q4.py:72)
+# ---------------------------------------------------------------------------------------------
+
+def cpu_gemv_baseline(budget_s=12.0):
+    import numpy as np
+
+    import golden_inputs as gi
+    from oracle import q4_oracle as O
+    qw, s, x = gi.gemv_inputs()
+    xf = x.astype(np.float32)[None]
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        W = O.dequantize_q4(qw, s, GEMV_G)
+        y = xf @ W.T
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 200:
+            break
+    assert y.shape == (1, GEMV_N)
+    med = statistics.median(times)
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"value": GEMV_BYTES / med / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{len(times)} calls of numpy dequantize_q4 + fp32 matmul on 5120x3072 g128 "
+                      f"(median {med * 1e3:.2f} ms/call; dequant single-threaded, BLAS on {cores} threads)"}
+
+
+# ---------------------------------------------------------------------------------------------
+# GPU GEMV workload
+# ---------------------------------------------------------------------------------------------
+
+def run_gemv(args, rank, world, local, dist_mod):
+    import numpy as np
+    import torch
+
+    import q4b
+    from q4b import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    # synthetic inputs of BASELINE config 1: uniform nibbles packed 8 per int32, |N(0,0.02)| fp16 scales
+    qws = [torch.randint(-2**31, 2**31 - 1, (GEMV_N, GEMV_K // 8), dtype=torch.int32, device=dev, generator=g)
+           for _ in range(GEMV_COPIES)]
+    scs = [(torch.randn(GEMV_N, GEMV_K // GEMV_G, device=dev, generator=g) * 0.02).abs().half()
+           for _ in range(GEMV_COPIES)]
+    x = torch.randn(1, GEMV_K, device=dev, generator=g).half()
+    ys = [torch.empty(1, GEMV_N, dtype=torch.float16, device=dev) for _ in range(GEMV_COPIES)]
+    stream = torch.cuda.Stream(device=dev)
+    cfg = json.loads(args.gemv_cfg) if args.gemv_cfg else None
+
+    def one_pass():
+        for i in range(GEMV_COPIES):
+            ops.q4_linear(x, qws[i], scs[i], GEMV_G, out=ys[i], cfg=cfg)
+
+    with torch.cuda.stream(stream):
+        one_pass()  # allocates the workspace outside the capture
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        graph.capture_begin()
+        one_pass()
+        graph.capture_end()
+    stream.synchronize()
+    for _ in range(args.warmup):
+        with torch.cuda.stream(stream):
+            graph.replay()
+    stream.synchronize()
+    if dist_mod:
+        dist_mod.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            ev1.record(stream)
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if dist_mod:
+        dist_mod.barrier()
+    torch.cuda.synchronize()
+    ms_max = max_over_ranks(ms, dist_mod)
+    ms_step = ms_max / args.steps
+    per_call_s = ms_step / 1e3 / GEMV_COPIES
+    value = world * GEMV_COPIES * GEMV_BYTES / (ms_step / 1e3) / 1e9
+
+    # correctness spot check of the last pass against the CPU oracle restatement (rank 0, copy 0)
+    check = None
+    if rank == 0:
+        from oracle import q4_oracle as O
+        y0 = ys[0].float().cpu().numpy()
+        ref = O.q4_linear(qws[0].cpu().numpy(), scs[0].cpu().numpy(), GEMV_G, x.float().cpu().numpy())
+        check = O.rel_err(y0, ref)
+
+    # end to end through the public API: pinned host x -> QLinear.forward -> pinned host y, per call
+    ql = q4b.QLinear.from_packed(qws[0], scs[0], GEMV_G)
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(1, GEMV_N, dtype=torch.float16).pin_memory()
+    e2e_steps = max(args.steps, 50)
+    for i in range(5):
+        xd = xh.to(dev, non_blocking=True)
+        yh.copy_(ql(xd), non_blocking=True)
+    torch.cuda.synchronize()
+    if dist_mod:
+        dist_mod.barrier()
+    t0 = time.perf_counter()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        xd = xh.to(dev, non_blocking=True)
+        yh.copy_(ql(xd), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    e1.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, dist_mod)
+    wall_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
+
+    if rank != 0:
+        return None
+    pk = peaks()
+    traffic = profile_traffic("q4_gemv_mma_5120x3072")
+    line = {
+        "metric": METRIC_GEMV, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int4 weights, fp16 x/y, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": "int4 GEMV 5120x3072 group 128 M=1 (BASELINE config 1)",
+                   "calls_per_step": GEMV_COPIES, "l2": f"inputs larger than L2: {GEMV_COPIES} distinct weight "
+                   f"copies x {GEMV_BYTES / 1e6:.2f} MB", "parallelism": f"replicas x{world}",
+                   "launch": "CUDA graph of separate launches with programmatic dependent launch"},
+        "roofline": {"bound": "hbm", "achieved": round(GEMV_BYTES / per_call_s / 1e9, 1), "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(GEMV_BYTES / per_call_s / 1e9 / pk["hbm_gbs"], 4),
+                     "traffic": traffic, "peak_source": pk["source"], "kernel": "q4_gemv_mma",
+                     "algorithmic_bytes_per_launch": GEMV_BYTES},
+        "e2e": {"value": round(world * GEMV_BYTES / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": GEMV_K * 2, "d2h_bytes_per_step": GEMV_N * 2,
+                "ms_per_call": round(e2e_ms, 4), "wall_ms_per_call": round(wall_ms, 4),
+                "path": "q4b.QLinear.forward per call with pinned-host x in and y out, synchronised"},
+        "gpu_launches": args.steps * GEMV_COPIES,
+        "clocks": clk.summary(),
+        "parity_rel_err": check,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_gemv_baseline()
+    return line
+
+
+def run_reference(args, rank, world):
+    """The reference arm: CPU restatement of the reference path on the host cores (rank 0 only)."""
+    if rank != 0:
+        return None
+    if args.workload == "gemv":
+        cb = cpu_gemv_baseline(budget_s=min(60.0, 3.0 * (args.steps + args.warmup)))
+        return {"metric": METRIC_GEMV, "value": round(cb["value"], 4), "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "int4 weights, fp32 compute", "data": "synthetic",
+                "impl": "reference",
+                "config": {"workload": "int4 GEMV 5120x3072 group 128 M=1 (BASELINE config 1)"},
+                "cpu_baseline": cb,
+                "e2e": {"value": round(cb["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+    raise SystemExit(f"unknown workload {args.workload}")
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--workload", default="gemv", choices=["gemv"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--gemv-cfg", default=None, help='JSON q4b_linear_cfg, e.g. {"warps":4,"tiles":2}')
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line:
+            print(json.dumps(line), flush=True)
+        return
+    dist_mod = init_dist(world, local)
+    try:
+        line = run_gemv(args, rank, world, local, dist_mod)
+    finally:
+        if dist_mod:
+            dist_mod.barrier()
+            dist_mod.destroy_process_group()
+    if line:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,97 @@
+/*
+ * q4b.h — C ABI of the B200-native int4 Llama hot path (libq4b.so, sm_100a).
+ *
+ * Conventions for every entry point:
+ *   - plain device pointers and sizes; no allocation inside a call (the caller owns all memory,
+ *     including workspaces); work is ordered on the given stream (a cudaStream_t passed as
+ *     q4b_stream_t, NULL = the legacy default stream); no host synchronisation, so calls can be
+ *     captured in a CUDA graph;
+ *   - the return value is Q4B_OK (0) or a negative Q4B_E* code; q4b_last_error() returns a
+ *     thread-local message for the last failing call on that thread;
+ *   - shape and alignment errors are reported before anything is launched.
+ *
+ * Layouts follow the reference (paths relative to the reference project):
+ *   qweight [N, K/8] int32, nibble b (bits 4b..4b+3) of word j holds k = 8j + b, stored as q + 8;
+ *   scales  [N, K/G] fp16 (passed as uint16_t bit patterns);        scripts/llm/llama_q4.py:25-38
+ *   activations row-major [M, K]; outputs row-major [M, N].
+ */
+#ifndef Q4B_H
+#define Q4B_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  Q4B_OK = 0,
+  Q4B_EINVAL = -1,       /* bad shape, dtype, alignment or null pointer */
+  Q4B_ELAUNCH = -2,      /* a kernel launch failed (cudaGetLastError) */
+  Q4B_ETIMEOUT = -3,     /* a bounded device-side wait gave up */
+  Q4B_ENOMEM = -4,       /* a create call could not allocate its state */
+  Q4B_EUNSUPPORTED = -5, /* valid input the library does not handle */
+  Q4B_ECUDA = -6,        /* another CUDA runtime error */
+  Q4B_ESTATE = -7        /* object used in the wrong state */
+};
+
+enum { Q4B_F32 = 0, Q4B_F16 = 1 };
+
+/* Epilogues of q4b_q4_linear:
+ *   STORE       y[m, n] = sum_k x[m, k] W[n, k]
+ *   ACCUMULATE  y[m, n] += sum_k x[m, k] W[n, k]            (residual add, llama_q4.py:233, 236)
+ *   SWIGLU      W has 2*I rows (gate rows then up rows, llama_q4.py:152); y is [M, I] with
+ *               y[m, i] = silu(gate_i . x_m) * (up_i . x_m)   (llama_q4.py:235-236)           */
+enum { Q4B_EPI_STORE = 0, Q4B_EPI_ACCUMULATE = 1, Q4B_EPI_SWIGLU = 2 };
+
+/* Kernel selection for q4b_q4_linear (NULL = tuned default).
+ *   kernel: 0 = auto, 1 = tensor-core dequant GEMV (needs G % 128 == 0, M <= 64), 2 = generic SIMT
+ *   warps (1..8), tiles (128-k tiles per warp kept in flight: 1, 2 or 4), split (k splits, >= 1):
+ *   0 = choose automatically.                                                                  */
+typedef struct q4b_linear_cfg {
+  int kernel;
+  int warps;
+  int tiles;
+  int split;
+} q4b_linear_cfg;
+
+typedef void* q4b_stream_t;
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* q4b_last_error(void);
+/* ABI version of this header (bumped on any incompatible change). */
+int q4b_abi_version(void);
+
+/* quantize_q4 (scripts/llm/llama_q4.py:25-38), bit-exact: w [n, k] fp32 on the device ->
+ * qweight [n, k/8] int32, scales [n, k/group] fp16. Needs k % group == 0 and group % 8 == 0. */
+int q4b_quantize_q4(const float* w, int n, int k, int group, int32_t* qweight, uint16_t* scales,
+                    q4b_stream_t stream);
+
+/* unpack_q4 (scripts/llm/llama_q4.py:41-45), bit-exact: qweight [n, k/8] -> nibbles [n, k] uint8. */
+int q4b_unpack_q4(const int32_t* qweight, int n, int k, uint8_t* nibbles, q4b_stream_t stream);
+
+/* dequantize_q4 (scripts/llm/llama_q4.py:48-51): -> out [n, k] of out_dtype (Q4B_F32 is exact). */
+int q4b_dequantize_q4(const int32_t* qweight, const uint16_t* scales, int n, int k, int group, void* out,
+                      int out_dtype, q4b_stream_t stream);
+
+/* Bytes of workspace q4b_q4_linear needs for this problem and configuration (0 if none). The
+ * workspace holds split-K partial sums and per-tile arrival counters; it must be zero-filled once
+ * before its first use, and every call leaves the counters at zero again. Calls that share one
+ * workspace must be ordered on one stream. */
+size_t q4b_q4_linear_workspace(int m, int n, int k, int group, int epilogue, const q4b_linear_cfg* cfg);
+
+/* QLinear.forward (scripts/llm/llama_q4.py:69-90): y = x @ dequantize_q4(qweight, scales)^T with
+ * fp32 accumulation, both reference forms in one call. x [m, k] of x_dtype, y of y_dtype
+ * ([m, n], or [m, n/2] for Q4B_EPI_SWIGLU). With fp32 x the tensor-core kernel splits x into two
+ * fp16 terms (hi + lo), so products keep ~22 bits of x. Launched with programmatic dependent launch:
+ * the weight stream starts before the previous kernel on the stream has finished. */
+int q4b_q4_linear(const int32_t* qweight, const uint16_t* scales, int group, const void* x, int x_dtype,
+                  void* y, int y_dtype, int m, int n, int k, int epilogue, const q4b_linear_cfg* cfg,
+                  void* workspace, size_t workspace_bytes, q4b_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q4B_H */

@@ -1,0 +1,10 @@
+"""q4b: B200-native (sm_100a) drop-in for the int4 Llama hot path of the reference's
+scripts/llm/llama_q4.py (QLinear, QEmbedding, LlamaQ4) and runner/llm_runner.c (the scheduler),
+computed by hand-written CUDA in libq4b.so behind the C ABI of include/q4b.h."""
+
+from ._lib import LIB_PATH, LinearCfg, Q4BError, lib
+from .ops import dequantize_q4, q4_linear, quantize_q4, unpack_q4
+from .qlinear import QEmbedding, QLinear
+
+__all__ = ["LIB_PATH", "LinearCfg", "Q4BError", "lib", "quantize_q4", "unpack_q4", "dequantize_q4", "q4_linear",
+           "QLinear", "QEmbedding"]

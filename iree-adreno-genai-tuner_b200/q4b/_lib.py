@@ -1,0 +1,76 @@
+"""ctypes binding of libq4b.so (the C ABI declared in include/q4b.h).
+
+The library is built in-tree by ``make -C iree-adreno-genai-tuner_b200/csrc`` (or
+``__graft_entry__.build()``). There is no fallback: importing an op without the library raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import pathlib
+
+_HERE = pathlib.Path(__file__).resolve().parent
+LIB_PATH = pathlib.Path(os.environ.get("Q4B_LIB", _HERE / "libq4b.so"))
+
+c_int, c_size_t, c_void_p, c_float, c_char_p = ctypes.c_int, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_float, ctypes.c_char_p
+
+Q4B_OK = 0
+Q4B_EINVAL = -1
+Q4B_ELAUNCH = -2
+Q4B_ETIMEOUT = -3
+Q4B_ENOMEM = -4
+Q4B_EUNSUPPORTED = -5
+Q4B_ECUDA = -6
+Q4B_ESTATE = -7
+F32, F16 = 0, 1
+EPI_STORE, EPI_ACCUMULATE, EPI_SWIGLU = 0, 1, 2
+
+_CODES = {Q4B_EINVAL: "EINVAL", Q4B_ELAUNCH: "ELAUNCH", Q4B_ETIMEOUT: "ETIMEOUT", Q4B_ENOMEM: "ENOMEM",
+          Q4B_EUNSUPPORTED: "EUNSUPPORTED", Q4B_ECUDA: "ECUDA", Q4B_ESTATE: "ESTATE"}
+
+
+class Q4BError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__(f"[{_CODES.get(code, code)}] {msg}")
+        self.code = code
+
+
+class LinearCfg(ctypes.Structure):
+    _fields_ = [("kernel", c_int), ("warps", c_int), ("tiles", c_int), ("split", c_int)]
+
+
+# name -> (restype, argtypes); must match include/q4b.h
+SIGNATURES = {
+    "q4b_last_error": (c_char_p, []),
+    "q4b_abi_version": (c_int, []),
+    "q4b_quantize_q4": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "q4b_unpack_q4": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "q4b_dequantize_q4": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_void_p]),
+    "q4b_q4_linear_workspace": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_void_p]),
+    "q4b_q4_linear": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
+                              c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
+}
+
+_lib = None
+
+
+def lib():
+    """Load libq4b.so once; raise if it is missing (no CPU fallback exists)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"libq4b.so not found at {LIB_PATH}; build it with "
+                              f"`make -C iree-adreno-genai-tuner_b200/csrc` or __graft_entry__.build()")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int, what: str):
+    if rc != Q4B_OK:
+        raise Q4BError(rc, f"{what}: {lib().q4b_last_error().decode(errors='replace')}")

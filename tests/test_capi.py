@@ -1,0 +1,91 @@
+"""CPU-side checks of the C ABI: the library loads, exports every symbol include/q4b.h declares,
+and rejects bad arguments on the host before any launch (no GPU needed)."""
+
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parents[1]
+
+
+def header_symbols():
+    text = (ROOT / "include" / "q4b.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(q4b_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def L():
+    from q4b import _lib
+    return _lib.lib()
+
+
+def test_header_symbols_exported(L):
+    syms = header_symbols()
+    assert len(syms) >= 7
+    missing = [s for s in syms if not hasattr(L, s)]
+    assert not missing, missing
+
+
+def test_bindings_cover_header():
+    from q4b import _lib
+    assert set(header_symbols()) == set(_lib.SIGNATURES)
+
+
+def test_abi_version(L):
+    assert L.q4b_abi_version() == 1
+
+
+def test_linear_rejects_bad_args_on_host(L):
+    from q4b import _lib
+    p = ctypes.c_void_p(16)  # never dereferenced: validation fails first
+    # null pointers
+    assert L.q4b_q4_linear(None, p, 128, p, 0, p, 0, 1, 16, 128, 0, None, None, 0, None) == _lib.Q4B_EINVAL
+    assert b"null" in L.q4b_last_error()
+    # K not a multiple of the group
+    assert L.q4b_q4_linear(p, p, 128, p, 0, p, 0, 1, 16, 200, 0, None, None, 0, None) == _lib.Q4B_EINVAL
+    assert b"group" in L.q4b_last_error()
+    # bad dtype, bad epilogue, odd rows for SwiGLU
+    assert L.q4b_q4_linear(p, p, 128, p, 7, p, 0, 1, 16, 128, 0, None, None, 0, None) == _lib.Q4B_EINVAL
+    assert L.q4b_q4_linear(p, p, 128, p, 0, p, 0, 1, 16, 128, 9, None, None, 0, None) == _lib.Q4B_EINVAL
+    assert L.q4b_q4_linear(p, p, 128, p, 0, p, 0, 1, 15, 128, 2, None, None, 0, None) == _lib.Q4B_EINVAL
+    # tensor-core kernel forced on a group it cannot handle
+    cfg = _lib.LinearCfg(kernel=1)
+    assert L.q4b_q4_linear(p, p, 32, p, 0, p, 0, 1, 16, 128, 0, ctypes.byref(cfg), None, 0,
+                           None) == _lib.Q4B_EUNSUPPORTED
+    # split that cannot be covered by warps * tiles
+    cfg = _lib.LinearCfg(kernel=1, warps=1, tiles=1, split=2)
+    assert L.q4b_q4_linear(p, p, 128, p, 0, p, 0, 1, 16, 3072, 0, ctypes.byref(cfg), None, 0,
+                           None) == _lib.Q4B_EINVAL
+
+
+def test_pack_rejects_bad_args_on_host(L):
+    from q4b import _lib
+    p = ctypes.c_void_p(16)
+    assert L.q4b_quantize_q4(p, 4, 100, 32, p, p, None) == _lib.Q4B_EINVAL
+    assert L.q4b_quantize_q4(p, 4, 96, 12, p, p, None) == _lib.Q4B_EINVAL
+    assert L.q4b_unpack_q4(p, 4, 12, p, None) == _lib.Q4B_EINVAL
+    assert L.q4b_dequantize_q4(p, p, 4, 128, 128, p, 5, None) == _lib.Q4B_EINVAL
+
+
+def test_linear_workspace_plan(L):
+    # 5120 x 3072, group 128, M = 1: split-K over 24 tiles of 128 -> partials + counters
+    ws = L.q4b_q4_linear_workspace(1, 5120, 3072, 128, 0, None)
+    assert ws > 0 and ws % 256 == 0
+    # a non-128 group uses the SIMT kernel, which needs no workspace
+    assert L.q4b_q4_linear_workspace(1, 256, 688, 16, 0, None) == 0
+    # a configuration without split needs none
+    from q4b import _lib
+    cfg = _lib.LinearCfg(kernel=1, warps=8, tiles=3, split=1)
+    assert L.q4b_q4_linear_workspace(1, 5120, 3072, 128, 0, ctypes.byref(cfg)) == 0
+
+
+def test_no_cpu_fallback_without_gpu():
+    """The product ops refuse CPU tensors instead of computing on the host."""
+    import torch
+
+    from q4b import ops
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.unpack_q4(torch.zeros(4, 4, dtype=torch.int32))
