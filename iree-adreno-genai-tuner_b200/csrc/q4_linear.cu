@@ -386,9 +386,15 @@ static size_t mma_smem(const Plan& pl, int M, bool xf32) {
   return std::max(stage, red);
 }
 
+// Workspace layout: [0, kCounterBytes) arrival counters, one per row tile, at a fixed place for
+// every call (each call leaves the counters it used at zero, so calls with different plans can
+// share one workspace), then the split-K partial sums of the current call.
+constexpr size_t kCounterBytes = 64 * 1024;
+constexpr int kMaxCounters = (int)(kCounterBytes / 4);
+
 static size_t mma_ws(const Plan& pl, int M) {
   if (pl.nsplit <= 1) return 0;
-  return align_up((size_t)pl.nsplit * M * pl.RT * 16 * 4, 256) + align_up((size_t)pl.RT * 4, 256);
+  return kCounterBytes + align_up((size_t)pl.nsplit * M * pl.RT * 16 * 4, 256);
 }
 
 // Tuned default: keep ~2 KB of weights per warp in flight and enough CTAs to fill 148 SMs several
@@ -433,7 +439,14 @@ static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, const q4b
     if (pl.kps > W * T)
       return set_error(Q4B_EINVAL, "q4_linear: split %d leaves %d tiles per CTA > warps*tiles %d", s, pl.kps, W * T);
     pl.smem = mma_smem(pl, M, xf32);
-    if (pl.smem <= kMaxSmem) break;
+    if (pl.smem <= kMaxSmem && (pl.nsplit == 1 || pl.RT <= kMaxCounters)) break;
+    if (pl.smem <= kMaxSmem) {  // too many row tiles for the counter region: no split
+      if (user_shape || (KT + T - 1) / T > 8) return set_error(Q4B_EUNSUPPORTED, "q4_linear: split-K limited to "
+                                                               "%d row tiles", kMaxCounters);
+      W = (KT + T - 1) / T;
+      S = 1;
+      continue;
+    }
     if (user_shape || W == 1) return set_error(Q4B_EUNSUPPORTED, "q4_linear: shared memory plan too large");
     W = W / 2;  // fewer tiles per CTA: a smaller staged slice of x
   }
@@ -550,9 +563,8 @@ extern "C" int q4b_q4_linear(const int32_t* qweight, const uint16_t* scales, int
   a.ws = nullptr;
   a.counters = nullptr;
   if (pl.kernel == 1 && pl.nsplit > 1) {
-    a.ws = reinterpret_cast<float*>(workspace);
-    a.counters = reinterpret_cast<unsigned*>(reinterpret_cast<char*>(workspace) +
-                                             align_up((size_t)pl.nsplit * m * pl.RT * 16 * 4, 256));
+    a.counters = reinterpret_cast<unsigned*>(workspace);
+    a.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kCounterBytes);
   }
   cudaStream_t st = as_stream(stream);
   cudaError_t e;

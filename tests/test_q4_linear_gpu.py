@@ -152,8 +152,14 @@ def test_workspace_counters_return_to_zero(dev):
     from q4b._lib import lib, LinearCfg
     import ctypes
     need = lib().q4b_q4_linear_workspace(1, 1024, 4096, 128, 0, ctypes.byref(LinearCfg(**cfg)))
-    counters = ws[need - 256: need].view(torch.int32)
+    assert need > 65536
+    counters = ws[:65536].view(torch.int32)  # the fixed counter region at the start
     assert int(counters.abs().sum()) == 0
+    # a call with another split plan (different partial-sum size) shares the workspace safely
+    q4b.q4_linear(torch.randn(16, 4096, device=dev), torch.from_numpy(qw).to(dev), torch.from_numpy(s).to(dev), 128,
+                  cfg=dict(kernel=1, warps=1, tiles=1, split=32))
+    torch.cuda.synchronize()
+    assert int(ws[:65536].view(torch.int32).abs().sum()) == 0
     y1 = q4b.q4_linear(x, torch.from_numpy(qw).to(dev), torch.from_numpy(s).to(dev), 128, cfg=cfg)
     assert torch.equal(y0, y1)
 
