@@ -90,6 +90,20 @@ int q4b_q4_linear(const int32_t* qweight, const uint16_t* scales, int group, con
                   void* y, int y_dtype, int m, int n, int k, int epilogue, const q4b_linear_cfg* cfg,
                   void* workspace, size_t workspace_bytes, q4b_stream_t stream);
 
+/* Allocation-free variant of q4b_q4_linear (no counterpart in the reference). For callers that
+ * cannot allocate device memory themselves: hosts that reach this library only through a plain C
+ * FFI with no CUDA allocator of their own, plugins that must not allocate while another framework
+ * owns the device memory pool, and code paths with a fixed memory budget. The split-K workspace is
+ * a static 8 MiB array inside libq4b.so instead of a caller buffer (every GPU that loads the
+ * library holds it until the process exits); the caller still passes x and y. Same arguments and
+ * results as q4b_q4_linear with the default configuration; returns Q4B_EINVAL, before launching
+ * anything, when the problem needs more than 8 MiB of workspace. The first call on a device looks
+ * up the array and zeroes its counters (synchronously); make that first call before any stream
+ * capture. All calls share the one array: calls that overlap on the GPU (other streams, other host
+ * threads) race, so order them on one stream. Never allocates (no cudaMalloc / cudaFree). */
+int q4b_q4_linear_noalloc(const int32_t* qweight, const uint16_t* scales, int group, const void* x, int x_dtype,
+                          void* y, int y_dtype, int m, int n, int k, int epilogue, q4b_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -580,3 +580,50 @@ extern "C" int q4b_q4_linear(const int32_t* qweight, const uint16_t* scales, int
   if (e != cudaSuccess) return set_error(Q4B_ELAUNCH, "q4_linear: launch failed: %s", cudaGetErrorString(e));
   return check_launch("q4_linear");
 }
+
+// ---- allocation-free variant ---------------------------------------------------------------
+// q4b_q4_linear with its split-K workspace in a file-scope device array instead of a caller
+// buffer, for callers that cannot allocate device memory. Host code must not pass the array's
+// name to a kernel (on the host it is only a stand-in symbol): the device address is looked up
+// once per device with cudaGetSymbolAddress and that pointer is what the kernels receive.
+#include <mutex>
+
+namespace q4b {
+constexpr size_t kStaticScratchBytes = 8u << 20;  // 8 MiB: counters (64 KiB) + split-K partials
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+static std::mutex g_scratch_mu;
+static void* g_scratch_ptr[64] = {};  // per device ordinal, filled at set-up
+}  // namespace q4b
+
+extern "C" int q4b_q4_linear_noalloc(const int32_t* qweight, const uint16_t* scales, int group, const void* x,
+                                     int x_dtype, void* y, int y_dtype, int m, int n, int k, int epilogue,
+                                     q4b_stream_t stream) {
+  int rc = validate_linear(qweight, scales, group, x, x_dtype, y, y_dtype, m, n, k, epilogue);
+  if (rc) return rc;
+  const size_t need = q4b_q4_linear_workspace(m, n, k, group, epilogue, nullptr);
+  if (need > kStaticScratchBytes)
+    return set_error(Q4B_EINVAL, "q4_linear_noalloc: this problem needs %zu bytes of workspace, above the %zu-byte "
+                     "static scratch", need, kStaticScratchBytes);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(Q4B_ECUDA, "q4_linear_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(Q4B_EUNSUPPORTED, "q4_linear_noalloc: device ordinal %d", dev);
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {  // set-up, once per device, with that device current
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_static_scratch);
+      if (e != cudaSuccess)
+        return set_error(Q4B_ECUDA, "q4_linear_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      e = cudaMemset(p, 0, kCounterBytes);  // the arrival counters must start at zero
+      if (e == cudaSuccess) e = cudaDeviceSynchronize();
+      if (e != cudaSuccess)
+        return set_error(Q4B_ECUDA, "q4_linear_noalloc: clearing the scratch counters: %s", cudaGetErrorString(e));
+      g_scratch_ptr[dev] = p;
+    }
+    scratch = g_scratch_ptr[dev];
+  }
+  return q4b_q4_linear(qweight, scales, group, x, x_dtype, y, y_dtype, m, n, k, epilogue, nullptr, scratch,
+                       kStaticScratchBytes, stream);
+}

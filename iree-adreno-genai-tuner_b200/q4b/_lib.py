@@ -50,6 +50,8 @@ SIGNATURES = {
     "q4b_q4_linear_workspace": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_void_p]),
     "q4b_q4_linear": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int,
                               c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "q4b_q4_linear_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
+                                      c_int, c_int, c_void_p]),
 }
 
 _lib = None
