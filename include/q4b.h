@@ -104,6 +104,73 @@ int q4b_q4_linear(const int32_t* qweight, const uint16_t* scales, int group, con
 int q4b_q4_linear_noalloc(const int32_t* qweight, const uint16_t* scales, int group, const void* x, int x_dtype,
                           void* y, int y_dtype, int m, int n, int k, int epilogue, q4b_stream_t stream);
 
+/* ---- model pieces (scripts/llm/llama_q4.py:93-142, 199-239) ------------------------------- */
+
+/* QEmbedding.lookup (:106-119): out[c, :] = dequantised row tokens[c] of the [vocab, dim] table, or
+ * zeros for ids outside [0, vocab). tokens are device int32; out fp32 [n_tokens, dim], 16-B aligned. */
+int q4b_embed_q4_lookup(const int32_t* tokens, int n_tokens, const int32_t* qweight, const uint16_t* scales,
+                        int vocab, int dim, int group, float* out, q4b_stream_t stream);
+
+/* rms_norm (:141-142): out = x * 1/sqrt(mean(x^2) + eps) * weight, fp32 [rows, dim]. */
+int q4b_rmsnorm(const float* x, const float* weight, float eps, int rows, int dim, float* out, q4b_stream_t stream);
+
+/* Bucketed GQA attention (:208-232) for n_rows query rows at positions *start + r over the fp16
+ * caches [max_ctx, n_kv_heads, head_dim]: keys 0..min(L, pos+1)-1 (the causal mask key <= pos on
+ * cache[:L]). q fp32 [n_rows, n_heads, head_dim] with RoPE applied; out fp32 [n_rows, n_heads *
+ * head_dim]. start is a device int32. head_dim 32, 64 or 128. Few rows (n_rows * heads per KV head
+ * <= 16) use the split-key form, which needs q4b_attention_workspace() bytes, zero-filled once. */
+size_t q4b_attention_workspace(int n_rows, int n_heads, int n_kv_heads, int head_dim, int L);
+int q4b_attention(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* start, int n_rows,
+                  int n_heads, int n_kv_heads, int head_dim, int L, float* out, void* workspace,
+                  size_t workspace_bytes, q4b_stream_t stream);
+
+/* ---- LlamaQ4 model (scripts/llm/llama_q4.py:145-243) --------------------------------------- */
+
+typedef struct q4b_model_cfg {
+  int n_layers, dim, n_heads, n_kv_heads, head_dim, inter, vocab;
+  float rms_eps;
+  int max_ctx;    /* KV cache rows (positions) */
+  int max_chunk;  /* most rows in one step (prefill chunk) */
+  int tp_rank, tp_size; /* tensor-parallel shard of this process (0, 1 on one GPU) */
+} q4b_model_cfg;
+
+/* One quantised matrix: qweight [n, k/8] int32, scales [n, k/group] fp16, device pointers. */
+typedef struct q4b_qmat {
+  const int32_t* qweight;
+  const uint16_t* scales;
+  int n, k, group;
+} q4b_qmat;
+
+/* Layer weights (:145-155) of this rank's shard: wqkv rows q|k|v of its heads, wo [dim, heads*hd],
+ * wgu rows gate|up of its slice of the intermediate size, wdown [dim, inter/tp]; fp32 norm weights;
+ * fp16 KV caches [max_ctx, n_kv_heads/tp, head_dim] (updated in place, :222-223). Borrowed. */
+typedef struct q4b_layer_weights {
+  q4b_qmat wqkv, wo, wgu, wdown;
+  const float* ln_in;
+  const float* ln_post;
+  uint16_t* k_cache;
+  uint16_t* v_cache;
+} q4b_layer_weights;
+
+typedef struct q4b_model q4b_model;
+
+/* Allocates the model's activations and workspaces on the current device (no weights). */
+int q4b_model_create(const q4b_model_cfg* cfg, q4b_model** out);
+int q4b_model_set_layer(q4b_model* model, int layer, const q4b_layer_weights* weights);
+/* Tied embedding / lm_head: the full [vocab, dim] table on every rank (rank r's lm_head uses rows
+ * [r*vocab/tp, (r+1)*vocab/tp)); final norm weight; RoPE tables cos, sin [max_ctx, head_dim] fp32. */
+int q4b_model_set_head(q4b_model* model, const q4b_qmat* embed, const float* ln_f, const float* rope_cos,
+                       const float* rope_sin);
+/* LlamaQ4.step (:199-239): tokens [n_tokens] device int32 at positions start.., KV written in place,
+ * attention over the bucket L; the greedy token of row `last` goes to *next_token (device, may be
+ * NULL) and the row's logits to logits (device fp32 [vocab], may be NULL). */
+int q4b_model_step(q4b_model* model, const int32_t* tokens, int n_tokens, int start, int last, int L,
+                   int32_t* next_token, float* logits, q4b_stream_t stream);
+void q4b_model_destroy(q4b_model* model);
+
+/* Q4B_ETIMEOUT if a bounded device-side wait gave up since the last reset, else Q4B_OK. */
+int q4b_device_status(int reset);
+
 #ifdef __cplusplus
 }
 #endif

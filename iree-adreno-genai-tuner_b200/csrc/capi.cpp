@@ -3,6 +3,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <string>
 
 #include "q4b.h"
@@ -22,6 +23,14 @@ int set_error(int code, const char* fmt, ...) {
 }
 
 void clear_error() { g_last_error.clear(); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("Q4B_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();

@@ -1,0 +1,364 @@
+// Elementwise and attention kernels of the LlamaQ4 step (scripts/llm/llama_q4.py:199-239):
+//   embed_q4_lookup   QEmbedding.lookup (:106-119): dequantised rows, zero for ids outside the vocab
+//   rmsnorm           rms_norm (:141-142)
+//   attention         GQA over the fp16 cache with the causal mask key_pos <= pos (:208-232),
+//                     reading only keys that can be unmasked (< min(L, pos + 1)): masked scores are
+//                     -1e30 in the reference and contribute exactly 0 after the softmax.
+//     decode form   (few query rows): split over key chunks; each CTA keeps an online softmax
+//                   (max, sum, weighted V) per query row; the last CTA of a KV head (arrival
+//                   counter) merges the chunks in chunk order.
+//     prefill form  one warp per (query row, head), online softmax over the row's keys.
+#include "fused.h"
+
+namespace q4b {
+
+// ---- embedding ----------------------------------------------------------------------------
+
+__global__ void embed_q4_kernel(const int32_t* __restrict__ tokens, int C, const int32_t* __restrict__ qw,
+                                const __half* __restrict__ scales, int vocab, int dim, int group, float* __restrict__ out) {
+  griddep_launch_dependents();
+  griddep_wait();
+  const int c = blockIdx.x;
+  const int t = tokens[c];
+  const bool valid = t >= 0 && t < vocab;
+  const int words = dim / 8, KG = dim / group;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) {
+    float v[8];
+    if (valid) {
+      const int32_t word = qw[(size_t)t * words + w];
+      const float s = __half2float(scales[(size_t)t * KG + (8 * w) / group]);
+#pragma unroll
+      for (int b = 0; b < 8; ++b) v[b] = (float)(((word >> (4 * b)) & 15) - 8) * s;
+    } else {
+#pragma unroll
+      for (int b = 0; b < 8; ++b) v[b] = 0.0f;
+    }
+    float4* o = reinterpret_cast<float4*>(out + (size_t)c * dim + 8 * w);
+    o[0] = make_float4(v[0], v[1], v[2], v[3]);
+    o[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+
+// ---- rmsnorm ------------------------------------------------------------------------------
+
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, float eps, int dim,
+                               const int32_t* __restrict__ row_sel, float* __restrict__ out) {
+  __shared__ float red[32];
+  griddep_launch_dependents();
+  griddep_wait();
+  const int r = blockIdx.x;
+  const float* xr = x + (size_t)((row_sel ? *row_sel : 0) + r) * dim;
+  float ss = 0.0f;
+  for (int k = threadIdx.x; k < dim; k += blockDim.x) ss += xr[k] * xr[k];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = 1.0f / sqrtf(v / (float)dim + eps);
+  }
+  __syncthreads();
+  const float rs = red[0];
+  for (int k = threadIdx.x; k < dim; k += blockDim.x) out[(size_t)r * dim + k] = xr[k] * rs * w[k];
+}
+
+// ---- attention ------------------------------------------------------------------------------
+
+constexpr int kMaxRows = 16;  // decode form: at most this many query rows (tokens x heads per KV head)
+constexpr int kChunk = 64;    // decode form: keys per CTA
+
+template <int EPL>
+__device__ __forceinline__ void load_half_vec(const __half* p, float (&v)[EPL]) {
+  if constexpr (EPL == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    v[0] = a.x;
+    v[1] = a.y;
+    v[2] = b.x;
+    v[3] = b.y;
+  } else if constexpr (EPL == 2) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(p));
+    v[0] = a.x;
+    v[1] = a.y;
+  } else {
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) v[e] = __half2float(p[e]);
+  }
+}
+
+// grid (Hkv, nchunk), block 128. Query row r of KV head kvh: token c = r / g, head kvh*g + r % g.
+// ROWS >= C * g query rows are kept in registers.
+template <int EPL, int ROWS>
+__global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
+  constexpr int HD = EPL * 32;
+  constexpr int kMaxRows = ROWS;
+  __shared__ float s_m[4][kMaxRows], s_l[4][kMaxRows];
+  __shared__ float s_o[4][kMaxRows][HD];
+  __shared__ int s_last;
+  const int kvh = blockIdx.x, chunk = blockIdx.y, nchunk = gridDim.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = a.H / a.Hkv;
+  const int R = a.C * g;
+  griddep_launch_dependents();
+  griddep_wait();
+  const int start = *a.pos0;
+  const int kend_cta = min(a.L, start + a.C);  // keys any row of this step can see
+  const int k0 = chunk * kChunk, k1 = min(k0 + kChunk, kend_cta);
+  const float scale = a.scale;
+
+  // q rows in registers (lane holds elements lane*EPL .. +EPL of each row)
+  float q[kMaxRows][EPL];
+  int nk[kMaxRows];
+#pragma unroll
+  for (int r = 0; r < kMaxRows; ++r) {
+    if (r < R) {
+      const int c = r / g, h = kvh * g + r % g;
+      const float* qp = a.q + ((size_t)c * a.H + h) * HD + lane * EPL;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) q[r][e] = qp[e];
+      nk[r] = min(a.L, start + c + 1);
+    } else {
+      nk[r] = 0;
+    }
+  }
+  float m[kMaxRows], l[kMaxRows], o[kMaxRows][EPL];
+#pragma unroll
+  for (int r = 0; r < kMaxRows; ++r) {
+    m[r] = -INFINITY;
+    l[r] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) o[r][e] = 0.0f;
+  }
+  const size_t kv_stride = (size_t)a.Hkv * HD;
+  for (int j = k0 + warp; j < k1; j += 4) {
+    float kv[EPL], vv[EPL];
+    load_half_vec<EPL>(a.k_cache + (size_t)j * kv_stride + (size_t)kvh * HD + lane * EPL, kv);
+    load_half_vec<EPL>(a.v_cache + (size_t)j * kv_stride + (size_t)kvh * HD + lane * EPL, vv);
+#pragma unroll
+    for (int r = 0; r < kMaxRows; ++r) {
+      if (r < R) {
+        float d = 0.0f;
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) d = fmaf(q[r][e], kv[e], d);
+        d = warp_sum(d) * scale;
+        if (j < nk[r]) {
+          const float mn = fmaxf(m[r], d);
+          const float cs = expf(m[r] - mn), p = expf(d - mn);
+          l[r] = l[r] * cs + p;
+#pragma unroll
+          for (int e = 0; e < EPL; ++e) o[r][e] = o[r][e] * cs + p * vv[e];
+          m[r] = mn;
+        }
+      }
+    }
+  }
+  // merge the 4 warps
+#pragma unroll
+  for (int r = 0; r < kMaxRows; ++r) {
+    if (r < R) {
+      if (lane == 0) {
+        s_m[warp][r] = m[r];
+        s_l[warp][r] = l[r];
+      }
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) s_o[warp][r][lane * EPL + e] = o[r][e];
+    }
+  }
+  __syncthreads();
+  float* part = a.ws + ((size_t)kvh * nchunk + chunk) * R * (HD + 2);  // [R][m, l, o[HD]]
+  for (int i = threadIdx.x; i < R * HD; i += blockDim.x) {
+    const int r = i / HD, e = i - r * HD;
+    float mm = -INFINITY;
+    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, s_m[w][r]);
+    float ll = 0.0f, oo = 0.0f;
+    for (int w = 0; w < 4; ++w) {
+      if (s_m[w][r] == -INFINITY) continue;
+      const float cs = expf(s_m[w][r] - mm);
+      ll += s_l[w][r] * cs;
+      oo += s_o[w][r][e] * cs;
+    }
+    part[r * (HD + 2) + 2 + e] = oo;
+    if (e == 0) {
+      part[r * (HD + 2)] = mm;
+      part[r * (HD + 2) + 1] = ll;
+    }
+  }
+  // the last chunk CTA of this KV head merges all chunks in order
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[kvh], 1u) == (unsigned)(nchunk - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float* all = a.ws + (size_t)kvh * nchunk * R * (HD + 2);
+  for (int i = threadIdx.x; i < R * HD; i += blockDim.x) {
+    const int r = i / HD, e = i - r * HD;
+    float mm = -INFINITY;
+    for (int ch = 0; ch < nchunk; ++ch) mm = fmaxf(mm, __ldcg(all + ((size_t)ch * R + r) * (HD + 2)));
+    float ll = 0.0f, oo = 0.0f;
+    for (int ch = 0; ch < nchunk; ++ch) {
+      const float* pp = all + ((size_t)ch * R + r) * (HD + 2);
+      const float mc = __ldcg(pp);
+      if (mc == -INFINITY) continue;
+      const float cs = expf(mc - mm);
+      ll += __ldcg(pp + 1) * cs;
+      oo += __ldcg(pp + 2 + e) * cs;
+    }
+    const int c = r / g, h = kvh * g + r % g;
+    a.out[((size_t)c * a.H + h) * HD + e] = oo / ll;
+  }
+  if (threadIdx.x == 0) a.counters[kvh] = 0u;
+}
+
+// grid (H, ceil(C / 4)), block 128: warp w handles query row 4 * blockIdx.y + w of head blockIdx.x.
+template <int EPL>
+__global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
+  constexpr int HD = EPL * 32;
+  const int h = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.y * 4 + warp;
+  griddep_launch_dependents();
+  griddep_wait();
+  if (c >= a.C) return;
+  const int g = a.H / a.Hkv, kvh = h / g;
+  const int start = *a.pos0;
+  const int nk = min(a.L, start + c + 1);
+  float q[EPL], o[EPL];
+  const float* qp = a.q + ((size_t)c * a.H + h) * HD + lane * EPL;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) {
+    q[e] = qp[e];
+    o[e] = 0.0f;
+  }
+  float m = -INFINITY, l = 0.0f;
+  const size_t kv_stride = (size_t)a.Hkv * HD;
+  const __half* kb = a.k_cache + (size_t)kvh * HD + lane * EPL;
+  const __half* vb = a.v_cache + (size_t)kvh * HD + lane * EPL;
+#pragma unroll 4
+  for (int j = 0; j < nk; ++j) {
+    float kv[EPL], vv[EPL];
+    load_half_vec<EPL>(kb + (size_t)j * kv_stride, kv);
+    load_half_vec<EPL>(vb + (size_t)j * kv_stride, vv);
+    float d = 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) d = fmaf(q[e], kv[e], d);
+    d = warp_sum(d) * a.scale;
+    const float mn = fmaxf(m, d);
+    const float cs = expf(m - mn), p = expf(d - mn);
+    l = l * cs + p;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) o[e] = o[e] * cs + p * vv[e];
+    m = mn;
+  }
+  float* op = a.out + ((size_t)c * a.H + h) * HD + lane * EPL;
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) op[e] = o[e] / l;
+}
+
+int attn_decode_chunks(int L) { return (L + kChunk - 1) / kChunk; }
+
+template <int ROWS>
+static cudaError_t launch_decode(const AttnArgs& a, dim3 grid, cudaStream_t st) {
+  switch (a.head_dim) {
+    case 32: return launch_pdl(attn_decode_kernel<1, ROWS>, grid, dim3(128), 0, st, a);
+    case 64: return launch_pdl(attn_decode_kernel<2, ROWS>, grid, dim3(128), 0, st, a);
+    default: return launch_pdl(attn_decode_kernel<4, ROWS>, grid, dim3(128), 0, st, a);
+  }
+}
+
+size_t attention_workspace(int C, int H, int Hkv, int head_dim, int L) {
+  const int g = H / Hkv;
+  if (C * g > kMaxRows) return 0;
+  return kCounterRegion + (size_t)Hkv * attn_decode_chunks(L) * C * g * (head_dim + 2) * sizeof(float);
+}
+
+int attention_run(const AttnArgs& in, cudaStream_t st) {
+  AttnArgs a = in;
+  const int g = a.H / a.Hkv;
+  if (a.H % a.Hkv || (a.head_dim != 32 && a.head_dim != 64 && a.head_dim != 128))
+    return set_error(Q4B_EUNSUPPORTED, "attention: head_dim must be 32, 64 or 128 and H %% Hkv == 0");
+  const bool decode = a.C * g <= kMaxRows;
+  cudaError_t e;
+  if (decode) {
+    const size_t need = attention_workspace(a.C, a.H, a.Hkv, a.head_dim, a.L);
+    if (!a.ws_base || a.ws_bytes < need)
+      return set_error(Q4B_EINVAL, "attention: workspace of %zu bytes needed, %zu given", need, a.ws_bytes);
+    a.counters = reinterpret_cast<unsigned*>(a.ws_base);
+    a.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(a.ws_base) + kCounterRegion);
+    const dim3 grid(a.Hkv, attn_decode_chunks(a.L));
+    const int R = a.C * g;
+    e = R <= 4 ? launch_decode<4>(a, grid, st) : R <= 8 ? launch_decode<8>(a, grid, st) : launch_decode<16>(a, grid, st);
+  } else {
+    const dim3 grid(a.H, (a.C + 3) / 4);
+    switch (a.head_dim) {
+      case 32: e = launch_pdl(attn_prefill_kernel<1>, grid, dim3(128), 0, st, a); break;
+      case 64: e = launch_pdl(attn_prefill_kernel<2>, grid, dim3(128), 0, st, a); break;
+      default: e = launch_pdl(attn_prefill_kernel<4>, grid, dim3(128), 0, st, a); break;
+    }
+  }
+  if (e != cudaSuccess) return set_error(Q4B_ELAUNCH, "attention: launch failed: %s", cudaGetErrorString(e));
+  return check_launch("attention");
+}
+
+int embed_run(const int32_t* tokens, int C, const int32_t* qw, const uint16_t* scales, int vocab, int dim, int group,
+              float* out, cudaStream_t st) {
+  if (dim % 8 || dim % group || group % 8) return set_error(Q4B_EINVAL, "embed: bad dim/group");
+  const cudaError_t e = launch_pdl(embed_q4_kernel, dim3(C), dim3(128), 0, st, tokens, C, qw,
+                                   reinterpret_cast<const __half*>(scales), vocab, dim, group, out);
+  if (e != cudaSuccess) return set_error(Q4B_ELAUNCH, "embed: launch failed: %s", cudaGetErrorString(e));
+  return check_launch("embed");
+}
+
+int rmsnorm_run(const float* x, const float* w, float eps, int rows, int dim, const int32_t* row_sel, float* out,
+                cudaStream_t st) {
+  const cudaError_t e = launch_pdl(rmsnorm_kernel, dim3(rows), dim3(256), 0, st, x, w, eps, dim, row_sel, out);
+  if (e != cudaSuccess) return set_error(Q4B_ELAUNCH, "rmsnorm: launch failed: %s", cudaGetErrorString(e));
+  return check_launch("rmsnorm");
+}
+
+}  // namespace q4b
+
+using namespace q4b;
+
+extern "C" int q4b_embed_q4_lookup(const int32_t* tokens, int n_tokens, const int32_t* qweight, const uint16_t* scales,
+                                   int vocab, int dim, int group, float* out, q4b_stream_t stream) {
+  if (!tokens || !qweight || !scales || !out || n_tokens < 1 || vocab < 1 || dim < 8)
+    return set_error(Q4B_EINVAL, "embed_q4_lookup: bad arguments");
+  if (!aligned(out, 16)) return set_error(Q4B_EINVAL, "embed_q4_lookup: out must be 16-byte aligned");
+  return embed_run(tokens, n_tokens, qweight, scales, vocab, dim, group, out, as_stream(stream));
+}
+
+extern "C" int q4b_rmsnorm(const float* x, const float* weight, float eps, int rows, int dim, float* out,
+                           q4b_stream_t stream) {
+  if (!x || !weight || !out || rows < 1 || dim < 1) return set_error(Q4B_EINVAL, "rmsnorm: bad arguments");
+  return rmsnorm_run(x, weight, eps, rows, dim, nullptr, out, as_stream(stream));
+}
+
+extern "C" size_t q4b_attention_workspace(int n_rows, int n_heads, int n_kv_heads, int head_dim, int L) {
+  if (n_rows < 1 || n_heads < 1 || n_kv_heads < 1 || n_heads % n_kv_heads) return 0;
+  return attention_workspace(n_rows, n_heads, n_kv_heads, head_dim, L);
+}
+
+extern "C" int q4b_attention(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* start,
+                             int n_rows, int n_heads, int n_kv_heads, int head_dim, int L, float* out,
+                             void* workspace, size_t workspace_bytes, q4b_stream_t stream) {
+  if (!q || !k_cache || !v_cache || !start || !out || n_rows < 1 || L < 1)
+    return set_error(Q4B_EINVAL, "attention: bad arguments");
+  AttnArgs a = {};
+  a.q = q;
+  a.k_cache = reinterpret_cast<const __half*>(k_cache);
+  a.v_cache = reinterpret_cast<const __half*>(v_cache);
+  a.pos0 = start;
+  a.C = n_rows;
+  a.H = n_heads;
+  a.Hkv = n_kv_heads;
+  a.head_dim = head_dim;
+  a.L = L;
+  a.scale = (float)(1.0 / sqrt((double)head_dim));  // the reference's 1 / math.sqrt(hd) in fp32
+  a.out = out;
+  a.ws_base = workspace;
+  a.ws_bytes = workspace_bytes;
+  return attention_run(a, as_stream(stream));
+}

@@ -1,0 +1,44 @@
+// Internal model object behind the q4b_model_* C ABI (model.cu), also used by the runner.
+#pragma once
+
+#include <vector>
+
+#include "linear.h"
+
+struct ncclComm;
+
+namespace q4b {
+
+struct Model {
+  q4b_model_cfg cfg{};
+  int H = 0, Hkv = 0, I = 0, V = 0, D = 0, hd = 0;  // per-rank (sharded) sizes
+  std::vector<q4b_layer_weights> layers;
+  q4b_qmat embed{};
+  const float* ln_f = nullptr;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  // owned device memory
+  DecodeState* state = nullptr;
+  int32_t* tokens = nullptr;
+  float *h = nullptr, *xn = nullptr, *q = nullptr, *o = nullptr, *a = nullptr, *y = nullptr;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  void* attn_ws = nullptr;
+  size_t attn_ws_bytes = 0;
+  std::vector<void*> owned;
+  // tensor parallelism (tp.cu)
+  ncclComm* comm = nullptr;
+  unsigned long long* gather = nullptr;  // [tp_size] per-rank argmax keys
+
+  ~Model();
+  int alloc(void** p, size_t bytes, bool zero);
+  int init(const q4b_model_cfg& c);
+  int check_ready() const;
+  int forward(const int32_t* toks, int C, int L, float* logits, int32_t* token_log, cudaStream_t st);
+  int residual_linear(const q4b_qmat& w, const float* x, int k, int C, cudaStream_t st);
+  int step(const int32_t* toks, int C, int start, int last, int L, int32_t* next, float* logits, cudaStream_t st);
+  int tp_allreduce_add(int C, cudaStream_t st);
+  int tp_finish_argmax(int32_t* token_log, cudaStream_t st);
+};
+
+}  // namespace q4b

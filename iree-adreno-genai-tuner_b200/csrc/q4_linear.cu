@@ -1,26 +1,32 @@
-// int4 weight-only linear: QLinear.forward of scripts/llm/llama_q4.py:69-90.
+// int4 weight-only linear: QLinear.forward of scripts/llm/llama_q4.py:69-90,
 //
 //   y[m, n] = sum_k x[m, k] * (nib(n, k) - 8) * scale(n, k / G)          (fp32 accumulation)
 //
-// Two kernels:
-//   q4_gemv_mma   G % 128 == 0, M <= 64: decode GEMV / small-M batch on the tensor cores
-//                 (mma.sync m16n8k16, fp16 operands, fp32 accumulate). A warp owns a 16-row x 128-k
-//                 tile; every lane issues two 16-byte streaming loads per tile (rows g and g + 8 of
-//                 the tile, 64 contiguous bytes per 4 lanes), all of a warp's tiles before any math.
-//                 Nibbles become fp16 (nib - 8) exactly with two LOP3 + one HSUB2/HFMA2 per pair;
-//                 the k order inside a word is permuted (slots hold nibbles b and b + 4) and x is
-//                 staged in shared memory in the same permuted order, so no shuffle is needed.
-//                 One 128-k tile lies inside one scale group, so the tile's MMA sum is scaled once
-//                 in fp32. fp32 x is split into hi + lo fp16 terms (two MMAs), keeping ~22 bits.
-//                 Split-K partials go to a workspace; the last CTA of a row tile (arrival counter)
-//                 sums them in a fixed order, so results are deterministic.
-//   q4_linear_simt any G % 8 == 0: one warp per output row (and up to 8 batch rows), fp32 FMAs on
-//                 the exactly dequantised weights (the reference's dequant + linear form).
-// Both start streaming weights before griddepcontrol.wait (programmatic dependent launch), so the
-// weight reads of one projection overlap the tail of the kernel before it.
+// with the model's neighbouring elementwise work fused in (prologue: RMSNorm of x,
+// llama_q4.py:141-142; epilogues: residual add :233/:236, SwiGLU :235-236, RoPE + KV-cache write
+// :219-223, greedy argmax :238-239).
+//
+// Every kernel works on tiles of 16 weight rows ("slots") x its k-range. Slot -> row maps:
+//   plain/accumulate: row = 16 rt + s;   SwiGLU: s < 8 gate row 8 rt + s, s >= 8 up row I + 8 rt + s - 8;
+//   RoPE: head rt / (hd/16), slots s and s + 8 hold head elements e and e + hd/2 (a rotation pair).
+// Kernels:
+//   1 q4_gemv_reg  G % 128 == 0, M <= 64: mma.sync m16n8k16 (fp16 operands, fp32 accumulate). Each
+//                  lane keeps T 128-k tiles of rows g and g + 8 in registers (two 16-byte streaming
+//                  loads per tile, 64 contiguous bytes per 4 lanes), all issued before
+//                  griddepcontrol.wait. Nibbles become exact fp16 (nib - 8) with LOP3 + HSUB2/HFMA2;
+//                  inside a word the k order is permuted (MMA k-slots hold nibbles b and b + 4) and x
+//                  is staged in shared memory in the same order. A 128-k tile lies inside one scale
+//                  group, so each tile's MMA sum is scaled once in fp32. fp32 x is split into two fp16
+//                  terms (hi + lo), keeping ~22 bits of x.
+//   3 q4_gemv_tma  the same math with the weight tile streamed into shared memory by the TMA engine
+//                  (one bulk copy per row, one mbarrier, bounded wait), M <= 16.
+//   2 q4_linear_simt any G % 8 == 0: fp32 FMAs on exactly dequantised weights (the reference's
+//                  dequant + linear form).
+// Split-K partials go to a workspace; the last CTA of a row tile (arrival counter) sums them in
+// split order, so results are deterministic.
 #include <algorithm>
 
-#include "common.cuh"
+#include "linear.h"
 
 namespace q4b {
 
@@ -39,7 +45,31 @@ struct LinArgs {
   int nsplit;  // k splits
   int epi;
   int y_f32;
+  int wstride;  // TMA kernel: bytes per staged weight row
+  int x_off;    // TMA kernel: byte offset of the x staging area in dynamic shared memory
+  // prologue
+  const float* ln_w;
+  float eps;
+  const int32_t* row_sel;
+  // RoPE / KV
+  const float* rope_cos;
+  const float* rope_sin;
+  const int32_t* pos0;
+  int pos_offset;
+  float* q_out;
+  __half* k_cache;
+  __half* v_cache;
+  int H, Hkv, hd;
+  // argmax
+  DecodeState* state;
+  int32_t* token_log;
+  float* logits;
+  int index_offset;
+  int finalize;
 };
+
+// status word of this file's kernels (bounded waits that gave up), read by linear_status()
+__device__ unsigned g_linear_status;
 
 // ---- PTX helpers ---------------------------------------------------------------------------
 
@@ -63,10 +93,10 @@ __device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) 
 // OR-ing a nibble into the mantissa of 1024.0 (0x6400) gives 1024 + nib; nibbles taken in place at
 // bits 4..7 give 1024 + 16 nib, rescaled by an exact FMA.
 __device__ __forceinline__ void dequant_word(uint32_t w, uint32_t (&o)[4]) {
-  const uint32_t kMagic = 0x64006400u;   // 1024.0 | 1024.0
-  const uint32_t k1032 = 0x64086408u;    // 1032.0
+  const uint32_t kMagic = 0x64006400u;      // 1024.0 | 1024.0
+  const uint32_t k1032 = 0x64086408u;       // 1032.0
   const uint32_t kSixteenth = 0x2C002C00u;  // 0.0625
-  const uint32_t kNeg72 = 0xD480D480u;   // -72.0
+  const uint32_t kNeg72 = 0xD480D480u;      // -72.0
   const uint32_t w8 = w >> 8;
   o[0] = hsub2_u(lop_and_or(w, 0x000F000Fu, kMagic), k1032);
   o[1] = hfma2_u(lop_and_or(w, 0x00F000F0u, kMagic), kSixteenth, kNeg72);
@@ -111,28 +141,281 @@ __device__ __forceinline__ void store_y(void* y, size_t i, float v, int f32) {
     reinterpret_cast<__half*>(y)[i] = __float2half_rn(v);
 }
 
-// ---- tensor-core kernel --------------------------------------------------------------------
+// ---- tile geometry, prologue, epilogue (shared by all kernels) ------------------------------
 
-template <int MT, bool XF32, int T>
-__global__ void __launch_bounds__(256) q4_gemv_mma(LinArgs p) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  __shared__ int s_last;
+__device__ __forceinline__ int tile_row(const LinArgs& p, int rt, int s) {
+  if (p.epi == EPI_SWIGLU) {
+    const int i = min(rt * 8 + (s & 7), p.n_out - 1);
+    return s < 8 ? i : p.n_out + i;
+  }
+  if (p.epi == EPI_ROPE_KV) {
+    const int per = p.hd / 16;
+    const int head = rt / per, j = rt - head * per;
+    const int e = s < 8 ? j * 8 + s : p.hd / 2 + j * 8 + (s - 8);
+    return min(head * p.hd + e, p.N - 1);
+  }
+  return min(rt * 16 + s, p.N - 1);
+}
+
+__device__ __forceinline__ int x_row(const LinArgs& p, int m) { return (p.row_sel ? *p.row_sel : 0) + m; }
+
+// RMSNorm prologue: rs[m] = 1 / sqrt(mean(x[row m]^2) + eps) over the full row (M <= 8).
+// Must be called by every thread of the CTA; ends with a barrier.
+__device__ void prologue_rms(const LinArgs& p, float* rs, float* scratch) {
+  const int warps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float part[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) part[m] = 0.0f;
+  const int k4 = p.K / 4;
+  const float* x = reinterpret_cast<const float*>(p.x);
+  for (int i = threadIdx.x; i < p.M * k4; i += blockDim.x) {
+    const int m = i / k4, c = i - m * k4;
+    const float4 v = *reinterpret_cast<const float4*>(x + (size_t)x_row(p, m) * p.K + 4 * c);
+    const float s = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+#pragma unroll
+    for (int mm = 0; mm < 8; ++mm)
+      if (mm == m) part[mm] += s;
+  }
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const float v = warp_sum(part[m]);
+    if (lane == 0) scratch[warp * 8 + m] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < p.M) {
+    float ss = 0.0f;
+    for (int w = 0; w < warps; ++w) ss += scratch[w * 8 + threadIdx.x];
+    rs[threadIdx.x] = 1.0f / sqrtf(ss / (float)p.K + p.eps);
+  }
+  __syncthreads();
+}
+
+// x value after the prologue (SIMT kernel)
+__device__ __forceinline__ float x_value(const LinArgs& p, const float* rs, int m, int k, bool xf32) {
+  const size_t off = (size_t)x_row(p, m) * p.K + k;
+  if (p.ln_w) return reinterpret_cast<const float*>(p.x)[off] * rs[m] * p.ln_w[k];
+  if (xf32) return __ldg(reinterpret_cast<const float*>(p.x) + off);
+  return __half2float(reinterpret_cast<const __half*>(p.x)[off]);
+}
+
+// Stage x[:, kt0*128 : kt0*128 + nwords*8) as permuted fp16 pairs (hi, and lo for fp32 x).
+template <bool XF32>
+__device__ __forceinline__ void stage_x(const LinArgs& p, const float* rs, uint4* xs_hi, uint4* xs_lo, int rstride,
+                                        int kt0, int nwords) {
+  for (int i = threadIdx.x; i < p.M * nwords; i += blockDim.x) {
+    const int m = i / nwords, w = i - m * nwords;
+    const int k0 = kt0 * TILE_K + 8 * w;
+    const size_t kb = (size_t)x_row(p, m) * p.K + k0;
+    uint4 hi;
+    if constexpr (XF32) {
+      float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + kb);
+      float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + kb + 4);
+      if (p.ln_w) {
+        const float r = rs[m];
+        const float4 wa = *reinterpret_cast<const float4*>(p.ln_w + k0);
+        const float4 wb = *reinterpret_cast<const float4*>(p.ln_w + k0 + 4);
+        a.x = a.x * r * wa.x;
+        a.y = a.y * r * wa.y;
+        a.z = a.z * r * wa.z;
+        a.w = a.w * r * wa.w;
+        b.x = b.x * r * wb.x;
+        b.y = b.y * r * wb.y;
+        b.z = b.z * r * wb.z;
+        b.w = b.w * r * wb.w;
+      }
+      uint4 lo;
+      split_pair(a.x, b.x, hi.x, lo.x);  // (x0, x4)
+      split_pair(a.y, b.y, hi.y, lo.y);  // (x1, x5)
+      split_pair(a.z, b.z, hi.z, lo.z);  // (x2, x6)
+      split_pair(a.w, b.w, hi.w, lo.w);  // (x3, x7)
+      xs_lo[m * rstride + xswz(w)] = lo;
+    } else {
+      const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(p.x) + kb);
+      hi.x = __byte_perm(v.x, v.z, 0x5410);
+      hi.y = __byte_perm(v.x, v.z, 0x7632);
+      hi.z = __byte_perm(v.y, v.w, 0x5410);
+      hi.w = __byte_perm(v.y, v.w, 0x7632);
+    }
+    xs_hi[m * rstride + xswz(w)] = hi;
+  }
+}
+
+// Epilogue of one finished tile: fin[m * 16 + s] holds the fp32 dot product of slot s, batch row m.
+__device__ void epilogue_tile(const LinArgs& p, const float* fin, int rt, int* s_flag) {
+  const int items = p.M * 16;
+  if (p.epi == EPI_ARGMAX) {  // m == 1
+    if (threadIdx.x < 16) {
+      const int row = rt * 16 + threadIdx.x;
+      if (row < p.N && p.logits) p.logits[row] = fin[threadIdx.x];
+    }
+    if (threadIdx.x == 0) {
+      unsigned long long best = 0;
+      for (int s = 0; s < 16; ++s) {
+        const int row = rt * 16 + s;
+        if (row < p.N) best = max(best, argmax_key(fin[s], (unsigned)(p.index_offset + row)));
+      }
+      atomicMax(&p.state->best, best);
+      __threadfence();
+      *s_flag = p.finalize && (atomicAdd(&p.state->counter, 1u) == gridDim.x - 1);
+      if (*s_flag) {
+        __threadfence();
+        const unsigned long long b = atomicExch(&p.state->best, 0ull);
+        p.state->counter = 0u;
+        publish_token(p.state, p.token_log, (int32_t)argmax_index(b));
+      }
+    }
+    return;
+  }
+  if (p.epi == EPI_ROPE_KV) {
+    const int per = p.hd / 16;
+    const int head = rt / per, j = rt - head * per;
+    for (int i = threadIdx.x; i < p.M * 8; i += blockDim.x) {
+      const int m = i >> 3, s = i & 7;
+      const int e1 = j * 8 + s, e2 = p.hd / 2 + j * 8 + s;
+      const float x1 = fin[m * 16 + s], x2 = fin[m * 16 + s + 8];
+      const int pos = *p.pos0 + p.pos_offset + m;
+      if (head < p.H + p.Hkv) {
+        // q * cos + rotate_half(q) * sin, rotate_half(x) = cat(-x[h:], x[:h]) (llama_q4.py:195-221)
+        const float* cs = p.rope_cos + (size_t)pos * p.hd;
+        const float* sn = p.rope_sin + (size_t)pos * p.hd;
+        const float o1 = __fadd_rn(__fmul_rn(x1, cs[e1]), __fmul_rn(-x2, sn[e1]));
+        const float o2 = __fadd_rn(__fmul_rn(x2, cs[e2]), __fmul_rn(x1, sn[e2]));
+        if (head < p.H) {
+          float* q = p.q_out + ((size_t)m * p.H + head) * p.hd;
+          q[e1] = o1;
+          q[e2] = o2;
+        } else {
+          __half* kc = p.k_cache + ((size_t)pos * p.Hkv + (head - p.H)) * p.hd;
+          kc[e1] = __float2half_rn(o1);
+          kc[e2] = __float2half_rn(o2);
+        }
+      } else {
+        __half* vc = p.v_cache + ((size_t)pos * p.Hkv + (head - p.H - p.Hkv)) * p.hd;
+        vc[e1] = __float2half_rn(x1);
+        vc[e2] = __float2half_rn(x2);
+      }
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    const int m = i >> 4, s = i & 15;
+    if (p.epi == EPI_SWIGLU) {
+      const int col = rt * 8 + s;
+      if (s < 8 && col < p.n_out) store_y(p.y, (size_t)m * p.n_out + col, silu(fin[i]) * fin[i + 8], p.y_f32);
+    } else {
+      const int col = rt * 16 + s;
+      if (col < p.N) {
+        float v = fin[i];
+        const size_t o = (size_t)m * p.N + col;
+        if (p.epi == EPI_ACCUMULATE) v += load_y(p.y, o, p.y_f32);
+        store_y(p.y, o, v, p.y_f32);
+      }
+    }
+  }
+}
+
+// After the MMAs: sum the warps' accumulators in shared memory (red: W * MT*8 * 16 floats, then
+// fin: M*16 floats, aliasing the x staging area), finish split-K through the workspace (last CTA
+// of a row tile, fixed order), then the epilogue.
+template <int MT>
+__device__ __forceinline__ void finish_tile(const LinArgs& p, float (&acc)[MT][4], float* red, int* s_flag) {
   const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int rt = blockIdx.x, sp = blockIdx.y;
-  const bool swiglu = p.epi == Q4B_EPI_SWIGLU;
-
-  // weight rows feeding A-fragment rows g and g + 8 (SwiGLU: gate row i and up row I + i)
-  int ra, rb;
-  if (swiglu) {
-    const int i = min(rt * 8 + g, p.n_out - 1);
-    ra = i;
-    rb = p.n_out + i;
-  } else {
-    ra = min(rt * 16 + g, p.N - 1);
-    rb = min(rt * 16 + g + 8, p.N - 1);
+  __syncthreads();
+  constexpr int MP = MT * 8;
+  float* fin = red + (size_t)W * MP * 16;
+#pragma unroll
+  for (int nt = 0; nt < MT; ++nt) {
+    const int m0 = nt * 8 + 2 * t;
+    red[(warp * MP + m0) * 16 + g] = acc[nt][0];
+    red[(warp * MP + m0 + 1) * 16 + g] = acc[nt][1];
+    red[(warp * MP + m0) * 16 + g + 8] = acc[nt][2];
+    red[(warp * MP + m0 + 1) * 16 + g + 8] = acc[nt][3];
   }
+  __syncthreads();
+  const int items = p.M * 16;
+  for (int i = threadIdx.x; i < items; i += blockDim.x) {
+    const int m = i >> 4, r = i & 15;
+    float v = 0.0f;
+    for (int w = 0; w < W; ++w) v += red[(w * MP + m) * 16 + r];
+    fin[i] = v;
+  }
+  __syncthreads();
+  if (p.nsplit > 1) {
+    const size_t NR = (size_t)gridDim.x * 16;
+    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+      const int m = i >> 4, r = i & 15;
+      p.ws[((size_t)sp * p.M + m) * NR + (size_t)rt * 16 + r] = fin[i];
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) *s_flag = (atomicAdd(&p.counters[rt], 1u) == (unsigned)(p.nsplit - 1));
+    __syncthreads();
+    if (!*s_flag) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+      const int m = i >> 4, r = i & 15;
+      float v = 0.0f;
+      for (int s = 0; s < p.nsplit; ++s) v += __ldcg(p.ws + ((size_t)s * p.M + m) * NR + (size_t)rt * 16 + r);
+      fin[i] = v;
+    }
+    if (threadIdx.x == 0) p.counters[rt] = 0u;
+    __syncthreads();
+  }
+  epilogue_tile(p, fin, rt, s_flag);
+}
+
+// One 128-k tile of MMAs: weights of rows g / g + 8 (4 words each) times staged x.
+template <int MT, bool XF32>
+__device__ __forceinline__ void mma_tile(const uint4& wa, const uint4& wb, float sa, float sb, const uint4* xs_hi,
+                                         const uint4* xs_lo, const int (&mrow)[MT], int wbase, float (&acc)[MT][4]) {
+  float part[MT][4];
+#pragma unroll
+  for (int nt = 0; nt < MT; ++nt) part[nt][0] = part[nt][1] = part[nt][2] = part[nt][3] = 0.0f;
+  const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
+  const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t A[4], B[4];
+    dequant_word(wav[q], A);
+    dequant_word(wbv[q], B);
+    const int ph = xswz(wbase + q);
+#pragma unroll
+    for (int nt = 0; nt < MT; ++nt) {
+      const uint4 xh = xs_hi[mrow[nt] + ph];
+      mma_16816(part[nt], A[0], B[0], A[1], B[1], xh.x, xh.y);
+      mma_16816(part[nt], A[2], B[2], A[3], B[3], xh.z, xh.w);
+      if constexpr (XF32) {
+        const uint4 xl = xs_lo[mrow[nt] + ph];
+        mma_16816(part[nt], A[0], B[0], A[1], B[1], xl.x, xl.y);
+        mma_16816(part[nt], A[2], B[2], A[3], B[3], xl.z, xl.w);
+      }
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < MT; ++nt) {
+    acc[nt][0] = fmaf(sa, part[nt][0], acc[nt][0]);
+    acc[nt][1] = fmaf(sa, part[nt][1], acc[nt][1]);
+    acc[nt][2] = fmaf(sb, part[nt][2], acc[nt][2]);
+    acc[nt][3] = fmaf(sb, part[nt][3], acc[nt][3]);
+  }
+}
+
+// ---- kernel 1: register-staged weights ------------------------------------------------------
+
+template <int MT, bool XF32, int T>
+__global__ void __launch_bounds__(256) q4_gemv_reg(LinArgs p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ int s_flag;
+  __shared__ float s_rs[8];
+  __shared__ float s_scratch[64];
+  const int W = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int rt = blockIdx.x, sp = blockIdx.y;
+  const int ra = tile_row(p, rt, g), rb = tile_row(p, rt, g + 8);
   const int kt0 = sp * p.kps;
   const int kt1 = min(kt0 + p.kps, p.KT);
   const size_t row_u4 = (size_t)p.K / 32;  // 16-byte chunks per weight row
@@ -159,219 +442,163 @@ __global__ void __launch_bounds__(256) q4_gemv_mma(LinArgs p) {
   griddep_launch_dependents();
   griddep_wait();
 
-  // 2) stage x[:, kt0*128 : kt1*128) as permuted fp16 pairs (hi, and lo for fp32 x)
+  // 2) prologue + x staging
+  if (p.ln_w) prologue_rms(p, s_rs, s_scratch);
   const int rstride = p.kps * 16 + 4;  // uint4 per staged row; +64 B keeps rows on other bank groups
   uint4* xs_hi = reinterpret_cast<uint4*>(smem_raw);
   uint4* xs_lo = xs_hi + (size_t)p.M * rstride;
-  const int nwords = (kt1 - kt0) * 16;
-  for (int i = threadIdx.x; i < p.M * nwords; i += blockDim.x) {
-    const int m = i / nwords, w = i - m * nwords;
-    const size_t kb = (size_t)m * p.K + (size_t)kt0 * TILE_K + 8 * (size_t)w;
-    uint4 hi;
-    if constexpr (XF32) {
-      const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + kb);
-      const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + kb + 4);
-      uint4 lo;
-      split_pair(a.x, b.x, hi.x, lo.x);  // (x0, x4)
-      split_pair(a.y, b.y, hi.y, lo.y);  // (x1, x5)
-      split_pair(a.z, b.z, hi.z, lo.z);  // (x2, x6)
-      split_pair(a.w, b.w, hi.w, lo.w);  // (x3, x7)
-      xs_lo[m * rstride + xswz(w)] = lo;
-    } else {
-      const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(p.x) + kb);
-      hi.x = __byte_perm(v.x, v.z, 0x5410);
-      hi.y = __byte_perm(v.x, v.z, 0x7632);
-      hi.z = __byte_perm(v.y, v.w, 0x5410);
-      hi.w = __byte_perm(v.y, v.w, 0x7632);
-    }
-    xs_hi[m * rstride + xswz(w)] = hi;
-  }
+  stage_x<XF32>(p, s_rs, xs_hi, xs_lo, rstride, kt0, (kt1 - kt0) * 16);
   __syncthreads();
 
-  // 3) MMAs: per tile, part = sum over its 128 k of (nib - 8) * x; acc += scale * part
+  // 3) MMAs
   float acc[MT][4];
 #pragma unroll
   for (int nt = 0; nt < MT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
   int mrow[MT];
 #pragma unroll
   for (int nt = 0; nt < MT; ++nt) mrow[nt] = min(nt * 8 + g, p.M - 1) * rstride;
-
 #pragma unroll
   for (int j = 0; j < T; ++j) {
     const int kt = kt0 + warp + W * j;
-    if (kt < kt1) {
-      float part[MT][4];
-#pragma unroll
-      for (int nt = 0; nt < MT; ++nt) part[nt][0] = part[nt][1] = part[nt][2] = part[nt][3] = 0.0f;
-      const int wbase = (kt - kt0) * 16 + 4 * t;
-      const uint32_t wav[4] = {wa[j].x, wa[j].y, wa[j].z, wa[j].w};
-      const uint32_t wbv[4] = {wb[j].x, wb[j].y, wb[j].z, wb[j].w};
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t A[4], B[4];
-        dequant_word(wav[q], A);
-        dequant_word(wbv[q], B);
-        const int ph = xswz(wbase + q);
-#pragma unroll
-        for (int nt = 0; nt < MT; ++nt) {
-          const uint4 xh = xs_hi[mrow[nt] + ph];
-          mma_16816(part[nt], A[0], B[0], A[1], B[1], xh.x, xh.y);
-          mma_16816(part[nt], A[2], B[2], A[3], B[3], xh.z, xh.w);
-          if constexpr (XF32) {
-            const uint4 xl = xs_lo[mrow[nt] + ph];
-            mma_16816(part[nt], A[0], B[0], A[1], B[1], xl.x, xl.y);
-            mma_16816(part[nt], A[2], B[2], A[3], B[3], xl.z, xl.w);
-          }
-        }
-      }
-#pragma unroll
-      for (int nt = 0; nt < MT; ++nt) {
-        acc[nt][0] = fmaf(sa[j], part[nt][0], acc[nt][0]);
-        acc[nt][1] = fmaf(sa[j], part[nt][1], acc[nt][1]);
-        acc[nt][2] = fmaf(sb[j], part[nt][2], acc[nt][2]);
-        acc[nt][3] = fmaf(sb[j], part[nt][3], acc[nt][3]);
-      }
-    }
+    if (kt < kt1) mma_tile<MT, XF32>(wa[j], wb[j], sa[j], sb[j], xs_hi, xs_lo, mrow, (kt - kt0) * 16 + 4 * t, acc);
   }
-
-  // 4) sum the W warps' tiles in shared memory: red[warp][m][r], then fin[m][r]
-  __syncthreads();
-  constexpr int MP = MT * 8;
-  float* red = reinterpret_cast<float*>(smem_raw);
-  float* fin = red + (size_t)W * MP * 16;
-#pragma unroll
-  for (int nt = 0; nt < MT; ++nt) {
-    const int m0 = nt * 8 + 2 * t;
-    red[(warp * MP + m0) * 16 + g] = acc[nt][0];
-    red[(warp * MP + m0 + 1) * 16 + g] = acc[nt][1];
-    red[(warp * MP + m0) * 16 + g + 8] = acc[nt][2];
-    red[(warp * MP + m0 + 1) * 16 + g + 8] = acc[nt][3];
-  }
-  __syncthreads();
-  const int items = p.M * 16;
-  for (int i = threadIdx.x; i < items; i += blockDim.x) {
-    const int m = i >> 4, r = i & 15;
-    float v = 0.0f;
-    for (int w = 0; w < W; ++w) v += red[(w * MP + m) * 16 + r];
-    fin[i] = v;
-  }
-  __syncthreads();
-
-  // 5) split-K: publish partials; the last CTA of this row tile sums them in split order
-  if (p.nsplit > 1) {
-    const size_t NR = (size_t)gridDim.x * 16;
-    for (int i = threadIdx.x; i < items; i += blockDim.x) {
-      const int m = i >> 4, r = i & 15;
-      p.ws[((size_t)sp * p.M + m) * NR + (size_t)rt * 16 + r] = fin[i];
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_last = (atomicAdd(&p.counters[rt], 1u) == (unsigned)(p.nsplit - 1));
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    for (int i = threadIdx.x; i < items; i += blockDim.x) {
-      const int m = i >> 4, r = i & 15;
-      float v = 0.0f;
-      for (int s = 0; s < p.nsplit; ++s) v += __ldcg(p.ws + ((size_t)s * p.M + m) * NR + (size_t)rt * 16 + r);
-      fin[i] = v;
-    }
-    if (threadIdx.x == 0) p.counters[rt] = 0u;
-    __syncthreads();
-  }
-
-  // 6) epilogue
-  for (int i = threadIdx.x; i < items; i += blockDim.x) {
-    const int m = i >> 4, r = i & 15;
-    if (swiglu) {
-      const int col = rt * 8 + r;
-      if (r < 8 && col < p.n_out) store_y(p.y, (size_t)m * p.n_out + col, silu(fin[i]) * fin[i + 8], p.y_f32);
-    } else {
-      const int col = rt * 16 + r;
-      if (col < p.N) {
-        float v = fin[i];
-        const size_t o = (size_t)m * p.N + col;
-        if (p.epi == Q4B_EPI_ACCUMULATE) v += load_y(p.y, o, p.y_f32);
-        store_y(p.y, o, v, p.y_f32);
-      }
-    }
-  }
+  finish_tile<MT>(p, acc, reinterpret_cast<float*>(smem_raw), &s_flag);
 }
 
-// ---- generic SIMT kernel -------------------------------------------------------------------
-
-template <bool XF32>
-__global__ void __launch_bounds__(256) q4_linear_simt(LinArgs p) {
-  const int warps = blockDim.x >> 5;
+// ---- kernel 3: weights streamed into shared memory by the TMA engine ---------------------------
+//
+// Thread 0 issues one bulk copy per weight row of the tile (k-range x 64 B per 128-k tile) into
+// shared memory, completing on one mbarrier, before griddepcontrol.wait: the weight tile is in
+// flight while the previous kernel finishes and no registers hold it. The row stride in shared
+// memory is padded so rows g and g + 8 of a quad land on other banks.
+template <int MT, bool XF32>
+__global__ void __launch_bounds__(256) q4_gemv_tma(LinArgs p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int s_flag;
+  __shared__ float s_rs[8];
+  __shared__ float s_scratch[64];
+  const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int mchunks = (p.M + 7) / 8;
-  const long long gw = (long long)blockIdx.x * warps + warp;
+  const int g = lane >> 2, t = lane & 3;
+  const int rt = blockIdx.x, sp = blockIdx.y;
+  const int kt0 = sp * p.kps;
+  const int kt1 = min(kt0 + p.kps, p.KT);
+  const int ntile = kt1 - kt0;
+  const int KG = p.K / p.G;
+  unsigned char* sw = smem_raw;                                       // [16][wstride] weights
+  __half* ss = reinterpret_cast<__half*>(smem_raw + 16 * p.wstride);  // [16][KG] scales
+  uint4* xs_hi = reinterpret_cast<uint4*>(smem_raw + p.x_off);
+  const int rstride = p.kps * 16 + 4;
+  uint4* xs_lo = xs_hi + (size_t)p.M * rstride;
+
+  // 1) bulk copies of the tile's weight rows (thread 0); scales by plain loads
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    const uint32_t wbytes = (uint32_t)ntile * 64;
+    mbar_arrive_expect_tx(&bar, 16u * wbytes);
+    const unsigned char* q8 = reinterpret_cast<const unsigned char*>(p.qw);
+    for (int s = 0; s < 16; ++s)
+      bulk_g2s(sw + s * p.wstride, q8 + (size_t)tile_row(p, rt, s) * (p.K / 2) + (size_t)kt0 * 64, wbytes, &bar);
+  }
+  for (int i = threadIdx.x; i < 16 * KG; i += blockDim.x) {
+    const int s = i / KG, c = i - s * KG;
+    ss[i] = p.scales[(size_t)tile_row(p, rt, s) * KG + c];
+  }
   griddep_launch_dependents();
   griddep_wait();
-  if (gw >= (long long)p.n_out * mchunks) return;
-  const int o = (int)(gw / mchunks), mc = (int)(gw % mchunks);
-  const bool swiglu = p.epi == Q4B_EPI_SWIGLU;
-  const int m0 = mc * 8, mcount = min(8, p.M - m0);
-  const int KW = p.K / 8, KG = p.K / p.G;
-  float acc[2][8];
-#pragma unroll
-  for (int r = 0; r < 2; ++r)
-#pragma unroll
-    for (int m = 0; m < 8; ++m) acc[r][m] = 0.0f;
 
-  for (int w = lane; w < KW; w += 32) {
+  // 2) prologue + x staging
+  if (p.ln_w) prologue_rms(p, s_rs, s_scratch);
+  stage_x<XF32>(p, s_rs, xs_hi, xs_lo, rstride, kt0, ntile * 16);
+  __syncthreads();  // also publishes the initialised barrier to every thread
+
+  // 3) weights landed? (bounded: a copy that never completes sets a status bit instead of hanging)
+  const bool ok = mbar_wait_bounded(&bar, 0, kWaitLimitNs);
+  if (__syncthreads_or(!ok)) {
+    if (threadIdx.x == 0) atomicOr(&g_linear_status, kStatusTimeout);
+    return;
+  }
+
+  // 4) MMAs from shared memory
+  float acc[MT][4];
 #pragma unroll
-    for (int rr = 0; rr < 2; ++rr) {
-      if (rr == 1 && !swiglu) break;
-      const int row = rr == 0 ? o : p.n_out + o;
-      const int32_t word = __ldg(p.qw + (size_t)row * KW + w);
-      const float s = __half2float(p.scales[(size_t)row * KG + (8 * w) / p.G]);
-      float wv[8];
+  for (int nt = 0; nt < MT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.0f;
+  int mrow[MT];
 #pragma unroll
-      for (int b = 0; b < 8; ++b) wv[b] = (float)(((word >> (4 * b)) & 15) - 8) * s;
+  for (int nt = 0; nt < MT; ++nt) mrow[nt] = min(nt * 8 + g, p.M - 1) * rstride;
+  const unsigned char* swa = sw + g * p.wstride + t * 16;
+  const unsigned char* swb = sw + (g + 8) * p.wstride + t * 16;
+  for (int kl = warp; kl < ntile; kl += W) {
+    const int grp = ((kt0 + kl) * TILE_K) / p.G;
+    const float sa = __half2float(ss[g * KG + grp]);
+    const float sb = __half2float(ss[(g + 8) * KG + grp]);
+    const uint4 wa = *reinterpret_cast<const uint4*>(swa + kl * 64);
+    const uint4 wb = *reinterpret_cast<const uint4*>(swb + kl * 64);
+    mma_tile<MT, XF32>(wa, wb, sa, sb, xs_hi, xs_lo, mrow, kl * 16 + 4 * t, acc);
+  }
+  finish_tile<MT>(p, acc, reinterpret_cast<float*>(smem_raw + p.x_off), &s_flag);
+}
+
+// ---- kernel 2: generic SIMT ---------------------------------------------------------------
+//
+// One CTA per 16-slot tile and all batch rows; warp w computes slots 2w and 2w + 1 with fp32 FMAs
+// on (nib - 8) * scale (exact), lanes striding over the words of the row.
+template <bool XF32>
+__global__ void __launch_bounds__(256) q4_linear_simt(LinArgs p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ int s_flag;
+  __shared__ float s_rs[8];
+  __shared__ float s_scratch[64];
+  float* fin = reinterpret_cast<float*>(smem_raw);  // [M][16]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rt = blockIdx.x;
+  griddep_launch_dependents();
+  griddep_wait();
+  if (p.ln_w) prologue_rms(p, s_rs, s_scratch);
+  const int KW = p.K / 8, KG = p.K / p.G;
+  for (int s = 2 * warp; s < 2 * warp + 2; ++s) {
+    const int row = tile_row(p, rt, s);
+    for (int m0 = 0; m0 < p.M; m0 += 8) {
+      const int mcount = min(8, p.M - m0);
+      float acc[8];
+#pragma unroll
+      for (int m = 0; m < 8; ++m) acc[m] = 0.0f;
+      for (int w = lane; w < KW; w += 32) {
+        const int32_t word = __ldg(p.qw + (size_t)row * KW + w);
+        const float sc = __half2float(p.scales[(size_t)row * KG + (8 * w) / p.G]);
+        float wv[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) wv[b] = (float)(((word >> (4 * b)) & 15) - 8) * sc;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          if (m < mcount) {
+            float d = 0.0f;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) d = fmaf(wv[b], x_value(p, s_rs, m0 + m, 8 * w + b, XF32), d);
+            acc[m] += d;
+          }
+        }
+      }
 #pragma unroll
       for (int m = 0; m < 8; ++m) {
-        if (m < mcount) {
-          const size_t xb = (size_t)(m0 + m) * p.K + 8 * (size_t)w;
-          float d = 0.0f;
-#pragma unroll
-          for (int b = 0; b < 8; ++b) {
-            const float xv = XF32 ? __ldg(reinterpret_cast<const float*>(p.x) + xb + b)
-                                  : __half2float(reinterpret_cast<const __half*>(p.x)[xb + b]);
-            d = fmaf(wv[b], xv, d);
-          }
-          acc[rr][m] += d;
-        }
+        const float v = warp_sum(acc[m]);
+        if (lane == 0 && m < mcount) fin[(m0 + m) * 16 + s] = v;
       }
     }
   }
-#pragma unroll
-  for (int rr = 0; rr < 2; ++rr)
-#pragma unroll
-    for (int m = 0; m < 8; ++m) acc[rr][m] = warp_sum(acc[rr][m]);
-  if (lane == 0) {
-#pragma unroll
-    for (int m = 0; m < 8; ++m) {
-      if (m < mcount) {
-        if (swiglu) {
-          store_y(p.y, (size_t)(m0 + m) * p.n_out + o, silu(acc[0][m]) * acc[1][m], p.y_f32);
-        } else {
-          const size_t off = (size_t)(m0 + m) * p.N + o;
-          float v = acc[0][m];
-          if (p.epi == Q4B_EPI_ACCUMULATE) v += load_y(p.y, off, p.y_f32);
-          store_y(p.y, off, v, p.y_f32);
-        }
-      }
-    }
-  }
+  __syncthreads();
+  epilogue_tile(p, fin, rt, &s_flag);
 }
 
 // ---- planning ------------------------------------------------------------------------------
 
 struct Plan {
-  int kernel = 2;  // 1 = mma, 2 = simt
+  int kernel = 2;  // 1 = register-staged MMA, 2 = SIMT, 3 = TMA-staged MMA
   int W = 4, T = 1, nsplit = 1, kps = 1, MT = 1;
-  int RT = 0;      // row tiles (grid.x)
+  int RT = 0;  // row tiles (grid.x)
+  int wstride = 0, x_off = 0;
   size_t smem = 0;
   size_t ws_bytes = 0;
 };
@@ -379,56 +606,88 @@ struct Plan {
 static size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 constexpr size_t kMaxSmem = 200 * 1024;
-
-static size_t mma_smem(const Plan& pl, int M, bool xf32) {
-  const size_t stage = (size_t)M * (pl.kps * 16 + 4) * 16 * (xf32 ? 2 : 1);
-  const size_t red = (size_t)pl.W * pl.MT * 8 * 16 * 4 + (size_t)M * 16 * 4;
-  return std::max(stage, red);
-}
-
 // Workspace layout: [0, kCounterBytes) arrival counters, one per row tile, at a fixed place for
 // every call (each call leaves the counters it used at zero, so calls with different plans can
 // share one workspace), then the split-K partial sums of the current call.
 constexpr size_t kCounterBytes = 64 * 1024;
 constexpr int kMaxCounters = (int)(kCounterBytes / 4);
+constexpr size_t kTmaSmemTarget = 112 * 1024;  // CTAs of two consecutive kernels fit on one SM
 
-static size_t mma_ws(const Plan& pl, int M) {
+static int row_tiles(int N, int n_out, int epi) { return epi == EPI_SWIGLU ? (n_out + 7) / 8 : (N + 15) / 16; }
+
+static size_t reg_smem(const Plan& pl, int M, bool xf32) {
+  const size_t stage = (size_t)M * (pl.kps * 16 + 4) * 16 * (xf32 ? 2 : 1);
+  const size_t red = (size_t)pl.W * pl.MT * 8 * 16 * 4 + (size_t)M * 16 * 4;
+  return std::max(stage, red);
+}
+
+static size_t split_ws(const Plan& pl, int M) {
   if (pl.nsplit <= 1) return 0;
   return kCounterBytes + align_up((size_t)pl.nsplit * M * pl.RT * 16 * 4, 256);
 }
 
-// Tuned default: keep ~2 KB of weights per warp in flight and enough CTAs to fill 148 SMs several
-// times; prefer no split when the row tiles alone give that many CTAs.
-static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, const q4b_linear_cfg* cfg, Plan& pl) {
-  const int n_out = epi == Q4B_EPI_SWIGLU ? N / 2 : N;
-  const bool mma_ok = (G % TILE_K == 0) && M <= 64;
-  const int want = cfg ? cfg->kernel : 0;
-  if (want == 1 && !mma_ok)
-    return set_error(Q4B_EUNSUPPORTED, "q4_linear: tensor-core kernel needs group %% 128 == 0 and m <= 64");
-  if (want == 2 || (want == 0 && !mma_ok)) {
-    pl.kernel = 2;
-    pl.W = 8;
-    return Q4B_OK;
+static bool tiles_supported(int MT, int T) {
+  if (MT <= 2) return T == 1 || T == 2 || T == 3 || T == 4 || T == 6 || T == 8;
+  return T == 1 || T == 2;
+}
+static int round_up_tiles(int MT, int T) {
+  for (int t = T; t <= 8; ++t)
+    if (tiles_supported(MT, t)) return t;
+  return 8;
+}
+
+static void tma_layout(Plan& pl, int M, int K, int G, bool xf32) {
+  pl.wstride = pl.kps * 64 + ((pl.kps % 2 == 0) ? 64 : 0);
+  pl.x_off = (int)(16 * (size_t)pl.wstride + align_up((size_t)16 * (K / G) * 2, 16));
+  const size_t stage = (size_t)M * (pl.kps * 16 + 4) * 16 * (xf32 ? 2 : 1);
+  const size_t red = (size_t)pl.W * pl.MT * 8 * 16 * 4 + (size_t)M * 16 * 4;
+  pl.smem = pl.x_off + std::max(stage, red);
+}
+
+static int plan_tma(int M, int K, int G, bool xf32, const q4b_linear_cfg* cfg, Plan& pl) {
+  pl.kernel = 3;
+  const int KT = K / TILE_K;
+  pl.W = cfg && cfg->warps ? cfg->warps : 4;
+  if (pl.W < 1 || pl.W > 8) return set_error(Q4B_EINVAL, "q4_linear: warps must be 1..8");
+  int S = cfg && cfg->split ? cfg->split : 1;
+  for (;;) {
+    pl.kps = (KT + S - 1) / S;
+    pl.nsplit = (KT + pl.kps - 1) / pl.kps;
+    tma_layout(pl, M, K, G, xf32);
+    if (pl.smem <= kTmaSmemTarget || (cfg && cfg->split) || pl.kps == 1) break;
+    ++S;
   }
+  if (pl.smem > kMaxSmem) return set_error(Q4B_EUNSUPPORTED, "q4_linear: shared memory plan too large");
+  if (pl.nsplit > 1 && pl.RT > kMaxCounters)
+    return set_error(Q4B_EUNSUPPORTED, "q4_linear: split-K limited to %d row tiles", kMaxCounters);
+  pl.ws_bytes = split_ws(pl, M);
+  return Q4B_OK;
+}
+
+static int plan_reg(int M, int K, bool xf32, const q4b_linear_cfg* cfg, Plan& pl) {
   pl.kernel = 1;
-  pl.MT = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8;
-  pl.RT = epi == Q4B_EPI_SWIGLU ? (n_out + 7) / 8 : (N + 15) / 16;
   const int KT = K / TILE_K;
   int W = cfg && cfg->warps ? cfg->warps : 0;
   int T = cfg && cfg->tiles ? cfg->tiles : 0;
   int S = cfg && cfg->split ? cfg->split : 0;
+  if (!W && !T && !S && pl.MT <= 2 && KT <= 64) {
+    // decode: up to 8 warps cover all of K with a few 128-k tiles in flight per warp and tile
+    // row, no split-K, so the post-wait path is x staging + MMAs + one shared-memory reduction
+    W = std::min(8, KT);
+    T = round_up_tiles(pl.MT, (KT + W - 1) / W);
+  }
   if (!T) T = pl.MT == 1 ? 2 : 1;
   if (!W) {
-    if (S) {
+    if (S)
       W = std::min(8, (((KT + S - 1) / S) + T - 1) / T);
-    } else if (pl.RT >= 148 * 6) {  // plenty of row tiles: cover K within the CTA if it fits
+    else if (pl.RT >= 148 * 6) {  // plenty of row tiles: cover K within the CTA if it fits
       W = std::min(8, (KT + T - 1) / T);
       if (W * T < KT) W = 4;
-    } else {
+    } else
       W = 4;
-    }
   }
-  if (W < 1 || W > 8 || T < 1 || T > 4) return set_error(Q4B_EINVAL, "q4_linear: warps must be 1..8, tiles 1..4");
+  if (W < 1 || W > 8 || !tiles_supported(pl.MT, T))
+    return set_error(Q4B_EINVAL, "q4_linear: warps must be 1..8 and tiles one of 1,2,3,4,6,8 (1,2 for m > 16)");
   const bool user_shape = cfg && (cfg->warps || cfg->split);
   for (;;) {
     const int s = S ? S : (KT + W * T - 1) / (W * T);
@@ -438,11 +697,11 @@ static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, const q4b
     pl.nsplit = (KT + pl.kps - 1) / pl.kps;
     if (pl.kps > W * T)
       return set_error(Q4B_EINVAL, "q4_linear: split %d leaves %d tiles per CTA > warps*tiles %d", s, pl.kps, W * T);
-    pl.smem = mma_smem(pl, M, xf32);
+    pl.smem = reg_smem(pl, M, xf32);
     if (pl.smem <= kMaxSmem && (pl.nsplit == 1 || pl.RT <= kMaxCounters)) break;
     if (pl.smem <= kMaxSmem) {  // too many row tiles for the counter region: no split
-      if (user_shape || (KT + T - 1) / T > 8) return set_error(Q4B_EUNSUPPORTED, "q4_linear: split-K limited to "
-                                                               "%d row tiles", kMaxCounters);
+      if (user_shape || (KT + T - 1) / T > 8)
+        return set_error(Q4B_EUNSUPPORTED, "q4_linear: split-K limited to %d row tiles", kMaxCounters);
       W = (KT + T - 1) / T;
       S = 1;
       continue;
@@ -450,67 +709,271 @@ static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, const q4b
     if (user_shape || W == 1) return set_error(Q4B_EUNSUPPORTED, "q4_linear: shared memory plan too large");
     W = W / 2;  // fewer tiles per CTA: a smaller staged slice of x
   }
-  pl.ws_bytes = mma_ws(pl, M);
+  pl.ws_bytes = split_ws(pl, M);
   return Q4B_OK;
 }
 
-template <int MT, bool XF32, int T>
-static cudaError_t launch_mma_t(const Plan& pl, const LinArgs& a, cudaStream_t st) {
-  auto kern = q4_gemv_mma<MT, XF32, T>;
-  static unsigned long long attr_set = 0;  // bit per device: opt-in to large dynamic shared memory
+static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, bool norm, const q4b_linear_cfg* cfg,
+                       Plan& pl) {
+  const int n_out = epi == EPI_SWIGLU ? N / 2 : N;
+  const bool mma_ok = (G % TILE_K == 0) && M <= 64 && (!norm || M <= 8);
+  const int want = cfg ? cfg->kernel : 0;
+  pl.RT = row_tiles(N, n_out, epi);
+  pl.MT = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8;
+  if ((want == 1 || want == 3) && !mma_ok)
+    return set_error(Q4B_EUNSUPPORTED, "q4_linear: tensor-core kernels need group %% 128 == 0 and m <= 64");
+  if (want == 2 || (want == 0 && !mma_ok)) {
+    pl.kernel = 2;
+    pl.W = 8;
+    pl.smem = (size_t)M * 16 * 4;
+    if (pl.smem > kMaxSmem) return set_error(Q4B_EUNSUPPORTED, "q4_linear: m too large");
+    return Q4B_OK;
+  }
+  if (want == 3) {
+    if (pl.MT > 2) return set_error(Q4B_EUNSUPPORTED, "q4_linear: TMA kernel needs m <= 16");
+    return plan_tma(M, K, G, xf32, cfg, pl);
+  }
+  return plan_reg(M, K, xf32, cfg, pl);
+}
+
+template <typename Kern>
+static cudaError_t set_smem_attr(Kern kern, unsigned long long& done) {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!(attr_set >> (dev & 63) & 1ull)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
-    if (e != cudaSuccess) return e;
-    attr_set |= 1ull << (dev & 63);
-  }
-  return launch_pdl(kern, dim3(pl.RT, pl.nsplit), dim3(pl.W * 32), pl.smem, st, a);
+  if (done >> (dev & 63) & 1ull) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+  if (e == cudaSuccess) done |= 1ull << (dev & 63);
+  return e;
+}
+
+template <int MT, bool XF32, int T>
+static cudaError_t launch_reg_t(const Plan& pl, const LinArgs& a, cudaStream_t st) {
+  static unsigned long long done = 0;
+  cudaError_t e = set_smem_attr(q4_gemv_reg<MT, XF32, T>, done);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(q4_gemv_reg<MT, XF32, T>, dim3(pl.RT, pl.nsplit), dim3(pl.W * 32), pl.smem, st, a);
 }
 
 template <int MT, bool XF32>
-static cudaError_t launch_mma_x(const Plan& pl, const LinArgs& a, cudaStream_t st) {
-  switch (pl.T) {
-    case 1: return launch_mma_t<MT, XF32, 1>(pl, a, st);
-    case 2: return launch_mma_t<MT, XF32, 2>(pl, a, st);
-    case 3: return launch_mma_t<MT, XF32, 3>(pl, a, st);
-    default: return launch_mma_t<MT, XF32, 4>(pl, a, st);
+static cudaError_t launch_reg_x(const Plan& pl, const LinArgs& a, cudaStream_t st) {
+  if constexpr (MT <= 2) {
+    switch (pl.T) {
+      case 1: return launch_reg_t<MT, XF32, 1>(pl, a, st);
+      case 2: return launch_reg_t<MT, XF32, 2>(pl, a, st);
+      case 3: return launch_reg_t<MT, XF32, 3>(pl, a, st);
+      case 4: return launch_reg_t<MT, XF32, 4>(pl, a, st);
+      case 6: return launch_reg_t<MT, XF32, 6>(pl, a, st);
+      default: return launch_reg_t<MT, XF32, 8>(pl, a, st);
+    }
+  } else {
+    if (pl.T == 1) return launch_reg_t<MT, XF32, 1>(pl, a, st);
+    return launch_reg_t<MT, XF32, 2>(pl, a, st);
   }
 }
 
 template <bool XF32>
-static cudaError_t launch_mma(const Plan& pl, const LinArgs& a, cudaStream_t st) {
+static cudaError_t launch_reg(const Plan& pl, const LinArgs& a, cudaStream_t st) {
   switch (pl.MT) {
-    case 1: return launch_mma_x<1, XF32>(pl, a, st);
-    case 2: return launch_mma_x<2, XF32>(pl, a, st);
-    case 4: return launch_mma_x<4, XF32>(pl, a, st);
-    default: return launch_mma_x<8, XF32>(pl, a, st);
+    case 1: return launch_reg_x<1, XF32>(pl, a, st);
+    case 2: return launch_reg_x<2, XF32>(pl, a, st);
+    case 4: return launch_reg_x<4, XF32>(pl, a, st);
+    default: return launch_reg_x<8, XF32>(pl, a, st);
   }
+}
+
+template <int MT, bool XF32>
+static cudaError_t launch_tma_t(const Plan& pl, const LinArgs& a, cudaStream_t st) {
+  static unsigned long long done = 0;
+  cudaError_t e = set_smem_attr(q4_gemv_tma<MT, XF32>, done);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(q4_gemv_tma<MT, XF32>, dim3(pl.RT, pl.nsplit), dim3(pl.W * 32), pl.smem, st, a);
+}
+
+template <bool XF32>
+static cudaError_t launch_tma(const Plan& pl, const LinArgs& a, cudaStream_t st) {
+  return pl.MT == 1 ? launch_tma_t<1, XF32>(pl, a, st) : launch_tma_t<2, XF32>(pl, a, st);
+}
+
+static int validate(const LinearOp& op) {
+  if (!op.qw || !op.scales || !op.x) return set_error(Q4B_EINVAL, "q4_linear: null pointer");
+  if (!op.y && op.epi != EPI_ROPE_KV && op.epi != EPI_ARGMAX) return set_error(Q4B_EINVAL, "q4_linear: null pointer");
+  if (op.m < 1 || op.n < 1 || op.k < 8 || op.k % 8)
+    return set_error(Q4B_EINVAL, "q4_linear: bad shape m=%d n=%d k=%d", op.m, op.n, op.k);
+  if (op.group < 8 || op.group % 8 || op.k % op.group)
+    return set_error(Q4B_EINVAL, "q4_linear: need k %% group == 0 and group %% 8 == 0 (k=%d group=%d)", op.k,
+                     op.group);
+  if ((op.x_dtype != Q4B_F32 && op.x_dtype != Q4B_F16) || (op.y_dtype != Q4B_F32 && op.y_dtype != Q4B_F16))
+    return set_error(Q4B_EINVAL, "q4_linear: bad dtype");
+  if (op.epi < EPI_STORE || op.epi > EPI_ARGMAX) return set_error(Q4B_EINVAL, "q4_linear: bad epilogue %d", op.epi);
+  if (op.epi == EPI_SWIGLU && op.n % 2) return set_error(Q4B_EINVAL, "q4_linear: SwiGLU needs an even row count");
+  if (op.ln_w && (op.x_dtype != Q4B_F32 || op.m > 8 || op.k % 4))
+    return set_error(Q4B_EINVAL, "q4_linear: fused RMSNorm needs fp32 x, m <= 8 and k %% 4 == 0");
+  if (op.epi == EPI_ROPE_KV &&
+      (!op.rope_cos || !op.rope_sin || !op.pos0 || !op.q_out || !op.k_cache || !op.v_cache || op.head_dim % 16 ||
+       op.n != (op.n_heads + 2 * op.n_kv) * op.head_dim))
+    return set_error(Q4B_EINVAL, "q4_linear: bad RoPE/KV epilogue arguments");
+  if (op.epi == EPI_ARGMAX && (!op.state || op.m != 1))
+    return set_error(Q4B_EINVAL, "q4_linear: argmax epilogue needs a state and m == 1");
+  return Q4B_OK;
+}
+
+static int plan_op(const LinearOp& op, Plan& pl) {
+  return plan_linear(op.m, op.n, op.k, op.group, op.epi, op.x_dtype == Q4B_F32, op.ln_w != nullptr, op.cfg, pl);
+}
+
+size_t linear_workspace(const LinearOp& op) {
+  if (validate(op) != Q4B_OK) return 0;
+  Plan a, b;
+  LinearOp o = op;
+  o.x_dtype = Q4B_F32;
+  const size_t wa = plan_op(o, a) == Q4B_OK ? a.ws_bytes : 0;
+  o.x_dtype = Q4B_F16;
+  o.ln_w = nullptr;
+  const size_t wb = plan_op(o, b) == Q4B_OK ? b.ws_bytes : 0;
+  return std::max(wa, wb);
+}
+
+static void simt_plan(const LinearOp& op, Plan& pl) {
+  pl = Plan();
+  pl.RT = row_tiles(op.n, op.epi == EPI_SWIGLU ? op.n / 2 : op.n, op.epi);
+  pl.kernel = 2;
+  pl.W = 8;
+  pl.smem = (size_t)op.m * 16 * 4;
+}
+
+int linear_run(const LinearOp& op, cudaStream_t st) {
+  int rc = validate(op);
+  if (rc) return rc;
+  const bool xf32 = op.x_dtype == Q4B_F32;
+  Plan pl;
+  if ((rc = plan_op(op, pl))) return rc;
+  const bool forced = op.cfg && op.cfg->kernel;
+  if (pl.kernel != 2 && (!aligned(op.qw, 16) || !aligned(op.x, 16) || (op.ln_w && !aligned(op.ln_w, 16)))) {
+    if (forced) return set_error(Q4B_EINVAL, "q4_linear: qweight, x and ln_w must be 16-byte aligned");
+    simt_plan(op, pl);
+  }
+  if (pl.kernel != 2 && pl.nsplit > 1 && (pl.ws_bytes > op.ws_bytes || !op.ws || !aligned(op.ws, 16))) {
+    if (op.cfg && op.cfg->split > 1)
+      return set_error(Q4B_EINVAL, "q4_linear: workspace of %zu bytes needed, %zu given", pl.ws_bytes, op.ws_bytes);
+    // no (or too little) workspace: all of K in one CTA when it fits, else the SIMT kernel
+    const int KT = op.k / TILE_K;
+    pl.kps = KT;
+    pl.nsplit = 1;
+    pl.ws_bytes = 0;
+    bool ok = false;
+    if (pl.kernel == 3) {
+      tma_layout(pl, op.m, op.k, op.group, xf32);
+      ok = pl.smem <= kMaxSmem;
+    } else if (KT <= 64 && (pl.MT <= 2 || KT <= 16)) {
+      pl.T = round_up_tiles(pl.MT, (KT + 7) / 8);
+      pl.W = (KT + pl.T - 1) / pl.T;
+      pl.smem = reg_smem(pl, op.m, xf32);
+      ok = pl.W <= 8 && pl.smem <= kMaxSmem;
+    }
+    if (!ok) simt_plan(op, pl);
+  }
+  LinArgs a = {};
+  a.qw = op.qw;
+  a.scales = reinterpret_cast<const __half*>(op.scales);
+  a.x = op.x;
+  a.y = op.y;
+  a.M = op.m;
+  a.N = op.n;
+  a.K = op.k;
+  a.G = op.group;
+  a.n_out = op.epi == EPI_SWIGLU ? op.n / 2 : op.n;
+  a.KT = op.k / TILE_K;
+  a.kps = pl.kps;
+  a.nsplit = pl.nsplit;
+  a.epi = op.epi;
+  a.y_f32 = op.y_dtype == Q4B_F32;
+  a.wstride = pl.wstride;
+  a.x_off = pl.x_off;
+  a.ln_w = op.ln_w;
+  a.eps = op.eps;
+  a.row_sel = op.row_sel;
+  a.rope_cos = op.rope_cos;
+  a.rope_sin = op.rope_sin;
+  a.pos0 = op.pos0;
+  a.pos_offset = op.pos_offset;
+  a.q_out = op.q_out;
+  a.k_cache = reinterpret_cast<__half*>(op.k_cache);
+  a.v_cache = reinterpret_cast<__half*>(op.v_cache);
+  a.H = op.n_heads;
+  a.Hkv = op.n_kv;
+  a.hd = op.head_dim;
+  a.state = op.state;
+  a.token_log = op.token_log;
+  a.logits = op.logits;
+  a.index_offset = op.index_offset;
+  a.finalize = op.finalize;
+  if (pl.kernel != 2 && pl.nsplit > 1) {
+    a.counters = reinterpret_cast<unsigned*>(op.ws);
+    a.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(op.ws) + kCounterBytes);
+  }
+  cudaError_t e;
+  if (pl.kernel == 3) {
+    e = xf32 ? launch_tma<true>(pl, a, st) : launch_tma<false>(pl, a, st);
+  } else if (pl.kernel == 1) {
+    e = xf32 ? launch_reg<true>(pl, a, st) : launch_reg<false>(pl, a, st);
+  } else {
+    static unsigned long long d0 = 0, d1 = 0;
+    e = xf32 ? set_smem_attr(q4_linear_simt<true>, d1) : set_smem_attr(q4_linear_simt<false>, d0);
+    if (e == cudaSuccess)
+      e = xf32 ? launch_pdl(q4_linear_simt<true>, dim3(pl.RT), dim3(256), pl.smem, st, a)
+               : launch_pdl(q4_linear_simt<false>, dim3(pl.RT), dim3(256), pl.smem, st, a);
+  }
+  if (e != cudaSuccess) return set_error(Q4B_ELAUNCH, "q4_linear: launch failed: %s", cudaGetErrorString(e));
+  return check_launch("q4_linear");
+}
+
+unsigned linear_status(bool reset) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, g_linear_status, sizeof(v));
+  if (reset && v) {
+    const unsigned z = 0;
+    cudaMemcpyToSymbol(g_linear_status, &z, sizeof(z));
+  }
+  return v;
 }
 
 }  // namespace q4b
 
 using namespace q4b;
 
+static LinearOp public_op(const int32_t* qweight, const uint16_t* scales, int group, const void* x, int x_dtype,
+                          void* y, int y_dtype, int m, int n, int k, int epilogue, const q4b_linear_cfg* cfg,
+                          void* workspace, size_t workspace_bytes) {
+  LinearOp op;
+  op.qw = qweight;
+  op.scales = scales;
+  op.group = group;
+  op.x = x;
+  op.x_dtype = x_dtype;
+  op.y = y;
+  op.y_dtype = y_dtype;
+  op.m = m;
+  op.n = n;
+  op.k = k;
+  op.epi = epilogue;
+  op.cfg = cfg;
+  op.ws = workspace;
+  op.ws_bytes = workspace_bytes;
+  return op;
+}
+
 static int validate_linear(const int32_t* qweight, const uint16_t* scales, int group, const void* x, int x_dtype,
                            void* y, int y_dtype, int m, int n, int k, int epi) {
   if (!qweight || !scales || !x || !y) return set_error(Q4B_EINVAL, "q4_linear: null pointer");
-  if (m < 1 || n < 1 || k < 8 || k % 8) return set_error(Q4B_EINVAL, "q4_linear: bad shape m=%d n=%d k=%d", m, n, k);
-  if (group < 8 || group % 8 || k % group)
-    return set_error(Q4B_EINVAL, "q4_linear: need k %% group == 0 and group %% 8 == 0 (k=%d group=%d)", k, group);
-  if ((x_dtype != Q4B_F32 && x_dtype != Q4B_F16) || (y_dtype != Q4B_F32 && y_dtype != Q4B_F16))
-    return set_error(Q4B_EINVAL, "q4_linear: bad dtype");
   if (epi < Q4B_EPI_STORE || epi > Q4B_EPI_SWIGLU) return set_error(Q4B_EINVAL, "q4_linear: bad epilogue %d", epi);
-  if (epi == Q4B_EPI_SWIGLU && n % 2) return set_error(Q4B_EINVAL, "q4_linear: SwiGLU needs an even row count");
-  return Q4B_OK;
+  return validate(public_op(qweight, scales, group, x, x_dtype, y, y_dtype, m, n, k, epi, nullptr, nullptr, 0));
 }
 
 extern "C" size_t q4b_q4_linear_workspace(int m, int n, int k, int group, int epilogue, const q4b_linear_cfg* cfg) {
-  if (m < 1 || n < 1 || k < 8 || group < 8 || k % group || group % 8) return 0;
-  Plan a, b;
-  const size_t wa = plan_linear(m, n, k, group, epilogue, true, cfg, a) == Q4B_OK ? a.ws_bytes : 0;
-  const size_t wb = plan_linear(m, n, k, group, epilogue, false, cfg, b) == Q4B_OK ? b.ws_bytes : 0;
-  return std::max(wa, wb);
+  if (epilogue < Q4B_EPI_STORE || epilogue > Q4B_EPI_SWIGLU) return 0;
+  static const int dummy[4] = {0, 0, 0, 0};  // never dereferenced: planning only
+  return linear_workspace(public_op(dummy, reinterpret_cast<const uint16_t*>(dummy), group, dummy, Q4B_F32,
+                                    const_cast<int*>(dummy), Q4B_F32, m, n, k, epilogue, cfg, nullptr, 0));
 }
 
 extern "C" int q4b_q4_linear(const int32_t* qweight, const uint16_t* scales, int group, const void* x, int x_dtype,
@@ -518,67 +981,9 @@ extern "C" int q4b_q4_linear(const int32_t* qweight, const uint16_t* scales, int
                              void* workspace, size_t workspace_bytes, q4b_stream_t stream) {
   int rc = validate_linear(qweight, scales, group, x, x_dtype, y, y_dtype, m, n, k, epilogue);
   if (rc) return rc;
-  const bool xf32 = x_dtype == Q4B_F32;
-  Plan pl;
-  if ((rc = plan_linear(m, n, k, group, epilogue, xf32, cfg, pl))) return rc;
-  if (pl.kernel == 1) {
-    if (!aligned(qweight, 16) || !aligned(x, 16)) {
-      if (cfg && cfg->kernel == 1) return set_error(Q4B_EINVAL, "q4_linear: qweight and x must be 16-byte aligned");
-      pl.kernel = 2;
-      pl.W = 8;
-    } else if (pl.ws_bytes > workspace_bytes || (pl.ws_bytes && !workspace) || !aligned(workspace, 16)) {
-      if (cfg && cfg->split > 1)
-        return set_error(Q4B_EINVAL, "q4_linear: workspace of %zu bytes needed, %zu given", pl.ws_bytes,
-                         workspace_bytes);
-      // no (or too little) workspace: cover K inside one CTA when possible, else the SIMT kernel
-      const int KT = k / TILE_K;
-      if (KT <= 32) {
-        pl.T = (KT + 7) / 8;
-        pl.W = (KT + pl.T - 1) / pl.T;
-        pl.kps = KT;
-        pl.nsplit = 1;
-        pl.smem = mma_smem(pl, m, xf32);
-        pl.ws_bytes = 0;
-      } else {
-        pl.kernel = 2;
-        pl.W = 8;
-      }
-    }
-  }
-  LinArgs a;
-  a.qw = qweight;
-  a.scales = reinterpret_cast<const __half*>(scales);
-  a.x = x;
-  a.y = y;
-  a.M = m;
-  a.N = n;
-  a.K = k;
-  a.G = group;
-  a.n_out = epilogue == Q4B_EPI_SWIGLU ? n / 2 : n;
-  a.KT = k / TILE_K;
-  a.kps = pl.kps;
-  a.nsplit = pl.nsplit;
-  a.epi = epilogue;
-  a.y_f32 = y_dtype == Q4B_F32;
-  a.ws = nullptr;
-  a.counters = nullptr;
-  if (pl.kernel == 1 && pl.nsplit > 1) {
-    a.counters = reinterpret_cast<unsigned*>(workspace);
-    a.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kCounterBytes);
-  }
-  cudaStream_t st = as_stream(stream);
-  cudaError_t e;
-  if (pl.kernel == 1) {
-    e = xf32 ? launch_mma<true>(pl, a, st) : launch_mma<false>(pl, a, st);
-  } else {
-    const long long warps = (long long)a.n_out * ((m + 7) / 8);
-    const int block = 256;
-    const long long grid = (warps + 7) / 8;
-    e = xf32 ? launch_pdl(q4_linear_simt<true>, dim3((unsigned)grid), dim3(block), 0, st, a)
-             : launch_pdl(q4_linear_simt<false>, dim3((unsigned)grid), dim3(block), 0, st, a);
-  }
-  if (e != cudaSuccess) return set_error(Q4B_ELAUNCH, "q4_linear: launch failed: %s", cudaGetErrorString(e));
-  return check_launch("q4_linear");
+  return linear_run(
+      public_op(qweight, scales, group, x, x_dtype, y, y_dtype, m, n, k, epilogue, cfg, workspace, workspace_bytes),
+      as_stream(stream));
 }
 
 // ---- allocation-free variant ---------------------------------------------------------------

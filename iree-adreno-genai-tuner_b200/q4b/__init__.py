@@ -3,8 +3,10 @@ scripts/llm/llama_q4.py (QLinear, QEmbedding, LlamaQ4) and runner/llm_runner.c (
 computed by hand-written CUDA in libq4b.so behind the C ABI of include/q4b.h."""
 
 from ._lib import LIB_PATH, LinearCfg, Q4BError, lib
-from .ops import dequantize_q4, q4_linear, quantize_q4, unpack_q4
+from .llama import LlamaQ4, StepFn, SyntheticStateDict, group_for, rope_tables
+from .ops import attention, dequantize_q4, embed_lookup, q4_linear, quantize_q4, rmsnorm, unpack_q4
 from .qlinear import QEmbedding, QLinear
 
 __all__ = ["LIB_PATH", "LinearCfg", "Q4BError", "lib", "quantize_q4", "unpack_q4", "dequantize_q4", "q4_linear",
-           "QLinear", "QEmbedding"]
+           "embed_lookup", "rmsnorm", "attention", "QLinear", "QEmbedding", "LlamaQ4", "StepFn", "SyntheticStateDict",
+           "group_for", "rope_tables"]

@@ -40,6 +40,21 @@ class LinearCfg(ctypes.Structure):
     _fields_ = [("kernel", c_int), ("warps", c_int), ("tiles", c_int), ("split", c_int)]
 
 
+class ModelCfg(ctypes.Structure):
+    _fields_ = [("n_layers", c_int), ("dim", c_int), ("n_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int),
+                ("inter", c_int), ("vocab", c_int), ("rms_eps", c_float), ("max_ctx", c_int), ("max_chunk", c_int),
+                ("tp_rank", c_int), ("tp_size", c_int)]
+
+
+class QMat(ctypes.Structure):
+    _fields_ = [("qweight", c_void_p), ("scales", c_void_p), ("n", c_int), ("k", c_int), ("group", c_int)]
+
+
+class LayerWeights(ctypes.Structure):
+    _fields_ = [("wqkv", QMat), ("wo", QMat), ("wgu", QMat), ("wdown", QMat), ("ln_in", c_void_p),
+                ("ln_post", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p)]
+
+
 # name -> (restype, argtypes); must match include/q4b.h
 SIGNATURES = {
     "q4b_last_error": (c_char_p, []),
@@ -52,6 +67,17 @@ SIGNATURES = {
                               c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "q4b_q4_linear_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
                                       c_int, c_int, c_void_p]),
+    "q4b_embed_q4_lookup": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "q4b_rmsnorm": (c_int, [c_void_p, c_void_p, c_float, c_int, c_int, c_void_p, c_void_p]),
+    "q4b_attention_workspace": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
+    "q4b_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                              c_void_p, c_size_t, c_void_p]),
+    "q4b_model_create": (c_int, [ctypes.POINTER(ModelCfg), ctypes.POINTER(c_void_p)]),
+    "q4b_model_set_layer": (c_int, [c_void_p, c_int, ctypes.POINTER(LayerWeights)]),
+    "q4b_model_set_head": (c_int, [c_void_p, ctypes.POINTER(QMat), c_void_p, c_void_p, c_void_p]),
+    "q4b_model_step": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "q4b_model_destroy": (None, [c_void_p]),
+    "q4b_device_status": (c_int, [c_int]),
 }
 
 _lib = None

@@ -122,3 +122,51 @@ def q4_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, grou
 def ctypes_byref(c):
     import ctypes
     return ctypes.byref(c)
+
+
+def embed_lookup(tokens: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, group: int):
+    """QEmbedding.lookup (scripts/llm/llama_q4.py:106-119): [C] ids -> [C, dim] fp32 rows (zeros
+    for ids outside the vocabulary)."""
+    _need_cuda(qweight, scales)
+    toks = tokens.reshape(-1).to(device=qweight.device, dtype=torch.int32).contiguous()
+    vocab, dim = qweight.shape[0], qweight.shape[1] * 8
+    out = torch.empty(toks.numel(), dim, dtype=torch.float32, device=qweight.device)
+    check(lib().q4b_embed_q4_lookup(toks.data_ptr(), toks.numel(), qweight.data_ptr(), scales.data_ptr(), vocab, dim,
+                                    group, out.data_ptr(), _stream()), "embed_q4_lookup")
+    return out
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float):
+    """rms_norm (scripts/llm/llama_q4.py:141-142) on fp32 [rows, dim]."""
+    _need_cuda(x, weight)
+    x2 = x.reshape(-1, x.shape[-1]).float().contiguous()
+    out = torch.empty_like(x2)
+    check(lib().q4b_rmsnorm(x2.data_ptr(), weight.float().contiguous().data_ptr(), eps, x2.shape[0], x2.shape[1],
+                            out.data_ptr(), _stream()), "rmsnorm")
+    return out.reshape(x.shape)
+
+
+_ATTN_WS = {}
+
+
+def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, start, L: int):
+    """Bucketed GQA attention (scripts/llm/llama_q4.py:208-232): q [C, H, hd] fp32 (RoPE applied),
+    caches fp16 [max_ctx, Hkv, hd], rows at positions start + c -> out [C, H * hd] fp32."""
+    _need_cuda(q, k_cache, v_cache)
+    C, H, hd = q.shape
+    Hkv = k_cache.shape[1]
+    st = torch.as_tensor([int(start)], dtype=torch.int32).to(q.device) if not torch.is_tensor(start) or \
+        not start.is_cuda else start.to(torch.int32)
+    out = torch.empty(C, H * hd, dtype=torch.float32, device=q.device)
+    need = lib().q4b_attention_workspace(C, H, Hkv, hd, L)
+    ws = None
+    if need:
+        key = (q.device.index, torch.cuda.current_stream().cuda_stream)
+        ws = _ATTN_WS.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.zeros(need, dtype=torch.uint8, device=q.device)
+            _ATTN_WS[key] = ws
+    check(lib().q4b_attention(q.float().contiguous().data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), st.data_ptr(),
+                              C, H, Hkv, hd, L, out.data_ptr(), 0 if ws is None else ws.data_ptr(),
+                              0 if ws is None else ws.numel(), _stream()), "attention")
+    return out

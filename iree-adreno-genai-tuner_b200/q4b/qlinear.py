@@ -83,8 +83,7 @@ class QEmbedding(nn.Module):
         return out
 
     def lookup(self, tokens: torch.Tensor) -> torch.Tensor:
-        from . import fused
-        return fused.embed_lookup(tokens, self.qweight, self.scales, self.group)
+        return ops.embed_lookup(tokens, self.qweight, self.scales, self.group)
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
         return ops.q4_linear(x.contiguous(), self.qweight, self.scales, self.group, out_dtype=torch.float32)

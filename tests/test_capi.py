@@ -71,9 +71,11 @@ def test_pack_rejects_bad_args_on_host(L):
 
 
 def test_linear_workspace_plan(L):
-    # 5120 x 3072, group 128, M = 1: split-K over 24 tiles of 128 -> partials + counters
-    ws = L.q4b_q4_linear_workspace(1, 5120, 3072, 128, 0, None)
-    assert ws > 0 and ws % 256 == 0
+    # decode 5120 x 3072, group 128, M = 1: all of K in one CTA, no workspace
+    assert L.q4b_q4_linear_workspace(1, 5120, 3072, 128, 0, None) == 0
+    # 16 rows of x over K = 8192 do not fit one CTA's shared memory: split-K partials + counters
+    ws = L.q4b_q4_linear_workspace(16, 3072, 8192, 128, 0, None)
+    assert ws > 65536 and ws % 256 == 0
     # a non-128 group uses the SIMT kernel, which needs no workspace
     assert L.q4b_q4_linear_workspace(1, 256, 688, 16, 0, None) == 0
     # a configuration without split needs none
