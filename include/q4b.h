@@ -168,6 +168,43 @@ int q4b_model_step(q4b_model* model, const int32_t* tokens, int n_tokens, int st
                    int32_t* next_token, float* logits, q4b_stream_t stream);
 void q4b_model_destroy(q4b_model* model);
 
+/* ---- runner (runner/llm_runner.c) ---------------------------------------------------------- */
+
+/* Scheduler options (llm_runner.c:35-45): prefill chunk, ascending KV buckets, schedule 0 =
+ * bucketed (smallest bucket >= tokens in cache) or 1 = max (always the largest); use_graphs: one
+ * captured CUDA graph per (phase, bucket); warmup: untimed calls per used (phase, bucket);
+ * sync_every_step: copy each decode step's inputs in and its token out and check stop ids on the
+ * host (the reference's per-call protocol) instead of running decode steps back to back. */
+typedef struct q4b_runner_opts {
+  int chunk;
+  const int32_t* buckets;
+  int n_buckets;
+  int schedule;
+  int use_graphs;
+  int warmup;
+  int sync_every_step;
+} q4b_runner_opts;
+
+/* Timings of one generate call (llm_runner.c:249-262). decode_ms sums the device time of the decode
+ * steps (CUDA events); decode_wall_ms is the host clock around the decode loop. */
+typedef struct q4b_report {
+  double warmup_ms, prefill_ms, ttft_ms, prefill_tok_s, decode_ms, decode_wall_ms, decode_tok_s;
+  int prompt_tokens, new_tokens, decode_steps;
+} q4b_report;
+
+typedef struct q4b_runner q4b_runner;
+
+/* The runner borrows the model (and its caches) for its lifetime. */
+int q4b_runner_create(q4b_model* model, const q4b_runner_opts* opts, q4b_runner** out);
+/* llm_runner.c:151-262: chunked prefill of prompt[n_prompt] (host ids), then greedy decode until
+ * max_new tokens (the prefill token included) or a stop id; out_tokens[max_new] receives them and
+ * *n_out their count. Errors as the reference: empty prompt, prompt + new > max_ctx, no bucket. */
+int q4b_runner_generate(q4b_runner* runner, const int32_t* prompt, int n_prompt, int max_new, const int32_t* stop_ids,
+                        int n_stop, int32_t* out_tokens, int* n_out, q4b_report* report);
+/* JSON report of the last generate call, in llm_runner.c's schema (valid until the next call). */
+const char* q4b_runner_report_json(q4b_runner* runner);
+void q4b_runner_destroy(q4b_runner* runner);
+
 /* Q4B_ETIMEOUT if a bounded device-side wait gave up since the last reset, else Q4B_OK. */
 int q4b_device_status(int reset);
 

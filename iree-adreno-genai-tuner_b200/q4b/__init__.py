@@ -6,7 +6,8 @@ from ._lib import LIB_PATH, LinearCfg, Q4BError, lib
 from .llama import LlamaQ4, StepFn, SyntheticStateDict, group_for, rope_tables
 from .ops import attention, dequantize_q4, embed_lookup, q4_linear, quantize_q4, rmsnorm, unpack_q4
 from .qlinear import QEmbedding, QLinear
+from .runner import SYNTHETIC, Runner
 
 __all__ = ["LIB_PATH", "LinearCfg", "Q4BError", "lib", "quantize_q4", "unpack_q4", "dequantize_q4", "q4_linear",
            "embed_lookup", "rmsnorm", "attention", "QLinear", "QEmbedding", "LlamaQ4", "StepFn", "SyntheticStateDict",
-           "group_for", "rope_tables"]
+           "group_for", "rope_tables", "Runner", "SYNTHETIC"]

@@ -55,6 +55,18 @@ class LayerWeights(ctypes.Structure):
                 ("ln_post", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p)]
 
 
+class RunnerOpts(ctypes.Structure):
+    _fields_ = [("chunk", c_int), ("buckets", c_void_p), ("n_buckets", c_int), ("schedule", c_int),
+                ("use_graphs", c_int), ("warmup", c_int), ("sync_every_step", c_int)]
+
+
+class Report(ctypes.Structure):
+    _fields_ = [("warmup_ms", ctypes.c_double), ("prefill_ms", ctypes.c_double), ("ttft_ms", ctypes.c_double),
+                ("prefill_tok_s", ctypes.c_double), ("decode_ms", ctypes.c_double),
+                ("decode_wall_ms", ctypes.c_double), ("decode_tok_s", ctypes.c_double), ("prompt_tokens", c_int),
+                ("new_tokens", c_int), ("decode_steps", c_int)]
+
+
 # name -> (restype, argtypes); must match include/q4b.h
 SIGNATURES = {
     "q4b_last_error": (c_char_p, []),
@@ -78,6 +90,11 @@ SIGNATURES = {
     "q4b_model_step": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "q4b_model_destroy": (None, [c_void_p]),
     "q4b_device_status": (c_int, [c_int]),
+    "q4b_runner_create": (c_int, [c_void_p, ctypes.POINTER(RunnerOpts), ctypes.POINTER(c_void_p)]),
+    "q4b_runner_generate": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p,
+                                    ctypes.POINTER(c_int), ctypes.POINTER(Report)]),
+    "q4b_runner_report_json": (c_char_p, [c_void_p]),
+    "q4b_runner_destroy": (None, [c_void_p]),
 }
 
 _lib = None
