@@ -3,6 +3,13 @@
   python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemv|decode] [--impl ours|reference]
 
 Prints ONE JSON line (rank 0). Workloads:
+  decode  (default) BASELINE config 4: Llama-3.2-3B-shape LlamaQ4 (28 layers, hidden 3072, 24 heads,
+          8 KV heads, head_dim 128, intermediate 8192, vocab 128256, tied, int4 group 128), seeded
+          random init generated on the GPU; 512-token random prompt, chunked prefill (chunk 128),
+          then greedy decode with KV buckets {256, ..., 4096} through the native runner (one CUDA
+          graph per bucket). One step = one decode token; --steps K times K decode tokens (K + 1
+          generated, the first from the prefill) after --warmup W untimed generate calls. At N > 1
+          the model is tensor-parallel over N GPUs (strong scaling). value = decode tokens/s.
   gemv    BASELINE config 1: int4 GEMV y[5120] = dequant(W)[5120, 3072] . x[3072], group 128, fp16 x/y.
           One step = 32 back-to-back calls over 32 distinct weight copies (260 MB > 126 MB L2), each
           a separate kernel launch captured in one CUDA graph (programmatic dependent launch lets a
@@ -33,6 +40,21 @@ GEMV_N, GEMV_K, GEMV_G = 5120, 3072, 128
 GEMV_BYTES = GEMV_N * GEMV_K // 2 + GEMV_N * (GEMV_K // GEMV_G) * 2 + GEMV_K * 2 + GEMV_N * 2  # 8,126,464
 GEMV_COPIES = 32
 METRIC_GEMV = "int4 GEMV HBM GB/s (5120x3072)"
+METRIC_DECODE = "3B-shape int4 batch-1 decode tokens/s"
+PROMPT_LEN, CHUNK, BUCKETS = 512, 128, [256, 512, 1024, 2048, 4096]
+
+
+def decode_bytes_per_token(cfg, pos, tp=1):
+    """Algorithmic HBM bytes of one decode token at position pos on one of tp GPUs: int4 weights +
+    fp16 scales of every projection and the lm_head shard, KV rows 0..pos read and row pos written."""
+    D, H, Hkv, hd = cfg["hidden_size"], cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
+    I, V, nl, G = cfg["intermediate_size"], cfg["vocab_size"], cfg["num_hidden_layers"], 128
+
+    def q4(n, k):
+        return n * k // 2 + n * (k // G) * 2
+    layer = q4((H + 2 * Hkv) * hd, D) + q4(D, H * hd) + q4(2 * I, D) + q4(D, I)
+    kv_row = nl * 2 * Hkv * hd * 2
+    return (nl * layer + q4(V, D) + kv_row * (pos + 1) + kv_row) / tp
 
 
 def peaks():
@@ -292,10 +314,181 @@ def run_gemv(args, rank, world, local, dist_mod):
     return line
 
 
+def cpu_decode_baseline(budget_s=20.0):
+    """Oracle port of one 3B decode token on the host cores, from a bounded sample: the four
+    projections of one layer (numpy dequantize_q4 + fp32 matmul, the reference's eager QLinear
+    form), GQA attention over 640 cached positions, and 1/8 of the lm_head rows; scaled to 28 layers
+    and the full vocabulary."""
+    import numpy as np
+
+    import golden_inputs as gi
+    from oracle import q4_oracle as O
+    D, H, Hkv, hd, I, V, n_layers = 3072, 24, 8, 128, 8192, 128256, 28
+    mats = [gi.synthetic_q4(n, k, 128, seed=n + k) for n, k in
+            [((H + 2 * Hkv) * hd, D), (D, H * hd), (2 * I, D), (D, I)]]
+    head = gi.synthetic_q4(V // 8, D, 128, seed=7)
+    rng = np.random.default_rng(0)
+    kc = rng.standard_normal((640, Hkv, hd)).astype(np.float16)
+    vc = rng.standard_normal((640, Hkv, hd)).astype(np.float16)
+    q = rng.standard_normal((1, H, hd)).astype(np.float32)
+    t_layer, t_head, n = [], [], 0
+    t_end = time.perf_counter() + budget_s
+    while (time.perf_counter() < t_end and n < 5) or n < 2:
+        t0 = time.perf_counter()
+        for (qw, sc) in mats:
+            W = O.dequantize_q4(qw, sc, 128)
+            _ = rng.standard_normal((1, W.shape[1])).astype(np.float32) @ W.T
+        O.attention(q, kc, vc, np.array([639]), 640, Hkv)
+        t1 = time.perf_counter()
+        W = O.dequantize_q4(head[0], head[1], 128)
+        _ = rng.standard_normal((1, D)).astype(np.float32) @ W.T
+        t2 = time.perf_counter()
+        t_layer.append(t1 - t0)
+        t_head.append(t2 - t1)
+        n += 1
+    tok_s = 1.0 / (n_layers * statistics.median(t_layer) + 8 * statistics.median(t_head))
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    return {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{n} x (one layer's 4 projections via numpy dequantize_q4 + fp32 matmul, attention over 640 "
+                      f"cached positions, 1/8 of the lm_head rows), scaled to 28 layers + full vocab; layer "
+                      f"{statistics.median(t_layer) * 1e3:.0f} ms, lm_head/8 {statistics.median(t_head) * 1e3:.0f} ms"}
+
+
+def run_decode(args, rank, world, local, dist_mod):
+    import numpy as np
+    import torch
+
+    import q4b
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = q4b.SYNTHETIC["3b"]
+    t0 = time.perf_counter()
+    model = q4b.LlamaQ4(None, group=128, max_ctx=4096, sd=q4b.SyntheticStateDict(cfg, seed=0, device=dev), cfg=cfg,
+                        max_chunk=CHUNK, tp_rank=rank, tp_size=world, device=dev)
+    if world > 1:
+        model.attach_tp(dist_mod)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    prompt = np.random.default_rng(0).integers(0, cfg["vocab_size"], PROMPT_LEN).tolist()
+    n_new = args.steps + 1
+    runner = q4b.Runner(model, CHUNK, BUCKETS, "bucketed", graphs=True)
+    for _ in range(args.warmup):
+        runner.generate(prompt, n_new)
+    if dist_mod:
+        dist_mod.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        toks, rep = runner.generate(prompt, n_new)
+    torch.cuda.synchronize()
+    if dist_mod:
+        dist_mod.barrier()
+    steps = rep["decode_steps"]
+    decode_ms = max_over_ranks(rep["decode_ms"], dist_mod)
+    value = steps / (decode_ms / 1e3)
+    # end to end through the public API with the reference's per-call protocol: each step copies its
+    # inputs in and its token out and the host checks stop ids
+    rs = q4b.Runner(model, CHUNK, BUCKETS, "bucketed", graphs=True, sync_every_step=True)
+    rs.generate(prompt, min(n_new, 17))
+    if dist_mod:
+        dist_mod.barrier()
+    toks_e2e, rep_e2e = rs.generate(prompt, n_new)
+    e2e_ms = max_over_ranks(rep_e2e["decode_wall_ms"], dist_mod)
+    same = toks_e2e == toks
+    gemv = None
+    if world == 1 and not args.no_gemv:
+        gemv = gemv_measure(dev, steps=50, warmup=5)
+    if rank != 0:
+        return None
+    pk = peaks()
+    pos = [PROMPT_LEN + i for i in range(steps)]
+    bytes_tok = statistics.mean(decode_bytes_per_token(cfg, p, world) for p in pos)
+    achieved = bytes_tok * value / 1e9
+    launches = 2 + 5 * cfg["num_hidden_layers"] + (0 if world == 1 else 2 * cfg["num_hidden_layers"] + 1)
+    line = {
+        "metric": METRIC_DECODE, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(decode_ms / steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights, fp32 activations, fp16 KV cache",
+        "data": "synthetic (seeded random init, random prompt ids)",
+        "config": {"workload": "Llama-3.2-3B-shape LlamaQ4 batch-1 decode (BASELINE config 4)",
+                   "prompt": PROMPT_LEN, "new_tokens": steps + 1, "chunk": CHUNK, "buckets": BUCKETS,
+                   "schedule": "bucketed", "parallelism": f"tp{world}",
+                   "l2": "inputs larger than L2: 1.66 GB of weights streamed per token",
+                   "graphs": "one CUDA graph per (phase, bucket), decode steps back to back on the device"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": profile_traffic("decode_step_3b"),
+                     "peak_source": pk["source"], "kernel": "decode step (q4_gemv_* dominant)",
+                     "algorithmic_bytes_per_token_per_gpu": round(bytes_tok)},
+        "e2e": {"value": round(steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
+                "h2d_bytes_per_step": 104, "d2h_bytes_per_step": 4,
+                "path": "q4b.Runner(sync_every_step=True).generate: per step state H2D, graph, token D2H, sync",
+                "tokens_match_async": same},
+        "gpu_launches": steps * launches,
+        "clocks": clk.summary(),
+        "prefill": {"ttft_ms": rep["ttft_ms"], "prefill_tok_s": rep["prefill_tok_s"], "chunks": rep["chunks"]},
+        "model_build_s": round(build_s, 1),
+        "tokens_head": toks[:8],
+    }
+    if gemv:
+        line["gemv_5120x3072"] = gemv
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_decode_baseline()
+    return line
+
+
+def gemv_measure(dev, steps=50, warmup=5):
+    """BASELINE config 1 inside the decode run: GB/s of 32 chained launches over distinct weights."""
+    import torch
+
+    from q4b import ops
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+    qws = [torch.randint(-2**31, 2**31 - 1, (GEMV_N, GEMV_K // 8), dtype=torch.int32, device=dev, generator=g)
+           for _ in range(GEMV_COPIES)]
+    scs = [(torch.randn(GEMV_N, GEMV_K // GEMV_G, device=dev, generator=g) * 0.02).abs().half()
+           for _ in range(GEMV_COPIES)]
+    x = torch.randn(1, GEMV_K, device=dev, generator=g).half()
+    ys = [torch.empty(1, GEMV_N, dtype=torch.float16, device=dev) for _ in range(GEMV_COPIES)]
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for i in range(GEMV_COPIES):
+            ops.q4_linear(x, qws[i], scs[i], GEMV_G, out=ys[i])
+        graph = torch.cuda.CUDAGraph()
+        graph.capture_begin()
+        for i in range(GEMV_COPIES):
+            ops.q4_linear(x, qws[i], scs[i], GEMV_G, out=ys[i])
+        graph.capture_end()
+        for _ in range(warmup):
+            graph.replay()
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    per_call = e0.elapsed_time(e1) / 1e3 / (steps * GEMV_COPIES)
+    pk = peaks()
+    gbs = GEMV_BYTES / per_call / 1e9
+    return {"metric": METRIC_GEMV, "value": round(gbs, 1), "unit": "GB/s", "us_per_call": round(per_call * 1e6, 3),
+            "frac": round(gbs / pk["hbm_gbs"], 4), "peak": pk["hbm_gbs"], "calls": steps * GEMV_COPIES,
+            "l2": f"{GEMV_COPIES} distinct weight copies (260 MB > L2)"}
+
+
 def run_reference(args, rank, world):
     """The reference arm: CPU restatement of the reference path on the host cores (rank 0 only)."""
     if rank != 0:
         return None
+    if args.workload == "decode":
+        cb = cpu_decode_baseline(budget_s=30.0)
+        return {"metric": METRIC_DECODE, "value": round(cb["value"], 4), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "int4 weights, fp32 compute", "data": "synthetic", "impl": "reference",
+                "config": {"workload": "Llama-3.2-3B-shape LlamaQ4 batch-1 decode (BASELINE config 4)",
+                           "prompt": PROMPT_LEN, "chunk": CHUNK, "buckets": BUCKETS},
+                "cpu_baseline": cb,
+                "e2e": {"value": round(cb["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
     if args.workload == "gemv":
         cb = cpu_gemv_baseline(budget_s=min(60.0, 3.0 * (args.steps + args.warmup)))
         return {"metric": METRIC_GEMV, "value": round(cb["value"], 4), "unit": "GB/s", "n_gpus": world,
@@ -312,15 +505,18 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", default="gemv", choices=["gemv"])
+    ap.add_argument("--steps", type=int, default=None, help="decode: tokens (255); gemv: graph replays (200)")
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
+    ap.add_argument("--no-gemv", action="store_true", help="decode: skip the config-1 GEMV sub-measurement")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gemv-cfg", default=None, help='JSON q4b_linear_cfg, e.g. {"warps":4,"tiles":2}')
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.steps is None:
+        args.steps = 255 if args.workload == "decode" else 200
     rank, world, local = dist_env()
     if args.impl == "reference":
         line = run_reference(args, rank, world)
@@ -329,7 +525,7 @@ def main():
         return
     dist_mod = init_dist(world, local)
     try:
-        line = run_gemv(args, rank, world, local, dist_mod)
+        line = (run_decode if args.workload == "decode" else run_gemv)(args, rank, world, local, dist_mod)
     finally:
         if dist_mod:
             dist_mod.barrier()
