@@ -168,6 +168,14 @@ int q4b_model_step(q4b_model* model, const int32_t* tokens, int n_tokens, int st
                    int32_t* next_token, float* logits, q4b_stream_t stream);
 void q4b_model_destroy(q4b_model* model);
 
+/* ---- tensor parallelism (one process per GPU, NCCL loaded at run time) ---------------------- */
+
+/* Rank 0 makes the communicator id (128 bytes) and shares it with the other ranks out of band. */
+int q4b_tp_unique_id(unsigned char* id, int id_bytes);
+/* Join the communicator of the model's tp_size ranks as tp_rank (collective across the ranks).
+ * Afterwards each step all-reduces the wo / wdown partial outputs and gathers the per-rank argmax. */
+int q4b_model_attach_tp(q4b_model* model, const unsigned char* id, int id_bytes);
+
 /* ---- runner (runner/llm_runner.c) ---------------------------------------------------------- */
 
 /* Scheduler options (llm_runner.c:35-45): prefill chunk, ascending KV buckets, schedule 0 =

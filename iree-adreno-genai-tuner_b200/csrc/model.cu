@@ -47,6 +47,7 @@ static LinearOp qop(const q4b_qmat& w, int m, const void* x, void* y, int epi) {
 }
 
 Model::~Model() {
+  tp_release();
   for (void* p : owned) cudaFree(p);
 }
 

@@ -39,6 +39,7 @@ struct Model {
   int step(const int32_t* toks, int C, int start, int last, int L, int32_t* next, float* logits, cudaStream_t st);
   int tp_allreduce_add(int C, cudaStream_t st);
   int tp_finish_argmax(int32_t* token_log, cudaStream_t st);
+  void tp_release();
 };
 
 }  // namespace q4b

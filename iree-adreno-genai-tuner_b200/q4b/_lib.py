@@ -90,6 +90,8 @@ SIGNATURES = {
     "q4b_model_step": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "q4b_model_destroy": (None, [c_void_p]),
     "q4b_device_status": (c_int, [c_int]),
+    "q4b_tp_unique_id": (c_int, [c_void_p, c_int]),
+    "q4b_model_attach_tp": (c_int, [c_void_p, c_void_p, c_int]),
     "q4b_runner_create": (c_int, [c_void_p, ctypes.POINTER(RunnerOpts), ctypes.POINTER(c_void_p)]),
     "q4b_runner_generate": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int, c_void_p,
                                     ctypes.POINTER(c_int), ctypes.POINTER(Report)]),

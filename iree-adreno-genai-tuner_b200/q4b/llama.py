@@ -102,16 +102,38 @@ class SyntheticStateDict:
             return False
 
 
+def shard_layer(cfg: dict, get, rank: int = 0, world: int = 1):
+    """Tensor-parallel shard of one layer's fp32 weights (scripts/llm/llama_q4.py:149-153 fused row
+    orders kept per rank). get(name) returns the full HF tensor "model.layers.i.<name>".
+      wqkv  rows q heads [rH/t, (r+1)H/t) | k heads [rHkv/t, ..) | v heads [rHkv/t, ..)  (column split)
+      wgu   rows gate [rI/t, (r+1)I/t) | up [rI/t, (r+1)I/t)                            (column split)
+      wo    columns of this rank's q heads; wdown columns [rI/t, (r+1)I/t)                (row split:
+            the partial outputs are summed across ranks)
+    Pure torch on whatever device get() returns."""
+    D, H, Hkv = cfg["hidden_size"], cfg["num_attention_heads"], cfg["num_key_value_heads"]
+    hd = cfg.get("head_dim") or D // H
+    I = cfg["intermediate_size"]
+    r, t = rank, world
+    if H % t or Hkv % t or I % t:
+        raise ValueError(f"heads {H}, KV heads {Hkv} and intermediate {I} must divide by {t}")
+
+    def rows(w, n):
+        return w[r * n:(r + 1) * n]
+
+    wqkv = torch.cat([rows(get("self_attn.q_proj.weight"), H // t * hd), rows(get("self_attn.k_proj.weight"),
+                      Hkv // t * hd), rows(get("self_attn.v_proj.weight"), Hkv // t * hd)], 0)
+    wo = get("self_attn.o_proj.weight")[:, r * (H // t) * hd:(r + 1) * (H // t) * hd].contiguous()
+    wgu = torch.cat([rows(get("mlp.gate_proj.weight"), I // t), rows(get("mlp.up_proj.weight"), I // t)], 0)
+    wdown = get("mlp.down_proj.weight")[:, r * (I // t):(r + 1) * (I // t)].contiguous()
+    return dict(wqkv=wqkv, wo=wo, wgu=wgu, wdown=wdown)
+
+
 class Layer(nn.Module):
     """scripts/llm/llama_q4.py:145-155 (fused q|k|v and gate|up), optionally one TP shard."""
 
     def __init__(self, cfg, sd, i, group, per_linear_group=False, tp_rank=0, tp_size=1, device="cuda"):
         super().__init__()
         p = f"model.layers.{i}."
-        D, H, Hkv = cfg["hidden_size"], cfg["num_attention_heads"], cfg["num_key_value_heads"]
-        hd = cfg.get("head_dim") or D // H
-        I = cfg["intermediate_size"]
-        r, t = tp_rank, tp_size
 
         def g(k):
             return group_for(k, group) if per_linear_group else group
@@ -119,20 +141,11 @@ class Layer(nn.Module):
         def get(name):
             return sd[p + name].to(device)
 
-        def rows(w, n, r):  # rank r's block of n rows
-            return w[r * n:(r + 1) * n]
-
-        q = rows(get("self_attn.q_proj.weight"), H // t * hd, r)
-        k = rows(get("self_attn.k_proj.weight"), Hkv // t * hd, r)
-        v = rows(get("self_attn.v_proj.weight"), Hkv // t * hd, r)
-        self.wqkv = QLinear(torch.cat([q, k, v], 0), g(D))
-        wo = get("self_attn.o_proj.weight")[:, r * (H // t) * hd:(r + 1) * (H // t) * hd]
-        self.wo = QLinear(wo.contiguous(), g(wo.shape[1]))
-        gate = rows(get("mlp.gate_proj.weight"), I // t, r)
-        up = rows(get("mlp.up_proj.weight"), I // t, r)
-        self.wgu = QLinear(torch.cat([gate, up], 0), g(D))
-        wd = get("mlp.down_proj.weight")[:, r * (I // t):(r + 1) * (I // t)]
-        self.wdown = QLinear(wd.contiguous(), g(wd.shape[1]))
+        w = shard_layer(cfg, get, tp_rank, tp_size)
+        for name in ("wqkv", "wo", "wgu", "wdown"):
+            if w[name].shape[1] % g(w[name].shape[1]):
+                raise ValueError(f"{name}: shard K={w[name].shape[1]} is not a multiple of its group")
+            setattr(self, name, QLinear(w[name], g(w[name].shape[1])))
         self.ln_in = nn.Parameter(get("input_layernorm.weight").float().contiguous(), requires_grad=False)
         self.ln_post = nn.Parameter(get("post_attention_layernorm.weight").float().contiguous(), requires_grad=False)
 
@@ -233,6 +246,22 @@ class LlamaQ4(nn.Module):
             _lib.check(L.q4b_model_set_head(h, ctypes.byref(head), self.ln_f.data_ptr(), self.cos.data_ptr(),
                                             self.sin.data_ptr()), "model_set_head")
         return self._handle
+
+    def attach_tp(self, dist_mod=None):
+        """Join this model's NCCL communicator (tp_size ranks, one process per GPU): rank 0 makes
+        the id and torch.distributed broadcasts it. Collective: every rank calls it."""
+        import torch.distributed as dist
+        dist_mod = dist_mod or dist
+        L = _lib.lib()
+        h = self.native()
+        uid = (ctypes.c_ubyte * 128)()
+        if self.tp_rank == 0:
+            _lib.check(L.q4b_tp_unique_id(uid, 128), "tp_unique_id")
+        obj = [bytes(uid)]
+        dist_mod.broadcast_object_list(obj, src=0)
+        uid = (ctypes.c_ubyte * 128).from_buffer_copy(obj[0])
+        with torch.cuda.device(self.device):
+            _lib.check(L.q4b_model_attach_tp(h, uid, 128), "model_attach_tp")
 
     def bind_caches(self, caches):
         """Point the native layers at these cache tensors (k0, v0, k1, v1, ...)."""
