@@ -66,7 +66,8 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
 // ---- attention ------------------------------------------------------------------------------
 
 constexpr int kMaxRows = 16;  // decode form: at most this many query rows (tokens x heads per KV head)
-constexpr int kChunk = 64;    // decode form: keys per CTA
+constexpr int kChunk = 256;   // decode form: keys per CTA
+constexpr int kMaxChunks = 64;  // decode form: chunks per KV head (L <= 16384)
 
 template <int EPL>
 __device__ __forceinline__ void load_half_vec(const __half* p, float (&v)[EPL]) {
@@ -88,14 +89,26 @@ __device__ __forceinline__ void load_half_vec(const __half* p, float (&v)[EPL]) 
   }
 }
 
-// grid (Hkv, nchunk), block 128. Query row r of KV head kvh: token c = r / g, head kvh*g + r % g.
-// ROWS >= C * g query rows are kept in registers.
-template <int EPL, int ROWS>
-__global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
-  constexpr int HD = EPL * 32;
-  constexpr int kMaxRows = ROWS;
-  __shared__ float s_m[4][kMaxRows], s_l[4][kMaxRows];
-  __shared__ float s_o[4][kMaxRows][HD];
+// grid (Hkv, nchunk), block 256 (8 warps x 32 keys = kChunk keys per CTA). Query row r of KV head
+// kvh: token c = r / g, head kvh*g + r % g; ROWS >= C * g rows.
+//   Q.K: lane j owns key k0 + 32 w + j; it loads the key's whole row and dots it with every query
+//        row (read from shared memory as broadcasts), so a warp covers 32 keys with no shuffles.
+//   softmax: max and sum over the warp's 32 keys per query row (two shuffle reductions per row).
+//   P.V: lanes own head elements (hd / 32 each); the warp's 32 V slices were loaded together with
+//        the K rows, so the CTA waits for DRAM once.
+// Warp partials (max, sum, weighted V) merge in shared memory. One chunk covers the context up to
+// kChunk keys and writes the output directly; longer contexts merge chunk partials through the
+// workspace (last CTA of a KV head, chunk order, loads issued in parallel).
+template <int HD, int ROWS>
+__global__ void __launch_bounds__(256) attn_decode_kernel(AttnArgs a) {
+  constexpr int EPL = HD / 32;  // head elements per lane in P.V
+  constexpr int KU4 = HD / 8;   // 16-byte pieces of one key row
+  constexpr int NW = kChunk / 32;
+  extern __shared__ __align__(16) float s_o[];  // [NW][ROWS][HD]
+  __shared__ float s_q[ROWS][HD];
+  __shared__ float s_m[NW][ROWS], s_l[NW][ROWS];
+  __shared__ float s_M[ROWS], s_L[ROWS];
+  __shared__ float s_cs[kMaxChunks][ROWS], s_lc[kMaxChunks][ROWS];
   __shared__ int s_last;
   const int kvh = blockIdx.x, chunk = blockIdx.y, nchunk = gridDim.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -104,88 +117,113 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
   griddep_launch_dependents();
   griddep_wait();
   const int start = *a.pos0;
-  const int kend_cta = min(a.L, start + a.C);  // keys any row of this step can see
-  const int k0 = chunk * kChunk, k1 = min(k0 + kChunk, kend_cta);
-  const float scale = a.scale;
+  const int kend = min(a.L, start + a.C);  // keys any row of this step can see
+  const int k0 = chunk * kChunk, k1 = min(k0 + kChunk, kend);
+  const int jbase = k0 + 32 * warp, j = jbase + lane;
+  const size_t row_stride = (size_t)a.Hkv * HD;
 
-  // q rows in registers (lane holds elements lane*EPL .. +EPL of each row)
-  float q[kMaxRows][EPL];
-  int nk[kMaxRows];
+  // all loads of this warp first: its lane's K row and the 32 V slices of its lane's elements
+  uint4 kr[KU4];
+  if (j < k1) {
+    const uint4* kp = reinterpret_cast<const uint4*>(a.k_cache + (size_t)j * row_stride + (size_t)kvh * HD);
 #pragma unroll
-  for (int r = 0; r < kMaxRows; ++r) {
-    if (r < R) {
-      const int c = r / g, h = kvh * g + r % g;
-      const float* qp = a.q + ((size_t)c * a.H + h) * HD + lane * EPL;
+    for (int u = 0; u < KU4; ++u) kr[u] = kp[u];
+  } else {
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) q[r][e] = qp[e];
-      nk[r] = min(a.L, start + c + 1);
-    } else {
-      nk[r] = 0;
-    }
+    for (int u = 0; u < KU4; ++u) kr[u] = make_uint4(0u, 0u, 0u, 0u);
   }
-  float m[kMaxRows], l[kMaxRows], o[kMaxRows][EPL];
+  float vv[32][EPL];
 #pragma unroll
-  for (int r = 0; r < kMaxRows; ++r) {
-    m[r] = -INFINITY;
-    l[r] = 0.0f;
+  for (int jj = 0; jj < 32; ++jj) {
+    if (jbase + jj < k1)
+      load_half_vec<EPL>(a.v_cache + (size_t)(jbase + jj) * row_stride + (size_t)kvh * HD + lane * EPL, vv[jj]);
+    else
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) o[r][e] = 0.0f;
+      for (int e = 0; e < EPL; ++e) vv[jj][e] = 0.0f;
   }
-  const size_t kv_stride = (size_t)a.Hkv * HD;
-  for (int j = k0 + warp; j < k1; j += 4) {
-    float kv[EPL], vv[EPL];
-    load_half_vec<EPL>(a.k_cache + (size_t)j * kv_stride + (size_t)kvh * HD + lane * EPL, kv);
-    load_half_vec<EPL>(a.v_cache + (size_t)j * kv_stride + (size_t)kvh * HD + lane * EPL, vv);
-#pragma unroll
-    for (int r = 0; r < kMaxRows; ++r) {
-      if (r < R) {
-        float d = 0.0f;
-#pragma unroll
-        for (int e = 0; e < EPL; ++e) d = fmaf(q[r][e], kv[e], d);
-        d = warp_sum(d) * scale;
-        if (j < nk[r]) {
-          const float mn = fmaxf(m[r], d);
-          const float cs = expf(m[r] - mn), p = expf(d - mn);
-          l[r] = l[r] * cs + p;
-#pragma unroll
-          for (int e = 0; e < EPL; ++e) o[r][e] = o[r][e] * cs + p * vv[e];
-          m[r] = mn;
-        }
-      }
-    }
-  }
-  // merge the 4 warps
-#pragma unroll
-  for (int r = 0; r < kMaxRows; ++r) {
-    if (r < R) {
-      if (lane == 0) {
-        s_m[warp][r] = m[r];
-        s_l[warp][r] = l[r];
-      }
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) s_o[warp][r][lane * EPL + e] = o[r][e];
-    }
+  for (int i = threadIdx.x; i < R * HD; i += blockDim.x) {
+    const int r = i / HD, e = i - r * HD;
+    s_q[r][e] = a.q[((size_t)(r / g) * a.H + kvh * g + r % g) * HD + e];
   }
   __syncthreads();
+
+  // scores of this lane's key, softmax over the warp's keys, weighted V
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) {
+    if (r >= R) continue;
+    float o[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) o[e] = 0.0f;
+    float mw = -INFINITY, lw = 0.0f;
+    float d = 0.0f;
+#pragma unroll
+    for (int u = 0; u < KU4; ++u) {
+      const __half2* h2 = reinterpret_cast<const __half2*>(&kr[u]);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __half22float2(h2[t]);
+        d = fmaf(s_q[r][8 * u + 2 * t], f.x, d);
+        d = fmaf(s_q[r][8 * u + 2 * t + 1], f.y, d);
+      }
+    }
+    const int nk = min(a.L, start + r / g + 1);  // keys 0..nk-1 are unmasked for this row
+    const float sc = j < nk ? d * a.scale : -INFINITY;
+    const float m = warp_max(sc);
+    if (m != -INFINITY) {  // else no visible key for this row in this warp
+      const float p = expf(sc - m);
+      mw = m;
+      lw = warp_sum(p);
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const float pj = __shfl_sync(0xffffffffu, p, jj);
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) o[e] = fmaf(pj, vv[jj][e], o[e]);
+      }
+    }
+    if (lane == 0) {
+      s_m[warp][r] = mw;
+      s_l[warp][r] = lw;
+    }
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) s_o[((size_t)warp * ROWS + r) * HD + lane * EPL + e] = o[e];
+  }
+  __syncthreads();
+  // merge the warps: this CTA's (max, sum, weighted V) per row
+  if (threadIdx.x < R) {
+    const int r = threadIdx.x;
+    float mm = -INFINITY;
+    for (int w = 0; w < NW; ++w) mm = fmaxf(mm, s_m[w][r]);
+    float ll = 0.0f;
+    for (int w = 0; w < NW; ++w) {
+      const float cs = s_m[w][r] == -INFINITY ? 0.0f : expf(s_m[w][r] - mm);
+      s_cs[w][r] = cs;
+      ll += s_l[w][r] * cs;
+    }
+    s_M[r] = mm;
+    s_L[r] = ll;
+  }
+  __syncthreads();
+  if (nchunk == 1) {  // the whole context in this CTA: write the output
+    for (int i = threadIdx.x; i < R * HD; i += blockDim.x) {
+      const int r = i / HD, e = i - r * HD;
+      float oo = 0.0f;
+      for (int w = 0; w < NW; ++w) oo += s_o[((size_t)w * ROWS + r) * HD + e] * s_cs[w][r];
+      a.out[((size_t)(r / g) * a.H + kvh * g + r % g) * HD + e] = oo / s_L[r];
+    }
+    return;
+  }
   float* part = a.ws + ((size_t)kvh * nchunk + chunk) * R * (HD + 2);  // [R][m, l, o[HD]]
   for (int i = threadIdx.x; i < R * HD; i += blockDim.x) {
     const int r = i / HD, e = i - r * HD;
-    float mm = -INFINITY;
-    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, s_m[w][r]);
-    float ll = 0.0f, oo = 0.0f;
-    for (int w = 0; w < 4; ++w) {
-      if (s_m[w][r] == -INFINITY) continue;
-      const float cs = expf(s_m[w][r] - mm);
-      ll += s_l[w][r] * cs;
-      oo += s_o[w][r][e] * cs;
-    }
+    float oo = 0.0f;
+    for (int w = 0; w < NW; ++w) oo += s_o[((size_t)w * ROWS + r) * HD + e] * s_cs[w][r];
     part[r * (HD + 2) + 2 + e] = oo;
     if (e == 0) {
-      part[r * (HD + 2)] = mm;
-      part[r * (HD + 2) + 1] = ll;
+      part[r * (HD + 2)] = s_M[r];
+      part[r * (HD + 2) + 1] = s_L[r];
     }
   }
-  // the last chunk CTA of this KV head merges all chunks in order
+  // the last chunk CTA of this KV head merges all chunks
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[kvh], 1u) == (unsigned)(nchunk - 1);
@@ -193,21 +231,33 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnArgs a) {
   if (!s_last) return;
   __threadfence();
   const float* all = a.ws + (size_t)kvh * nchunk * R * (HD + 2);
+  // every chunk's (max, sum) in one parallel round of loads, then per-chunk weights
+  for (int i = threadIdx.x; i < nchunk * R; i += blockDim.x) {
+    const int ch = i / R, r = i - ch * R;
+    s_cs[ch][r] = __ldcg(all + ((size_t)ch * R + r) * (HD + 2));
+    s_lc[ch][r] = __ldcg(all + ((size_t)ch * R + r) * (HD + 2) + 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < R) {
+    const int r = threadIdx.x;
+    float mm = -INFINITY;
+    for (int ch = 0; ch < nchunk; ++ch) mm = fmaxf(mm, s_cs[ch][r]);
+    float ll = 0.0f;
+    for (int ch = 0; ch < nchunk; ++ch) {
+      const float mc = s_cs[ch][r];
+      const float cs = mc == -INFINITY ? 0.0f : expf(mc - mm);
+      ll += s_lc[ch][r] * cs;
+      s_cs[ch][r] = cs;
+    }
+    s_L[r] = ll;
+  }
+  __syncthreads();
   for (int i = threadIdx.x; i < R * HD; i += blockDim.x) {
     const int r = i / HD, e = i - r * HD;
-    float mm = -INFINITY;
-    for (int ch = 0; ch < nchunk; ++ch) mm = fmaxf(mm, __ldcg(all + ((size_t)ch * R + r) * (HD + 2)));
-    float ll = 0.0f, oo = 0.0f;
-    for (int ch = 0; ch < nchunk; ++ch) {
-      const float* pp = all + ((size_t)ch * R + r) * (HD + 2);
-      const float mc = __ldcg(pp);
-      if (mc == -INFINITY) continue;
-      const float cs = expf(mc - mm);
-      ll += __ldcg(pp + 1) * cs;
-      oo += __ldcg(pp + 2 + e) * cs;
-    }
-    const int c = r / g, h = kvh * g + r % g;
-    a.out[((size_t)c * a.H + h) * HD + e] = oo / ll;
+    float oo = 0.0f;
+#pragma unroll 8
+    for (int ch = 0; ch < nchunk; ++ch) oo += s_cs[ch][r] * __ldcg(all + ((size_t)ch * R + r) * (HD + 2) + 2 + e);
+    a.out[((size_t)(r / g) * a.H + kvh * g + r % g) * HD + e] = oo / s_L[r];
   }
   if (threadIdx.x == 0) a.counters[kvh] = 0u;
 }
@@ -259,12 +309,27 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
 
 int attn_decode_chunks(int L) { return (L + kChunk - 1) / kChunk; }
 
+template <int HD, int ROWS>
+static cudaError_t launch_decode_hd(const AttnArgs& a, dim3 grid, cudaStream_t st) {
+  const size_t smem = (size_t)(kChunk / 32) * ROWS * HD * sizeof(float);
+  static unsigned long long done = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(done >> (dev & 63) & 1ull)) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(attn_decode_kernel<HD, ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    done |= 1ull << (dev & 63);
+  }
+  return launch_pdl(attn_decode_kernel<HD, ROWS>, grid, dim3(256), smem, st, a);
+}
+
 template <int ROWS>
 static cudaError_t launch_decode(const AttnArgs& a, dim3 grid, cudaStream_t st) {
   switch (a.head_dim) {
-    case 32: return launch_pdl(attn_decode_kernel<1, ROWS>, grid, dim3(128), 0, st, a);
-    case 64: return launch_pdl(attn_decode_kernel<2, ROWS>, grid, dim3(128), 0, st, a);
-    default: return launch_pdl(attn_decode_kernel<4, ROWS>, grid, dim3(128), 0, st, a);
+    case 32: return launch_decode_hd<32, ROWS>(a, grid, st);
+    case 64: return launch_decode_hd<64, ROWS>(a, grid, st);
+    default: return launch_decode_hd<128, ROWS>(a, grid, st);
   }
 }
 
@@ -280,6 +345,8 @@ int attention_run(const AttnArgs& in, cudaStream_t st) {
   if (a.H % a.Hkv || (a.head_dim != 32 && a.head_dim != 64 && a.head_dim != 128))
     return set_error(Q4B_EUNSUPPORTED, "attention: head_dim must be 32, 64 or 128 and H %% Hkv == 0");
   const bool decode = a.C * g <= kMaxRows;
+  if (decode && attn_decode_chunks(a.L) > kMaxChunks)
+    return set_error(Q4B_EUNSUPPORTED, "attention: bucket %d above %d keys", a.L, kMaxChunks * kChunk);
   cudaError_t e;
   if (decode) {
     const size_t need = attention_workspace(a.C, a.H, a.Hkv, a.head_dim, a.L);

@@ -202,10 +202,10 @@ int Model::forward(const int32_t* toks, int C, int L, float* logits, int32_t* to
   head.qweight = embed.qweight + (size_t)cfg.tp_rank * V * (D / 8);
   head.scales = embed.scales + (size_t)cfg.tp_rank * V * (D / embed.group);
   head.n = V;
-  LinearOp op = qop(head, 1, h, nullptr, EPI_ARGMAX);
-  op.ln_w = ln_f;
-  op.eps = cfg.rms_eps;
-  op.row_sel = &state->last;
+  // the final norm of the one selected row, once (the lm_head has thousands of CTAs; a fused
+  // prologue would re-read and re-reduce the row in every one of them)
+  if ((rc = rmsnorm_run(h, ln_f, cfg.rms_eps, 1, D, &state->last, xn, st))) return rc;
+  LinearOp op = qop(head, 1, xn, nullptr, EPI_ARGMAX);
   op.state = state;
   op.token_log = token_log;
   op.logits = logits;
