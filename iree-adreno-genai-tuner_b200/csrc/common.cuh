@@ -84,7 +84,7 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + expf(-x)); }
 
-// ---- mbarrier + bulk copy (TMA engine; never with .multicast::cluster) -------------------------
+// ---- mbarrier + bulk copy (TMA engine; each copy lands in this CTA's own shared memory) ----------------
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -66,6 +66,7 @@ struct LinArgs {
   float* logits;
   int index_offset;
   int finalize;
+  int RT;  // row tiles of the whole problem (the argmax epilogue counts finished tiles)
 };
 
 // status word of this file's kernels (bounded waits that gave up), read by linear_status()
@@ -256,7 +257,7 @@ __device__ void epilogue_tile(const LinArgs& p, const float* fin, int rt, int* s
       }
       atomicMax(&p.state->best, best);
       __threadfence();
-      *s_flag = p.finalize && (atomicAdd(&p.state->counter, 1u) == gridDim.x - 1);
+      *s_flag = p.finalize && (atomicAdd(&p.state->counter, 1u) == (unsigned)(p.RT - 1));
       if (*s_flag) {
         __threadfence();
         const unsigned long long b = atomicExch(&p.state->best, 0ull);
@@ -318,11 +319,11 @@ __device__ void epilogue_tile(const LinArgs& p, const float* fin, int rt, int* s
 // fin: M*16 floats, aliasing the x staging area), finish split-K through the workspace (last CTA
 // of a row tile, fixed order), then the epilogue.
 template <int MT>
-__device__ __forceinline__ void finish_tile(const LinArgs& p, float (&acc)[MT][4], float* red, int* s_flag) {
+__device__ __forceinline__ void finish_tile(const LinArgs& p, float (&acc)[MT][4], float* red, int* s_flag, int rt,
+                                            int sp) {
   const int W = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int rt = blockIdx.x, sp = blockIdx.y;
   __syncthreads();
   constexpr int MP = MT * 8;
   float* fin = red + (size_t)W * MP * 16;
@@ -344,7 +345,7 @@ __device__ __forceinline__ void finish_tile(const LinArgs& p, float (&acc)[MT][4
   }
   __syncthreads();
   if (p.nsplit > 1) {
-    const size_t NR = (size_t)gridDim.x * 16;
+    const size_t NR = (size_t)p.RT * 16;
     for (int i = threadIdx.x; i < items; i += blockDim.x) {
       const int m = i >> 4, r = i & 15;
       p.ws[((size_t)sp * p.M + m) * NR + (size_t)rt * 16 + r] = fin[i];
@@ -371,9 +372,15 @@ __device__ __forceinline__ void finish_tile(const LinArgs& p, float (&acc)[MT][4
 template <int MT, bool XF32>
 __device__ __forceinline__ void mma_tile(const uint4& wa, const uint4& wb, float sa, float sb, const uint4* xs_hi,
                                          const uint4* xs_lo, const int (&mrow)[MT], int wbase, float (&acc)[MT][4]) {
-  float part[MT][4];
+  // two independent accumulator chains per n-tile (even / odd MMA of each word, and the lo terms
+  // in a third / fourth) so consecutive MMAs do not wait on each other
+  float part[MT][2][4], partl[MT][2][4];
 #pragma unroll
-  for (int nt = 0; nt < MT; ++nt) part[nt][0] = part[nt][1] = part[nt][2] = part[nt][3] = 0.0f;
+  for (int nt = 0; nt < MT; ++nt)
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) part[nt][c][e] = partl[nt][c][e] = 0.0f;
   const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
   const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
@@ -385,21 +392,24 @@ __device__ __forceinline__ void mma_tile(const uint4& wa, const uint4& wb, float
 #pragma unroll
     for (int nt = 0; nt < MT; ++nt) {
       const uint4 xh = xs_hi[mrow[nt] + ph];
-      mma_16816(part[nt], A[0], B[0], A[1], B[1], xh.x, xh.y);
-      mma_16816(part[nt], A[2], B[2], A[3], B[3], xh.z, xh.w);
+      mma_16816(part[nt][0], A[0], B[0], A[1], B[1], xh.x, xh.y);
+      mma_16816(part[nt][1], A[2], B[2], A[3], B[3], xh.z, xh.w);
       if constexpr (XF32) {
         const uint4 xl = xs_lo[mrow[nt] + ph];
-        mma_16816(part[nt], A[0], B[0], A[1], B[1], xl.x, xl.y);
-        mma_16816(part[nt], A[2], B[2], A[3], B[3], xl.z, xl.w);
+        mma_16816(partl[nt][0], A[0], B[0], A[1], B[1], xl.x, xl.y);
+        mma_16816(partl[nt][1], A[2], B[2], A[3], B[3], xl.z, xl.w);
       }
     }
   }
 #pragma unroll
   for (int nt = 0; nt < MT; ++nt) {
-    acc[nt][0] = fmaf(sa, part[nt][0], acc[nt][0]);
-    acc[nt][1] = fmaf(sa, part[nt][1], acc[nt][1]);
-    acc[nt][2] = fmaf(sb, part[nt][2], acc[nt][2]);
-    acc[nt][3] = fmaf(sb, part[nt][3], acc[nt][3]);
+    float v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = (part[nt][0][e] + part[nt][1][e]) + (partl[nt][0][e] + partl[nt][1][e]);
+    acc[nt][0] = fmaf(sa, v[0], acc[nt][0]);
+    acc[nt][1] = fmaf(sa, v[1], acc[nt][1]);
+    acc[nt][2] = fmaf(sb, v[2], acc[nt][2]);
+    acc[nt][3] = fmaf(sb, v[3], acc[nt][3]);
   }
 }
 
@@ -462,7 +472,7 @@ __global__ void __launch_bounds__(256) q4_gemv_reg(LinArgs p) {
     const int kt = kt0 + warp + W * j;
     if (kt < kt1) mma_tile<MT, XF32>(wa[j], wb[j], sa[j], sb[j], xs_hi, xs_lo, mrow, (kt - kt0) * 16 + 4 * t, acc);
   }
-  finish_tile<MT>(p, acc, reinterpret_cast<float*>(smem_raw), &s_flag);
+  finish_tile<MT>(p, acc, reinterpret_cast<float*>(smem_raw), &s_flag, rt, sp);
 }
 
 // ---- kernel 3: weights streamed into shared memory by the TMA engine ---------------------------
@@ -538,7 +548,152 @@ __global__ void __launch_bounds__(256) q4_gemv_tma(LinArgs p) {
     const uint4 wb = *reinterpret_cast<const uint4*>(swb + kl * 64);
     mma_tile<MT, XF32>(wa, wb, sa, sb, xs_hi, xs_lo, mrow, kl * 16 + 4 * t, acc);
   }
-  finish_tile<MT>(p, acc, reinterpret_cast<float*>(smem_raw + p.x_off), &s_flag);
+  finish_tile<MT>(p, acc, reinterpret_cast<float*>(smem_raw + p.x_off), &s_flag, rt, sp);
+}
+
+// ---- kernel 4: persistent, weights streamed through a TMA ring ---------------------------------
+//
+// For decode (M == 1, G == 128, K % 1024 == 0, K <= 8192). One CTA per SM loops over row tiles
+// rt = blockIdx.x, + gridDim.x, ...; a stage is one row tile's 16 rows x SK k (SK = K up to 4096,
+// else K / 2), i.e. 24 or 32 KB, kept kStreamRing stages deep. Warp 0's lanes issue the stage's
+// bulk copies in parallel (lane r < 16 the weight row r, lane 16 + r its scales) onto one mbarrier
+// per ring slot; the first stages are issued before griddepcontrol.wait, so the projection's
+// weight stream starts while the previous kernel finishes. x is staged once per CTA. Each warp
+// computes its 128-k tiles of a stage; a row tile's 16 sums are reduced across warps in shared
+// memory, the residual operand is fetched when the tile starts, and the greedy-head keys are
+// folded per CTA (one atomic per CTA).
+constexpr int kStreamRing = 3;
+
+__device__ __forceinline__ int stream_sk(int K) { return K <= 4096 ? K : K / 2; }
+
+template <bool XF32>
+__global__ void __launch_bounds__(768) q4_gemv_stream(LinArgs p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t full[kStreamRing];
+  __shared__ float s_red[2][24][16];  // by row-tile parity: warps may finish the next tile first
+  __shared__ float s_fin[16];
+  __shared__ int s_flag;
+  __shared__ float s_rs[8];
+  __shared__ float s_scratch[64];
+  const int W = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int SK = stream_sk(p.K);
+  const int KC = p.K / SK;            // stages per row tile
+  const int TPS = SK / TILE_K;        // 128-k tiles per stage
+  const int SWB = 16 * SK / 2;        // weight bytes per stage
+  const int SSB = 16 * (SK / 128) * 2;  // scale bytes per stage
+  const int my_tiles = (p.RT - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int nstages = my_tiles * KC;
+  unsigned char* ring_w = smem_raw;
+  __half* ring_s = reinterpret_cast<__half*>(smem_raw + kStreamRing * SWB);
+  uint4* xs_hi = reinterpret_cast<uint4*>(smem_raw + p.x_off);
+  const int rstride = p.K / 8 + 4;  // all of K is staged
+  uint4* xs_lo = xs_hi + rstride;
+  const unsigned char* q8 = reinterpret_cast<const unsigned char*>(p.qw);
+  const int KG = p.K / 128;
+
+  auto issue = [&](int i) {  // warp 0: stage i into ring slot i % kStreamRing
+    const int slot = i % kStreamRing;
+    const int rt = (int)blockIdx.x + (i / KC) * (int)gridDim.x, kc = i % KC;
+    if (lane == 0) mbar_arrive_expect_tx(&full[slot], SWB + SSB);
+    __syncwarp();
+    const int r = lane & 15;
+    const int row = tile_row(p, rt, r);
+    if (lane < 16)
+      bulk_g2s(ring_w + slot * SWB + r * (SK / 2), q8 + (size_t)row * (p.K / 2) + (size_t)kc * (SK / 2), SK / 2,
+               &full[slot]);
+    else
+      bulk_g2s(ring_s + slot * (SSB / 2) + r * (SK / 128), p.scales + (size_t)row * KG + kc * (SK / 128),
+               (SK / 128) * 2, &full[slot]);
+  };
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int s = 0; s < kStreamRing; ++s) mbar_init(&full[s], 1);
+      fence_mbar_init();
+    }
+    __syncwarp();
+    for (int i = 0; i < kStreamRing && i < nstages; ++i) issue(i);
+  }
+  griddep_launch_dependents();
+  griddep_wait();
+
+  if (p.ln_w) prologue_rms(p, s_rs, s_scratch);
+  stage_x<XF32>(p, s_rs, xs_hi, xs_lo, rstride, 0, p.K / 8);
+  __syncthreads();
+
+  unsigned long long best = 0;  // thread 0: this CTA's greedy-head key
+  float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+  int mrow[1];
+  mrow[0] = 0;
+  float yres = 0.0f;  // thread s < 16: residual operand of slot s of the current row tile
+  for (int i = 0; i < nstages; ++i) {
+    const int slot = i % kStreamRing;
+    const int rt = (int)blockIdx.x + (i / KC) * (int)gridDim.x, kc = i % KC;
+    if (kc == 0 && p.epi == EPI_ACCUMULATE && threadIdx.x < 16) {
+      const int col = rt * 16 + threadIdx.x;
+      yres = col < p.N ? load_y(p.y, col, p.y_f32) : 0.0f;
+    }
+    const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)((i / kStreamRing) & 1), kWaitLimitNs);
+    if (__syncthreads_or(!ok)) {
+      if (threadIdx.x == 0) atomicOr(&g_linear_status, kStatusTimeout);
+      return;
+    }
+    const unsigned char* sw = ring_w + slot * SWB + t * 16;
+    const __half* ss = ring_s + slot * (SSB / 2);
+    for (int tl = warp; tl < TPS; tl += W) {
+      const uint4 wa = *reinterpret_cast<const uint4*>(sw + g * (SK / 2) + tl * 64);
+      const uint4 wb = *reinterpret_cast<const uint4*>(sw + (g + 8) * (SK / 2) + tl * 64);
+      const float sa = __half2float(ss[g * (SK / 128) + tl]);
+      const float sb = __half2float(ss[(g + 8) * (SK / 128) + tl]);
+      mma_tile<1, XF32>(wa, wb, sa, sb, xs_hi, xs_lo, mrow, (kc * TPS + tl) * 16 + 4 * t, acc);
+    }
+    if (kc == KC - 1) {  // row tile done: column 0 of the accumulators (lanes with t == 0)
+      if (t == 0) {
+        s_red[(i / KC) & 1][warp][g] = acc[0][0];
+        s_red[(i / KC) & 1][warp][g + 8] = acc[0][2];
+      }
+      acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.0f;
+    }
+    __syncthreads();  // the slot is free again; s_red is complete
+    if (warp == 0 && i + kStreamRing < nstages) issue(i + kStreamRing);
+    if (kc == KC - 1) {
+      if (threadIdx.x < 16) {
+        float v = 0.0f;
+        for (int w = 0; w < W; ++w) v += s_red[(i / KC) & 1][w][threadIdx.x];
+        if (p.epi == EPI_ARGMAX) {
+          const int row = rt * 16 + threadIdx.x;
+          unsigned long long key = 0;
+          if (row < p.N) {
+            if (p.logits) p.logits[row] = v;
+            key = argmax_key(v, (unsigned)(p.index_offset + row));
+          }
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0x0000ffffu, key, o));
+          if (threadIdx.x == 0) best = max(best, key);
+        } else if (p.epi == EPI_ACCUMULATE) {
+          const int col = rt * 16 + threadIdx.x;
+          if (col < p.N) store_y(p.y, col, yres + v, p.y_f32);
+        } else {
+          s_fin[threadIdx.x] = v;
+        }
+      }
+      if (p.epi != EPI_ARGMAX && p.epi != EPI_ACCUMULATE) {
+        __syncthreads();
+        epilogue_tile(p, s_fin, rt, &s_flag);
+      }
+    }
+  }
+  if (p.epi == EPI_ARGMAX && threadIdx.x == 0) {
+    atomicMax(&p.state->best, best);
+    __threadfence();
+    if (p.finalize && atomicAdd(&p.state->counter, 1u) == gridDim.x - 1) {
+      __threadfence();
+      const unsigned long long b = atomicExch(&p.state->best, 0ull);
+      p.state->counter = 0u;
+      publish_token(p.state, p.token_log, (int32_t)argmax_index(b));
+    }
+  }
 }
 
 // ---- kernel 2: generic SIMT ---------------------------------------------------------------
@@ -713,6 +868,28 @@ static int plan_reg(int M, int K, bool xf32, const q4b_linear_cfg* cfg, Plan& pl
   return Q4B_OK;
 }
 
+constexpr int kStreamCtas = 148;  // one CTA per SM of a B200
+
+static int plan_stream(int M, int K, bool xf32, const q4b_linear_cfg* cfg, Plan& pl) {
+  pl.kernel = 4;
+  pl.W = cfg && cfg->warps ? cfg->warps : 16;
+  if (pl.W < 1 || pl.W > 24) return set_error(Q4B_EINVAL, "q4_linear: streaming kernel takes 1..24 warps");
+  pl.nsplit = 1;
+  pl.kps = K / TILE_K;
+  const int SK = K <= 4096 ? K : K / 2;
+  const size_t ring = (size_t)kStreamRing * (16 * SK / 2 + 16 * (SK / 128) * 2);
+  pl.x_off = (int)align_up(ring, 128);
+  const size_t stage = (size_t)M * (K / 8 + 4) * 16 * (xf32 ? 2 : 1);
+  pl.smem = pl.x_off + stage;
+  pl.ws_bytes = 0;
+  return pl.smem <= kMaxSmem ? Q4B_OK : set_error(Q4B_EUNSUPPORTED, "q4_linear: streaming plan too large");
+}
+
+static bool stream_ok(int M, int K, int G, bool norm) {
+  (void)norm;
+  return M == 1 && G == 128 && K % 1024 == 0 && K <= 8192;
+}
+
 static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, bool norm, const q4b_linear_cfg* cfg,
                        Plan& pl) {
   const int n_out = epi == EPI_SWIGLU ? N / 2 : N;
@@ -733,6 +910,13 @@ static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, bool norm
     if (pl.MT > 2) return set_error(Q4B_EUNSUPPORTED, "q4_linear: TMA kernel needs m <= 16");
     return plan_tma(M, K, G, xf32, cfg, pl);
   }
+  if (want == 4) {
+    if (!stream_ok(M, K, G, norm))
+      return set_error(Q4B_EUNSUPPORTED, "q4_linear: streaming kernel needs m == 1, group 128, k %% 1024 == 0, k <= 8192");
+    return plan_stream(M, K, xf32, cfg, pl);
+  }
+  // the streaming kernel (4) is selectable but not the default: chained in a decode step its
+  // one-CTA-per-SM ring cannot overlap the neighbouring launches and measures slower than kernel 1
   return plan_reg(M, K, xf32, cfg, pl);
 }
 
@@ -848,7 +1032,8 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
   Plan pl;
   if ((rc = plan_op(op, pl))) return rc;
   const bool forced = op.cfg && op.cfg->kernel;
-  if (pl.kernel != 2 && (!aligned(op.qw, 16) || !aligned(op.x, 16) || (op.ln_w && !aligned(op.ln_w, 16)))) {
+  if (pl.kernel != 2 && (!aligned(op.qw, 16) || !aligned(op.x, 16) || (op.ln_w && !aligned(op.ln_w, 16)) ||
+                         (pl.kernel == 4 && !aligned(op.scales, 16)))) {
     if (forced) return set_error(Q4B_EINVAL, "q4_linear: qweight, x and ln_w must be 16-byte aligned");
     simt_plan(op, pl);
   }
@@ -907,12 +1092,20 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
   a.logits = op.logits;
   a.index_offset = op.index_offset;
   a.finalize = op.finalize;
+  a.RT = pl.RT;
   if (pl.kernel != 2 && pl.nsplit > 1) {
     a.counters = reinterpret_cast<unsigned*>(op.ws);
     a.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(op.ws) + kCounterBytes);
   }
   cudaError_t e;
-  if (pl.kernel == 3) {
+  if (pl.kernel == 4) {
+    static unsigned long long d0 = 0, d1 = 0;
+    e = xf32 ? set_smem_attr(q4_gemv_stream<true>, d1) : set_smem_attr(q4_gemv_stream<false>, d0);
+    const int grid = std::min(pl.RT, kStreamCtas);
+    if (e == cudaSuccess)
+      e = xf32 ? launch_pdl(q4_gemv_stream<true>, dim3(grid), dim3(pl.W * 32), pl.smem, st, a)
+               : launch_pdl(q4_gemv_stream<false>, dim3(grid), dim3(pl.W * 32), pl.smem, st, a);
+  } else if (pl.kernel == 3) {
     e = xf32 ? launch_tma<true>(pl, a, st) : launch_tma<false>(pl, a, st);
   } else if (pl.kernel == 1) {
     e = xf32 ? launch_reg<true>(pl, a, st) : launch_reg<false>(pl, a, st);
