@@ -104,6 +104,29 @@ int q4b_q4_linear(const int32_t* qweight, const uint16_t* scales, int group, con
 int q4b_q4_linear_noalloc(const int32_t* qweight, const uint16_t* scales, int group, const void* x, int x_dtype,
                           void* y, int y_dtype, int m, int n, int k, int epilogue, q4b_stream_t stream);
 
+/* ---- fp16 GEMM (prefill; the gemm/ tuner's problem, gemm/shapes.py:1-66) --------------------- */
+
+/* Kernel choice and schedule of q4b_gemm_f16 (the CUDA counterpart of gemm/schedule.py:43-103's
+ * Schedule; all zero = the built-in default for the shape). */
+typedef struct q4b_gemm_cfg {
+  int kernel; /* 0 = default, 1 = tcgen05 (TMA + TMEM accumulator), 2 = CUDA-core 64x64 tiles */
+  int bn;     /* kernel 1: output tile width 64 | 128 | 256 (tile height is 128); 0 = auto */
+  int stages; /* kernel 1: shared-memory ring depth, 2 .. as many as fit in 200 KB; 0 = max */
+  int split;  /* kernel 1: k splits (fp32 partials in the workspace); 0 = auto, 1 = none */
+} q4b_gemm_cfg;
+
+/* Bytes of workspace q4b_gemm_f16 needs (0 if none; -1 if the problem or cfg is invalid, with
+ * q4b_last_error() saying why). Same zero-fill-once rule as q4b_q4_linear_workspace. */
+long long q4b_gemm_f16_workspace(int m, int n, int k, char la, char lb, const q4b_gemm_cfg* cfg);
+
+/* C[m, n] = op(A) op(B), fp16 in and out, fp32 accumulation (gemm/shapes.py:1-6, 56-66; the
+ * harness contract of gemm/harness/vk_gemm_bench.c:5-13). Layout letters as BLAS: la 'N' = A stored
+ * [m][k], 'T' = stored [k][m]; lb 'N' = B stored [k][n], 'T' = stored [n][k]. C is row-major [m][n].
+ * The tcgen05 kernel needs 16-byte aligned A / B and row pitches (k or m for A, n or k for B) that
+ * are multiples of 8; the default falls back to kernel 2 otherwise. */
+int q4b_gemm_f16(const void* a, const void* b, void* c, int m, int n, int k, char la, char lb,
+                 const q4b_gemm_cfg* cfg, void* workspace, size_t workspace_bytes, q4b_stream_t stream);
+
 /* ---- model pieces (scripts/llm/llama_q4.py:93-142, 199-239) ------------------------------- */
 
 /* QEmbedding.lookup (:106-119): out[c, :] = dequantised row tokens[c] of the [vocab, dim] table, or

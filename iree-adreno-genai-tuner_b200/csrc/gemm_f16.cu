@@ -1,0 +1,460 @@
+// fp16 GEMM C[M,N] = op(A) . op(B) with fp32 accumulation and fp16 output: the prefill / tuner GEMM
+// of gemm/shapes.py:1-6 (BLAS layout letters: A 'N' = [M][K] row-major, 'T' = stored [K][M];
+// B 'N' = [K][N] row-major, 'T' = stored [N][K], a torch Linear weight) and gemm/schedule.py's
+// generated kernels, rebuilt for sm_100a.
+//
+// Kernel 1 (tcgen05): one 128 x BN output tile per CTA (BN = 64 / 128 / 256), K in 64-wide steps.
+// TMA brings each operand tile into a 128-byte-swizzled shared-memory ring (K-major tiles for
+// A 'N' / B 'T', MN-major tiles for A 'T' / B 'N': the layout letter only changes the tensor map and
+// the descriptor's major bit, no transpose kernel); one thread issues tcgen05.mma (M=128, N=BN,
+// K=16) into a TMEM accumulator and commits each ring slot back to the producer; all four warps
+// then read TMEM (32 lanes each) and store fp16. Split-K (grid.z) writes fp32 partials to the
+// workspace and the last CTA of a tile adds them in split order (deterministic) before storing.
+// Kernel 2 (CUDA cores): 64 x 64 tiles for any size or alignment TMA cannot describe.
+#include <mutex>
+
+#include "tc.cuh"
+
+namespace q4b {
+
+namespace {
+
+constexpr int kBM = 128, kBK = 64;
+constexpr int kGemmSmemBudget = 200 * 1024;
+constexpr size_t kGemmCounterBytes = 64 * 1024;  // per-tile split-K arrival counters (16384 tiles)
+
+__device__ unsigned g_gemm_status = 0;
+
+struct GemmArgs {
+  int M, N, K;
+  int kt;      // number of 64-wide k steps
+  int split;   // k splits (grid.z)
+  int vec;     // C rows keep 16-byte alignment (n % 8 == 0, aligned base): vector stores
+  __half* C;
+  float* partial;       // split > 1: [split][tiles][128][BN] fp32
+  unsigned* counters;   // split > 1: [tiles]
+};
+
+template <int BN>
+struct GemmTile {
+  static constexpr int A_BYTES = kBM * kBK * 2;  // 16 KB
+  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int MAX_STAGES = kGemmSmemBudget / STAGE;
+};
+
+__device__ __forceinline__ void store_row_f16(__half* crow, int col0, int ncols, int N, const float* v, bool vec) {
+  // 32 consecutive outputs of one row; vector stores when the row pitch keeps 16-byte alignment
+  if (vec && col0 + 32 <= N) {
+    uint4* dst = reinterpret_cast<uint4*>(crow + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      __half2 h[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
+      dst[q] = *reinterpret_cast<uint4*>(h);
+    }
+  } else {
+    for (int j = 0; j < 32 && j < ncols; ++j)
+      if (col0 + j < N) crow[col0 + j] = __float2half_rn(v[j]);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(128, 1)
+    gemm_f16_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, GemmArgs p,
+                int stages) {
+  using T = GemmTile<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full[T::MAX_STAGES], empty[T::MAX_STAGES], acc_full;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_last, s_fail;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
+  const int z = blockIdx.z;
+  const int k_begin = (int)((long long)z * p.kt / p.split), k_end = (int)((long long)(z + 1) * p.kt / p.split);
+  const int nk = k_end - k_begin;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(&acc_full, 1);
+    s_fail = 0;
+    fence_mbar_init();
+    tma_prefetch_map(&ta);
+    tma_prefetch_map(&tb);
+  }
+  if (warp == 0) tmem_alloc(&s_tmem, BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  griddep_wait();  // A / B may be written by the previous kernel on the stream
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer: TMA loads into the ring
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % stages, r = it / stages;
+        if (r > 0 && !mbar_wait_bounded(&empty[s], (r - 1) & 1, kWaitLimitNs)) {
+          s_fail = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], T::STAGE);
+        uint8_t* a = smem + s * T::STAGE;
+        uint8_t* b = a + T::A_BYTES;
+        const int kx = (k_begin + it) * kBK;
+        if constexpr (!A_MN) {
+          tma_load_2d(a, &ta, kx, m0, &full[s]);
+        } else {
+          tma_load_2d(a, &ta, m0, kx, &full[s]);
+          tma_load_2d(a + 8192, &ta, m0 + 64, kx, &full[s]);
+        }
+        if constexpr (!B_MN) {
+          tma_load_2d(b, &tb, kx, n0, &full[s]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 8192, &tb, n0 + 64 * j, kx, &full[s]);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issue: 4 x (128 x BN x 16) per ring slot, accumulating in TMEM
+      constexpr uint32_t idesc = idesc_f16_f32(kBM, BN, A_MN, B_MN);
+      for (int it = 0; it < nk; ++it) {
+        const int s = it % stages, r = it / stages;
+        if (!mbar_wait_bounded(&full[s], r & 1, kWaitLimitNs)) {
+          s_fail = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + s * T::STAGE), b = a + T::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          const uint64_t ad = A_MN ? sw128_desc(a + kk * 2048, 8192, 1024) : sw128_desc(a + kk * 32, 16, 1024);
+          const uint64_t bd = B_MN ? sw128_desc(b + kk * 2048, 8192, 1024) : sw128_desc(b + kk * 32, 16, 1024);
+          tc_mma_f16(tmem, ad, bd, idesc, (it | kk) != 0);
+        }
+        tc_commit(&empty[s]);  // the slot is free once these MMAs have read it
+      }
+      tc_commit(&acc_full);
+    }
+    __syncwarp();
+  }
+
+  // epilogue: warp w owns accumulator rows 32w..32w+31 (TMEM lanes), one row per thread
+  if (!mbar_wait_bounded(&acc_full, 0, kWaitLimitNs)) s_fail = 1;
+  __syncthreads();
+  const bool ok = !s_fail;
+  tc_fence_after();
+  const int row = m0 + warp * 32 + lane;
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  const bool vec = p.vec != 0;
+  const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+  if (!ok) {
+    if (threadIdx.x == 0) atomicOr(&g_gemm_status, kStatusTimeout);
+  } else if (p.split == 1) {
+    __half* crow = p.C + (size_t)row * p.N;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32(trow + c * 32, r);
+      if (row < p.M && n0 + c * 32 < p.N) store_row_f16(crow, n0 + c * 32, 32, p.N, reinterpret_cast<float*>(r), vec);
+    }
+  } else {
+    float* mine = p.partial + ((size_t)z * gridDim.x * gridDim.y + tile) * (kBM * BN) + (size_t)(warp * 32 + lane) * BN;
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32(trow + c * 32, r);
+      float4* d = reinterpret_cast<float4*>(mine + c * 32);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        d[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                           __uint_as_float(r[4 * q + 3]));
+    }
+    __threadfence();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+  if (p.split > 1 && ok) {
+    if (threadIdx.x == 0) {
+      const unsigned prev = atomicAdd(&p.counters[tile], 1u);
+      s_last = prev == (unsigned)(p.split - 1);
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      const size_t zstride = (size_t)gridDim.x * gridDim.y * (kBM * BN);
+      const float* base = p.partial + (size_t)tile * (kBM * BN) + (size_t)(warp * 32 + lane) * BN;
+      __half* crow = p.C + (size_t)row * p.N;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+        for (int zz = 0; zz < p.split; ++zz) {
+          const float4* src = reinterpret_cast<const float4*>(base + zz * zstride + c * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 t = __ldcg(src + q);
+            v[4 * q] += t.x;
+            v[4 * q + 1] += t.y;
+            v[4 * q + 2] += t.z;
+            v[4 * q + 3] += t.w;
+          }
+        }
+        if (row < p.M && n0 + c * 32 < p.N) store_row_f16(crow, n0 + c * 32, 32, p.N, v, vec);
+      }
+      if (threadIdx.x == 0) p.counters[tile] = 0u;  // ready for the next call (graph replays)
+    }
+  }
+  griddep_launch_dependents();
+}
+
+// ---- kernel 2: CUDA-core tiles, any layout and alignment ----------------------------------------
+
+template <bool A_T, bool B_T>
+__global__ void __launch_bounds__(256) gemm_f16_simt(const __half* __restrict__ A, const __half* __restrict__ B,
+                                                     __half* __restrict__ C, int M, int N, int K) {
+  __shared__ float As[16][65];
+  __shared__ float Bs[16][65];
+  griddep_wait();
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+      const int mm = i / 16, kk = i % 16;       // A element (m0+mm, k0+kk)
+      const int m = m0 + mm, k = k0 + kk;
+      float a = 0.f;
+      if (m < M && k < K) a = __half2float(A_T ? A[(size_t)k * M + m] : A[(size_t)m * K + k]);
+      As[kk][mm] = a;
+      const int nn = i % 64, kb = i / 64;       // B element (k0+kb, n0+nn)
+      const int n = n0 + nn, k2 = k0 + kb;
+      float b = 0.f;
+      if (n < N && k2 < K) b = __half2float(B_T ? B[(size_t)n * K + k2] : B[(size_t)k2 * N + n]);
+      Bs[kb][nn] = b;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int m = m0 + ty + 16 * i, n = n0 + tx + 16 * j;
+      if (m < M && n < N) C[(size_t)m * N + n] = __float2half_rn(acc[i][j]);
+    }
+  griddep_launch_dependents();
+}
+
+// ---- host --------------------------------------------------------------------------------------
+
+struct GemmPlan {
+  int kernel = 1, bn = 128, stages = 4, split = 1;
+  int tiles_m = 0, tiles_n = 0;
+  size_t smem = 0, ws = 0;
+};
+
+bool tma_ok(int M, int N, int K, char la, char lb) {
+  const long long lda = la == 'N' ? K : M, ldb = lb == 'N' ? N : K;
+  return lda % 8 == 0 && ldb % 8 == 0;
+}
+
+int plan_gemm(int M, int N, int K, char la, char lb, const q4b_gemm_cfg* cfg, GemmPlan& pl) {
+  if (M <= 0 || N <= 0 || K <= 0) return set_error(Q4B_EINVAL, "gemm_f16: sizes must be positive");
+  if ((la != 'N' && la != 'T') || (lb != 'N' && lb != 'T'))
+    return set_error(Q4B_EINVAL, "gemm_f16: layouts are 'N' or 'T'");
+  const int want = cfg ? cfg->kernel : 0;
+  if (want != 0 && want != 1 && want != 2) return set_error(Q4B_EINVAL, "gemm_f16: kernel is 0, 1 or 2");
+  const bool tma = tma_ok(M, N, K, la, lb);
+  if (want == 1 && !tma)
+    return set_error(Q4B_EUNSUPPORTED, "gemm_f16: the tcgen05 kernel needs row pitches that are multiples of 8");
+  if (want == 2 || !tma) {
+    pl.kernel = 2;
+    pl.split = 1;
+    pl.smem = 0;
+    pl.ws = 0;
+    return Q4B_OK;
+  }
+  pl.kernel = 1;
+  const int kt = (K + kBK - 1) / kBK;
+  const int tm = (M + kBM - 1) / kBM;
+  int bn = cfg && cfg->bn ? cfg->bn : 0;
+  if (bn && bn != 64 && bn != 128 && bn != 256) return set_error(Q4B_EINVAL, "gemm_f16: bn is 64, 128 or 256");
+  if (!bn) {
+    // widest tile that still fills the GPU, narrower tiles (and split-K below) for small problems
+    bn = 256;
+    while (bn > 64 && (long long)tm * ((N + bn - 1) / bn) < 148) bn /= 2;
+  }
+  const int tn = (N + bn - 1) / bn;
+  int split = cfg && cfg->split ? cfg->split : 0;
+  if (split < 0 || split > kt) return set_error(Q4B_EINVAL, "gemm_f16: split must be in [1, %d]", kt);
+  if (!split) {
+    split = 1;
+    // fill the SMs while keeping at least 4 k steps (256 of K) per split
+    while ((long long)tm * tn * split < 148 && kt / (split * 2) >= 4) split *= 2;
+  }
+  const int stage = (kBM + bn) * kBK * 2;
+  const int max_stages = kGemmSmemBudget / stage;
+  int stages = cfg && cfg->stages ? cfg->stages : max_stages;
+  if (stages < 2 || stages > max_stages)
+    return set_error(Q4B_EINVAL, "gemm_f16: stages must be in [2, %d] for bn %d", max_stages, bn);
+  const long long tiles = (long long)tm * tn;
+  if (split > 1 && tiles * 4 > (long long)kGemmCounterBytes)
+    return set_error(Q4B_EUNSUPPORTED, "gemm_f16: too many tiles for split-K");
+  pl.bn = bn;
+  pl.stages = stages;
+  pl.split = split;
+  pl.tiles_m = tm;
+  pl.tiles_n = tn;
+  pl.smem = (size_t)stages * stage + 1024;
+  pl.ws = split > 1 ? kGemmCounterBytes + (size_t)split * tiles * kBM * bn * 4 : 0;
+  return Q4B_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, const GemmPlan& pl,
+                      cudaStream_t st) {
+  auto kern = gemm_f16_tc<BN, A_MN, B_MN>;
+  static unsigned long long done = 0;  // per device: the smem attribute is set once
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(done >> (dev & 63) & 1ull)) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemBudget + 1024);
+    if (e != cudaSuccess) return e;
+    done |= 1ull << (dev & 63);
+  }
+  return launch_pdl(kern, dim3(pl.tiles_m, pl.tiles_n, pl.split), dim3(128), pl.smem, st, ta, tb, a, pl.stages);
+}
+
+template <int BN>
+cudaError_t launch_tc_bn(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                         const GemmPlan& pl, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_tc<BN, false, false>(ta, tb, a, pl, st);
+  if (!a_mn && b_mn) return launch_tc<BN, false, true>(ta, tb, a, pl, st);
+  if (a_mn && !b_mn) return launch_tc<BN, true, false>(ta, tb, a, pl, st);
+  return launch_tc<BN, true, true>(ta, tb, a, pl, st);
+}
+
+}  // namespace
+
+int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return set_error(Q4B_EUNSUPPORTED, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(Q4B_EINVAL, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return Q4B_OK;
+}
+
+unsigned gemm_status(bool reset) {
+  unsigned v = 0;
+  cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(v));
+  if (reset && v) {
+    const unsigned zero = 0;
+    cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(zero));
+  }
+  return v;
+}
+
+}  // namespace q4b
+
+using namespace q4b;
+
+extern "C" long long q4b_gemm_f16_workspace(int M, int N, int K, char la, char lb, const q4b_gemm_cfg* cfg) {
+  GemmPlan pl;
+  if (plan_gemm(M, N, K, la, lb, cfg, pl)) return -1;
+  return (long long)pl.ws;
+}
+
+extern "C" int q4b_gemm_f16(const void* A, const void* B, void* C, int M, int N, int K, char la, char lb,
+                            const q4b_gemm_cfg* cfg, void* workspace, size_t ws_bytes, q4b_stream_t stream) {
+  clear_error();
+  if (!A || !B || !C) return set_error(Q4B_EINVAL, "gemm_f16: null pointer");
+  GemmPlan pl;
+  int rc = plan_gemm(M, N, K, la, lb, cfg, pl);
+  if (rc) return rc;
+  cudaStream_t st = as_stream(stream);
+  if (pl.kernel == 2) {
+    const dim3 grid((N + 63) / 64, (M + 63) / 64);
+    const auto* a = static_cast<const __half*>(A);
+    const auto* b = static_cast<const __half*>(B);
+    auto* c = static_cast<__half*>(C);
+    cudaError_t e;
+    if (la == 'N' && lb == 'N') e = launch_pdl(gemm_f16_simt<false, false>, grid, dim3(256), 0, st, a, b, c, M, N, K);
+    else if (la == 'N') e = launch_pdl(gemm_f16_simt<false, true>, grid, dim3(256), 0, st, a, b, c, M, N, K);
+    else if (lb == 'N') e = launch_pdl(gemm_f16_simt<true, false>, grid, dim3(256), 0, st, a, b, c, M, N, K);
+    else e = launch_pdl(gemm_f16_simt<true, true>, grid, dim3(256), 0, st, a, b, c, M, N, K);
+    if (e != cudaSuccess) return set_error(Q4B_ELAUNCH, "gemm_f16 (cuda cores): %s", cudaGetErrorString(e));
+    return Q4B_OK;
+  }
+  if (!aligned(A, 16) || !aligned(B, 16)) return set_error(Q4B_EINVAL, "gemm_f16: A and B must be 16-byte aligned");
+  if (pl.ws && (!workspace || ws_bytes < pl.ws || !aligned(workspace, 256)))
+    return set_error(Q4B_EINVAL, "gemm_f16: needs a 256-byte aligned workspace of %zu bytes", pl.ws);
+  const bool a_mn = la == 'T', b_mn = lb == 'N';
+  CUtensorMap ta, tb;
+  if ((rc = a_mn ? make_tmap_f16(&ta, A, M, K, M, 64) : make_tmap_f16(&ta, A, K, M, K, kBM))) return rc;
+  if ((rc = b_mn ? make_tmap_f16(&tb, B, N, K, N, 64) : make_tmap_f16(&tb, B, K, N, K, pl.bn))) return rc;
+  GemmArgs a;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.kt = (K + kBK - 1) / kBK;
+  a.split = pl.split;
+  a.vec = (N % 8 == 0) && aligned(C, 16);
+  a.C = static_cast<__half*>(C);
+  a.counters = pl.ws ? static_cast<unsigned*>(workspace) : nullptr;
+  a.partial = pl.ws ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kGemmCounterBytes) : nullptr;
+  cudaError_t e = pl.bn == 256 ? launch_tc_bn<256>(a_mn, b_mn, ta, tb, a, pl, st)
+                  : pl.bn == 128 ? launch_tc_bn<128>(a_mn, b_mn, ta, tb, a, pl, st)
+                                 : launch_tc_bn<64>(a_mn, b_mn, ta, tb, a, pl, st);
+  if (e != cudaSuccess) return set_error(Q4B_ELAUNCH, "gemm_f16 (tcgen05): %s", cudaGetErrorString(e));
+  return Q4B_OK;
+}

@@ -93,5 +93,7 @@ __device__ __forceinline__ unsigned argmax_index(unsigned long long key) {
 }
 
 unsigned linear_status(bool reset);
+// Status bits of the GEMM kernels (kStatusTimeout when a bounded wait gave up).
+unsigned gemm_status(bool reset);
 
 }  // namespace q4b

@@ -40,6 +40,10 @@ class LinearCfg(ctypes.Structure):
     _fields_ = [("kernel", c_int), ("warps", c_int), ("tiles", c_int), ("split", c_int)]
 
 
+class GemmCfg(ctypes.Structure):
+    _fields_ = [("kernel", c_int), ("bn", c_int), ("stages", c_int), ("split", c_int)]
+
+
 class ModelCfg(ctypes.Structure):
     _fields_ = [("n_layers", c_int), ("dim", c_int), ("n_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int),
                 ("inter", c_int), ("vocab", c_int), ("rms_eps", c_float), ("max_ctx", c_int), ("max_chunk", c_int),
@@ -79,6 +83,9 @@ SIGNATURES = {
                               c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "q4b_q4_linear_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
                                       c_int, c_int, c_void_p]),
+    "q4b_gemm_f16_workspace": (ctypes.c_longlong, [c_int, c_int, c_int, ctypes.c_char, ctypes.c_char, c_void_p]),
+    "q4b_gemm_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, ctypes.c_char, ctypes.c_char, c_void_p,
+                             c_void_p, c_size_t, c_void_p]),
     "q4b_embed_q4_lookup": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "q4b_rmsnorm": (c_int, [c_void_p, c_void_p, c_float, c_int, c_int, c_void_p, c_void_p]),
     "q4b_attention_workspace": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),

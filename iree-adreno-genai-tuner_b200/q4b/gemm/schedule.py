@@ -1,0 +1,142 @@
+"""The CUDA schedule space of q4b_gemm_f16 (the counterpart of gemm/schedule.py:43-103's Schedule)
+and the index algebra of its kernels, restated here so the verifier can replay it.
+
+Kernel 1 (tcgen05): a CTA computes one 128 x bn tile of C over the k steps [k_begin, k_end) of its
+split z (64 wide each); grid = (ceil(M/128), ceil(N/bn), split); a shared-memory ring of `stages`
+slots, each holding A's 128 x 64 tile (16 KB) and B's bn x 64 tile; a TMEM accumulator of bn
+columns. Kernel 2 (CUDA cores): 64 x 64 tiles, no options.
+
+A schedule's candidate string is what the harness manifest carries: "1:bn=128,stages=6,split=2".
+"""
+
+from __future__ import annotations
+
+import dataclasses
+import math
+
+BM, BK = 128, 64
+SMEM_BUDGET = 200 * 1024  # ring bytes the kernel may use (csrc/gemm_f16.cu kGemmSmemBudget)
+COUNTER_TILES = 16384     # split-K arrival counters in the workspace (64 KB of u32)
+
+
+@dataclasses.dataclass(frozen=True)
+class Schedule:
+    kernel: int = 1   # 1 = tcgen05 + TMA + TMEM, 2 = CUDA-core tiles
+    bn: int = 128     # output tile width (64 | 128 | 256)
+    stages: int = 0   # ring depth (0 = as many as fit)
+    split: int = 1    # k splits
+
+    def key(self):
+        # stages 0 means "as many as fit": the same kernel as naming that depth
+        st = self.stages or SMEM_BUDGET // ((BM + self.bn) * BK * 2)
+        return (self.kernel, self.bn, st, self.split) if self.kernel == 1 else (2,)
+
+    def candidate(self) -> str:
+        if self.kernel == 2:
+            return "2:"
+        return f"1:bn={self.bn},stages={self.stages},split={self.split}"
+
+    def short(self) -> str:
+        return "simt" if self.kernel == 2 else f"tc bn{self.bn} st{self.stages or 'max'} sk{self.split}"
+
+    def cfg(self) -> dict:
+        if self.kernel == 2:
+            return dict(kernel=2)
+        return dict(kernel=1, bn=self.bn, stages=self.stages, split=self.split)
+
+    @staticmethod
+    def parse(text: str) -> "Schedule":
+        kern, _, rest = text.partition(":")
+        kw = dict(kernel=int(kern))
+        for item in filter(None, rest.split(",")):
+            k, _, v = item.partition("=")
+            kw[k] = int(v)
+        return Schedule(**kw)
+
+
+def stage_bytes(sc: Schedule) -> int:
+    return (BM + sc.bn) * BK * 2
+
+
+def max_stages(sc: Schedule) -> int:
+    return SMEM_BUDGET // stage_bytes(sc)
+
+
+def eff_stages(sc: Schedule) -> int:
+    return sc.stages or max_stages(sc)
+
+
+def smem_bytes(sc: Schedule) -> int:
+    """Dynamic shared memory of one CTA (ring + 1 KB alignment slack)."""
+    if sc.kernel == 2:
+        return 2 * 16 * 65 * 4
+    return eff_stages(sc) * stage_bytes(sc) + 1024
+
+
+def k_steps(s) -> int:
+    return -(-s.K // BK)
+
+
+def grid(s, sc: Schedule):
+    if sc.kernel == 2:
+        return (-(-s.N // 64), -(-s.M // 64), 1)
+    return (-(-s.M // BM), -(-s.N // sc.bn), sc.split)
+
+
+def k_range(s, sc: Schedule, z: int):
+    """The k steps split z reduces: [z*kt/split, (z+1)*kt/split), as the kernel computes them."""
+    kt = k_steps(s)
+    return (z * kt) // sc.split, ((z + 1) * kt) // sc.split
+
+
+def tma_loads(s, sc: Schedule, m_tile: int, n_tile: int, k_step: int):
+    """The TMA boxes one ring slot receives: (operand, x, y, box_w, box_h) with x the innermost
+    (contiguous) coordinate, as gemm_f16_tc issues them."""
+    m0, n0, kx = m_tile * BM, n_tile * sc.bn, k_step * BK
+    out = []
+    if s.la == "N":
+        out.append(("A", kx, m0, 64, BM))
+    else:
+        out += [("A", m0, kx, 64, 64), ("A", m0 + 64, kx, 64, 64)]
+    if s.lb == "T":
+        out.append(("B", kx, n0, 64, sc.bn))
+    else:
+        out += [("B", n0 + 64 * j, kx, 64, 64) for j in range(sc.bn // 64)]
+    return out
+
+
+def workspace_bytes(s, sc: Schedule) -> int:
+    if sc.kernel == 2 or sc.split == 1:
+        return 0
+    gx, gy, _ = grid(s, sc)
+    return 64 * 1024 + sc.split * gx * gy * BM * sc.bn * 4
+
+
+def domains(s):
+    kt = k_steps(s)
+    return {
+        "bn": [64, 128, 256],
+        "stages": [0, 2, 3, 4, 5, 6, 8],
+        "split": sorted({x for x in (1, 2, 3, 4, 6, 8, 12, 16) if x <= kt}),
+    }
+
+
+def default_schedule(s) -> Schedule:
+    """The library's built-in choice (plan_gemm in csrc/gemm_f16.cu): the widest tile that still
+    gives 148 tiles, then split-K while that fills more SMs and each split keeps >= 4 k steps."""
+    if s.la == "N" and s.K % 8 or s.la == "T" and s.M % 8 or s.lb == "N" and s.N % 8 or s.lb == "T" and s.K % 8:
+        return Schedule(kernel=2)
+    tm = -(-s.M // BM)
+    bn = 256
+    while bn > 64 and tm * -(-s.N // bn) < 148:
+        bn //= 2
+    tn = -(-s.N // bn)
+    kt = k_steps(s)
+    split = 1
+    while tm * tn * split < 148 and kt // (split * 2) >= 4:
+        split *= 2
+    return Schedule(kernel=1, bn=bn, stages=0, split=split)
+
+
+def log2i(x: int) -> float:
+    return math.log2(max(1, x))

@@ -5,7 +5,7 @@ from __future__ import annotations
 
 import torch
 
-from ._lib import EPI_ACCUMULATE, EPI_STORE, EPI_SWIGLU, F16, F32, LinearCfg, check, lib
+from ._lib import EPI_ACCUMULATE, EPI_STORE, EPI_SWIGLU, F16, F32, GemmCfg, LinearCfg, Q4B_EINVAL as _lib_EINVAL, Q4BError, check, lib
 
 _DT = {torch.float32: F32, torch.float16: F16}
 
@@ -83,6 +83,39 @@ def _cfg(cfg):
     if isinstance(cfg, LinearCfg):
         return cfg
     return LinearCfg(**cfg)
+
+
+def gemm_f16(a: torch.Tensor, b: torch.Tensor, la: str = "N", lb: str = "N", *, out=None, cfg=None):
+    """C = op(A) @ op(B) in fp16 with fp32 accumulation (gemm/shapes.py:1-6, 56-66).
+
+    ``a`` and ``b`` are the STORED fp16 matrices: la "N" -> a is [M, K], "T" -> a is [K, M];
+    lb "N" -> b is [K, N], "T" -> b is [N, K] (a torch Linear weight). Returns C [M, N] fp16."""
+    _need_cuda(a, b)
+    if a.dtype != torch.float16 or b.dtype != torch.float16:
+        raise ValueError("gemm_f16 takes fp16 A and B")
+    if la not in ("N", "T") or lb not in ("N", "T"):
+        raise ValueError("layouts are 'N' or 'T'")
+    if a.dim() != 2 or b.dim() != 2 or not a.is_contiguous() or not b.is_contiguous():
+        raise ValueError("A and B must be contiguous 2-D tensors")
+    m, k = a.shape if la == "N" else (a.shape[1], a.shape[0])
+    kb, n = b.shape if lb == "N" else (b.shape[1], b.shape[0])
+    if k != kb:
+        raise ValueError(f"op(A) has K={k}, op(B) has K={kb}")
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.float16, device=a.device)
+    elif tuple(out.shape) != (m, n) or out.dtype != torch.float16 or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous fp16 [{m}, {n}] tensor")
+    c = None if cfg is None else (cfg if isinstance(cfg, GemmCfg) else GemmCfg(**cfg))
+    cp = None if c is None else ctypes_byref(c)
+    L = lib()
+    wsb = L.q4b_gemm_f16_workspace(m, n, k, la.encode(), lb.encode(), cp)
+    if wsb < 0:
+        raise Q4BError(_lib_EINVAL, "gemm_f16: " + L.q4b_last_error().decode(errors="replace"))
+    ws = WORKSPACE.get(wsb, a.device)
+    check(L.q4b_gemm_f16(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k, la.encode(), lb.encode(), cp,
+                         0 if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(), _stream()),
+          "gemm_f16")
+    return out
 
 
 def q4_linear(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, group: int, *, out=None,
