@@ -127,7 +127,7 @@ def tune(s, method, budget, batch, model, data_dir, out_dir, log, seed=0, pool=4
                 model.add(s, sc, us)
         pairs = [(pr, res.get(sc.key())) for sc, pr in zip(pick, preds) if pr and res.get(sc.key())]
         rho = None
-        if len(pairs) >= 5:
+        if len(pairs) >= 5 and len({p for p, _ in pairs}) > 1 and len({m for _, m in pairs}) > 1:
             from scipy.stats import spearmanr
             rho = float(spearmanr([p for p, _ in pairs], [m for _, m in pairs]).correlation)
         model.fit()

@@ -1,0 +1,177 @@
+"""CPU checks of the GEMM tuner (q4b.gemm): problem files, verifier vs the library's own plan
+check, the verifier's replay catching planted index errors, the harness driver's device_lost
+recovery (against a fake harness), the cost model and one search run end to end on the fake
+harness. No GPU: the library's plan check runs on the host."""
+
+import json
+import pathlib
+import random
+import stat
+import sys
+
+import numpy as np
+import pytest
+
+from oracle import q4_oracle as O
+
+
+def _gemm():
+    from q4b import gemm
+    return gemm
+
+
+def test_shapes_cover_the_sweep():
+    g = _gemm()
+    got = {(s.M, s.N, s.K, s.layout) for s in g.SHAPES}
+    want = {(m, n, k, "NN") for m in (128, 2048) for n, k in [(5120, 3072), (3072, 3072), (16384, 3072), (3072, 8192)]}
+    assert got == want and len(g.SHAPES) == 8
+    assert {s.M for s in g.EXTRA} == {1}
+    assert len(g.REF_SHAPES) == 8 and g.TOL == 5e-3
+
+
+@pytest.mark.parametrize("sid", ["S3", "S5", "S8"])
+def test_make_data_files_match_the_oracle(tmp_path, sid):
+    g = _gemm()
+    s = g.BY_ID[sid]
+    d = g.make_data(s, tmp_path / sid, seed=0)
+    assert g.read_meta(d) == (s.M, s.N, s.K, s.la, s.lb, g.TOL)
+    a, b, c = O.gemm_make_data(s.M, s.N, s.K, s.la, s.lb, seed=int(sid[1:]))
+    assert np.array_equal(np.fromfile(d / "A.bin", dtype=np.float16), a.ravel())
+    assert np.array_equal(np.fromfile(d / "B.bin", dtype=np.float16), b.ravel())
+    cref = np.fromfile(d / "Cref.bin", dtype=np.float32).reshape(s.M, s.N)
+    assert O.rel_err(cref, c) < 1e-6
+
+
+def test_verifier_never_passes_what_the_library_rejects():
+    g = _gemm()
+    from q4b.gemm import search
+    rng = random.Random(1)
+    ragged = [g.Shape("R1", "r", 100, 200, 136, "NN"), g.Shape("R2", "r", 37, 100, 64, "TN"),
+              g.Shape("R3", "r", 3, 5, 7, "TT"), g.Shape("R4", "r", 257, 264, 8, "NT")]
+    n_ok = 0
+    for s in g.SHAPES + g.EXTRA + g.REF_SHAPES + ragged:
+        for _ in range(120):
+            sc = search.random_sched(s, rng)
+            v = g.verify(s, sc)
+            lib_ok = g.library_accepts(s, sc)
+            assert not (v.ok and not lib_ok), (s, sc, v)
+            n_ok += v.ok
+        assert g.verify(s, g.Schedule(kernel=2)).ok
+    assert n_ok > 500
+
+
+def test_verifier_reason_codes():
+    g = _gemm()
+    s = g.BY_ID["B5"]
+    assert "tile-width" in g.verify(s, g.Schedule(kernel=1, bn=96)).reasons
+    assert "ring-depth" in g.verify(s, g.Schedule(kernel=1, bn=256, stages=9)).reasons
+    assert "split-range" in g.verify(g.BY_ID["S6"], g.Schedule(kernel=1, bn=128, split=2)).reasons
+    assert "tma-pitch-B" in g.verify(g.Shape("X1", "x", 64, 100, 64, "NN"), g.Schedule(kernel=1, bn=64)).reasons
+    assert "tile-exceeds-problem" in g.verify(g.BY_ID["S3"], g.Schedule(kernel=1, bn=256)).reasons
+
+
+def test_mapping_check_catches_planted_errors(monkeypatch):
+    """Plant index mistakes in the replayed algebra (CPU only) and see the verifier object."""
+    g = _gemm()
+    from q4b.gemm import schedule, verifier
+    s = g.BY_ID["B2"]
+    sc = g.Schedule(kernel=1, bn=128, stages=0, split=4)
+    assert g.verify(s, sc).ok
+    # overlapping k splits
+    monkeypatch.setattr(verifier, "k_range", lambda s_, sc_, z: (0, schedule.k_steps(s_) // sc_.split + 1))
+    assert "reduction-coverage" in g.verify(s, sc).reasons
+    monkeypatch.undo()
+    # a B box shifted by 8 elements: misaligned and not covering the tile
+    real = schedule.tma_loads
+
+    def shifted(s_, sc_, mt, nt, ks):
+        return [(op, x + 8 if op == "B" else x, y, w, h) for op, x, y, w, h in real(s_, sc_, mt, nt, ks)]
+    monkeypatch.setattr(verifier, "tma_loads", shifted)
+    r = g.verify(s, sc).reasons
+    assert "tile-coverage" in r
+    # a box of the wrong height: expect_tx no longer matches
+    monkeypatch.setattr(verifier, "tma_loads",
+                        lambda *a: [(op, x, y, w, h // 2) for op, x, y, w, h in real(*a)])
+    assert "expect-tx-mismatch" in g.verify(s, sc).reasons
+
+
+def test_default_schedule_matches_the_library():
+    """The Python restatement of plan_gemm's default agrees with the library's workspace size."""
+    import ctypes
+
+    from q4b import _lib
+    from q4b.gemm.schedule import workspace_bytes
+    g = _gemm()
+    L = _lib.lib()
+    for s in g.SHAPES + g.EXTRA + g.REF_SHAPES:
+        sc = g.default_schedule(s)
+        ws = L.q4b_gemm_f16_workspace(s.M, s.N, s.K, s.la.encode(), s.lb.encode(), None)
+        assert ws == workspace_bytes(s, sc), (s, sc)
+        c = _lib.GemmCfg(**sc.cfg())
+        assert L.q4b_gemm_f16_workspace(s.M, s.N, s.K, s.la.encode(), s.lb.encode(), ctypes.byref(c)) == ws
+
+
+def test_cost_model_sanity():
+    g = _gemm()
+    from q4b.gemm import cost_model
+    s = g.BY_ID["B7"]  # 2048 x 16384 x 3072
+    t_tc = cost_model.analytic_us(s, g.Schedule(kernel=1, bn=256))
+    t_simt = cost_model.analytic_us(s, g.Schedule(kernel=2))
+    assert 0 < t_tc < t_simt
+    # bounded below by the compulsory DRAM bytes and the tensor peak
+    assert t_tc >= s.flops / (cost_model.TENSOR_TFLOPS * 1e6)
+    m = cost_model.Learned(min_samples=8)
+    rng = random.Random(0)
+    from q4b.gemm import search
+    for _ in range(12):
+        sc = search.random_sched(s, rng)
+        m.add(s, sc, cost_model.analytic_us(s, sc) * rng.uniform(0.9, 1.1))
+    m.fit()
+    assert m.kind == "learned"
+    assert m.predict_us(s, [g.Schedule(kernel=1, bn=128)]).shape == (1,)
+
+
+FAKE = r'''#!{py}
+import json, sys
+man = [a.split("=", 1)[1] for a in sys.argv[1:] if a.startswith("--manifest=")][0]
+bad = "{bad}"
+for line in open(man):
+    name, shape_dir, cand = line.split()
+    if name == bad:
+        print(json.dumps({{"name": name, "ok": False, "error": "device_lost"}}), flush=True)
+        sys.exit(3)
+    bn = int(cand.split("bn=")[1].split(",")[0]) if "bn=" in cand else 64
+    print(json.dumps({{"name": name, "ok": True, "err": 1e-4, "us": 100.0 / bn, "us_min": 90.0 / bn,
+                       "iters": 1, "reps": 1}}), flush=True)
+'''
+
+
+def _fake_bench(tmp_path, bad="none"):
+    p = tmp_path / "fake_bench"
+    p.write_text(FAKE.format(py=sys.executable, bad=bad))
+    p.chmod(p.stat().st_mode | stat.S_IEXEC)
+    return p
+
+
+def test_harness_blames_device_lost_and_reruns_the_rest(tmp_path):
+    from q4b.gemm import harness
+    bench = _fake_bench(tmp_path, bad="c1")
+    cands = [{"name": f"c{i}", "shape_dir": "x", "candidate": f"1:bn={64 << (i % 3)},stages=0,split=1"}
+             for i in range(4)]
+    res = harness.run_batch(cands, tmp_path / "out", "t", bench=bench)
+    assert res["c1"]["ok"] is False and res["c1"]["error"] == "device_lost"
+    assert all(res[f"c{i}"]["ok"] for i in (0, 2, 3))
+    # the rerun manifest holds only what the failed process had not reached, minus the blamed one
+    rerun = (tmp_path / "out" / "t.1.manifest").read_text().split()
+    assert "c1" not in rerun and "c2" in rerun and "c0" not in rerun
+
+
+def test_search_runs_end_to_end_on_a_fake_harness(tmp_path, monkeypatch):
+    from q4b.gemm import search
+    monkeypatch.setenv("Q4B_GEMM_BENCH", str(_fake_bench(tmp_path)))
+    rc = search.main(["--shapes", "B1", "--budget", "10", "--batch", "5", "--tag", "t", "--out", str(tmp_path / "r")])
+    assert rc == 0
+    best = json.loads((tmp_path / "r" / "t" / "best.json").read_text())
+    assert best["B1"]["candidate"].startswith("1:bn=256")  # the fake harness rewards wide tiles
+    log = [json.loads(x) for x in (tmp_path / "r" / "t" / "log.jsonl").read_text().splitlines()]
+    assert sum(1 for r in log if r.get("stage") == "gpu" and r["method"] in ("model", "random")) == 20
