@@ -89,14 +89,14 @@ int Model::init(const q4b_model_cfg& c) {
   if ((rc = alloc((void**)&y, sizeof(float) * Cm * D, true))) return rc;
   // split-K workspace: the largest any projection plan of this model asks for
   size_t need = 0;
-  const int ms[] = {1, 2, 4, 8, 16, 32, 64};
+  const int ms[] = {1, 2, 4, 8, 16, 32, 64, Cm};
   q4b_qmat shapes[5] = {{nullptr, nullptr, (H + 2 * Hkv) * hd, D, 128}, {nullptr, nullptr, D, H * hd, 128},
                         {nullptr, nullptr, 2 * I, D, 128}, {nullptr, nullptr, D, I, 128},
                         {nullptr, nullptr, V, D, 128}};
   static const int32_t dummy[4] = {0, 0, 0, 0};
   for (const q4b_qmat& s : shapes)
     for (int m : ms) {
-      if (m > Cm && m != 1) continue;
+      if (m > Cm && m != 1) continue;  // (Cm: the whole chunk in one tcgen05 GEMM)
       q4b_qmat w = s;
       w.qweight = dummy;
       w.scales = reinterpret_cast<const uint16_t*>(dummy);
@@ -133,8 +133,8 @@ int Model::forward(const int32_t* toks, int C, int L, float* logits, int32_t* to
   for (size_t li = 0; li < layers.size(); ++li) {
     const q4b_layer_weights& Lw = layers[li];
     // 1. q|k|v projection with RoPE and the cache write
-    for (int r0 = 0; r0 < C; r0 += 64) {
-      const int m = std::min(64, C - r0);
+    for (int r0 = 0; r0 < C; r0 += row_block(C)) {
+      const int m = std::min(row_block(C), C - r0);
       const float* xin = h + (size_t)r0 * D;
       if (!fuse_norm) {
         if ((rc = rmsnorm_run(h + (size_t)r0 * D, Lw.ln_in, cfg.rms_eps, m, D, nullptr, xn, st))) return rc;
@@ -178,8 +178,8 @@ int Model::forward(const int32_t* toks, int C, int L, float* logits, int32_t* to
     // 3. h += o Wo^T
     if ((rc = residual_linear(Lw.wo, o, H * hd, C, st))) return rc;
     // 4. a = silu(gate) * up of rmsnorm(h)
-    for (int r0 = 0; r0 < C; r0 += 64) {
-      const int m = std::min(64, C - r0);
+    for (int r0 = 0; r0 < C; r0 += row_block(C)) {
+      const int m = std::min(row_block(C), C - r0);
       const float* xin = h + (size_t)r0 * D;
       if (!fuse_norm) {
         if ((rc = rmsnorm_run(h + (size_t)r0 * D, Lw.ln_post, cfg.rms_eps, m, D, nullptr, xn, st))) return rc;
@@ -222,8 +222,8 @@ int Model::forward(const int32_t* toks, int C, int L, float* logits, int32_t* to
 int Model::residual_linear(const q4b_qmat& w, const float* x, int k, int C, cudaStream_t st) {
   int rc;
   (void)k;
-  for (int r0 = 0; r0 < C; r0 += 64) {
-    const int m = std::min(64, C - r0);
+  for (int r0 = 0; r0 < C; r0 += row_block(C)) {
+    const int m = std::min(row_block(C), C - r0);
     const bool tp = cfg.tp_size > 1;
     LinearOp op = qop(w, m, x + (size_t)r0 * w.k, tp ? (void*)(y + (size_t)r0 * D) : (void*)(h + (size_t)r0 * D),
                       tp ? EPI_STORE : EPI_ACCUMULATE);

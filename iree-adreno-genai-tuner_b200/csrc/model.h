@@ -36,6 +36,9 @@ struct Model {
   int check_ready() const;
   int forward(const int32_t* toks, int C, int L, float* logits, int32_t* token_log, cudaStream_t st);
   int residual_linear(const q4b_qmat& w, const float* x, int k, int C, cudaStream_t st);
+  // rows of a chunk per projection call: up to 64 for the register-staged MMA kernel, the whole
+  // chunk once it is large enough for the tcgen05 GEMM (more than 32 rows)
+  static int row_block(int C) { return C > 32 ? C : 64; }
   int step(const int32_t* toks, int C, int start, int last, int L, int32_t* next, float* logits, cudaStream_t st);
   int tp_allreduce_add(int C, cudaStream_t st);
   int tp_finish_argmax(int32_t* token_log, cudaStream_t st);

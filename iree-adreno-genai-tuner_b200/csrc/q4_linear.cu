@@ -27,6 +27,7 @@
 #include <algorithm>
 
 #include "linear.h"
+#include "tc.cuh"
 
 namespace q4b {
 
@@ -747,11 +748,325 @@ __global__ void __launch_bounds__(256) q4_linear_simt(LinArgs p) {
   epilogue_tile(p, fin, rt, &s_flag);
 }
 
+// ---- kernel 5: tcgen05 int4-weight GEMM (prefill, many x rows) ----------------------------------
+//
+// One CTA per (128 x rows, BN weight rows = BN/16 row tiles, k split). A pre-pass writes x as two
+// fp16 matrices hi / lo (x = hi + lo, ~22 bits) in the nibble-permuted k order of dequant_word;
+// the TMA engine streams their 128 x 64 tiles into a 128-byte-swizzled ring. Raw int4 rows arrive
+// by bulk copies (32 bytes per row and 64-k stage, rows picked by tile_row, so SwiGLU and RoPE
+// tiles keep their row pairs); four dequant warps turn them into exact fp16 (nib - 8) tiles in the
+// same swizzled K-major layout. One thread issues tcgen05.mma (M=128, N=BN, K=16; hi and lo into
+// one TMEM accumulator) per stage, alternating between two TMEM accumulators by scale group;
+// eight epilogue warps read each finished group from TMEM, scale it by the group's fp16 scales
+// and add it to fp32 registers -- the same arithmetic as kernels 1 and 3 (per-group fp32 sum of
+// exact products, then one fmaf with the scale). Split-K partials go through the workspace as in
+// the other kernels; the shared epilogue_tile then handles store / accumulate / SwiGLU / RoPE+KV.
+constexpr int K5_BM = 128, K5_BK = 64;
+constexpr int K5_RAW = 8, K5_XS = 3, K5_DS = 3;
+constexpr int K5_THREADS = 15 * 32;  // 8 epilogue, 4 dequant, 1 weight producer, 1 MMA, 1 x producer
+constexpr int K5_MAX_GROUPS = 64;    // scales of up to 64 groups per CTA stay in shared memory
+
+template <int BN>
+struct K5 {
+  static constexpr int X_BYTES = K5_BM * K5_BK * 2;  // one of hi / lo
+  static constexpr int XSTAGE = 2 * X_BYTES;
+  static constexpr int W_BYTES = BN * K5_BK * 2;
+  static constexpr int RAW_BYTES = BN * K5_BK / 2;
+  static constexpr int X_OFF = 0;
+  static constexpr int W_OFF = X_OFF + K5_XS * XSTAGE;
+  static constexpr int RAW_OFF = W_OFF + K5_DS * W_BYTES;
+  static constexpr int SC_OFF = RAW_OFF + K5_RAW * RAW_BYTES;
+  static constexpr int SMEM = SC_OFF + K5_MAX_GROUPS * BN * 2 + 1024;  // + alignment slack
+  static_assert(BN * K5_BM * 4 <= K5_XS * XSTAGE, "final tile must fit in the x ring");
+};
+
+// x [M, K] (fp32 or fp16, rows from x_row) -> hi / lo fp16 [M, K] in the permuted k order
+template <bool XF32>
+__global__ void __launch_bounds__(256) q4_xsplit(LinArgs p, __half* xh, __half* xl) {
+  griddep_wait();
+  const int kw = p.K / 8;
+  const int n = p.M * kw;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int m = i / kw, w = i - m * kw;
+    const size_t src = (size_t)x_row(p, m) * p.K + 8 * w;
+    uint4 hi, lo = make_uint4(0, 0, 0, 0);
+    if constexpr (XF32) {
+      const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + src);
+      const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + src + 4);
+      split_pair(a.x, b.x, hi.x, lo.x);
+      split_pair(a.y, b.y, hi.y, lo.y);
+      split_pair(a.z, b.z, hi.z, lo.z);
+      split_pair(a.w, b.w, hi.w, lo.w);
+    } else {
+      const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(p.x) + src);
+      hi.x = __byte_perm(v.x, v.z, 0x5410);
+      hi.y = __byte_perm(v.x, v.z, 0x7632);
+      hi.z = __byte_perm(v.y, v.w, 0x5410);
+      hi.w = __byte_perm(v.y, v.w, 0x7632);
+    }
+    *reinterpret_cast<uint4*>(xh + (size_t)m * p.K + 8 * w) = hi;
+    if constexpr (XF32) *reinterpret_cast<uint4*>(xl + (size_t)m * p.K + 8 * w) = lo;
+  }
+  griddep_launch_dependents();
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int BN, bool XF32>
+__global__ void __launch_bounds__(K5_THREADS, 1)
+    q4_gemm_tc(const __grid_constant__ CUtensorMap txh, const __grid_constant__ CUtensorMap txl, LinArgs p) {
+  using L = K5<BN>;
+  constexpr int RTS = BN / 16;  // row tiles per CTA
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t raw_full[K5_RAW], raw_empty[K5_RAW], x_full[K5_XS], x_empty[K5_XS], deq_full[K5_DS],
+      deq_empty[K5_DS], acc_full[2], acc_free[2];
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_fail, s_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * K5_BM;
+  const int rt0 = blockIdx.y * RTS;
+  const int z = blockIdx.z;
+  const int NG = p.K / p.G, SPG = p.G / K5_BK;
+  const int g0 = (int)((long long)z * NG / p.nsplit), g1 = (int)((long long)(z + 1) * NG / p.nsplit);
+  const int NGL = g1 - g0, NS = NGL * SPG;
+  const int KW = p.K / 8;
+  __half* s_sc = reinterpret_cast<__half*>(smem + L::SC_OFF);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < K5_RAW; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], 4);
+    }
+    for (int i = 0; i < K5_XS; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);
+    }
+    for (int i = 0; i < K5_DS; ++i) {
+      mbar_init(&deq_full[i], 4);
+      mbar_init(&deq_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_free[i], 8);
+    }
+    s_fail = 0;
+    fence_mbar_init();
+  }
+  if (warp == 13) tmem_alloc(&s_tmem, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  if (warp == 12) {
+    // weight producer: raw int4 rows (no dependence on the previous kernel: starts before the wait)
+    for (int i = 0; i < NS; ++i) {
+      const int rs = i % K5_RAW, rr = i / K5_RAW;
+      if (rr > 0 && !mbar_wait_bounded(&raw_empty[rs], (rr - 1) & 1, kWaitLimitNs)) {
+        s_fail = 1;
+        break;
+      }
+      if (lane == 0) mbar_arrive_expect_tx(&raw_full[rs], L::RAW_BYTES);
+      __syncwarp();
+      const int j = g0 * SPG + i;
+      uint8_t* dst = smem + L::RAW_OFF + rs * L::RAW_BYTES;
+      for (int r = lane; r < BN; r += 32) {
+        const int row = tile_row(p, rt0 + r / 16, r % 16);
+        bulk_g2s(dst + r * 32, p.qw + (size_t)row * KW + j * 8, 32, &raw_full[rs]);
+      }
+    }
+  } else if (warp == 8 + 4 + 2) {
+    // x producer (waits for the pre-pass that wrote hi / lo)
+    griddep_wait();
+    if (lane == 0) {
+      for (int i = 0; i < NS; ++i) {
+        const int xs = i % K5_XS, xr = i / K5_XS;
+        if (xr > 0 && !mbar_wait_bounded(&x_empty[xs], (xr - 1) & 1, kWaitLimitNs)) {
+          s_fail = 1;
+          break;
+        }
+        const int kx = (g0 * SPG + i) * K5_BK;
+        uint8_t* dst = smem + L::X_OFF + xs * L::XSTAGE;
+        mbar_arrive_expect_tx(&x_full[xs], XF32 ? L::XSTAGE : L::X_BYTES);
+        tma_load_2d(dst, &txh, kx, m0, &x_full[xs]);
+        if constexpr (XF32) tma_load_2d(dst + L::X_BYTES, &txl, kx, m0, &x_full[xs]);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 8 && warp < 12) {
+    // dequant warps: scales of this CTA's groups once, then exact fp16 (nib - 8) tiles
+    const int t = threadIdx.x - 256;
+    for (int idx = t; idx < NGL * BN; idx += 128) {
+      const int gl = idx / BN, c = idx - gl * BN;
+      const int row = tile_row(p, rt0 + c / 16, c % 16);
+      s_sc[idx] = p.scales[(size_t)row * NG + g0 + gl];
+    }
+    asm volatile("bar.sync 1, 384;" ::: "memory");  // scales visible to the epilogue warps
+    for (int i = 0; i < NS; ++i) {
+      const int rs = i % K5_RAW, ds = i % K5_DS;
+      bool ok = mbar_wait_bounded(&raw_full[rs], (i / K5_RAW) & 1, kWaitLimitNs);
+      if (ok && i >= K5_DS) ok = mbar_wait_bounded(&deq_empty[ds], ((i / K5_DS) - 1) & 1, kWaitLimitNs);
+      if (!ok) {
+        s_fail = 1;
+        break;
+      }
+      const uint32_t* raw = reinterpret_cast<const uint32_t*>(smem + L::RAW_OFF + rs * L::RAW_BYTES);
+      uint8_t* wt = smem + L::W_OFF + ds * L::W_BYTES;
+#pragma unroll
+      for (int v = 0; v < BN * 8 / 128; ++v) {
+        const int wi = t + 128 * v;
+        const int r = wi >> 3, c = wi & 7;
+        const uint32_t w = raw[wi];
+        uint4 o;
+        o.x = hsub2_u(lop_and_or(w, 0x000F000Fu, 0x64006400u), 0x64086408u);
+        o.y = hsub2_u(lop_and_or(w >> 4, 0x000F000Fu, 0x64006400u), 0x64086408u);
+        o.z = hsub2_u(lop_and_or(w >> 8, 0x000F000Fu, 0x64006400u), 0x64086408u);
+        o.w = hsub2_u(lop_and_or(w >> 12, 0x000F000Fu, 0x64006400u), 0x64086408u);
+        *reinterpret_cast<uint4*>(wt + r * 128 + ((c ^ (r & 7)) << 4)) = o;
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&deq_full[ds]);
+        mbar_arrive(&raw_empty[rs]);
+      }
+    }
+  } else if (warp == 13) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(K5_BM, BN, false, false);
+      for (int i = 0; i < NS; ++i) {
+        const int xs = i % K5_XS, ds = i % K5_DS;
+        const int gl = i / SPG, kg = i - gl * SPG, b = gl & 1;
+        bool ok = true;
+        if (kg == 0 && gl >= 2) ok = mbar_wait_bounded(&acc_free[b], ((gl >> 1) - 1) & 1, kWaitLimitNs);
+        ok = ok && mbar_wait_bounded(&x_full[xs], (i / K5_XS) & 1, kWaitLimitNs);
+        ok = ok && mbar_wait_bounded(&deq_full[ds], (i / K5_DS) & 1, kWaitLimitNs);
+        if (!ok) {
+          s_fail = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t xa = smem_u32(smem + L::X_OFF + xs * L::XSTAGE);
+        const uint32_t wb = smem_u32(smem + L::W_OFF + ds * L::W_BYTES);
+        const uint32_t d = tmem + b * BN;
+#pragma unroll
+        for (int kk = 0; kk < K5_BK / 16; ++kk) {
+          const uint64_t bd = sw128_desc(wb + kk * 32, 16, 1024);
+          tc_mma_f16(d, sw128_desc(xa + kk * 32, 16, 1024), bd, idesc, (kg | kk) != 0);
+          if constexpr (XF32) tc_mma_f16(d, sw128_desc(xa + L::X_BYTES + kk * 32, 16, 1024), bd, idesc, 1u);
+        }
+        tc_commit(&x_empty[xs]);
+        tc_commit(&deq_empty[ds]);
+        if (kg == SPG - 1) tc_commit(&acc_full[b]);
+      }
+    }
+    __syncwarp();
+  }
+
+  // epilogue warps: scale each finished group and accumulate in registers
+  constexpr int HC = BN / 2;  // columns per epilogue thread
+  float acc[HC];
+#pragma unroll
+  for (int c = 0; c < HC; ++c) acc[c] = 0.0f;
+  const int q = warp & 3, h = warp >> 2;
+  if (warp < 8) {
+    asm volatile("bar.sync 1, 384;" ::: "memory");
+    for (int gl = 0; gl < NGL; ++gl) {
+      const int b = gl & 1;
+      if (!mbar_wait_bounded(&acc_full[b], (gl >> 1) & 1, kWaitLimitNs)) {
+        s_fail = 1;
+        break;
+      }
+      tc_fence_after();
+      const __half* sc = s_sc + gl * BN + h * HC;
+#pragma unroll
+      for (int cc = 0; cc < HC; cc += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32(tmem + ((uint32_t)(q * 32) << 16) + b * BN + h * HC + cc, r);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) acc[cc + e] = fmaf(__half2float(sc[cc + e]), __uint_as_float(r[e]), acc[cc + e]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_free[b]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 13) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * BN);
+  }
+  if (s_fail) {
+    if (threadIdx.x == 0) atomicOr(&g_linear_status, kStatusTimeout);
+    griddep_launch_dependents();
+    return;
+  }
+  griddep_wait();  // the epilogue reads / writes y, q_out and the caches
+  // the x ring is free now: fin[rt][m][16] for this CTA's row tiles
+  float* fin = reinterpret_cast<float*>(smem + L::X_OFF);
+  const int m = q * 32 + lane;
+  const int rows = min(K5_BM, p.M - m0);
+  const int n_tiles = gridDim.y;
+  if (p.nsplit == 1) {
+    if (warp < 8) {
+#pragma unroll
+      for (int c = 0; c < HC; ++c) {
+        const int col = h * HC + c;
+        fin[((col >> 4) * K5_BM + m) * 16 + (col & 15)] = acc[c];
+      }
+    }
+    __syncthreads();
+  } else {
+    // partial tile [128][BN] of split z, then the last CTA of the tile sums the splits in order
+    const size_t tile = (size_t)blockIdx.x * n_tiles + blockIdx.y;
+    const size_t tiles = (size_t)gridDim.x * n_tiles;
+    if (warp < 8) {
+      float* dst = p.ws + ((size_t)z * tiles + tile) * (K5_BM * BN) + (size_t)m * BN + h * HC;
+#pragma unroll
+      for (int c = 0; c < HC; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_flag = atomicAdd(&p.counters[tile], 1u) == (unsigned)(p.nsplit - 1);
+    __syncthreads();
+    if (!s_flag) {
+      griddep_launch_dependents();
+      return;
+    }
+    __threadfence();
+    for (int i = threadIdx.x; i < K5_BM * BN; i += blockDim.x) {
+      const int mm = i / BN, col = i - mm * BN;
+      float v = 0.0f;
+      for (int s = 0; s < p.nsplit; ++s) v += __ldcg(p.ws + ((size_t)s * tiles + tile) * (K5_BM * BN) + i);
+      fin[((col >> 4) * K5_BM + mm) * 16 + (col & 15)] = v;
+    }
+    if (threadIdx.x == 0) p.counters[tile] = 0u;
+    __syncthreads();
+  }
+  // rows [m0, m0 + rows) as a problem of their own for the shared epilogue
+  LinArgs e = p;
+  e.M = rows;
+  const size_t yrow = (size_t)(p.epi == EPI_SWIGLU ? p.n_out : p.N) * (p.y_f32 ? 4 : 2);
+  if (p.y) e.y = reinterpret_cast<char*>(p.y) + (size_t)m0 * yrow;
+  if (p.q_out) e.q_out = p.q_out + (size_t)m0 * p.H * p.hd;
+  e.pos_offset = p.pos_offset + m0;
+  for (int r = 0; r < RTS; ++r) {
+    if (rt0 + r >= p.RT) break;
+    epilogue_tile(e, fin + (size_t)r * K5_BM * 16, rt0 + r, &s_flag);
+  }
+  griddep_launch_dependents();
+}
+
 // ---- planning ------------------------------------------------------------------------------
 
 struct Plan {
-  int kernel = 2;  // 1 = register-staged MMA, 2 = SIMT, 3 = TMA-staged MMA
+  int kernel = 2;  // 1 = register-staged MMA, 2 = SIMT, 3 = TMA-staged MMA, 4 = streaming, 5 = tcgen05 GEMM
   int W = 4, T = 1, nsplit = 1, kps = 1, MT = 1;
+  int bn = 128, tiles_m = 1, tiles_n = 1;  // kernel 5
   int RT = 0;  // row tiles (grid.x)
   int wstride = 0, x_off = 0;
   size_t smem = 0;
@@ -885,6 +1200,40 @@ static int plan_stream(int M, int K, bool xf32, const q4b_linear_cfg* cfg, Plan&
   return pl.smem <= kMaxSmem ? Q4B_OK : set_error(Q4B_EUNSUPPORTED, "q4_linear: streaming plan too large");
 }
 
+// kernel 5: weight rows per CTA from cfg->tiles (row tiles of 16: 4 or 8), k split at scale-group
+// granularity; workspace = counters | x hi | x lo | split partials
+static bool tc_ok(int M, int K, int G, int epi, bool norm) {
+  return M > 32 && G % 128 == 0 && !norm && epi != EPI_ARGMAX && K / G <= 64 * 64;
+}
+
+static int plan_tc(int M, int K, int G, bool xf32, const q4b_linear_cfg* cfg, Plan& pl) {
+  pl.kernel = 5;
+  const int T = cfg && cfg->tiles ? cfg->tiles : 0;
+  if (T && T != 4 && T != 8) return set_error(Q4B_EINVAL, "q4_linear: kernel 5 takes tiles 4 or 8 (64 or 128 rows)");
+  const int NG = K / G;
+  pl.tiles_m = (M + 127) / 128;
+  pl.bn = T ? T * 16 : 128;
+  if (!T && (long long)pl.tiles_m * ((pl.RT + 7) / 8) < 100) pl.bn = 64;  // few tiles: narrower ones
+  pl.tiles_n = (pl.RT + pl.bn / 16 - 1) / (pl.bn / 16);
+  const long long tiles = (long long)pl.tiles_m * pl.tiles_n;
+  int S = cfg && cfg->split ? cfg->split : 0;
+  if (S < 0 || S > NG) return set_error(Q4B_EINVAL, "q4_linear: split must be in [1, %d] (scale groups)", NG);
+  if (!S) {
+    S = 1;
+    while (tiles * S < 148 && NG / (S * 2) >= 2) S *= 2;
+  }
+  while ((NG + S - 1) / S > K5_MAX_GROUPS) ++S;
+  if (S > 1 && tiles > kMaxCounters)
+    return set_error(Q4B_EUNSUPPORTED, "q4_linear: split-K limited to %d tiles", kMaxCounters);
+  pl.nsplit = S;
+  pl.kps = NG;
+  pl.smem = pl.bn == 128 ? K5<128>::SMEM : K5<64>::SMEM;
+  const size_t xbytes = align_up((size_t)M * K * 2, 256);
+  pl.ws_bytes = kCounterBytes + (xf32 ? 2 : 1) * xbytes +
+                (S > 1 ? (size_t)S * tiles * K5_BM * pl.bn * 4 : 0);
+  return Q4B_OK;
+}
+
 static bool stream_ok(int M, int K, int G, bool norm) {
   (void)norm;
   return M == 1 && G == 128 && K % 1024 == 0 && K <= 8192;
@@ -897,6 +1246,12 @@ static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, bool norm
   const int want = cfg ? cfg->kernel : 0;
   pl.RT = row_tiles(N, n_out, epi);
   pl.MT = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8;
+  if (want == 5) {
+    if (!tc_ok(M, K, G, epi, norm) && !(M >= 1 && G % 128 == 0 && !norm && epi != EPI_ARGMAX))
+      return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 5 needs group %% 128 == 0, no fused norm, no argmax");
+    return plan_tc(M, K, G, xf32, cfg, pl);
+  }
+  if (want == 0 && tc_ok(M, K, G, epi, norm)) return plan_tc(M, K, G, xf32, cfg, pl);
   if ((want == 1 || want == 3) && !mma_ok)
     return set_error(Q4B_EUNSUPPORTED, "q4_linear: tensor-core kernels need group %% 128 == 0 and m <= 64");
   if (want == 2 || (want == 0 && !mma_ok)) {
@@ -1037,7 +1392,13 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
     if (forced) return set_error(Q4B_EINVAL, "q4_linear: qweight, x and ln_w must be 16-byte aligned");
     simt_plan(op, pl);
   }
-  if (pl.kernel != 2 && pl.nsplit > 1 && (pl.ws_bytes > op.ws_bytes || !op.ws || !aligned(op.ws, 16))) {
+  if (pl.kernel == 5 && (pl.ws_bytes > op.ws_bytes || !op.ws || !aligned(op.ws, 256))) {
+    if (forced) return set_error(Q4B_EINVAL, "q4_linear: workspace of %zu bytes needed, %zu given", pl.ws_bytes,
+                                 op.ws_bytes);
+    simt_plan(op, pl);  // the x conversion and split partials need the workspace
+  }
+  if (pl.kernel != 2 && pl.kernel != 5 && pl.nsplit > 1 &&
+      (pl.ws_bytes > op.ws_bytes || !op.ws || !aligned(op.ws, 16))) {
     if (op.cfg && op.cfg->split > 1)
       return set_error(Q4B_EINVAL, "q4_linear: workspace of %zu bytes needed, %zu given", pl.ws_bytes, op.ws_bytes);
     // no (or too little) workspace: all of K in one CTA when it fits, else the SIMT kernel
@@ -1093,12 +1454,45 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
   a.index_offset = op.index_offset;
   a.finalize = op.finalize;
   a.RT = pl.RT;
-  if (pl.kernel != 2 && pl.nsplit > 1) {
+  if (pl.kernel != 2 && pl.kernel != 5 && pl.nsplit > 1) {
     a.counters = reinterpret_cast<unsigned*>(op.ws);
     a.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(op.ws) + kCounterBytes);
   }
   cudaError_t e;
-  if (pl.kernel == 4) {
+  if (pl.kernel == 5) {
+    char* w = reinterpret_cast<char*>(op.ws);
+    const size_t xbytes = align_up((size_t)op.m * op.k * 2, 256);
+    auto* xh = reinterpret_cast<__half*>(w + kCounterBytes);
+    auto* xl = reinterpret_cast<__half*>(w + kCounterBytes + xbytes);
+    a.counters = reinterpret_cast<unsigned*>(w);
+    a.ws = reinterpret_cast<float*>(w + kCounterBytes + (xf32 ? 2 : 1) * xbytes);
+    CUtensorMap th, tl;
+    int rc2 = make_tmap_f16(&th, xh, op.k, op.m, op.k, K5_BM);
+    if (!rc2) rc2 = make_tmap_f16(&tl, xf32 ? xl : xh, op.k, op.m, op.k, K5_BM);
+    if (rc2) return rc2;
+    const int chunks = op.m * (op.k / 8);
+    const int pgrid = std::min((chunks + 255) / 256, 148 * 8);
+    e = xf32 ? launch_pdl(q4_xsplit<true>, dim3(pgrid), dim3(256), 0, st, a, xh, xl)
+             : launch_pdl(q4_xsplit<false>, dim3(pgrid), dim3(256), 0, st, a, xh, xl);
+    if (e == cudaSuccess) {
+      static unsigned long long d[4] = {0, 0, 0, 0};
+      const dim3 grid(pl.tiles_m, pl.tiles_n, pl.nsplit);
+      auto go = [&](auto kern, unsigned long long& done) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (!(done >> (dev & 63) & 1ull)) {
+          cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
+          if (r != cudaSuccess) return r;
+          done |= 1ull << (dev & 63);
+        }
+        return launch_pdl(kern, grid, dim3(K5_THREADS), pl.smem, st, th, tl, a);
+      };
+      if (pl.bn == 128)
+        e = xf32 ? go(q4_gemm_tc<128, true>, d[0]) : go(q4_gemm_tc<128, false>, d[1]);
+      else
+        e = xf32 ? go(q4_gemm_tc<64, true>, d[2]) : go(q4_gemm_tc<64, false>, d[3]);
+    }
+  } else if (pl.kernel == 4) {
     static unsigned long long d0 = 0, d1 = 0;
     e = xf32 ? set_smem_attr(q4_gemv_stream<true>, d1) : set_smem_attr(q4_gemv_stream<false>, d0);
     const int grid = std::min(pl.RT, kStreamCtas);

@@ -225,3 +225,61 @@ def test_qlinear_dropin(dev):
     y = ql(torch.from_numpy(x).to(dev))
     assert y.dtype == torch.float32
     assert O.rel_err(y.cpu().numpy(), O.q4_linear(rq, rs, 32, x)) <= TOL
+
+
+# ---- kernel 5: the tcgen05 int4-weight GEMM (prefill row counts) -------------------------------
+K5_CASES = [(5120, 3072, 128), (3072, 8192, 100), (1000, 1024, 33), (384, 3072, 257), (72, 1024, 64)]
+K5_CFGS = [None, dict(kernel=5), dict(kernel=5, tiles=4), dict(kernel=5, tiles=8, split=1),
+           dict(kernel=5, tiles=4, split=3), dict(kernel=5, tiles=8, split=5)]
+_K5_REF = {}
+
+
+def _k5_case(N, K, M):
+    if (N, K, M) not in _K5_REF:
+        qw, s = gi.synthetic_q4(N, K, 128, seed=N + K + M)
+        x = np.random.default_rng(M).standard_normal((M, K)).astype(np.float32)
+        _K5_REF[(N, K, M)] = (qw, s, x, O.q4_linear(qw, s, 128, x),
+                              O.q4_linear(qw, s, 128, x.astype(np.float16).astype(np.float32)))
+    return _K5_REF[(N, K, M)]
+
+
+@pytest.mark.parametrize("cfg", K5_CFGS, ids=[str(c) for c in K5_CFGS])
+def test_tcgen05_gemm_kernel(dev, cfg):
+    """Many x rows: TMA-fed tcgen05 MMAs on exact (nib - 8) tiles, per-group fp32 scaling."""
+    import q4b
+    for (N, K, M) in K5_CASES:
+        qw, s, x, ref32, ref16 = _k5_case(N, K, M)
+        if cfg and cfg.get("split", 1) > K // 128:
+            continue
+        qwt, st = torch.from_numpy(qw).to(dev), torch.from_numpy(s).to(dev)
+        for xdt, ref in ((torch.float32, ref32), (torch.float16, ref16)):
+            xt = torch.from_numpy(x).to(dev).to(xdt)
+            y = q4b.q4_linear(xt, qwt, st, 128, out=poisoned((M, N), torch.float32, dev), cfg=cfg)
+            assert O.rel_err(y.cpu().numpy(), ref) <= TOL, (N, K, M, xdt, cfg)
+        # SwiGLU (gate rows first) and accumulate (residual add) epilogues on the same tiles
+        I = N // 2
+        xt = torch.from_numpy(x).to(dev)
+        y = q4b.q4_linear(xt, qwt, st, 128, epilogue="swiglu", out=poisoned((M, I), torch.float32, dev), cfg=cfg)
+        sw = (O.silu(ref32[:, :I]) * ref32[:, I:]).astype(np.float32)
+        assert O.rel_err(y.cpu().numpy(), sw) <= TOL, ("swiglu", N, K, M, cfg)
+        h0 = np.random.default_rng(N).standard_normal((M, N)).astype(np.float32)
+        h = torch.from_numpy(h0).to(dev)
+        q4b.q4_linear(xt, qwt, st, 128, epilogue="accumulate", out=h, cfg=cfg)
+        assert O.rel_err(h.cpu().numpy(), h0 + ref32) <= TOL, ("accumulate", N, K, M, cfg)
+    from q4b import _lib
+    assert _lib.lib().q4b_device_status(1) == 0
+
+
+def test_tcgen05_gemm_is_deterministic_and_leaves_counters_zero(dev):
+    import q4b
+    from q4b import ops
+    qw, s, x, ref32, _ = _k5_case(3072, 8192, 100)
+    qwt, st = torch.from_numpy(qw).to(dev), torch.from_numpy(s).to(dev)
+    xt = torch.from_numpy(x).to(dev)
+    cfg = dict(kernel=5, tiles=4, split=7)
+    y1 = q4b.q4_linear(xt, qwt, st, 128, cfg=cfg)
+    y2 = q4b.q4_linear(xt, qwt, st, 128, cfg=cfg)
+    torch.cuda.synchronize()
+    assert torch.equal(y1, y2)
+    ws = ops.WORKSPACE.bufs[(dev.index, torch.cuda.current_stream().cuda_stream)]
+    assert int(ws[:65536].view(torch.int32).abs().sum()) == 0

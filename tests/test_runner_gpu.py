@@ -68,3 +68,19 @@ def test_runner_rejects_like_the_reference(golden_model):
     with pytest.raises(q4b.Q4BError, match="bucket"):
         small = q4b.Runner(model, spec["chunk"], [spec["buckets"][0]])
         small.generate([1] * (spec["buckets"][0] + 1), 2)
+
+
+def test_runner_whole_chunk_prefill_on_tensor_cores(golden_model):
+    """A 64-row prefill chunk goes through the tcgen05 int4 GEMM (q|k|v with RoPE + KV write,
+    SwiGLU, residual adds); the greedy tokens still equal the reference's (the oracle gives the
+    same tokens for chunk 64 as for the golden's chunk)."""
+    import q4b
+    name, z = golden_model
+    spec = gi.MODEL_SPECS[name]
+    if name != "tiny_baseline":
+        pytest.skip("needs a group-128 model with a prompt of at least 64 tokens")
+    model = q4b.LlamaQ4.from_packed(spec["cfg"], z, spec["max_ctx"], vocab_chunk=spec["vocab_chunk"], max_chunk=64)
+    r = q4b.Runner(model, 64, spec["buckets"], "bucketed")
+    toks, rep = r.generate(z["prompt"].tolist(), spec["max_new"])
+    assert toks == z["bucketed_tokens"].tolist()
+    assert [c[0] for c in rep["chunks"]] == [128]

@@ -46,10 +46,18 @@ def test_noalloc_matches_workspace_entry_point(N, K, G, M, xdt):
 
 
 def test_noalloc_rejects_sizes_beyond_the_static_scratch():
+    """Real (allocated) buffers, so nothing can read a bad address even if a future plan accepted
+    the shape: 1024 rows of x over K = 4096 need 16 MiB of converted activations, over 8 MiB."""
     from q4b import _lib
     L = _lib.lib()
-    p = ctypes.c_void_p(256)  # never dereferenced: the size check fails before any launch
-    # a 64-row lm_head-sized problem needs far more than 8 MiB of split-K partials
-    rc = L.q4b_q4_linear_noalloc(p, p, 128, p, _lib.F32, p, _lib.F32, 64, 128256, 3072, _lib.EPI_STORE, None)
+    dev = torch.device("cuda:0")
+    M, N, K = 1024, 64, 4096
+    qw = torch.zeros(N, K // 8, dtype=torch.int32, device=dev)
+    s = torch.ones(N, K // 128, dtype=torch.float16, device=dev)
+    x = torch.zeros(M, K, device=dev)
+    y = torch.zeros(M, N, device=dev)
+    rc = L.q4b_q4_linear_noalloc(qw.data_ptr(), s.data_ptr(), 128, x.data_ptr(), _lib.F32, y.data_ptr(), _lib.F32,
+                                 M, N, K, _lib.EPI_STORE, None)
     assert rc == _lib.Q4B_EINVAL
     assert b"static scratch" in L.q4b_last_error()
+    torch.cuda.synchronize()
