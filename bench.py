@@ -403,7 +403,11 @@ def run_decode(args, rank, world, local, dist_mod):
     pos = [PROMPT_LEN + i for i in range(steps)]
     bytes_tok = statistics.mean(decode_bytes_per_token(cfg, p, world) for p in pos)
     achieved = bytes_tok * value / 1e9
-    launches = 2 + 5 * cfg["num_hidden_layers"] + (0 if world == 1 else 2 * cfg["num_hidden_layers"] + 1)
+    persistent = world == 1 and os.environ.get("Q4B_PERSISTENT", "0") == "1"
+    # persistent decode: one cooperative kernel per token (plus a 8-byte counter reset); else per layer
+    # q|k|v, attention, o, gate|up, down, and embedding + final norm + lm_head (+ TP collectives)
+    launches = 1 if persistent else 2 + 5 * cfg["num_hidden_layers"] + (
+        0 if world == 1 else 2 * cfg["num_hidden_layers"] + 1)
     line = {
         "metric": METRIC_DECODE, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": round(decode_ms / steps, 4), "higher_is_better": True,
@@ -413,10 +417,12 @@ def run_decode(args, rank, world, local, dist_mod):
                    "prompt": PROMPT_LEN, "new_tokens": steps + 1, "chunk": CHUNK, "buckets": BUCKETS,
                    "schedule": "bucketed", "parallelism": f"tp{world}",
                    "l2": "inputs larger than L2: 1.66 GB of weights streamed per token",
-                   "graphs": "one CUDA graph per (phase, bucket), decode steps back to back on the device"},
+                   "graphs": "one CUDA graph per (phase, bucket), decode steps back to back on the device",
+                   "decode_kernel": "persistent (one cooperative launch per token)" if persistent
+                   else "per projection"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": profile_traffic("decode_step_3b"),
-                     "peak_source": pk["source"], "kernel": "decode step (q4_gemv_* dominant)",
+                     "peak_source": pk["source"], "kernel": "decode_step_kernel" if persistent else "decode step (q4_gemv_* dominant)",
                      "algorithmic_bytes_per_token_per_gpu": round(bytes_tok)},
         "e2e": {"value": round(steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
                 "h2d_bytes_per_step": 104, "d2h_bytes_per_step": 4,

@@ -1,0 +1,790 @@
+// Persistent decode step (one token, batch 1): the whole LlamaQ4.step of scripts/llm/llama_q4.py:
+// 199-239 for C = 1 in ONE cooperative launch of one CTA per SM, instead of ~5 launches per layer.
+//
+// Why: at batch 1 every projection is a weight stream (1.66 GB per token for the 3B shape) and a
+// chain of separate kernels pays a launch ramp, a tail and an x-staging round trip per projection.
+// Here one producer warp per CTA streams this CTA's share of every projection's weights, in
+// consumption order and across layer boundaries, into a shared-memory ring with TMA (never
+// waiting for activations), while eight consumer warps follow through the dependency chain:
+//
+//   per layer  QKV  (RMSNorm of h fused into the x staging; RoPE + fp16 KV-cache write epilogue)
+//              ATTN (split-key GQA over the cache: (KV head, 256-key chunk) items)
+//              WO   (merge of the attention partials fused into the x staging; h += o Wo^T)
+//              WGU  (RMSNorm; SwiGLU epilogue into a)
+//              WDOWN (h += a Wdown^T)
+//   then       LM   (final RMSNorm; lm_head rows with the greedy argmax; the last CTA publishes)
+//
+// Stages are ordered by one arrival counter in global memory: a CTA adds 1 when it has written
+// its part of a stage (after a gpu-scope fence); a stage starts once the counter reaches
+// stage x CTAs. Every wait (ring slots, the counter) is bounded by %globaltimer (1 s); a wait that
+// gives up raises an abort flag that every other wait also checks, the step reports Q4B_ETIMEOUT
+// through the state, and the kernel returns.
+//
+// The arithmetic per 128-k group is that of q4_linear.cu's kernel 1 (exact fp16 (nib - 8) by LOP3,
+// m16n8k16 with fp32 accumulation, x as fp16 hi + lo, one fmaf with the group scale), so decode
+// results match the per-projection path up to fp32 summation order.
+#include <cuda.h>
+
+#include <mutex>
+
+#include "fused.h"
+#include "model.h"
+#include "q4dev.cuh"
+#include "tc.cuh"
+
+namespace q4b {
+
+namespace {
+
+constexpr int MK_CW = 8;                       // consumer warps
+constexpr int MK_THREADS = (MK_CW + 1) * 32;   // + one producer warp (warp 0)
+constexpr int MK_UK = 1024;                    // k per weight unit
+constexpr int MK_WBYTES = 16 * MK_UK / 2;      // 16 rows x 512 B of int4
+constexpr int MK_SLOT = MK_WBYTES + 16 * 16;   // + 16 rows x 8 fp16 scales = 8448 B (66 x 128)
+constexpr int MK_NSLOT = 16;
+constexpr int MK_MAXK = 8192;
+constexpr int MK_XROW = MK_MAXK / 8 + 4;       // staged x: uint4 per row (+64 B, as kernel 1)
+constexpr int MK_HD = 128;
+constexpr int MK_KCHUNK = 256;                 // keys per attention item (8 warps x 32)
+constexpr int MK_MAXCH = 64;                   // attention chunks (contexts up to 16384)
+constexpr int MK_ROWS = 4;                     // query rows per KV head (GQA group) at most
+constexpr int MK_PAD = 4;                      // partial row: m, l and two pad floats before o (16-B aligned)
+
+enum { ST_QKV = 0, ST_ATTN = 1, ST_WO = 2, ST_WGU = 3, ST_WDOWN = 4, ST_PER_LAYER = 5 };
+
+// Per projection: weight and scale tensor maps (global memory), rows per tile pairing, geometry.
+struct MkProj {
+  CUtensorMap w;   // int32 [n, k/8], box {128 words, 16 or 8 rows}
+  CUtensorMap s;   // fp16 [n, k/G], box {8 groups, 16 or 8 rows}
+};
+
+struct MkArgs {
+  const MkProj* proj;  // [layers * 4 + 1]: qkv, o, gu, down per layer, then the lm_head
+  const q4b_layer_weights* layers;
+  int n_layers;
+  const int32_t* emb_qw;
+  const __half* emb_s;
+  const float* ln_f;
+  const float* rope_cos;
+  const float* rope_sin;
+  int D, H, Hkv, hd, I, V;
+  float eps, scale;
+  int L;
+  const int32_t* token;
+  DecodeState* state;
+  int32_t* token_log;
+  float* logits;
+  float* h;      // [D] residual stream
+  float* q;      // [H * hd]
+  float* a;      // [I]
+  float* part;   // attention partials [Hkv][MK_MAXCH][MK_ROWS][hd + 4]: m, l, -, -, o[hd]
+  unsigned* sync;  // [0] stage arrivals, [1] abort
+};
+
+struct MkSmem {
+  uint8_t ring[MK_NSLOT][MK_SLOT];
+  uint4 xs_hi[MK_XROW];
+  uint4 xs_lo[MK_XROW];
+  float red[MK_CW][16];
+  float fin[16];
+  float scratch[64];
+  float att_q[MK_ROWS][MK_HD];
+  float att_o[MK_CW][MK_ROWS][MK_HD];
+  float att_m[MK_CW][MK_ROWS], att_l[MK_CW][MK_ROWS];
+  float att_cs[MK_CW][MK_ROWS];
+  float mw[32][MK_MAXCH];  // WO merge weights per q head and chunk (32 >= H)
+  float mL[32];
+  unsigned long long best[MK_CW];
+  uint64_t full[MK_NSLOT], empty[MK_NSLOT];
+  unsigned done[MK_NSLOT];  // lm_head: rounds of each ring slot consumed so far
+  int abort_flag;
+  int last;
+};
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(MK_CW * 32) : "memory"); }
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t* bar, uint32_t n) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(n) : "memory");
+}
+
+// Sum over the consumer threads (256); every consumer thread gets the total.
+__device__ float consumer_sum(float v, float* scratch) {
+  const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
+  v = warp_sum(v);
+  if (lane == 0) scratch[w] = v;
+  consumer_sync();
+  float t = 0.0f;
+#pragma unroll
+  for (int i = 0; i < MK_CW; ++i) t += scratch[i];
+  consumer_sync();
+  return t;
+}
+
+// Stage-start wait (first consumer thread spins, bounded; then the consumer warps sync).
+__device__ bool stage_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
+  if (threadIdx.x == 32) {
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire(&a.sync[0]) < target) {
+      if (ld_acquire(&a.sync[1])) {
+        sm.abort_flag = 1;
+        break;
+      }
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicExch(&a.sync[1], 1u);
+        sm.abort_flag = 1;
+        break;
+      }
+    }
+  }
+  consumer_sync();
+  return !sm.abort_flag;
+}
+// Stage-end arrival: all consumer writes of this stage happen before the gpu-scope release.
+__device__ void stage_arrive(const MkArgs& a) {
+  consumer_sync();
+  if (threadIdx.x == 32) {
+    __threadfence();
+    atomicAdd(&a.sync[0], 1u);
+  }
+}
+
+// Projection of a stage: rows per tile pairing and geometry.
+struct ProjGeo {
+  int K, RT, NU;  // reduction dim, row tiles, 1024-k units per tile
+  bool paired;    // two runs of 8 rows per tile (SwiGLU gate/up, RoPE element halves)
+};
+__device__ __forceinline__ ProjGeo geo(const MkArgs& a, int st) {
+  switch (st) {
+    case ST_QKV: return {a.D, (a.H + 2 * a.Hkv) * a.hd / 16, a.D / MK_UK, true};
+    case ST_WO: return {a.H * a.hd, a.D / 16, a.H * a.hd / MK_UK, false};
+    case ST_WGU: return {a.D, a.I / 8, a.D / MK_UK, true};
+    case ST_WDOWN: return {a.I, a.D / 16, a.I / MK_UK, false};
+    default: return {a.D, a.V / 16, a.D / MK_UK, false};  // lm_head
+  }
+}
+// first weight row of run b (0 / 1) of a paired tile
+__device__ __forceinline__ int pair_row(const MkArgs& a, int st, int rt, int b) {
+  if (st == ST_WGU) return (b ? a.I : 0) + rt * 8;
+  const int per = a.hd / 16, head = rt / per, j = rt - head * per;  // RoPE
+  return head * a.hd + b * (a.hd / 2) + 8 * j;
+}
+
+// ---- producer --------------------------------------------------------------------------------
+
+__device__ bool produce_stage(const MkArgs& a, MkSmem& sm, const MkProj& pj, int st, unsigned& seq) {
+  const ProjGeo gp = geo(a, st);
+  for (int rt = blockIdx.x; rt < gp.RT; rt += gridDim.x) {
+    for (int u = 0; u < gp.NU; ++u, ++seq) {
+      const int slot = seq % MK_NSLOT, round = seq / MK_NSLOT;
+      if (round > 0 && !mbar_wait_bounded(&sm.empty[slot], (round - 1) & 1, kWaitLimitNs)) return false;
+      if (sm.abort_flag) return false;
+      uint8_t* dst = sm.ring[slot];
+      mbar_arrive_expect_tx(&sm.full[slot], MK_SLOT);
+      if (gp.paired) {
+        const int r0 = pair_row(a, st, rt, 0), r1 = pair_row(a, st, rt, 1);
+        tma_load_2d(dst, &pj.w, u * (MK_UK / 8), r0, &sm.full[slot]);
+        tma_load_2d(dst + MK_WBYTES / 2, &pj.w, u * (MK_UK / 8), r1, &sm.full[slot]);
+        tma_load_2d(dst + MK_WBYTES, &pj.s, u * 4, r0, &sm.full[slot]);
+        tma_load_2d(dst + MK_WBYTES + 128, &pj.s, u * 4, r1, &sm.full[slot]);
+      } else {
+        tma_load_2d(dst, &pj.w, u * (MK_UK / 8), rt * 16, &sm.full[slot]);
+        tma_load_2d(dst + MK_WBYTES, &pj.s, u * 4, rt * 16, &sm.full[slot]);
+      }
+    }
+  }
+  return true;
+}
+
+// ---- consumers: x staging --------------------------------------------------------------------
+
+// x[k] (fp32, k < K) -> hi / lo fp16 pairs in the permuted order of dequant_word
+__device__ __forceinline__ void stage_word(MkSmem& sm, int w, const float (&v)[8]) {
+  uint4 hi, lo;
+  split_pair(v[0], v[4], hi.x, lo.x);
+  split_pair(v[1], v[5], hi.y, lo.y);
+  split_pair(v[2], v[6], hi.z, lo.z);
+  split_pair(v[3], v[7], hi.w, lo.w);
+  sm.xs_hi[xswz(w)] = hi;
+  sm.xs_lo[xswz(w)] = lo;
+}
+
+// x = rmsnorm(h) * w (rms_norm, llama_q4.py:141-142); the first layer's h is the embedding row of
+// the token (QEmbedding.lookup, :106-119), written to the residual stream by CTA 0.
+__device__ __forceinline__ void norm_src(const MkArgs& a, int w, bool embed, int token, float (&v)[8]) {
+  if (embed) {
+    const int words = a.D / 8;
+    const bool ok = token >= 0 && token < a.V;
+    const int32_t word = ok ? a.emb_qw[(size_t)token * words + w] : 0;
+    const float s = ok ? __half2float(a.emb_s[(size_t)token * (a.D / 128) + (8 * w) / 128]) : 0.0f;
+#pragma unroll
+    for (int b = 0; b < 8; ++b) v[b] = (float)(((word >> (4 * b)) & 15) - 8) * s;
+  } else {
+    const float4 p0 = __ldcg(reinterpret_cast<const float4*>(a.h + 8 * w));
+    const float4 p1 = __ldcg(reinterpret_cast<const float4*>(a.h + 8 * w) + 1);
+    v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+    v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+  }
+}
+
+__device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float* lnw, bool embed, int token) {
+  const int ct = threadIdx.x - 32;
+  const int words = a.D / 8;
+  float ss = 0.0f;
+  for (int w = ct; w < words; w += MK_CW * 32) {
+    float v[8];
+    norm_src(a, w, embed, token, v);
+#pragma unroll
+    for (int b = 0; b < 8; ++b) ss += v[b] * v[b];
+    if (embed && blockIdx.x == 0) {
+      float4* hp = reinterpret_cast<float4*>(a.h + 8 * w);
+      hp[0] = make_float4(v[0], v[1], v[2], v[3]);
+      hp[1] = make_float4(v[4], v[5], v[6], v[7]);
+    }
+  }
+  const float tot = consumer_sum(ss, sm.scratch);
+  const float rs = 1.0f / sqrtf(tot / (float)a.D + a.eps);
+  for (int w = ct; w < words; w += MK_CW * 32) {
+    float v[8];
+    if (embed) {
+      norm_src(a, w, true, token, v);
+    } else {  // this thread's own words of h: read back through L2 like the first pass
+      norm_src(a, w, false, token, v);
+    }
+    const float4 w0 = *reinterpret_cast<const float4*>(lnw + 8 * w);
+    const float4 w1 = *reinterpret_cast<const float4*>(lnw + 8 * w + 4);
+    v[0] = v[0] * rs * w0.x; v[1] = v[1] * rs * w0.y; v[2] = v[2] * rs * w0.z; v[3] = v[3] * rs * w0.w;
+    v[4] = v[4] * rs * w1.x; v[5] = v[5] * rs * w1.y; v[6] = v[6] * rs * w1.z; v[7] = v[7] * rs * w1.w;
+    stage_word(sm, w, v);
+  }
+}
+
+// x = a (the SwiGLU output), plain
+__device__ void stage_plain(const MkArgs& a, MkSmem& sm, const float* src, int K) {
+  const int ct = threadIdx.x - 32;
+  for (int w = ct; w < K / 8; w += MK_CW * 32) {
+    const float4 p0 = __ldcg(reinterpret_cast<const float4*>(src + 8 * w));
+    const float4 p1 = __ldcg(reinterpret_cast<const float4*>(src + 8 * w) + 1);
+    const float v[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+    stage_word(sm, w, v);
+  }
+}
+
+// x = attention output o [H * hd]: the chunk partials of every head merged (max, sum, weighted V)
+__device__ void stage_attn_merge(const MkArgs& a, MkSmem& sm, int nch) {
+  const int ct = threadIdx.x - 32;
+  const int g = a.H / a.Hkv, HD = a.hd;
+  // per (q head, chunk) weight exp(m_c - M) and per head the total L
+  for (int i = ct; i < a.H; i += MK_CW * 32) {
+    const int kvh = i / g, r = i - kvh * g;
+    const float* base = a.part + ((size_t)kvh * MK_MAXCH * MK_ROWS + r) * (HD + MK_PAD);
+    float M = -INFINITY;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, __ldcg(base + (size_t)c * MK_ROWS * (HD + MK_PAD)));
+    float Lsum = 0.0f;
+    for (int c = 0; c < nch; ++c) {
+      const float mc = __ldcg(base + (size_t)c * MK_ROWS * (HD + MK_PAD));
+      const float cs = mc == -INFINITY ? 0.0f : expf(mc - M);
+      Lsum += __ldcg(base + (size_t)c * MK_ROWS * (HD + MK_PAD) + 1) * cs;
+      sm.mw[i][c] = cs;
+    }
+    sm.mL[i] = Lsum;
+  }
+  consumer_sync();
+  for (int w = ct; w < a.H * HD / 8; w += MK_CW * 32) {
+    const int hq = (8 * w) / HD, e0 = 8 * w - hq * HD;
+    const int kvh = hq / g, r = hq - kvh * g;
+    const float* base = a.part + ((size_t)kvh * MK_MAXCH * MK_ROWS + r) * (HD + MK_PAD) + MK_PAD + e0;
+    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int c = 0; c < nch; ++c) {
+      const float cs = sm.mw[hq][c];
+      const float4 p0 = __ldcg(reinterpret_cast<const float4*>(base + (size_t)c * MK_ROWS * (HD + MK_PAD)));
+      const float4 p1 = __ldcg(reinterpret_cast<const float4*>(base + (size_t)c * MK_ROWS * (HD + MK_PAD)) + 1);
+      v[0] += cs * p0.x; v[1] += cs * p0.y; v[2] += cs * p0.z; v[3] += cs * p0.w;
+      v[4] += cs * p1.x; v[5] += cs * p1.y; v[6] += cs * p1.z; v[7] += cs * p1.w;
+    }
+    const float inv = sm.mL[hq];
+#pragma unroll
+    for (int b = 0; b < 8; ++b) v[b] = v[b] / inv;
+    stage_word(sm, w, v);
+  }
+}
+
+// ---- consumers: projections ------------------------------------------------------------------
+
+// Epilogue of one 16-row tile, fin[s] = dot product of slot s. Called by consumer threads 0..15.
+__device__ void tile_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, int rt, int pos) {
+  const int s = threadIdx.x - 32;
+  if (st == ST_QKV) {
+    if (s >= 8) return;
+    const int per = a.hd / 16, head = rt / per, j = rt - head * per;
+    const int e1 = j * 8 + s, e2 = a.hd / 2 + j * 8 + s;
+    const float x1 = sm.fin[s], x2 = sm.fin[s + 8];
+    const q4b_layer_weights& Lw = a.layers[layer];
+    if (head < a.H + a.Hkv) {
+      // q * cos + rotate_half(q) * sin, rotate_half(x) = cat(-x[h:], x[:h]) (llama_q4.py:195-221)
+      const float* cs = a.rope_cos + (size_t)pos * a.hd;
+      const float* sn = a.rope_sin + (size_t)pos * a.hd;
+      const float o1 = __fadd_rn(__fmul_rn(x1, cs[e1]), __fmul_rn(-x2, sn[e1]));
+      const float o2 = __fadd_rn(__fmul_rn(x2, cs[e2]), __fmul_rn(x1, sn[e2]));
+      if (head < a.H) {
+        a.q[head * a.hd + e1] = o1;
+        a.q[head * a.hd + e2] = o2;
+      } else {
+        __half* kc = reinterpret_cast<__half*>(Lw.k_cache) + ((size_t)pos * a.Hkv + (head - a.H)) * a.hd;
+        kc[e1] = __float2half_rn(o1);
+        kc[e2] = __float2half_rn(o2);
+      }
+    } else {
+      __half* vc = reinterpret_cast<__half*>(Lw.v_cache) + ((size_t)pos * a.Hkv + (head - a.H - a.Hkv)) * a.hd;
+      vc[e1] = __float2half_rn(x1);
+      vc[e2] = __float2half_rn(x2);
+    }
+  } else if (st == ST_WGU) {
+    if (s < 8) a.a[rt * 8 + s] = silu(sm.fin[s]) * sm.fin[s + 8];
+  } else {  // WO / WDOWN: residual add (one CTA owns each row)
+    if (s < 16) {
+      const int row = rt * 16 + s;
+      a.h[row] = __ldcg(a.h + row) + sm.fin[s];
+    }
+  }
+}
+
+// K split across the consumer warps: warp w takes the 128-k group w of every 1024-k unit.
+__device__ bool consume_stage(const MkArgs& a, MkSmem& sm, int st, int layer, unsigned& seq, int pos) {
+  const ProjGeo gp = geo(a, st);
+  const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int mrow[1] = {0};
+  for (int rt = blockIdx.x; rt < gp.RT; rt += gridDim.x) {
+    float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+    for (int u = 0; u < gp.NU; ++u, ++seq) {
+      const int slot = seq % MK_NSLOT;
+      if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, kWaitLimitNs)) {
+        sm.abort_flag = 1;
+        return false;
+      }
+      const uint8_t* sl = sm.ring[slot];
+      const uint4 wa = *reinterpret_cast<const uint4*>(sl + g * 512 + w * 64 + t * 16);
+      const uint4 wb = *reinterpret_cast<const uint4*>(sl + (g + 8) * 512 + w * 64 + t * 16);
+      const __half* sc = reinterpret_cast<const __half*>(sl + MK_WBYTES);
+      const float sa = __half2float(sc[g * 8 + w]), sb = __half2float(sc[(g + 8) * 8 + w]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cnt(&sm.empty[slot], 1);
+      mma_tile<1, true, true>(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, mrow, u * 128 + w * 16 + 4 * t, acc);
+    }
+    if (t == 0) {
+      sm.red[w][g] = acc[0][0];
+      sm.red[w][g + 8] = acc[0][2];
+    }
+    consumer_sync();
+    if (ct < 16) {
+      float v = 0.0f;
+#pragma unroll
+      for (int i = 0; i < MK_CW; ++i) v += sm.red[i][ct];
+      sm.fin[ct] = v;
+    }
+    consumer_sync();
+    if (ct < 16) tile_epilogue(a, sm, st, layer, rt, pos);
+  }
+  return true;
+}
+
+// lm_head: whole row tiles per warp (tiles of this CTA round-robin over the warps), greedy argmax.
+__device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq) {
+  const ProjGeo gp = geo(a, ST_PER_LAYER);
+  const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int mrow[1] = {0};
+  unsigned long long best = 0ull;
+  // Warps take whole tiles here, so a slot's rounds are consumed by different warps, out of step
+  // with each other. A warp must not wait on a slot's full barrier before the slot's previous
+  // round has been consumed: the parity test would then match the earlier phase. done[slot] counts
+  // consumed rounds (all earlier stages consumed their slots in order: rounds so far = uses so far).
+  if (ct < MK_NSLOT) sm.done[ct] = seq > (unsigned)ct ? (seq - ct + MK_NSLOT - 1) / MK_NSLOT : 0u;
+  consumer_sync();
+  volatile unsigned* done = sm.done;
+  int i = 0;
+  for (int rt = blockIdx.x; rt < gp.RT; rt += gridDim.x, ++i, seq += gp.NU) {
+    if ((i % MK_CW) != w) continue;
+    float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+    for (int u = 0; u < gp.NU; ++u) {
+      const unsigned sq = seq + u;
+      const int slot = sq % MK_NSLOT;
+      const unsigned round = sq / MK_NSLOT;
+      bool ok = true;
+      if (lane == 0) {
+        const uint64_t t0 = globaltimer_ns();
+        while (done[slot] < round) {
+          if (sm.abort_flag || globaltimer_ns() - t0 > kWaitLimitNs) {
+            ok = false;
+            break;
+          }
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok || !mbar_wait_bounded(&sm.full[slot], round & 1, kWaitLimitNs)) {
+        sm.abort_flag = 1;
+        return false;
+      }
+      const uint8_t* sl = sm.ring[slot];
+      const __half* sc = reinterpret_cast<const __half*>(sl + MK_WBYTES);
+#pragma unroll 2
+      for (int j = 0; j < MK_CW; ++j) {
+        const uint4 wa = *reinterpret_cast<const uint4*>(sl + g * 512 + j * 64 + t * 16);
+        const uint4 wb = *reinterpret_cast<const uint4*>(sl + (g + 8) * 512 + j * 64 + t * 16);
+        const float sa = __half2float(sc[g * 8 + j]), sb = __half2float(sc[(g + 8) * 8 + j]);
+        mma_tile<1, true, true>(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, mrow, u * 128 + j * 16 + 4 * t, acc);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_cnt(&sm.empty[slot], MK_CW);
+        __threadfence_block();
+        done[slot] = round + 1;
+      }
+    }
+    if (t == 0) {
+      const int r0 = rt * 16 + g, r1 = r0 + 8;
+      if (a.logits) {
+        a.logits[r0] = acc[0][0];
+        a.logits[r1] = acc[0][2];
+      }
+      best = max(best, max(argmax_key(acc[0][0], (unsigned)r0), argmax_key(acc[0][2], (unsigned)r1)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+  if (lane == 0) sm.best[w] = best;
+  consumer_sync();
+  if (ct == 0) {
+    unsigned long long b = 0ull;
+    for (int k = 0; k < MK_CW; ++k) b = max(b, sm.best[k]);
+    atomicMax(&a.state->best, b);
+    __threadfence();
+    sm.last = atomicAdd(&a.state->counter, 1u) == gridDim.x - 1;
+    if (sm.last) {
+      __threadfence();
+      const unsigned long long bb = atomicExch(&a.state->best, 0ull);
+      a.state->counter = 0u;
+      publish_token(a.state, a.token_log, (int32_t)argmax_index(bb));
+    }
+  }
+  return true;
+}
+
+// Attention item (KV head kvh, keys [256 ch, 256 ch + 256) of ctx): per query row of the group, the
+// chunk's (max, sum, weighted V), the same online-softmax pieces as attn_decode_kernel.
+__device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int ch, int ctx) {
+  constexpr int HD = MK_HD, EPL = HD / 32, KU4 = HD / 8;
+  const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
+  const int g = a.H / a.Hkv;
+  const q4b_layer_weights& Lw = a.layers[layer];
+  const __half* kc = reinterpret_cast<const __half*>(Lw.k_cache);
+  const __half* vc = reinterpret_cast<const __half*>(Lw.v_cache);
+  const size_t row_stride = (size_t)a.Hkv * HD;
+  const int k0 = ch * MK_KCHUNK, k1 = min(k0 + MK_KCHUNK, ctx);
+  const int jbase = k0 + 32 * w, j = jbase + lane;
+  for (int i = ct; i < g * HD; i += MK_CW * 32) sm.att_q[i / HD][i % HD] = __ldcg(a.q + (size_t)kvh * g * HD + i);
+  consumer_sync();
+  // scores of this lane's key for every query row, the K row read in two halves
+  float dr[MK_ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t)min(j, k1 - 1) * row_stride + (size_t)kvh * HD);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    uint4 kr[KU4 / 2];
+#pragma unroll
+    for (int u = 0; u < KU4 / 2; ++u) kr[u] = __ldcg(kp + half * (KU4 / 2) + u);
+#pragma unroll
+    for (int u = 0; u < KU4 / 2; ++u) {
+      const __half2* h2 = reinterpret_cast<const __half2*>(&kr[u]);
+#pragma unroll
+      for (int tt = 0; tt < 4; ++tt) {
+        const float2 f = __half22float2(h2[tt]);
+        const int e = 8 * (half * (KU4 / 2) + u) + 2 * tt;
+#pragma unroll
+        for (int r = 0; r < MK_ROWS; ++r) {
+          if (r < g) {
+            dr[r] = fmaf(sm.att_q[r][e], f.x, dr[r]);
+            dr[r] = fmaf(sm.att_q[r][e + 1], f.y, dr[r]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < MK_ROWS; ++r) {
+    if (r >= g) break;
+    const float sc = j < k1 ? dr[r] * a.scale : -INFINITY;
+    const float m = warp_max(sc);
+    float o[EPL] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float lw = 0.0f;
+    if (m != -INFINITY) {
+      const float p = expf(sc - m);
+      lw = warp_sum(p);
+      for (int jj = 0; jj < 32; ++jj) {
+        const float pj = __shfl_sync(0xffffffffu, p, jj);
+        if (jbase + jj < k1) {
+          const uint2 u2 = __ldcg(reinterpret_cast<const uint2*>(vc + (size_t)(jbase + jj) * row_stride +
+                                                                  (size_t)kvh * HD + lane * EPL));
+          const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&u2.x));
+          const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&u2.y));
+          o[0] = fmaf(pj, v0.x, o[0]);
+          o[1] = fmaf(pj, v0.y, o[1]);
+          o[2] = fmaf(pj, v1.x, o[2]);
+          o[3] = fmaf(pj, v1.y, o[3]);
+        }
+      }
+    }
+    if (lane == 0) {
+      sm.att_m[w][r] = m;
+      sm.att_l[w][r] = lw;
+    }
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) sm.att_o[w][r][lane * EPL + e] = o[e];
+  }
+  consumer_sync();
+  // merge the warps into this chunk's partial
+  float* part = a.part + ((size_t)kvh * MK_MAXCH + ch) * MK_ROWS * (HD + MK_PAD);
+  if (ct < g) {
+    const int r = ct;
+    float M = -INFINITY;
+    for (int i = 0; i < MK_CW; ++i) M = fmaxf(M, sm.att_m[i][r]);
+    float l = 0.0f;
+    for (int i = 0; i < MK_CW; ++i) {
+      const float cs = sm.att_m[i][r] == -INFINITY ? 0.0f : expf(sm.att_m[i][r] - M);
+      sm.att_cs[i][r] = cs;
+      l += sm.att_l[i][r] * cs;
+    }
+    part[r * (HD + MK_PAD)] = M;
+    part[r * (HD + MK_PAD) + 1] = l;
+  }
+  consumer_sync();
+  for (int i = ct; i < g * HD; i += MK_CW * 32) {
+    const int r = i / HD, e = i - r * HD;
+    float v = 0.0f;
+    for (int k = 0; k < MK_CW; ++k) v += sm.att_o[k][r][e] * sm.att_cs[k][r];
+    part[r * (HD + MK_PAD) + MK_PAD + e] = v;
+  }
+}
+
+__global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  MkSmem& sm = *reinterpret_cast<MkSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < MK_NSLOT; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], MK_CW);
+    }
+    sm.abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int pos = a.state->start;
+  const int token = *a.token;
+  const int ctx = min(a.L, pos + 1);
+  const int nch = (ctx + MK_KCHUNK - 1) / MK_KCHUNK;
+
+  if (warp == 0) {
+    // producer: every projection's weights for this CTA, in consumption order
+    unsigned seq = 0;
+    if (lane == 0) {
+      bool ok = true;
+      for (int l = 0; l < a.n_layers && ok; ++l) {
+        ok = ok && produce_stage(a, sm, a.proj[4 * l + 0], ST_QKV, seq);
+        ok = ok && produce_stage(a, sm, a.proj[4 * l + 1], ST_WO, seq);
+        ok = ok && produce_stage(a, sm, a.proj[4 * l + 2], ST_WGU, seq);
+        ok = ok && produce_stage(a, sm, a.proj[4 * l + 3], ST_WDOWN, seq);
+      }
+      ok = ok && produce_stage(a, sm, a.proj[4 * a.n_layers], ST_PER_LAYER, seq);
+      if (!ok) {
+        atomicExch(&a.sync[1], 1u);
+        sm.abort_flag = 1;
+      }
+    }
+    __syncwarp();
+    return;
+  }
+
+  unsigned seq = 0;
+  unsigned stage = 0;
+  const unsigned n = gridDim.x;
+  bool ok = true;
+  for (int l = 0; l < a.n_layers && ok; ++l) {
+    const q4b_layer_weights& Lw = a.layers[l];
+    // QKV
+    ok = stage == 0 || stage_wait(a, sm, stage * n);
+    if (!ok) break;
+    stage_norm(a, sm, Lw.ln_in, l == 0, token);
+    consumer_sync();
+    ok = consume_stage(a, sm, ST_QKV, l, seq, pos);
+    stage_arrive(a);
+    ++stage;
+    if (!ok) break;
+    // attention
+    if (!(ok = stage_wait(a, sm, stage * n))) break;
+    for (int it = blockIdx.x; it < a.Hkv * nch; it += gridDim.x) {
+      attn_item(a, sm, l, it / nch, it % nch, ctx);
+      consumer_sync();
+    }
+    stage_arrive(a);
+    ++stage;
+    // WO
+    if (!(ok = stage_wait(a, sm, stage * n))) break;
+    stage_attn_merge(a, sm, nch);
+    consumer_sync();
+    ok = consume_stage(a, sm, ST_WO, l, seq, pos);
+    stage_arrive(a);
+    ++stage;
+    if (!ok) break;
+    // WGU
+    if (!(ok = stage_wait(a, sm, stage * n))) break;
+    stage_norm(a, sm, Lw.ln_post, false, token);
+    consumer_sync();
+    ok = consume_stage(a, sm, ST_WGU, l, seq, pos);
+    stage_arrive(a);
+    ++stage;
+    if (!ok) break;
+    // WDOWN
+    if (!(ok = stage_wait(a, sm, stage * n))) break;
+    stage_plain(a, sm, a.a, a.I);
+    consumer_sync();
+    ok = consume_stage(a, sm, ST_WDOWN, l, seq, pos);
+    stage_arrive(a);
+    ++stage;
+  }
+  if (ok && (ok = stage_wait(a, sm, stage * n))) {
+    stage_norm(a, sm, a.ln_f, false, token);
+    consumer_sync();
+    ok = consume_lm(a, sm, seq);
+  }
+  if (!ok && threadIdx.x == 32) {
+    atomicExch(&a.sync[1], 1u);
+    a.state->status = 1;
+  }
+}
+
+}  // namespace
+
+// ---- host ----------------------------------------------------------------------------------------
+
+static bool mk_shapes_ok(const Model& m) {
+  return m.cfg.tp_size == 1 && m.hd == MK_HD && m.H % m.Hkv == 0 && m.H / m.Hkv <= MK_ROWS && m.H <= 32 &&
+         m.D % MK_UK == 0 && (m.H * m.hd) % MK_UK == 0 && m.I % MK_UK == 0 && m.I <= MK_MAXK && m.D <= MK_MAXK &&
+         m.H * m.hd <= MK_MAXK && m.V % 16 == 0 && m.cfg.max_ctx <= MK_MAXCH * MK_KCHUNK;
+}
+
+// Q4B_PERSISTENT=1 selects the persistent kernel for decode, anything else the per-projection
+// kernels (read on every step)
+static bool persistent_enabled() {
+  const char* e = std::getenv("Q4B_PERSISTENT");
+  return e && e[0] == '1';
+}
+
+// Tensor maps and the layer table on the device; needs every weight set and no stream capture.
+int Model::mk_prepare() {
+  if (mk_ready) return Q4B_OK;
+  if (!mk_shapes_ok(*this)) return set_error(Q4B_EUNSUPPORTED, "persistent decode: unsupported shape");
+  int rc = check_ready();
+  if (rc) return rc;
+  const auto groups_ok = [](const q4b_qmat& w) { return w.group == 128; };
+  for (const auto& L : layers)
+    if (!groups_ok(L.wqkv) || !groups_ok(L.wo) || !groups_ok(L.wgu) || !groups_ok(L.wdown))
+      return set_error(Q4B_EUNSUPPORTED, "persistent decode: group 128 only");
+  if (embed.group != 128) return set_error(Q4B_EUNSUPPORTED, "persistent decode: group 128 only");
+  std::vector<MkProj> proj(layers.size() * 4 + 1);
+  auto mk = [](MkProj& p, const q4b_qmat& w, bool paired) {
+    int r = make_tmap_i32(&p.w, w.qweight, w.k / 8, w.n, w.k / 8, MK_UK / 8, paired ? 8 : 16);
+    if (r) return r;
+    // scales: fp16 [n, k/G] as 16-bit elements: the int32 helper is for 4-byte elements, so describe
+    // the scale rows as [n, k/G/2] int32 pairs (the box is 8 groups = 4 pairs = 16 bytes)
+    return make_tmap_i32(&p.s, w.scales, w.k / w.group / 2, w.n, w.k / w.group / 2, 4, paired ? 8 : 16);
+  };
+  for (size_t l = 0; l < layers.size(); ++l) {
+    if ((rc = mk(proj[4 * l + 0], layers[l].wqkv, true))) return rc;
+    if ((rc = mk(proj[4 * l + 1], layers[l].wo, false))) return rc;
+    if ((rc = mk(proj[4 * l + 2], layers[l].wgu, true))) return rc;
+    if ((rc = mk(proj[4 * l + 3], layers[l].wdown, false))) return rc;
+  }
+  if ((rc = mk(proj[4 * layers.size()], embed, false))) return rc;
+  if (!mk_proj && (rc = alloc(&mk_proj, sizeof(MkProj) * proj.size(), false))) return rc;
+  if (!mk_layers && (rc = alloc(&mk_layers, sizeof(q4b_layer_weights) * layers.size(), false))) return rc;
+  if (!mk_part && (rc = alloc((void**)&mk_part, sizeof(float) * Hkv * MK_MAXCH * MK_ROWS * (hd + MK_PAD), true))) return rc;
+  if (!mk_sync && (rc = alloc((void**)&mk_sync, 2 * sizeof(unsigned), true))) return rc;
+  cudaError_t e = cudaMemcpy(mk_proj, proj.data(), sizeof(MkProj) * proj.size(), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cudaMemcpy(mk_layers, layers.data(), sizeof(q4b_layer_weights) * layers.size(), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return set_error(Q4B_ECUDA, "persistent decode: table upload: %s", cudaGetErrorString(e));
+  int dev = 0, sms = 0, per = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const size_t smem = sizeof(MkSmem) + 1024;
+  e = cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, decode_step_kernel, MK_THREADS, smem);
+  if (e != cudaSuccess || per < 1)
+    return set_error(Q4B_EUNSUPPORTED, "persistent decode: kernel does not fit an SM (%s)", cudaGetErrorString(e));
+  mk_ctas = sms;
+  mk_ready = true;
+  return Q4B_OK;
+}
+
+bool Model::mk_usable(int C, cudaStream_t st) {
+  if (C != 1 || !persistent_enabled() || !mk_shapes_ok(*this)) return false;
+  if (mk_ready) return true;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
+  if (mk_prepare() != Q4B_OK) {
+    clear_error();
+    return false;
+  }
+  return true;
+}
+
+int Model::mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_log, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(mk_sync, 0, 2 * sizeof(unsigned), st);
+  if (e != cudaSuccess) return set_error(Q4B_ECUDA, "persistent decode: reset: %s", cudaGetErrorString(e));
+  MkArgs a = {};
+  a.proj = reinterpret_cast<const MkProj*>(mk_proj);
+  a.layers = reinterpret_cast<const q4b_layer_weights*>(mk_layers);
+  a.n_layers = (int)layers.size();
+  a.emb_qw = embed.qweight;
+  a.emb_s = reinterpret_cast<const __half*>(embed.scales);
+  a.ln_f = ln_f;
+  a.rope_cos = rope_cos;
+  a.rope_sin = rope_sin;
+  a.D = D;
+  a.H = H;
+  a.Hkv = Hkv;
+  a.hd = hd;
+  a.I = I;
+  a.V = V;
+  a.eps = cfg.rms_eps;
+  a.scale = (float)(1.0 / sqrt((double)hd));
+  a.L = L;
+  a.token = toks;
+  a.state = state;
+  a.token_log = token_log;
+  a.logits = logits;
+  a.h = h;
+  a.q = q;
+  a.a = this->a;
+  a.part = mk_part;
+  a.sync = mk_sync;
+  cudaLaunchConfig_t cfgl = {};
+  cfgl.gridDim = dim3(mk_ctas);
+  cfgl.blockDim = dim3(MK_THREADS);
+  cfgl.dynamicSmemBytes = sizeof(MkSmem) + 1024;
+  cfgl.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfgl.attrs = attr;
+  cfgl.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfgl, decode_step_kernel, a);
+  if (e != cudaSuccess) return set_error(Q4B_ELAUNCH, "persistent decode: launch: %s", cudaGetErrorString(e));
+  return check_launch("persistent decode");
+}
+
+}  // namespace q4b

@@ -394,6 +394,21 @@ int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t ro
   return Q4B_OK;
 }
 
+int make_tmap_i32(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
+                  uint32_t box_rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return set_error(Q4B_EUNSUPPORTED, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 4};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(Q4B_EINVAL, "cuTensorMapEncodeTiled (int32) failed (%d)", (int)r);
+  return Q4B_OK;
+}
+
 unsigned gemm_status(bool reset) {
   unsigned v = 0;
   cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(v));

@@ -127,6 +127,7 @@ int Model::forward(const int32_t* toks, int C, int L, float* logits, int32_t* to
   if (C < 1 || C > cfg.max_chunk) return set_error(Q4B_EINVAL, "model: %d rows, max_chunk %d", C, cfg.max_chunk);
   if (L < 1 || L > cfg.max_ctx) return set_error(Q4B_EINVAL, "model: bucket %d outside 1..max_ctx %d", L, cfg.max_ctx);
   if ((rc = check_ready())) return rc;
+  if (mk_usable(C, st)) return mk_forward(toks, L, logits, token_log, st);
   if ((rc = embed_run(toks, C, embed.qweight, embed.scales, cfg.vocab, D, embed.group, h, st))) return rc;
   const bool fuse_norm = C <= 8;
   const int* start = &state->start;
@@ -283,6 +284,7 @@ extern "C" int q4b_model_set_layer(q4b_model* model, int layer, const q4b_layer_
   if (!w->ln_in || !w->ln_post || !w->k_cache || !w->v_cache)
     return set_error(Q4B_EINVAL, "model_set_layer: null norm weight or cache");
   m->layers[layer] = *w;
+  m->mk_ready = false;
   return Q4B_OK;
 }
 
@@ -297,6 +299,7 @@ extern "C" int q4b_model_set_head(q4b_model* model, const q4b_qmat* embed, const
   m->ln_f = ln_f;
   m->rope_cos = rope_cos;
   m->rope_sin = rope_sin;
+  m->mk_ready = false;
   return Q4B_OK;
 }
 

@@ -26,6 +26,16 @@ struct Model {
   void* attn_ws = nullptr;
   size_t attn_ws_bytes = 0;
   std::vector<void*> owned;
+  // persistent decode step (decode_mk.cu): tensor maps + layer table on the device
+  void* mk_proj = nullptr;
+  void* mk_layers = nullptr;
+  float* mk_part = nullptr;
+  unsigned* mk_sync = nullptr;
+  int mk_ctas = 0;
+  bool mk_ready = false;
+  int mk_prepare();
+  bool mk_usable(int C, cudaStream_t st);
+  int mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_log, cudaStream_t st);
   // tensor parallelism (tp.cu)
   ncclComm* comm = nullptr;
   unsigned long long* gather = nullptr;  // [tp_size] per-rank argmax keys

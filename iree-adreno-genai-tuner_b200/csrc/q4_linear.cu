@@ -27,6 +27,7 @@
 #include <algorithm>
 
 #include "linear.h"
+#include "q4dev.cuh"
 #include "tc.cuh"
 
 namespace q4b {
@@ -73,65 +74,7 @@ struct LinArgs {
 // status word of this file's kernels (bounded waits that gave up), read by linear_status()
 __device__ unsigned g_linear_status;
 
-// ---- PTX helpers ---------------------------------------------------------------------------
-
-__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));  // (a & b) | c
-  return d;
-}
-__device__ __forceinline__ uint32_t hsub2_u(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("sub.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
-
-// 8 nibbles of one word -> 4 fp16 pairs of exact (nib - 8): {(n0,n4), (n1,n5), (n2,n6), (n3,n7)}.
-// OR-ing a nibble into the mantissa of 1024.0 (0x6400) gives 1024 + nib; nibbles taken in place at
-// bits 4..7 give 1024 + 16 nib, rescaled by an exact FMA.
-__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t (&o)[4]) {
-  const uint32_t kMagic = 0x64006400u;      // 1024.0 | 1024.0
-  const uint32_t k1032 = 0x64086408u;       // 1032.0
-  const uint32_t kSixteenth = 0x2C002C00u;  // 0.0625
-  const uint32_t kNeg72 = 0xD480D480u;      // -72.0
-  const uint32_t w8 = w >> 8;
-  o[0] = hsub2_u(lop_and_or(w, 0x000F000Fu, kMagic), k1032);
-  o[1] = hfma2_u(lop_and_or(w, 0x00F000F0u, kMagic), kSixteenth, kNeg72);
-  o[2] = hsub2_u(lop_and_or(w8, 0x000F000Fu, kMagic), k1032);
-  o[3] = hfma2_u(lop_and_or(w8, 0x00F000F0u, kMagic), kSixteenth, kNeg72);
-}
-
-__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                          uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  uint32_t d;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-  return d;
-}
-
-// fp32 pair (a, b) -> hi = fp16(a), fp16(b); lo = fp16(a - hi_a), fp16(b - hi_b)
-__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
-  hi = pack_half2(a, b);
-  const __half2 h = *reinterpret_cast<const __half2*>(&hi);
-  const float2 f = __half22float2(h);
-  lo = pack_half2(a - f.x, b - f.y);
-}
-
-// staged-x word position: XOR the low two bits with bits 2..3, which spreads the 16-byte reads of
-// the four lanes of a quad over distinct bank groups
-__device__ __forceinline__ int xswz(int w) { return w ^ ((w >> 2) & 3); }
+// ---- PTX helpers: q4dev.cuh -------------------------------------------------------------------
 
 __device__ __forceinline__ float load_y(const void* y, size_t i, int f32) {
   return f32 ? reinterpret_cast<const float*>(y)[i] : __half2float(reinterpret_cast<const __half*>(y)[i]);
@@ -242,8 +185,9 @@ __device__ __forceinline__ void stage_x(const LinArgs& p, const float* rs, uint4
   }
 }
 
-// Epilogue of one finished tile: fin[m * 16 + s] holds the fp32 dot product of slot s, batch row m.
-__device__ void epilogue_tile(const LinArgs& p, const float* fin, int rt, int* s_flag) {
+// Epilogue of one finished tile: fin[m * fs + s] holds the fp32 dot product of slot s, batch row m
+// (fs = 16, or 17 where a padded stride avoids shared-memory bank conflicts when it is written).
+__device__ void epilogue_tile(const LinArgs& p, const float* fin, int rt, int* s_flag, int fs = 16) {
   const int items = p.M * 16;
   if (p.epi == EPI_ARGMAX) {  // m == 1
     if (threadIdx.x < 16) {
@@ -274,7 +218,7 @@ __device__ void epilogue_tile(const LinArgs& p, const float* fin, int rt, int* s
     for (int i = threadIdx.x; i < p.M * 8; i += blockDim.x) {
       const int m = i >> 3, s = i & 7;
       const int e1 = j * 8 + s, e2 = p.hd / 2 + j * 8 + s;
-      const float x1 = fin[m * 16 + s], x2 = fin[m * 16 + s + 8];
+      const float x1 = fin[m * fs + s], x2 = fin[m * fs + s + 8];
       const int pos = *p.pos0 + p.pos_offset + m;
       if (head < p.H + p.Hkv) {
         // q * cos + rotate_half(q) * sin, rotate_half(x) = cat(-x[h:], x[:h]) (llama_q4.py:195-221)
@@ -303,11 +247,12 @@ __device__ void epilogue_tile(const LinArgs& p, const float* fin, int rt, int* s
     const int m = i >> 4, s = i & 15;
     if (p.epi == EPI_SWIGLU) {
       const int col = rt * 8 + s;
-      if (s < 8 && col < p.n_out) store_y(p.y, (size_t)m * p.n_out + col, silu(fin[i]) * fin[i + 8], p.y_f32);
+      if (s < 8 && col < p.n_out)
+        store_y(p.y, (size_t)m * p.n_out + col, silu(fin[m * fs + s]) * fin[m * fs + s + 8], p.y_f32);
     } else {
       const int col = rt * 16 + s;
       if (col < p.N) {
-        float v = fin[i];
+        float v = fin[m * fs + s];
         const size_t o = (size_t)m * p.N + col;
         if (p.epi == EPI_ACCUMULATE) v += load_y(p.y, o, p.y_f32);
         store_y(p.y, o, v, p.y_f32);
@@ -369,54 +314,9 @@ __device__ __forceinline__ void finish_tile(const LinArgs& p, float (&acc)[MT][4
   epilogue_tile(p, fin, rt, s_flag);
 }
 
-// One 128-k tile of MMAs: weights of rows g / g + 8 (4 words each) times staged x.
-template <int MT, bool XF32>
-__device__ __forceinline__ void mma_tile(const uint4& wa, const uint4& wb, float sa, float sb, const uint4* xs_hi,
-                                         const uint4* xs_lo, const int (&mrow)[MT], int wbase, float (&acc)[MT][4]) {
-  // two independent accumulator chains per n-tile (even / odd MMA of each word, and the lo terms
-  // in a third / fourth) so consecutive MMAs do not wait on each other
-  float part[MT][2][4], partl[MT][2][4];
-#pragma unroll
-  for (int nt = 0; nt < MT; ++nt)
-#pragma unroll
-    for (int c = 0; c < 2; ++c)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) part[nt][c][e] = partl[nt][c][e] = 0.0f;
-  const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
-  const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint32_t A[4], B[4];
-    dequant_word(wav[q], A);
-    dequant_word(wbv[q], B);
-    const int ph = xswz(wbase + q);
-#pragma unroll
-    for (int nt = 0; nt < MT; ++nt) {
-      const uint4 xh = xs_hi[mrow[nt] + ph];
-      mma_16816(part[nt][0], A[0], B[0], A[1], B[1], xh.x, xh.y);
-      mma_16816(part[nt][1], A[2], B[2], A[3], B[3], xh.z, xh.w);
-      if constexpr (XF32) {
-        const uint4 xl = xs_lo[mrow[nt] + ph];
-        mma_16816(partl[nt][0], A[0], B[0], A[1], B[1], xl.x, xl.y);
-        mma_16816(partl[nt][1], A[2], B[2], A[3], B[3], xl.z, xl.w);
-      }
-    }
-  }
-#pragma unroll
-  for (int nt = 0; nt < MT; ++nt) {
-    float v[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = (part[nt][0][e] + part[nt][1][e]) + (partl[nt][0][e] + partl[nt][1][e]);
-    acc[nt][0] = fmaf(sa, v[0], acc[nt][0]);
-    acc[nt][1] = fmaf(sa, v[1], acc[nt][1]);
-    acc[nt][2] = fmaf(sb, v[2], acc[nt][2]);
-    acc[nt][3] = fmaf(sb, v[3], acc[nt][3]);
-  }
-}
-
 // ---- kernel 1: register-staged weights ------------------------------------------------------
 
-template <int MT, bool XF32, int T>
+template <int MT, bool XF32, int T, bool ILP = false>
 __global__ void __launch_bounds__(256) q4_gemv_reg(LinArgs p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ int s_flag;
@@ -471,7 +371,7 @@ __global__ void __launch_bounds__(256) q4_gemv_reg(LinArgs p) {
 #pragma unroll
   for (int j = 0; j < T; ++j) {
     const int kt = kt0 + warp + W * j;
-    if (kt < kt1) mma_tile<MT, XF32>(wa[j], wb[j], sa[j], sb[j], xs_hi, xs_lo, mrow, (kt - kt0) * 16 + 4 * t, acc);
+    if (kt < kt1) mma_tile<MT, XF32, ILP>(wa[j], wb[j], sa[j], sb[j], xs_hi, xs_lo, mrow, (kt - kt0) * 16 + 4 * t, acc);
   }
   finish_tile<MT>(p, acc, reinterpret_cast<float*>(smem_raw), &s_flag, rt, sp);
 }
@@ -547,7 +447,7 @@ __global__ void __launch_bounds__(256) q4_gemv_tma(LinArgs p) {
     const float sb = __half2float(ss[(g + 8) * KG + grp]);
     const uint4 wa = *reinterpret_cast<const uint4*>(swa + kl * 64);
     const uint4 wb = *reinterpret_cast<const uint4*>(swb + kl * 64);
-    mma_tile<MT, XF32>(wa, wb, sa, sb, xs_hi, xs_lo, mrow, kl * 16 + 4 * t, acc);
+    mma_tile<MT, XF32, false>(wa, wb, sa, sb, xs_hi, xs_lo, mrow, kl * 16 + 4 * t, acc);
   }
   finish_tile<MT>(p, acc, reinterpret_cast<float*>(smem_raw + p.x_off), &s_flag, rt, sp);
 }
@@ -647,7 +547,7 @@ __global__ void __launch_bounds__(768) q4_gemv_stream(LinArgs p) {
       const uint4 wb = *reinterpret_cast<const uint4*>(sw + (g + 8) * (SK / 2) + tl * 64);
       const float sa = __half2float(ss[g * (SK / 128) + tl]);
       const float sb = __half2float(ss[(g + 8) * (SK / 128) + tl]);
-      mma_tile<1, XF32>(wa, wb, sa, sb, xs_hi, xs_lo, mrow, (kc * TPS + tl) * 16 + 4 * t, acc);
+      mma_tile<1, XF32, true>(wa, wb, sa, sb, xs_hi, xs_lo, mrow, (kc * TPS + tl) * 16 + 4 * t, acc);
     }
     if (kc == KC - 1) {  // row tile done: column 0 of the accumulators (lanes with t == 0)
       if (t == 0) {
@@ -765,6 +665,7 @@ constexpr int K5_BM = 128, K5_BK = 64;
 constexpr int K5_RAW = 8, K5_XS = 3, K5_DS = 3;
 constexpr int K5_THREADS = 15 * 32;  // 8 epilogue, 4 dequant, 1 weight producer, 1 MMA, 1 x producer
 constexpr int K5_MAX_GROUPS = 64;    // scales of up to 64 groups per CTA stay in shared memory
+constexpr int K5_FS = 17;            // padded fin row stride (conflict-free column writes)
 
 template <int BN>
 struct K5 {
@@ -777,7 +678,7 @@ struct K5 {
   static constexpr int RAW_OFF = W_OFF + K5_DS * W_BYTES;
   static constexpr int SC_OFF = RAW_OFF + K5_RAW * RAW_BYTES;
   static constexpr int SMEM = SC_OFF + K5_MAX_GROUPS * BN * 2 + 1024;  // + alignment slack
-  static_assert(BN * K5_BM * 4 <= K5_XS * XSTAGE, "final tile must fit in the x ring");
+  static_assert(BN * K5_BM * 4 / 16 * K5_FS <= K5_XS * XSTAGE, "final tile must fit in the x ring");
 };
 
 // x [M, K] (fp32 or fp16, rows from x_row) -> hi / lo fp16 [M, K] in the permuted k order
@@ -810,13 +711,53 @@ __global__ void __launch_bounds__(256) q4_xsplit(LinArgs p, __half* xh, __half* 
   griddep_launch_dependents();
 }
 
+// The BN weight rows of a kernel-5 CTA, as NB runs of consecutive rows (one TMA box each): row
+// tiles rt0 .. rt0 + RTS - 1 hold 16 consecutive rows (store / accumulate), gate rows then the
+// matching up rows (SwiGLU), or per head the first and second halves of its elements (RoPE, where
+// slots s and s + 8 pair elements e and e + hd/2).
+__host__ __device__ __forceinline__ int k5_nb(int epi, int RTS, int hd) {
+  if (epi == EPI_SWIGLU) return 2;
+  if (epi == EPI_ROPE_KV) {
+    const int per = hd / 16;
+    return RTS <= per ? 2 : 2 * (RTS / per);
+  }
+  return 1;
+}
+__device__ __forceinline__ int k5_run_row(const LinArgs& p, int rt0, int RTS, int b) {
+  if (p.epi == EPI_SWIGLU) return (b ? p.n_out : 0) + rt0 * 8;
+  if (p.epi == EPI_ROPE_KV) {
+    const int per = p.hd / 16;
+    if (RTS <= per) {
+      const int h = rt0 / per, j0 = rt0 - h * per;
+      return h * p.hd + b * (p.hd / 2) + 8 * j0;
+    }
+    return (rt0 / per + (b >> 1)) * p.hd + (b & 1) * (p.hd / 2);
+  }
+  return rt0 * 16;
+}
+// shared-memory weight row c -> (row tile - rt0, slot)
+__device__ __forceinline__ void k5_col(const LinArgs& p, int RTS, int c, int& rtl, int& s) {
+  if (p.epi == EPI_SWIGLU || p.epi == EPI_ROPE_KV) {
+    const int nb = k5_nb(p.epi, RTS, p.hd), rpb = RTS * 16 / nb;
+    const int b = c / rpb, cc = c - b * rpb;
+    const int per = p.hd / 16;
+    const int hb = (p.epi == EPI_ROPE_KV && RTS > per) ? (b >> 1) * per : 0;
+    rtl = hb + (cc >> 3);
+    s = (cc & 7) + 8 * (b & 1);
+  } else {
+    rtl = c >> 4;
+    s = c & 15;
+  }
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 template <int BN, bool XF32>
 __global__ void __launch_bounds__(K5_THREADS, 1)
-    q4_gemm_tc(const __grid_constant__ CUtensorMap txh, const __grid_constant__ CUtensorMap txl, LinArgs p) {
+    q4_gemm_tc(const __grid_constant__ CUtensorMap txh, const __grid_constant__ CUtensorMap txl,
+               const __grid_constant__ CUtensorMap tw, LinArgs p) {
   using L = K5<BN>;
   constexpr int RTS = BN / 16;  // row tiles per CTA
   extern __shared__ uint8_t smem_raw[];
@@ -862,22 +803,23 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
   const uint32_t tmem = s_tmem;
 
   if (warp == 12) {
-    // weight producer: raw int4 rows (no dependence on the previous kernel: starts before the wait)
-    for (int i = 0; i < NS; ++i) {
-      const int rs = i % K5_RAW, rr = i / K5_RAW;
-      if (rr > 0 && !mbar_wait_bounded(&raw_empty[rs], (rr - 1) & 1, kWaitLimitNs)) {
-        s_fail = 1;
-        break;
-      }
-      if (lane == 0) mbar_arrive_expect_tx(&raw_full[rs], L::RAW_BYTES);
-      __syncwarp();
-      const int j = g0 * SPG + i;
-      uint8_t* dst = smem + L::RAW_OFF + rs * L::RAW_BYTES;
-      for (int r = lane; r < BN; r += 32) {
-        const int row = tile_row(p, rt0 + r / 16, r % 16);
-        bulk_g2s(dst + r * 32, p.qw + (size_t)row * KW + j * 8, 32, &raw_full[rs]);
+    // weight producer: NB TMA boxes of raw int4 rows per 64-k stage (no dependence on the previous
+    // kernel: starts before the wait)
+    if (lane == 0) {
+      const int nb = k5_nb(p.epi, RTS, p.hd), rpb = BN / nb;
+      for (int i = 0; i < NS; ++i) {
+        const int rs = i % K5_RAW, rr = i / K5_RAW;
+        if (rr > 0 && !mbar_wait_bounded(&raw_empty[rs], (rr - 1) & 1, kWaitLimitNs)) {
+          s_fail = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&raw_full[rs], L::RAW_BYTES);
+        const int j = g0 * SPG + i;
+        uint8_t* dst = smem + L::RAW_OFF + rs * L::RAW_BYTES;
+        for (int b = 0; b < nb; ++b) tma_load_2d(dst + b * rpb * 32, &tw, j * 8, k5_run_row(p, rt0, RTS, b), &raw_full[rs]);
       }
     }
+    __syncwarp();
   } else if (warp == 8 + 4 + 2) {
     // x producer (waits for the pre-pass that wrote hi / lo)
     griddep_wait();
@@ -899,9 +841,10 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
   } else if (warp >= 8 && warp < 12) {
     // dequant warps: scales of this CTA's groups once, then exact fp16 (nib - 8) tiles
     const int t = threadIdx.x - 256;
+    const int nb = k5_nb(p.epi, RTS, p.hd), rpb = BN / nb;
     for (int idx = t; idx < NGL * BN; idx += 128) {
       const int gl = idx / BN, c = idx - gl * BN;
-      const int row = tile_row(p, rt0 + c / 16, c % 16);
+      const int row = min(k5_run_row(p, rt0, RTS, c / rpb) + c % rpb, p.N - 1);  // rows past N are zero
       s_sc[idx] = p.scales[(size_t)row * NG + g0 + gl];
     }
     asm volatile("bar.sync 1, 384;" ::: "memory");  // scales visible to the epilogue warps
@@ -1015,8 +958,9 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
     if (warp < 8) {
 #pragma unroll
       for (int c = 0; c < HC; ++c) {
-        const int col = h * HC + c;
-        fin[((col >> 4) * K5_BM + m) * 16 + (col & 15)] = acc[c];
+        int rtl, sl;
+        k5_col(p, RTS, h * HC + c, rtl, sl);
+        fin[(rtl * K5_BM + m) * K5_FS + sl] = acc[c];
       }
     }
     __syncthreads();
@@ -1038,11 +982,35 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
       return;
     }
     __threadfence();
-    for (int i = threadIdx.x; i < K5_BM * BN; i += blockDim.x) {
-      const int mm = i / BN, col = i - mm * BN;
-      float v = 0.0f;
-      for (int s = 0; s < p.nsplit; ++s) v += __ldcg(p.ws + ((size_t)s * tiles + tile) * (K5_BM * BN) + i);
-      fin[((col >> 4) * K5_BM + mm) * 16 + (col & 15)] = v;
+    // four columns per thread and step, the splits' loads issued together, summed in split order
+    const float4* part = reinterpret_cast<const float4*>(p.ws + (size_t)tile * (K5_BM * BN));
+    const size_t zs = tiles * (K5_BM * BN) / 4;
+    for (int i = threadIdx.x; i < K5_BM * BN / 4; i += blockDim.x) {
+      float4 v = __ldcg(part + i);
+      int sp = 1;
+      for (; sp + 4 <= p.nsplit; sp += 4) {
+        const float4 a0 = __ldcg(part + sp * zs + i), a1 = __ldcg(part + (sp + 1) * zs + i);
+        const float4 a2 = __ldcg(part + (sp + 2) * zs + i), a3 = __ldcg(part + (sp + 3) * zs + i);
+        v.x = (((v.x + a0.x) + a1.x) + a2.x) + a3.x;
+        v.y = (((v.y + a0.y) + a1.y) + a2.y) + a3.y;
+        v.z = (((v.z + a0.z) + a1.z) + a2.z) + a3.z;
+        v.w = (((v.w + a0.w) + a1.w) + a2.w) + a3.w;
+      }
+      for (; sp < p.nsplit; ++sp) {
+        const float4 a0 = __ldcg(part + sp * zs + i);
+        v.x += a0.x;
+        v.y += a0.y;
+        v.z += a0.z;
+        v.w += a0.w;
+      }
+      const int mm = (4 * i) / BN, col = 4 * i - mm * BN;
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int rtl, sl;
+        k5_col(p, RTS, col + e, rtl, sl);
+        fin[(rtl * K5_BM + mm) * K5_FS + sl] = vv[e];
+      }
     }
     if (threadIdx.x == 0) p.counters[tile] = 0u;
     __syncthreads();
@@ -1056,7 +1024,7 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
   e.pos_offset = p.pos_offset + m0;
   for (int r = 0; r < RTS; ++r) {
     if (rt0 + r >= p.RT) break;
-    epilogue_tile(e, fin + (size_t)r * K5_BM * 16, rt0 + r, &s_flag);
+    epilogue_tile(e, fin + (size_t)r * K5_BM * K5_FS, rt0 + r, &s_flag, K5_FS);
   }
   griddep_launch_dependents();
 }
@@ -1067,6 +1035,7 @@ struct Plan {
   int kernel = 2;  // 1 = register-staged MMA, 2 = SIMT, 3 = TMA-staged MMA, 4 = streaming, 5 = tcgen05 GEMM
   int W = 4, T = 1, nsplit = 1, kps = 1, MT = 1;
   int bn = 128, tiles_m = 1, tiles_n = 1;  // kernel 5
+  bool ilp = false;                        // kernel 1: two accumulator chains
   int RT = 0;  // row tiles (grid.x)
   int wstride = 0, x_off = 0;
   size_t smem = 0;
@@ -1180,6 +1149,7 @@ static int plan_reg(int M, int K, bool xf32, const q4b_linear_cfg* cfg, Plan& pl
     W = W / 2;  // fewer tiles per CTA: a smaller staged slice of x
   }
   pl.ws_bytes = split_ws(pl, M);
+  pl.ilp = (long long)pl.RT * pl.nsplit <= 3 * 148;  // few CTAs per SM: latency, not occupancy, limits
   return Q4B_OK;
 }
 
@@ -1204,6 +1174,12 @@ static int plan_stream(int M, int K, bool xf32, const q4b_linear_cfg* cfg, Plan&
 // granularity; workspace = counters | x hi | x lo | split partials
 static bool tc_ok(int M, int K, int G, int epi, bool norm) {
   return M > 32 && G % 128 == 0 && !norm && epi != EPI_ARGMAX && K / G <= 64 * 64;
+}
+// RoPE tiles map onto TMA boxes of whole half-heads (row tiles per head and per CTA nest)
+static bool tc_rope_ok(int epi, int hd, int bn) {
+  if (epi != EPI_ROPE_KV) return true;
+  const int per = hd / 16, rts = bn / 16;
+  return hd % 16 == 0 && per > 0 && (per % rts == 0 || rts % per == 0);
 }
 
 static int plan_tc(int M, int K, int G, bool xf32, const q4b_linear_cfg* cfg, Plan& pl) {
@@ -1287,6 +1263,14 @@ static cudaError_t set_smem_attr(Kern kern, unsigned long long& done) {
 
 template <int MT, bool XF32, int T>
 static cudaError_t launch_reg_t(const Plan& pl, const LinArgs& a, cudaStream_t st) {
+  if constexpr (MT == 1 && (T == 3 || T == 8)) {  // the decode shapes: few-CTA launches take the ILP form
+    if (pl.ilp) {
+      static unsigned long long done_ilp = 0;
+      cudaError_t e = set_smem_attr(q4_gemv_reg<MT, XF32, T, true>, done_ilp);
+      if (e != cudaSuccess) return e;
+      return launch_pdl(q4_gemv_reg<MT, XF32, T, true>, dim3(pl.RT, pl.nsplit), dim3(pl.W * 32), pl.smem, st, a);
+    }
+  }
   static unsigned long long done = 0;
   cudaError_t e = set_smem_attr(q4_gemv_reg<MT, XF32, T>, done);
   if (e != cudaSuccess) return e;
@@ -1392,6 +1376,10 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
     if (forced) return set_error(Q4B_EINVAL, "q4_linear: qweight, x and ln_w must be 16-byte aligned");
     simt_plan(op, pl);
   }
+  if (pl.kernel == 5 && !tc_rope_ok(op.epi, op.head_dim, pl.bn)) {
+    if (forced) return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 5 RoPE tiles need head_dim / 16 and the tile to nest");
+    simt_plan(op, pl);
+  }
   if (pl.kernel == 5 && (pl.ws_bytes > op.ws_bytes || !op.ws || !aligned(op.ws, 256))) {
     if (forced) return set_error(Q4B_EINVAL, "q4_linear: workspace of %zu bytes needed, %zu given", pl.ws_bytes,
                                  op.ws_bytes);
@@ -1466,9 +1454,11 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
     auto* xl = reinterpret_cast<__half*>(w + kCounterBytes + xbytes);
     a.counters = reinterpret_cast<unsigned*>(w);
     a.ws = reinterpret_cast<float*>(w + kCounterBytes + (xf32 ? 2 : 1) * xbytes);
-    CUtensorMap th, tl;
+    CUtensorMap th, tl, tw;
     int rc2 = make_tmap_f16(&th, xh, op.k, op.m, op.k, K5_BM);
     if (!rc2) rc2 = make_tmap_f16(&tl, xf32 ? xl : xh, op.k, op.m, op.k, K5_BM);
+    const int nb = k5_nb(op.epi, pl.bn / 16, op.head_dim);
+    if (!rc2) rc2 = make_tmap_i32(&tw, op.qw, op.k / 8, op.n, op.k / 8, 8, pl.bn / nb);
     if (rc2) return rc2;
     const int chunks = op.m * (op.k / 8);
     const int pgrid = std::min((chunks + 255) / 256, 148 * 8);
@@ -1485,7 +1475,7 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
           if (r != cudaSuccess) return r;
           done |= 1ull << (dev & 63);
         }
-        return launch_pdl(kern, grid, dim3(K5_THREADS), pl.smem, st, th, tl, a);
+        return launch_pdl(kern, grid, dim3(K5_THREADS), pl.smem, st, th, tl, tw, a);
       };
       if (pl.bn == 128)
         e = xf32 ? go(q4_gemm_tc<128, true>, d[0]) : go(q4_gemm_tc<128, false>, d[1]);

@@ -136,6 +136,8 @@ int Runner::generate(const int32_t* prompt, int n, int max_new, const int32_t* s
   if (n + max_new > max_ctx || (n + C - 1) / C * C > max_ctx)
     return set_error(Q4B_EINVAL, "runner_generate: prompt %d + new %d exceeds max_ctx %d", n, max_new, max_ctx);
   int rc;
+  if ((rc = model->check_ready())) return rc;
+  model->mk_usable(1, stream);  // persistent decode tables are built here, before any graph capture
   if ((rc = ensure_events(2 * ((n + C - 1) / C + max_new) + 4))) return rc;
   // functions the schedule will use (:181-189)
   std::vector<int> used_prefill, used_decode;

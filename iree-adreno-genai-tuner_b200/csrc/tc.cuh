@@ -105,5 +105,9 @@ __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.a
 // 2-D fp16 tensor map over a row-major [rows, cols] matrix with row pitch `ld` elements; box
 // {64 cols (128 B), box_rows}, 128-byte swizzle, out-of-bounds elements read as zero.
 int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_rows);
+// 2-D int32 tensor map (no swizzle) over [rows, cols] with row pitch `ld` elements, box
+// {box_cols, box_rows}; box_cols * 4 must be a multiple of 16 bytes.
+int make_tmap_i32(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint64_t ld, uint32_t box_cols,
+                  uint32_t box_rows);
 
 }  // namespace q4b

@@ -1,0 +1,162 @@
+"""The persistent decode step (one cooperative launch per token, csrc/decode_mk.cu) against the
+per-projection kernels and the CPU oracle: same greedy tokens, logits within 1e-3 of max|logit|
+(the reference's tolerance, scripts/debug/op_test.py:75), and the same tokens through the runner's
+captured CUDA graphs. Q4B_PERSISTENT=1 selects the persistent step, anything else the per-projection
+path."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import q4_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+# the smallest shape the persistent step takes: head_dim 128, K dims multiples of 1024
+CFG = dict(hidden_size=1024, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2, head_dim=128,
+           intermediate_size=2048, vocab_size=4096, rms_norm_eps=1e-5, rope_theta=500000.0,
+           max_position_embeddings=4096, tie_word_embeddings=True, hidden_act="silu", attention_bias=False,
+           initializer_range=0.2)
+MAX_CTX, PROMPT, STEPS = 1024, 40, 12
+
+
+class _Persistent:
+    def __init__(self, on):
+        self.on = on
+
+    def __enter__(self):
+        self.prev = os.environ.get("Q4B_PERSISTENT")
+        os.environ["Q4B_PERSISTENT"] = "1" if self.on else "0"
+
+    def __exit__(self, *exc):
+        if self.prev is None:
+            os.environ.pop("Q4B_PERSISTENT", None)
+        else:
+            os.environ["Q4B_PERSISTENT"] = self.prev
+
+
+@pytest.fixture(scope="module")
+def model():
+    import q4b
+    sd = q4b.SyntheticStateDict(CFG, seed=5)
+    return q4b.LlamaQ4(None, group=128, max_ctx=MAX_CTX, vocab_chunk=CFG["vocab_size"], sd=sd, cfg=CFG, max_chunk=64), sd
+
+
+def _prompt():
+    return np.random.default_rng(7).integers(0, CFG["vocab_size"], PROMPT).astype(np.int32)
+
+
+def _decode(m, persistent):
+    """Prefill (per-projection path) then STEPS single-token steps; (tokens, logits of each step)."""
+    caches = m.new_caches()
+    p = _prompt()
+    nxt, _ = m.step(torch.from_numpy(p).reshape(1, -1), torch.tensor([0]), torch.tensor([PROMPT - 1]), caches, 64)
+    toks, logits = [int(nxt)], []
+    with _Persistent(persistent):
+        for i in range(STEPS):
+            pos = PROMPT + i
+            L = 64 if pos < 64 else 128 if pos < 128 else 256
+            nxt, lg = m.step(nxt.reshape(1, 1), torch.tensor([pos]), torch.tensor([0]), caches, L)
+            toks.append(int(nxt))
+            logits.append(lg.cpu().numpy()[0])
+    return toks, np.stack(logits)
+
+
+def _kernels_of_one_step(m, persistent):
+    """Names of the CUDA kernels one decode step launches (torch profiler, no ncu)."""
+    from torch.profiler import ProfilerActivity, profile
+    caches = m.new_caches()
+    with _Persistent(persistent):
+        m.step(torch.tensor([[3]], dtype=torch.int32), torch.tensor([5]), torch.tensor([0]), caches, 64)
+        torch.cuda.synchronize()
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            m.step(torch.tensor([[3]], dtype=torch.int32), torch.tensor([6]), torch.tensor([0]), caches, 64)
+            torch.cuda.synchronize()
+    return {e.name for e in prof.events() if e.device_type.name == "CUDA"}
+
+
+def test_persistent_kernel_is_the_one_that_runs(model):
+    m, _ = model
+    on = _kernels_of_one_step(m, True)
+    off = _kernels_of_one_step(m, False)
+    assert any("decode_step_kernel" in k for k in on), on
+    assert not any("q4_gemv" in k for k in on), on
+    assert not any("decode_step_kernel" in k for k in off) and any("q4_gemv" in k for k in off), off
+
+
+def test_persistent_matches_per_projection_path(model):
+    m, _ = model
+    t_on, l_on = _decode(m, True)
+    t_off, l_off = _decode(m, False)
+    assert t_on == t_off
+    assert np.abs(l_on - l_off).max() <= 1e-3 * max(1.0, np.abs(l_off).max())
+    from q4b import _lib
+    assert _lib.lib().q4b_device_status(1) == 0
+
+
+def test_persistent_matches_oracle(model):
+    m, sd = model
+    t_on, l_on = _decode(m, True)
+    ref_sd = {k: sd[k].float().cpu().numpy() for k in _state_keys()}
+    om = O.OracleModel.from_state_dict(CFG, ref_sd, MAX_CTX, group=128)
+    caches = om.new_caches()
+    p = _prompt()
+    nxt, _ = om.step(p, 0, PROMPT - 1, caches, 64)
+    toks, logits = [int(nxt)], []
+    for i in range(STEPS):
+        pos = PROMPT + i
+        L = 64 if pos < 64 else 128 if pos < 128 else 256
+        nxt, lg = om.step(np.array([nxt]), pos, 0, caches, L)
+        toks.append(int(nxt))
+        logits.append(np.asarray(lg).reshape(-1))
+    ref = np.stack(logits)
+    assert t_on == toks
+    assert np.abs(l_on - ref).max() <= 1e-3 * max(1.0, np.abs(ref).max())
+
+
+def test_persistent_through_runner_graphs(model):
+    """Decode steps captured as CUDA graphs (the cooperative launch inside a graph)."""
+    import q4b
+    m, _ = model
+    outs = {}
+    for on in (True, False):
+        with _Persistent(on):
+            r = q4b.Runner(m, 16, [64, 128, 256], "bucketed", graphs=True)
+            outs[on], _ = r.generate(_prompt().tolist(), 24)
+    assert outs[True] == outs[False]
+
+
+def _state_keys():
+    ks = ["model.embed_tokens.weight", "model.norm.weight"]
+    for i in range(CFG["num_hidden_layers"]):
+        p = f"model.layers.{i}."
+        ks += [p + n for n in ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",
+                               "self_attn.o_proj.weight", "mlp.gate_proj.weight", "mlp.up_proj.weight",
+                               "mlp.down_proj.weight", "input_layernorm.weight", "post_attention_layernorm.weight")]
+    return ks
+
+
+def test_persistent_3b_shape_two_layers():
+    """The 3B projection shapes (D 3072, 24/8 heads, I 8192, V 128256) with two layers: tokens and
+    logits of the persistent step equal the per-projection path's."""
+    import q4b
+    cfg = dict(q4b.SYNTHETIC["3b"], num_hidden_layers=2)
+    m = q4b.LlamaQ4(None, group=128, max_ctx=1024, vocab_chunk=cfg["vocab_size"], sd=q4b.SyntheticStateDict(cfg),
+                    cfg=cfg, max_chunk=8)
+    res = {}
+    for on in (True, False):
+        caches = m.new_caches()
+        tok = torch.tensor([[17]], dtype=torch.int32)
+        toks, lgs = [], []
+        with _Persistent(on):
+            for i in range(6):
+                pos = 100 + 150 * i  # one to four attention chunks
+                tok, lg = m.step(tok.reshape(1, 1), torch.tensor([pos]), torch.tensor([0]), caches, 1024)
+                toks.append(int(tok))
+                lgs.append(lg.cpu().numpy()[0])
+        res[on] = (toks, np.stack(lgs))
+    assert res[True][0] == res[False][0]
+    ref = res[False][1]
+    assert np.abs(res[True][1] - ref).max() <= 1e-3 * max(1.0, np.abs(ref).max())
