@@ -48,6 +48,8 @@ constexpr int MK_HD = 128;
 constexpr int MK_KCHUNK = 256;                 // keys per attention item (8 warps x 32)
 constexpr int MK_MAXCH = 64;                   // attention chunks (contexts up to 16384)
 constexpr int MK_ROWS = 4;                     // query rows per KV head (GQA group) at most
+constexpr int MK_TB = 8;                       // tiles of one stage per batched epilogue
+constexpr int MK_MAXD = 4096;                  // hidden size: at most two staged words per thread
 constexpr int MK_PAD = 4;                      // partial row: m, l and two pad floats before o (16-B aligned)
 
 enum { ST_QKV = 0, ST_ATTN = 1, ST_WO = 2, ST_WGU = 3, ST_WDOWN = 4, ST_PER_LAYER = 5 };
@@ -85,14 +87,16 @@ struct MkSmem {
   uint8_t ring[MK_NSLOT][MK_SLOT];
   uint4 xs_hi[MK_XROW];
   uint4 xs_lo[MK_XROW];
-  float red[MK_CW][16];
-  float fin[16];
+  float red[MK_TB][MK_CW][16];  // per-warp partial sums of up to MK_TB tiles of one stage
   float scratch[64];
+  float rope_c[MK_HD], rope_s[MK_HD];  // RoPE rows of this step's position
+  float hown[2][16];                   // this CTA's rows of the residual stream (its o / down tiles)
   float att_q[MK_ROWS][MK_HD];
   float att_o[MK_CW][MK_ROWS][MK_HD];
   float att_m[MK_CW][MK_ROWS], att_l[MK_CW][MK_ROWS];
   float att_cs[MK_CW][MK_ROWS];
-  float mw[32][MK_MAXCH];  // WO merge weights per q head and chunk (32 >= H)
+  float mw[32][MK_MAXCH];  // WO merge: per q head and chunk, the chunk max, then its weight
+  float ml[32][MK_MAXCH];  // and the chunk sum
   float mL[32];
   unsigned long long best[MK_CW];
   uint64_t full[MK_NSLOT], empty[MK_NSLOT];
@@ -129,6 +133,7 @@ __device__ bool stage_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
   if (threadIdx.x == 32) {
     const uint64_t t0 = globaltimer_ns();
     while (ld_acquire(&a.sync[0]) < target) {
+      __nanosleep(32);
       if (ld_acquire(&a.sync[1])) {
         sm.abort_flag = 1;
         break;
@@ -148,7 +153,7 @@ __device__ void stage_arrive(const MkArgs& a) {
   consumer_sync();
   if (threadIdx.x == 32) {
     __threadfence();
-    atomicAdd(&a.sync[0], 1u);
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync) : "memory");
   }
 }
 
@@ -177,6 +182,8 @@ __device__ __forceinline__ int pair_row(const MkArgs& a, int st, int rt, int b) 
 
 __device__ bool produce_stage(const MkArgs& a, MkSmem& sm, const MkProj& pj, int st, unsigned& seq) {
   const ProjGeo gp = geo(a, st);
+  tma_prefetch_map(&pj.w);
+  tma_prefetch_map(&pj.s);
   for (int rt = blockIdx.x; rt < gp.RT; rt += gridDim.x) {
     for (int u = 0; u < gp.NU; ++u, ++seq) {
       const int slot = seq % MK_NSLOT, round = seq / MK_NSLOT;
@@ -233,32 +240,45 @@ __device__ __forceinline__ void norm_src(const MkArgs& a, int w, bool embed, int
 __device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float* lnw, bool embed, int token) {
   const int ct = threadIdx.x - 32;
   const int words = a.D / 8;
+  // one round of loads: this thread's (at most two) words of h and of the norm weight
+  float v[2][8], lw[2][8];
   float ss = 0.0f;
-  for (int w = ct; w < words; w += MK_CW * 32) {
-    float v[8];
-    norm_src(a, w, embed, token, v);
 #pragma unroll
-    for (int b = 0; b < 8; ++b) ss += v[b] * v[b];
-    if (embed && blockIdx.x == 0) {
-      float4* hp = reinterpret_cast<float4*>(a.h + 8 * w);
-      hp[0] = make_float4(v[0], v[1], v[2], v[3]);
-      hp[1] = make_float4(v[4], v[5], v[6], v[7]);
+  for (int i = 0; i < 2; ++i) {
+    const int w = ct + i * (MK_CW * 32);
+    if (w < words) {
+      norm_src(a, w, embed, token, v[i]);
+      const float4 w0 = *reinterpret_cast<const float4*>(lnw + 8 * w);
+      const float4 w1 = *reinterpret_cast<const float4*>(lnw + 8 * w + 4);
+      lw[i][0] = w0.x; lw[i][1] = w0.y; lw[i][2] = w0.z; lw[i][3] = w0.w;
+      lw[i][4] = w1.x; lw[i][5] = w1.y; lw[i][6] = w1.z; lw[i][7] = w1.w;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) ss += v[i][b] * v[i][b];
+      if (embed) {
+        if (blockIdx.x == 0) {
+          float4* hp = reinterpret_cast<float4*>(a.h + 8 * w);
+          hp[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+          hp[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
+        }
+        const int rt = w >> 1;  // 16-row tile of these 8 elements: kept if this CTA owns it
+        if (rt % (int)gridDim.x == (int)blockIdx.x) {
+#pragma unroll
+          for (int b = 0; b < 8; ++b) sm.hown[rt / gridDim.x][(8 * w + b) & 15] = v[i][b];
+        }
+      }
     }
   }
   const float tot = consumer_sum(ss, sm.scratch);
   const float rs = 1.0f / sqrtf(tot / (float)a.D + a.eps);
-  for (int w = ct; w < words; w += MK_CW * 32) {
-    float v[8];
-    if (embed) {
-      norm_src(a, w, true, token, v);
-    } else {  // this thread's own words of h: read back through L2 like the first pass
-      norm_src(a, w, false, token, v);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int w = ct + i * (MK_CW * 32);
+    if (w < words) {
+      float x[8];
+#pragma unroll
+      for (int b = 0; b < 8; ++b) x[b] = v[i][b] * rs * lw[i][b];
+      stage_word(sm, w, x);
     }
-    const float4 w0 = *reinterpret_cast<const float4*>(lnw + 8 * w);
-    const float4 w1 = *reinterpret_cast<const float4*>(lnw + 8 * w + 4);
-    v[0] = v[0] * rs * w0.x; v[1] = v[1] * rs * w0.y; v[2] = v[2] * rs * w0.z; v[3] = v[3] * rs * w0.w;
-    v[4] = v[4] * rs * w1.x; v[5] = v[5] * rs * w1.y; v[6] = v[6] * rs * w1.z; v[7] = v[7] * rs * w1.w;
-    stage_word(sm, w, v);
   }
 }
 
@@ -273,35 +293,59 @@ __device__ void stage_plain(const MkArgs& a, MkSmem& sm, const float* src, int K
   }
 }
 
-// x = attention output o [H * hd]: the chunk partials of every head merged (max, sum, weighted V)
+// x = attention output o [H * hd]: the chunk partials of every head merged (max, sum, weighted V).
+// Two rounds of loads: every (head, chunk) max and sum together, then the weighted partials.
 __device__ void stage_attn_merge(const MkArgs& a, MkSmem& sm, int nch) {
   const int ct = threadIdx.x - 32;
   const int g = a.H / a.Hkv, HD = a.hd;
-  // per (q head, chunk) weight exp(m_c - M) and per head the total L
-  for (int i = ct; i < a.H; i += MK_CW * 32) {
-    const int kvh = i / g, r = i - kvh * g;
-    const float* base = a.part + ((size_t)kvh * MK_MAXCH * MK_ROWS + r) * (HD + MK_PAD);
+  const size_t PS = HD + MK_PAD;
+  for (int i = ct; i < a.H * nch; i += MK_CW * 32) {
+    const int hq = i / nch, c = i - hq * nch;
+    const int kvh = hq / g, r = hq - kvh * g;
+    const float* p = a.part + (((size_t)kvh * MK_MAXCH + c) * MK_ROWS + r) * PS;
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(p));
+    sm.mw[hq][c] = ml.x;
+    sm.ml[hq][c] = ml.y;
+  }
+  consumer_sync();
+  if (ct < a.H) {
     float M = -INFINITY;
-    for (int c = 0; c < nch; ++c) M = fmaxf(M, __ldcg(base + (size_t)c * MK_ROWS * (HD + MK_PAD)));
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, sm.mw[ct][c]);
     float Lsum = 0.0f;
     for (int c = 0; c < nch; ++c) {
-      const float mc = __ldcg(base + (size_t)c * MK_ROWS * (HD + MK_PAD));
+      const float mc = sm.mw[ct][c];
       const float cs = mc == -INFINITY ? 0.0f : expf(mc - M);
-      Lsum += __ldcg(base + (size_t)c * MK_ROWS * (HD + MK_PAD) + 1) * cs;
-      sm.mw[i][c] = cs;
+      Lsum += sm.ml[ct][c] * cs;
+      sm.mw[ct][c] = cs;
     }
-    sm.mL[i] = Lsum;
+    sm.mL[ct] = Lsum;
   }
   consumer_sync();
   for (int w = ct; w < a.H * HD / 8; w += MK_CW * 32) {
     const int hq = (8 * w) / HD, e0 = 8 * w - hq * HD;
     const int kvh = hq / g, r = hq - kvh * g;
-    const float* base = a.part + ((size_t)kvh * MK_MAXCH * MK_ROWS + r) * (HD + MK_PAD) + MK_PAD + e0;
+    const float* base = a.part + ((size_t)kvh * MK_MAXCH * MK_ROWS + r) * PS + MK_PAD + e0;
     float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int c = 0; c < nch; ++c) {
+    int c = 0;
+    for (; c + 4 <= nch; c += 4) {  // four chunks' loads in flight together
+      float4 p[4][2];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4* q = reinterpret_cast<const float4*>(base + (size_t)(c + k) * MK_ROWS * PS);
+        p[k][0] = __ldcg(q);
+        p[k][1] = __ldcg(q + 1);
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float cs = sm.mw[hq][c + k];
+        v[0] += cs * p[k][0].x; v[1] += cs * p[k][0].y; v[2] += cs * p[k][0].z; v[3] += cs * p[k][0].w;
+        v[4] += cs * p[k][1].x; v[5] += cs * p[k][1].y; v[6] += cs * p[k][1].z; v[7] += cs * p[k][1].w;
+      }
+    }
+    for (; c < nch; ++c) {
       const float cs = sm.mw[hq][c];
-      const float4 p0 = __ldcg(reinterpret_cast<const float4*>(base + (size_t)c * MK_ROWS * (HD + MK_PAD)));
-      const float4 p1 = __ldcg(reinterpret_cast<const float4*>(base + (size_t)c * MK_ROWS * (HD + MK_PAD)) + 1);
+      const float4* q = reinterpret_cast<const float4*>(base + (size_t)c * MK_ROWS * PS);
+      const float4 p0 = __ldcg(q), p1 = __ldcg(q + 1);
       v[0] += cs * p0.x; v[1] += cs * p0.y; v[2] += cs * p0.z; v[3] += cs * p0.w;
       v[4] += cs * p1.x; v[5] += cs * p1.y; v[6] += cs * p1.z; v[7] += cs * p1.w;
     }
@@ -314,21 +358,17 @@ __device__ void stage_attn_merge(const MkArgs& a, MkSmem& sm, int nch) {
 
 // ---- consumers: projections ------------------------------------------------------------------
 
-// Epilogue of one 16-row tile, fin[s] = dot product of slot s. Called by consumer threads 0..15.
-__device__ void tile_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, int rt, int pos) {
-  const int s = threadIdx.x - 32;
+// Epilogue of slot pair (s, s + 8) of a 16-row tile: v0 / v1 are their dot products.
+__device__ void pair_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, int rt, int j, int s, float v0,
+                              float v1, int pos) {
   if (st == ST_QKV) {
-    if (s >= 8) return;
-    const int per = a.hd / 16, head = rt / per, j = rt - head * per;
-    const int e1 = j * 8 + s, e2 = a.hd / 2 + j * 8 + s;
-    const float x1 = sm.fin[s], x2 = sm.fin[s + 8];
+    const int per = a.hd / 16, head = rt / per, jj = rt - head * per;
+    const int e1 = jj * 8 + s, e2 = a.hd / 2 + jj * 8 + s;
     const q4b_layer_weights& Lw = a.layers[layer];
     if (head < a.H + a.Hkv) {
       // q * cos + rotate_half(q) * sin, rotate_half(x) = cat(-x[h:], x[:h]) (llama_q4.py:195-221)
-      const float* cs = a.rope_cos + (size_t)pos * a.hd;
-      const float* sn = a.rope_sin + (size_t)pos * a.hd;
-      const float o1 = __fadd_rn(__fmul_rn(x1, cs[e1]), __fmul_rn(-x2, sn[e1]));
-      const float o2 = __fadd_rn(__fmul_rn(x2, cs[e2]), __fmul_rn(x1, sn[e2]));
+      const float o1 = __fadd_rn(__fmul_rn(v0, sm.rope_c[e1]), __fmul_rn(-v1, sm.rope_s[e1]));
+      const float o2 = __fadd_rn(__fmul_rn(v1, sm.rope_c[e2]), __fmul_rn(v0, sm.rope_s[e2]));
       if (head < a.H) {
         a.q[head * a.hd + e1] = o1;
         a.q[head * a.hd + e2] = o2;
@@ -339,55 +379,65 @@ __device__ void tile_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, in
       }
     } else {
       __half* vc = reinterpret_cast<__half*>(Lw.v_cache) + ((size_t)pos * a.Hkv + (head - a.H - a.Hkv)) * a.hd;
-      vc[e1] = __float2half_rn(x1);
-      vc[e2] = __float2half_rn(x2);
+      vc[e1] = __float2half_rn(v0);
+      vc[e2] = __float2half_rn(v1);
     }
   } else if (st == ST_WGU) {
-    if (s < 8) a.a[rt * 8 + s] = silu(sm.fin[s]) * sm.fin[s + 8];
-  } else {  // WO / WDOWN: residual add (one CTA owns each row)
-    if (s < 16) {
-      const int row = rt * 16 + s;
-      a.h[row] = __ldcg(a.h + row) + sm.fin[s];
-    }
+    a.a[rt * 8 + s] = silu(v0) * v1;
+  } else {  // WO / WDOWN: residual add on this CTA's own rows
+    const float h0 = sm.hown[j][s] + v0, h1 = sm.hown[j][s + 8] + v1;
+    sm.hown[j][s] = h0;
+    sm.hown[j][s + 8] = h1;
+    a.h[rt * 16 + s] = h0;
+    a.h[rt * 16 + s + 8] = h1;
   }
 }
 
-// K split across the consumer warps: warp w takes the 128-k group w of every 1024-k unit.
+// K split across the consumer warps: warp w takes the 128-k group w of every 1024-k unit. The
+// per-warp sums of up to MK_TB tiles are reduced and finished together (one barrier pair per batch).
 __device__ bool consume_stage(const MkArgs& a, MkSmem& sm, int st, int layer, unsigned& seq, int pos) {
   const ProjGeo gp = geo(a, st);
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
   const int g = lane >> 2, t = lane & 3;
   const int mrow[1] = {0};
-  for (int rt = blockIdx.x; rt < gp.RT; rt += gridDim.x) {
-    float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
-    for (int u = 0; u < gp.NU; ++u, ++seq) {
-      const int slot = seq % MK_NSLOT;
-      if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, kWaitLimitNs)) {
-        sm.abort_flag = 1;
-        return false;
+  const int ntile = gp.RT > (int)blockIdx.x ? (gp.RT - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  for (int b0 = 0; b0 < ntile; b0 += MK_TB) {
+    const int nb = min(MK_TB, ntile - b0);
+    for (int j = 0; j < nb; ++j) {
+      float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+      for (int u = 0; u < gp.NU; ++u, ++seq) {
+        const int slot = seq % MK_NSLOT;
+        if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, kWaitLimitNs)) {
+          sm.abort_flag = 1;
+          return false;
+        }
+        const uint8_t* sl = sm.ring[slot];
+        const uint4 wa = *reinterpret_cast<const uint4*>(sl + g * 512 + w * 64 + t * 16);
+        const uint4 wb = *reinterpret_cast<const uint4*>(sl + (g + 8) * 512 + w * 64 + t * 16);
+        const __half* sc = reinterpret_cast<const __half*>(sl + MK_WBYTES);
+        const float sa = __half2float(sc[g * 8 + w]), sb = __half2float(sc[(g + 8) * 8 + w]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cnt(&sm.empty[slot], 1);
+        mma_tile<1, true, true>(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, mrow, u * 128 + w * 16 + 4 * t, acc);
       }
-      const uint8_t* sl = sm.ring[slot];
-      const uint4 wa = *reinterpret_cast<const uint4*>(sl + g * 512 + w * 64 + t * 16);
-      const uint4 wb = *reinterpret_cast<const uint4*>(sl + (g + 8) * 512 + w * 64 + t * 16);
-      const __half* sc = reinterpret_cast<const __half*>(sl + MK_WBYTES);
-      const float sa = __half2float(sc[g * 8 + w]), sb = __half2float(sc[(g + 8) * 8 + w]);
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cnt(&sm.empty[slot], 1);
-      mma_tile<1, true, true>(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, mrow, u * 128 + w * 16 + 4 * t, acc);
-    }
-    if (t == 0) {
-      sm.red[w][g] = acc[0][0];
-      sm.red[w][g + 8] = acc[0][2];
+      if (t == 0) {
+        sm.red[j][w][g] = acc[0][0];
+        sm.red[j][w][g + 8] = acc[0][2];
+      }
     }
     consumer_sync();
-    if (ct < 16) {
-      float v = 0.0f;
+    for (int i = ct; i < nb * 8; i += MK_CW * 32) {
+      const int j = i >> 3, sl = i & 7;
+      float v0 = 0.0f, v1 = 0.0f;
 #pragma unroll
-      for (int i = 0; i < MK_CW; ++i) v += sm.red[i][ct];
-      sm.fin[ct] = v;
+      for (int k = 0; k < MK_CW; ++k) {
+        v0 += sm.red[j][k][sl];
+        v1 += sm.red[j][k][sl + 8];
+      }
+      const int jt = b0 + j;
+      pair_epilogue(a, sm, st, layer, blockIdx.x + jt * gridDim.x, jt, sl, v0, v1, pos);
     }
     consumer_sync();
-    if (ct < 16) tile_epilogue(a, sm, st, layer, rt, pos);
   }
   return true;
 }
@@ -488,9 +538,17 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
   const int jbase = k0 + 32 * w, j = jbase + lane;
   for (int i = ct; i < g * HD; i += MK_CW * 32) sm.att_q[i / HD][i % HD] = __ldcg(a.q + (size_t)kvh * g * HD + i);
   consumer_sync();
-  // scores of this lane's key for every query row, the K row read in two halves
+  // one round of loads for the warp's 32 keys: this lane's 4 elements of every V row (8 bytes per
+  // key) and the first half of this lane's K row; the second K half follows
+  const int jc = min(j, k1 - 1);
+  uint2 vv[32];
+#pragma unroll
+  for (int jj = 0; jj < 32; ++jj) {
+    const int key = min(jbase + jj, k1 - 1);
+    vv[jj] = __ldcg(reinterpret_cast<const uint2*>(vc + (size_t)key * row_stride + (size_t)kvh * HD + lane * EPL));
+  }
   float dr[MK_ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
-  const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t)min(j, k1 - 1) * row_stride + (size_t)kvh * HD);
+  const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t)jc * row_stride + (size_t)kvh * HD);
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     uint4 kr[KU4 / 2];
@@ -521,28 +579,24 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
     float o[EPL] = {0.0f, 0.0f, 0.0f, 0.0f};
     float lw = 0.0f;
     if (m != -INFINITY) {
-      const float p = expf(sc - m);
+      const float p = expf(sc - m);  // 0 for keys past the context: their V slices are never used
       lw = warp_sum(p);
+#pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
         const float pj = __shfl_sync(0xffffffffu, p, jj);
-        if (jbase + jj < k1) {
-          const uint2 u2 = __ldcg(reinterpret_cast<const uint2*>(vc + (size_t)(jbase + jj) * row_stride +
-                                                                  (size_t)kvh * HD + lane * EPL));
-          const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&u2.x));
-          const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&u2.y));
-          o[0] = fmaf(pj, v0.x, o[0]);
-          o[1] = fmaf(pj, v0.y, o[1]);
-          o[2] = fmaf(pj, v1.x, o[2]);
-          o[3] = fmaf(pj, v1.y, o[3]);
-        }
+        const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj].x));
+        const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj].y));
+        o[0] = fmaf(pj, v0.x, o[0]);
+        o[1] = fmaf(pj, v0.y, o[1]);
+        o[2] = fmaf(pj, v1.x, o[2]);
+        o[3] = fmaf(pj, v1.y, o[3]);
       }
     }
     if (lane == 0) {
       sm.att_m[w][r] = m;
       sm.att_l[w][r] = lw;
     }
-#pragma unroll
-    for (int e = 0; e < EPL; ++e) sm.att_o[w][r][lane * EPL + e] = o[e];
+    *reinterpret_cast<float4*>(&sm.att_o[w][r][lane * EPL]) = make_float4(o[0], o[1], o[2], o[3]);
   }
   consumer_sync();
   // merge the warps into this chunk's partial
@@ -608,6 +662,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     return;
   }
 
+  {
+    const int ct = threadIdx.x - 32;
+    for (int e = ct; e < a.hd; e += MK_CW * 32) {
+      sm.rope_c[e] = a.rope_cos[(size_t)pos * a.hd + e];
+      sm.rope_s[e] = a.rope_sin[(size_t)pos * a.hd + e];
+    }
+    consumer_sync();
+  }
   unsigned seq = 0;
   unsigned stage = 0;
   const unsigned n = gridDim.x;
@@ -672,6 +734,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
 
 static bool mk_shapes_ok(const Model& m) {
   return m.cfg.tp_size == 1 && m.hd == MK_HD && m.H % m.Hkv == 0 && m.H / m.Hkv <= MK_ROWS && m.H <= 32 &&
+         m.D <= MK_MAXD &&
          m.D % MK_UK == 0 && (m.H * m.hd) % MK_UK == 0 && m.I % MK_UK == 0 && m.I <= MK_MAXK && m.D <= MK_MAXK &&
          m.H * m.hd <= MK_MAXK && m.V % 16 == 0 && m.cfg.max_ctx <= MK_MAXCH * MK_KCHUNK;
 }
@@ -725,6 +788,7 @@ int Model::mk_prepare() {
   if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, decode_step_kernel, MK_THREADS, smem);
   if (e != cudaSuccess || per < 1)
     return set_error(Q4B_EUNSUPPORTED, "persistent decode: kernel does not fit an SM (%s)", cudaGetErrorString(e));
+  if (D / 16 > 2 * sms) return set_error(Q4B_EUNSUPPORTED, "persistent decode: more than two o / down tiles per SM");
   mk_ctas = sms;
   mk_ready = true;
   return Q4B_OK;
