@@ -49,6 +49,7 @@ constexpr int MK_KCHUNK = 256;                 // keys per attention item (8 war
 constexpr int MK_MAXCH = 64;                   // attention chunks (contexts up to 16384)
 constexpr int MK_ROWS = 4;                     // query rows per KV head (GQA group) at most
 constexpr int MK_TB = 8;                       // tiles of one stage per batched epilogue
+constexpr int MK_MAXKS = 3;                    // K splits of the o / down projections
 constexpr int MK_MAXD = 4096;                  // hidden size: at most two staged words per thread
 constexpr int MK_PAD = 4;                      // partial row: m, l and two pad floats before o (16-B aligned)
 
@@ -76,7 +77,8 @@ struct MkArgs {
   DecodeState* state;
   int32_t* token_log;
   float* logits;
-  float* h;      // [D] residual stream
+  float* hb;     // [2][D] residual stream, ping-pong: QKV staging writes hb[1], WGU staging hb[0]
+  float* psum;   // [MK_MAXKS][D] K-split partial sums of the o / down projections
   float* q;      // [H * hd]
   float* a;      // [I]
   float* part;   // attention partials [Hkv][MK_MAXCH][MK_ROWS][hd + 4]: m, l, -, -, o[hd]
@@ -90,7 +92,6 @@ struct MkSmem {
   float red[MK_TB][MK_CW][16];  // per-warp partial sums of up to MK_TB tiles of one stage
   float scratch[64];
   float rope_c[MK_HD], rope_s[MK_HD];  // RoPE rows of this step's position
-  float hown[2][16];                   // this CTA's rows of the residual stream (its o / down tiles)
   float att_q[MK_ROWS][MK_HD];
   float att_o[MK_CW][MK_ROWS][MK_HD];
   float att_m[MK_CW][MK_ROWS], att_l[MK_CW][MK_ROWS];
@@ -100,7 +101,6 @@ struct MkSmem {
   float mL[32];
   unsigned long long best[MK_CW];
   uint64_t full[MK_NSLOT], empty[MK_NSLOT];
-  unsigned done[MK_NSLOT];  // lm_head: rounds of each ring slot consumed so far
   int abort_flag;
   int last;
 };
@@ -161,14 +161,23 @@ __device__ void stage_arrive(const MkArgs& a) {
 struct ProjGeo {
   int K, RT, NU;  // reduction dim, row tiles, 1024-k units per tile
   bool paired;    // two runs of 8 rows per tile (SwiGLU gate/up, RoPE element halves)
+  int KS;         // K splits: work items are (row tile, unit range); partial sums go to psum
 };
+__host__ __device__ __forceinline__ int k_splits(int nu) {
+  for (int k = MK_MAXKS; k > 1; --k)
+    if (nu % k == 0) return k;
+  return 1;
+}
+// The o / down projections have D / 16 row tiles (192 for the 3B shape), too few to balance over
+// the SMs (one or two per CTA); splitting their K gives several smaller items per CTA. Their
+// partial sums are added to the residual stream in fixed order by the next stage's x staging.
 __device__ __forceinline__ ProjGeo geo(const MkArgs& a, int st) {
   switch (st) {
-    case ST_QKV: return {a.D, (a.H + 2 * a.Hkv) * a.hd / 16, a.D / MK_UK, true};
-    case ST_WO: return {a.H * a.hd, a.D / 16, a.H * a.hd / MK_UK, false};
-    case ST_WGU: return {a.D, a.I / 8, a.D / MK_UK, true};
-    case ST_WDOWN: return {a.I, a.D / 16, a.I / MK_UK, false};
-    default: return {a.D, a.V / 16, a.D / MK_UK, false};  // lm_head
+    case ST_QKV: return {a.D, (a.H + 2 * a.Hkv) * a.hd / 16, a.D / MK_UK, true, 1};
+    case ST_WO: return {a.H * a.hd, a.D / 16, a.H * a.hd / MK_UK, false, k_splits(a.H * a.hd / MK_UK)};
+    case ST_WGU: return {a.D, a.I / 8, a.D / MK_UK, true, 1};
+    case ST_WDOWN: return {a.I, a.D / 16, a.I / MK_UK, false, k_splits(a.I / MK_UK)};
+    default: return {a.D, a.V / 16, a.D / MK_UK, false, 1};  // lm_head
   }
 }
 // first weight row of run b (0 / 1) of a paired tile
@@ -184,8 +193,10 @@ __device__ bool produce_stage(const MkArgs& a, MkSmem& sm, const MkProj& pj, int
   const ProjGeo gp = geo(a, st);
   tma_prefetch_map(&pj.w);
   tma_prefetch_map(&pj.s);
-  for (int rt = blockIdx.x; rt < gp.RT; rt += gridDim.x) {
-    for (int u = 0; u < gp.NU; ++u, ++seq) {
+  const int upi = gp.NU / gp.KS;  // units per item
+  for (int it = blockIdx.x; it < gp.RT * gp.KS; it += gridDim.x) {
+    const int rt = it / gp.KS, ks = it - rt * gp.KS;
+    for (int u = ks * upi; u < (ks + 1) * upi; ++u, ++seq) {
       const int slot = seq % MK_NSLOT, round = seq / MK_NSLOT;
       if (round > 0 && !mbar_wait_bounded(&sm.empty[slot], (round - 1) & 1, kWaitLimitNs)) return false;
       if (sm.abort_flag) return false;
@@ -219,9 +230,11 @@ __device__ __forceinline__ void stage_word(MkSmem& sm, int w, const float (&v)[8
   sm.xs_lo[xswz(w)] = lo;
 }
 
-// x = rmsnorm(h) * w (rms_norm, llama_q4.py:141-142); the first layer's h is the embedding row of
-// the token (QEmbedding.lookup, :106-119), written to the residual stream by CTA 0.
-__device__ __forceinline__ void norm_src(const MkArgs& a, int w, bool embed, int token, float (&v)[8]) {
+// The residual stream before a norm: the first layer's h is the embedding row of the token
+// (QEmbedding.lookup, llama_q4.py:106-119); later it is h + the K-split partial sums of the o / down
+// projection (added in split order).
+__device__ __forceinline__ void norm_src(const MkArgs& a, int w, bool embed, int token, const float* hsrc,
+                                         int nparts, float (&v)[8]) {
   if (embed) {
     const int words = a.D / 8;
     const bool ok = token >= 0 && token < a.V;
@@ -230,41 +243,55 @@ __device__ __forceinline__ void norm_src(const MkArgs& a, int w, bool embed, int
 #pragma unroll
     for (int b = 0; b < 8; ++b) v[b] = (float)(((word >> (4 * b)) & 15) - 8) * s;
   } else {
-    const float4 p0 = __ldcg(reinterpret_cast<const float4*>(a.h + 8 * w));
-    const float4 p1 = __ldcg(reinterpret_cast<const float4*>(a.h + 8 * w) + 1);
+    const float4 p0 = __ldcg(reinterpret_cast<const float4*>(hsrc + 8 * w));
+    const float4 p1 = __ldcg(reinterpret_cast<const float4*>(hsrc + 8 * w) + 1);
+    float4 q0[MK_MAXKS], q1[MK_MAXKS];
+#pragma unroll
+    for (int k = 0; k < MK_MAXKS; ++k) {
+      if (k < nparts) {
+        q0[k] = __ldcg(reinterpret_cast<const float4*>(a.psum + (size_t)k * a.D + 8 * w));
+        q1[k] = __ldcg(reinterpret_cast<const float4*>(a.psum + (size_t)k * a.D + 8 * w) + 1);
+      }
+    }
     v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
     v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+    float d[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int k = 0; k < MK_MAXKS; ++k) {
+      if (k < nparts) {
+        d[0] += q0[k].x; d[1] += q0[k].y; d[2] += q0[k].z; d[3] += q0[k].w;
+        d[4] += q1[k].x; d[5] += q1[k].y; d[6] += q1[k].z; d[7] += q1[k].w;
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < 8; ++b) v[b] += d[b];
   }
 }
 
-__device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float* lnw, bool embed, int token) {
+// x = rmsnorm(h) * w (rms_norm, llama_q4.py:141-142). With hdst the updated residual stream is also
+// written (each word by one CTA) to the other ping-pong buffer.
+__device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float* lnw, bool embed, int token, const float* hsrc,
+                           int nparts, float* hdst) {
   const int ct = threadIdx.x - 32;
   const int words = a.D / 8;
-  // one round of loads: this thread's (at most two) words of h and of the norm weight
+  // one round of loads: this thread's (at most two) words of h (+ partials) and of the norm weight
   float v[2][8], lw[2][8];
   float ss = 0.0f;
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int w = ct + i * (MK_CW * 32);
     if (w < words) {
-      norm_src(a, w, embed, token, v[i]);
+      norm_src(a, w, embed, token, hsrc, nparts, v[i]);
       const float4 w0 = *reinterpret_cast<const float4*>(lnw + 8 * w);
       const float4 w1 = *reinterpret_cast<const float4*>(lnw + 8 * w + 4);
       lw[i][0] = w0.x; lw[i][1] = w0.y; lw[i][2] = w0.z; lw[i][3] = w0.w;
       lw[i][4] = w1.x; lw[i][5] = w1.y; lw[i][6] = w1.z; lw[i][7] = w1.w;
 #pragma unroll
       for (int b = 0; b < 8; ++b) ss += v[i][b] * v[i][b];
-      if (embed) {
-        if (blockIdx.x == 0) {
-          float4* hp = reinterpret_cast<float4*>(a.h + 8 * w);
-          hp[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
-          hp[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
-        }
-        const int rt = w >> 1;  // 16-row tile of these 8 elements: kept if this CTA owns it
-        if (rt % (int)gridDim.x == (int)blockIdx.x) {
-#pragma unroll
-          for (int b = 0; b < 8; ++b) sm.hown[rt / gridDim.x][(8 * w + b) & 15] = v[i][b];
-        }
+      if (hdst && w % (int)gridDim.x == (int)blockIdx.x) {
+        float4* hp = reinterpret_cast<float4*>(hdst + 8 * w);
+        hp[0] = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+        hp[1] = make_float4(v[i][4], v[i][5], v[i][6], v[i][7]);
       }
     }
   }
@@ -359,7 +386,7 @@ __device__ void stage_attn_merge(const MkArgs& a, MkSmem& sm, int nch) {
 // ---- consumers: projections ------------------------------------------------------------------
 
 // Epilogue of slot pair (s, s + 8) of a 16-row tile: v0 / v1 are their dot products.
-__device__ void pair_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, int rt, int j, int s, float v0,
+__device__ void pair_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, int rt, int ks, int s, float v0,
                               float v1, int pos) {
   if (st == ST_QKV) {
     const int per = a.hd / 16, head = rt / per, jj = rt - head * per;
@@ -384,28 +411,31 @@ __device__ void pair_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, in
     }
   } else if (st == ST_WGU) {
     a.a[rt * 8 + s] = silu(v0) * v1;
-  } else {  // WO / WDOWN: residual add on this CTA's own rows
-    const float h0 = sm.hown[j][s] + v0, h1 = sm.hown[j][s + 8] + v1;
-    sm.hown[j][s] = h0;
-    sm.hown[j][s + 8] = h1;
-    a.h[rt * 16 + s] = h0;
-    a.h[rt * 16 + s + 8] = h1;
+  } else {  // WO / WDOWN: this K split's partial sums (added to h by the next norm's staging)
+    float* p = a.psum + (size_t)ks * a.D + rt * 16;
+    p[s] = v0;
+    p[s + 8] = v1;
   }
 }
 
-// K split across the consumer warps: warp w takes the 128-k group w of every 1024-k unit. The
-// per-warp sums of up to MK_TB tiles are reduced and finished together (one barrier pair per batch).
+// K split across the consumer warps: warp w takes the 128-k group w of every 1024-k unit of an item
+// (a row tile and a range of its units). The per-warp sums of up to MK_TB items are reduced and
+// finished together (one barrier pair per batch).
 __device__ bool consume_stage(const MkArgs& a, MkSmem& sm, int st, int layer, unsigned& seq, int pos) {
   const ProjGeo gp = geo(a, st);
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
   const int g = lane >> 2, t = lane & 3;
   const int mrow[1] = {0};
-  const int ntile = gp.RT > (int)blockIdx.x ? (gp.RT - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  for (int b0 = 0; b0 < ntile; b0 += MK_TB) {
-    const int nb = min(MK_TB, ntile - b0);
+  const int upi = gp.NU / gp.KS;
+  const int nitems = gp.RT * gp.KS;
+  const int nmine = nitems > (int)blockIdx.x ? (nitems - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  for (int b0 = 0; b0 < nmine; b0 += MK_TB) {
+    const int nb = min(MK_TB, nmine - b0);
     for (int j = 0; j < nb; ++j) {
+      const int it = blockIdx.x + (b0 + j) * gridDim.x;
+      const int ks = it % gp.KS;
       float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
-      for (int u = 0; u < gp.NU; ++u, ++seq) {
+      for (int u = ks * upi; u < (ks + 1) * upi; ++u, ++seq) {
         const int slot = seq % MK_NSLOT;
         if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, kWaitLimitNs)) {
           sm.abort_flag = 1;
@@ -434,75 +464,59 @@ __device__ bool consume_stage(const MkArgs& a, MkSmem& sm, int st, int layer, un
         v0 += sm.red[j][k][sl];
         v1 += sm.red[j][k][sl + 8];
       }
-      const int jt = b0 + j;
-      pair_epilogue(a, sm, st, layer, blockIdx.x + jt * gridDim.x, jt, sl, v0, v1, pos);
+      const int it = blockIdx.x + (b0 + j) * gridDim.x;
+      pair_epilogue(a, sm, st, layer, it / gp.KS, it % gp.KS, sl, v0, v1, pos);
     }
     consumer_sync();
   }
   return true;
 }
 
-// lm_head: whole row tiles per warp (tiles of this CTA round-robin over the warps), greedy argmax.
+// lm_head: the same split of K over the warps as consume_stage, each batch of tiles finished with
+// logits (optional) and greedy argmax keys; the CTA's best key goes to the step state, the last CTA
+// publishes the token (first maximum on ties, like torch.argmax).
 __device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq) {
   const ProjGeo gp = geo(a, ST_PER_LAYER);
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
   const int g = lane >> 2, t = lane & 3;
   const int mrow[1] = {0};
   unsigned long long best = 0ull;
-  // Warps take whole tiles here, so a slot's rounds are consumed by different warps, out of step
-  // with each other. A warp must not wait on a slot's full barrier before the slot's previous
-  // round has been consumed: the parity test would then match the earlier phase. done[slot] counts
-  // consumed rounds (all earlier stages consumed their slots in order: rounds so far = uses so far).
-  if (ct < MK_NSLOT) sm.done[ct] = seq > (unsigned)ct ? (seq - ct + MK_NSLOT - 1) / MK_NSLOT : 0u;
-  consumer_sync();
-  volatile unsigned* done = sm.done;
-  int i = 0;
-  for (int rt = blockIdx.x; rt < gp.RT; rt += gridDim.x, ++i, seq += gp.NU) {
-    if ((i % MK_CW) != w) continue;
-    float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
-    for (int u = 0; u < gp.NU; ++u) {
-      const unsigned sq = seq + u;
-      const int slot = sq % MK_NSLOT;
-      const unsigned round = sq / MK_NSLOT;
-      bool ok = true;
-      if (lane == 0) {
-        const uint64_t t0 = globaltimer_ns();
-        while (done[slot] < round) {
-          if (sm.abort_flag || globaltimer_ns() - t0 > kWaitLimitNs) {
-            ok = false;
-            break;
-          }
+  const int ntile = gp.RT > (int)blockIdx.x ? (gp.RT - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  for (int b0 = 0; b0 < ntile; b0 += MK_TB) {
+    const int nb = min(MK_TB, ntile - b0);
+    for (int j = 0; j < nb; ++j) {
+      float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+      for (int u = 0; u < gp.NU; ++u, ++seq) {
+        const int slot = seq % MK_NSLOT;
+        if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, kWaitLimitNs)) {
+          sm.abort_flag = 1;
+          return false;
         }
+        const uint8_t* sl = sm.ring[slot];
+        const uint4 wa = *reinterpret_cast<const uint4*>(sl + g * 512 + w * 64 + t * 16);
+        const uint4 wb = *reinterpret_cast<const uint4*>(sl + (g + 8) * 512 + w * 64 + t * 16);
+        const __half* sc = reinterpret_cast<const __half*>(sl + MK_WBYTES);
+        const float sa = __half2float(sc[g * 8 + w]), sb = __half2float(sc[(g + 8) * 8 + w]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cnt(&sm.empty[slot], 1);
+        mma_tile<1, true, true>(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, mrow, u * 128 + w * 16 + 4 * t, acc);
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok || !mbar_wait_bounded(&sm.full[slot], round & 1, kWaitLimitNs)) {
-        sm.abort_flag = 1;
-        return false;
-      }
-      const uint8_t* sl = sm.ring[slot];
-      const __half* sc = reinterpret_cast<const __half*>(sl + MK_WBYTES);
-#pragma unroll 2
-      for (int j = 0; j < MK_CW; ++j) {
-        const uint4 wa = *reinterpret_cast<const uint4*>(sl + g * 512 + j * 64 + t * 16);
-        const uint4 wb = *reinterpret_cast<const uint4*>(sl + (g + 8) * 512 + j * 64 + t * 16);
-        const float sa = __half2float(sc[g * 8 + j]), sb = __half2float(sc[(g + 8) * 8 + j]);
-        mma_tile<1, true, true>(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, mrow, u * 128 + j * 16 + 4 * t, acc);
-      }
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive_cnt(&sm.empty[slot], MK_CW);
-        __threadfence_block();
-        done[slot] = round + 1;
+      if (t == 0) {
+        sm.red[j][w][g] = acc[0][0];
+        sm.red[j][w][g + 8] = acc[0][2];
       }
     }
-    if (t == 0) {
-      const int r0 = rt * 16 + g, r1 = r0 + 8;
-      if (a.logits) {
-        a.logits[r0] = acc[0][0];
-        a.logits[r1] = acc[0][2];
-      }
-      best = max(best, max(argmax_key(acc[0][0], (unsigned)r0), argmax_key(acc[0][2], (unsigned)r1)));
+    consumer_sync();
+    for (int i = ct; i < nb * 16; i += MK_CW * 32) {
+      const int j = i >> 4, sl = i & 15;
+      float v = 0.0f;
+#pragma unroll
+      for (int k = 0; k < MK_CW; ++k) v += sm.red[j][k][sl];
+      const int row = (blockIdx.x + (b0 + j) * gridDim.x) * 16 + sl;
+      if (a.logits) a.logits[row] = v;
+      best = max(best, argmax_key(v, (unsigned)row));
     }
+    consumer_sync();
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
@@ -524,9 +538,11 @@ __device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq) {
   return true;
 }
 
-// Attention item (KV head kvh, keys [256 ch, 256 ch + 256) of ctx): per query row of the group, the
-// chunk's (max, sum, weighted V), the same online-softmax pieces as attn_decode_kernel.
-__device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int ch, int ctx) {
+// Attention item (query row r of KV head kvh's group, keys [256 ch, 256 ch + 256) of ctx): the
+// chunk's (max, sum, weighted V) for that row -- the online-softmax pieces of attn_decode_kernel.
+// One row per item spreads a layer's attention over three times as many CTAs as one item per KV
+// head (the rows of a group share K and V, which L2 serves again).
+__device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int ch, int r, int ctx) {
   constexpr int HD = MK_HD, EPL = HD / 32, KU4 = HD / 8;
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
   const int g = a.H / a.Hkv;
@@ -536,7 +552,7 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
   const size_t row_stride = (size_t)a.Hkv * HD;
   const int k0 = ch * MK_KCHUNK, k1 = min(k0 + MK_KCHUNK, ctx);
   const int jbase = k0 + 32 * w, j = jbase + lane;
-  for (int i = ct; i < g * HD; i += MK_CW * 32) sm.att_q[i / HD][i % HD] = __ldcg(a.q + (size_t)kvh * g * HD + i);
+  for (int i = ct; i < HD; i += MK_CW * 32) sm.att_q[0][i] = __ldcg(a.q + ((size_t)kvh * g + r) * HD + i);
   consumer_sync();
   // one round of loads for the warp's 32 keys: this lane's 4 elements of every V row (8 bytes per
   // key) and the first half of this lane's K row; the second K half follows
@@ -547,7 +563,7 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
     const int key = min(jbase + jj, k1 - 1);
     vv[jj] = __ldcg(reinterpret_cast<const uint2*>(vc + (size_t)key * row_stride + (size_t)kvh * HD + lane * EPL));
   }
-  float dr[MK_ROWS] = {0.0f, 0.0f, 0.0f, 0.0f};
+  float d = 0.0f;
   const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t)jc * row_stride + (size_t)kvh * HD);
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
@@ -561,65 +577,54 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
       for (int tt = 0; tt < 4; ++tt) {
         const float2 f = __half22float2(h2[tt]);
         const int e = 8 * (half * (KU4 / 2) + u) + 2 * tt;
-#pragma unroll
-        for (int r = 0; r < MK_ROWS; ++r) {
-          if (r < g) {
-            dr[r] = fmaf(sm.att_q[r][e], f.x, dr[r]);
-            dr[r] = fmaf(sm.att_q[r][e + 1], f.y, dr[r]);
-          }
-        }
+        d = fmaf(sm.att_q[0][e], f.x, d);
+        d = fmaf(sm.att_q[0][e + 1], f.y, d);
       }
     }
   }
+  const float sc = j < k1 ? d * a.scale : -INFINITY;
+  const float m = warp_max(sc);
+  float o[EPL] = {0.0f, 0.0f, 0.0f, 0.0f};
+  float lw = 0.0f;
+  if (m != -INFINITY) {
+    const float p = expf(sc - m);  // 0 for keys past the context: their V slices are never used
+    lw = warp_sum(p);
 #pragma unroll
-  for (int r = 0; r < MK_ROWS; ++r) {
-    if (r >= g) break;
-    const float sc = j < k1 ? dr[r] * a.scale : -INFINITY;
-    const float m = warp_max(sc);
-    float o[EPL] = {0.0f, 0.0f, 0.0f, 0.0f};
-    float lw = 0.0f;
-    if (m != -INFINITY) {
-      const float p = expf(sc - m);  // 0 for keys past the context: their V slices are never used
-      lw = warp_sum(p);
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const float pj = __shfl_sync(0xffffffffu, p, jj);
-        const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj].x));
-        const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj].y));
-        o[0] = fmaf(pj, v0.x, o[0]);
-        o[1] = fmaf(pj, v0.y, o[1]);
-        o[2] = fmaf(pj, v1.x, o[2]);
-        o[3] = fmaf(pj, v1.y, o[3]);
-      }
+    for (int jj = 0; jj < 32; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, p, jj);
+      const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj].x));
+      const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj].y));
+      o[0] = fmaf(pj, v0.x, o[0]);
+      o[1] = fmaf(pj, v0.y, o[1]);
+      o[2] = fmaf(pj, v1.x, o[2]);
+      o[3] = fmaf(pj, v1.y, o[3]);
     }
-    if (lane == 0) {
-      sm.att_m[w][r] = m;
-      sm.att_l[w][r] = lw;
-    }
-    *reinterpret_cast<float4*>(&sm.att_o[w][r][lane * EPL]) = make_float4(o[0], o[1], o[2], o[3]);
   }
+  if (lane == 0) {
+    sm.att_m[w][0] = m;
+    sm.att_l[w][0] = lw;
+  }
+  *reinterpret_cast<float4*>(&sm.att_o[w][0][lane * EPL]) = make_float4(o[0], o[1], o[2], o[3]);
   consumer_sync();
-  // merge the warps into this chunk's partial
-  float* part = a.part + ((size_t)kvh * MK_MAXCH + ch) * MK_ROWS * (HD + MK_PAD);
-  if (ct < g) {
-    const int r = ct;
+  // merge the warps into this chunk's partial for row r
+  float* part = a.part + (((size_t)kvh * MK_MAXCH + ch) * MK_ROWS + r) * (HD + MK_PAD);
+  if (ct == 0) {
     float M = -INFINITY;
-    for (int i = 0; i < MK_CW; ++i) M = fmaxf(M, sm.att_m[i][r]);
+    for (int i = 0; i < MK_CW; ++i) M = fmaxf(M, sm.att_m[i][0]);
     float l = 0.0f;
     for (int i = 0; i < MK_CW; ++i) {
-      const float cs = sm.att_m[i][r] == -INFINITY ? 0.0f : expf(sm.att_m[i][r] - M);
-      sm.att_cs[i][r] = cs;
-      l += sm.att_l[i][r] * cs;
+      const float cs = sm.att_m[i][0] == -INFINITY ? 0.0f : expf(sm.att_m[i][0] - M);
+      sm.att_cs[i][0] = cs;
+      l += sm.att_l[i][0] * cs;
     }
-    part[r * (HD + MK_PAD)] = M;
-    part[r * (HD + MK_PAD) + 1] = l;
+    part[0] = M;
+    part[1] = l;
   }
   consumer_sync();
-  for (int i = ct; i < g * HD; i += MK_CW * 32) {
-    const int r = i / HD, e = i - r * HD;
+  for (int e = ct; e < HD; e += MK_CW * 32) {
     float v = 0.0f;
-    for (int k = 0; k < MK_CW; ++k) v += sm.att_o[k][r][e] * sm.att_cs[k][r];
-    part[r * (HD + MK_PAD) + MK_PAD + e] = v;
+    for (int k = 0; k < MK_CW; ++k) v += sm.att_o[k][0][e] * sm.att_cs[k][0];
+    part[MK_PAD + e] = v;
   }
 }
 
@@ -673,13 +678,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
   unsigned seq = 0;
   unsigned stage = 0;
   const unsigned n = gridDim.x;
+  const int nwo = geo(a, ST_WO).KS, nwd = geo(a, ST_WDOWN).KS;  // partial sums the norms add
   bool ok = true;
   for (int l = 0; l < a.n_layers && ok; ++l) {
     const q4b_layer_weights& Lw = a.layers[l];
     // QKV
     ok = stage == 0 || stage_wait(a, sm, stage * n);
     if (!ok) break;
-    stage_norm(a, sm, Lw.ln_in, l == 0, token);
+    stage_norm(a, sm, Lw.ln_in, l == 0, token, a.hb, nwd, a.hb + a.D);
     consumer_sync();
     ok = consume_stage(a, sm, ST_QKV, l, seq, pos);
     stage_arrive(a);
@@ -687,8 +693,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     if (!ok) break;
     // attention
     if (!(ok = stage_wait(a, sm, stage * n))) break;
-    for (int it = blockIdx.x; it < a.Hkv * nch; it += gridDim.x) {
-      attn_item(a, sm, l, it / nch, it % nch, ctx);
+    const int g = a.H / a.Hkv;
+    for (int it = blockIdx.x; it < a.H * nch; it += gridDim.x) {  // (query row, chunk) items
+      const int hq = it / nch, ch = it - hq * nch;
+      attn_item(a, sm, l, hq / g, ch, hq % g, ctx);
       consumer_sync();
     }
     stage_arrive(a);
@@ -703,7 +711,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     if (!ok) break;
     // WGU
     if (!(ok = stage_wait(a, sm, stage * n))) break;
-    stage_norm(a, sm, Lw.ln_post, false, token);
+    stage_norm(a, sm, Lw.ln_post, false, token, a.hb + a.D, nwo, a.hb);
     consumer_sync();
     ok = consume_stage(a, sm, ST_WGU, l, seq, pos);
     stage_arrive(a);
@@ -718,7 +726,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     ++stage;
   }
   if (ok && (ok = stage_wait(a, sm, stage * n))) {
-    stage_norm(a, sm, a.ln_f, false, token);
+    stage_norm(a, sm, a.ln_f, false, token, a.hb, nwd, nullptr);
     consumer_sync();
     ok = consume_lm(a, sm, seq);
   }
@@ -776,6 +784,7 @@ int Model::mk_prepare() {
   if (!mk_layers && (rc = alloc(&mk_layers, sizeof(q4b_layer_weights) * layers.size(), false))) return rc;
   if (!mk_part && (rc = alloc((void**)&mk_part, sizeof(float) * Hkv * MK_MAXCH * MK_ROWS * (hd + MK_PAD), true))) return rc;
   if (!mk_sync && (rc = alloc((void**)&mk_sync, 2 * sizeof(unsigned), true))) return rc;
+  if (!mk_h && (rc = alloc((void**)&mk_h, sizeof(float) * (2 + MK_MAXKS) * D, true))) return rc;
   cudaError_t e = cudaMemcpy(mk_proj, proj.data(), sizeof(MkProj) * proj.size(), cudaMemcpyHostToDevice);
   if (e == cudaSuccess)
     e = cudaMemcpy(mk_layers, layers.data(), sizeof(q4b_layer_weights) * layers.size(), cudaMemcpyHostToDevice);
@@ -831,7 +840,8 @@ int Model::mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_
   a.state = state;
   a.token_log = token_log;
   a.logits = logits;
-  a.h = h;
+  a.hb = mk_h;
+  a.psum = mk_h + 2 * D;
   a.q = q;
   a.a = this->a;
   a.part = mk_part;

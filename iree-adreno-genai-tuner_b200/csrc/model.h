@@ -31,6 +31,7 @@ struct Model {
   void* mk_layers = nullptr;
   float* mk_part = nullptr;
   unsigned* mk_sync = nullptr;
+  float* mk_h = nullptr;  // residual ping-pong [2][D] + K-split partials [4][D]
   int mk_ctas = 0;
   bool mk_ready = false;
   int mk_prepare();
