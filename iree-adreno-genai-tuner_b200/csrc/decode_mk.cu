@@ -45,6 +45,7 @@ constexpr int MK_NSLOT = 16;
 constexpr int MK_MAXK = 8192;
 constexpr int MK_XROW = MK_MAXK / 8 + 4;       // staged x: uint4 per row (+64 B, as kernel 1)
 constexpr int MK_HD = 128;
+static_assert(MK_HD <= MK_CW * 32, "one query element per consumer thread");
 constexpr int MK_KCHUNK = 256;                 // keys per attention item (8 warps x 32)
 constexpr int MK_MAXCH = 64;                   // attention chunks (contexts up to 16384)
 constexpr int MK_ROWS = 4;                     // query rows per KV head (GQA group) at most
@@ -96,9 +97,6 @@ struct MkSmem {
   float att_o[MK_CW][MK_ROWS][MK_HD];
   float att_m[MK_CW][MK_ROWS], att_l[MK_CW][MK_ROWS];
   float att_cs[MK_CW][MK_ROWS];
-  float mw[32][MK_MAXCH];  // WO merge: per q head and chunk, the chunk max, then its weight
-  float ml[32][MK_MAXCH];  // and the chunk sum
-  float mL[32];
   unsigned long long best[MK_CW];
   uint64_t full[MK_NSLOT], empty[MK_NSLOT];
   int abort_flag;
@@ -320,65 +318,50 @@ __device__ void stage_plain(const MkArgs& a, MkSmem& sm, const float* src, int K
   }
 }
 
-// x = attention output o [H * hd]: the chunk partials of every head merged (max, sum, weighted V).
-// Two rounds of loads: every (head, chunk) max and sum together, then the weighted partials.
+// x = attention output o [H * hd]: the chunk partials of every head merged (max, sum, weighted V),
+// online over the chunks; the (max, sum) pair and the 8 elements of each chunk are loaded together,
+// four chunks per round (one round up to 1024 keys).
 __device__ void stage_attn_merge(const MkArgs& a, MkSmem& sm, int nch) {
   const int ct = threadIdx.x - 32;
   const int g = a.H / a.Hkv, HD = a.hd;
   const size_t PS = HD + MK_PAD;
-  for (int i = ct; i < a.H * nch; i += MK_CW * 32) {
-    const int hq = i / nch, c = i - hq * nch;
-    const int kvh = hq / g, r = hq - kvh * g;
-    const float* p = a.part + (((size_t)kvh * MK_MAXCH + c) * MK_ROWS + r) * PS;
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(p));
-    sm.mw[hq][c] = ml.x;
-    sm.ml[hq][c] = ml.y;
-  }
-  consumer_sync();
-  if (ct < a.H) {
-    float M = -INFINITY;
-    for (int c = 0; c < nch; ++c) M = fmaxf(M, sm.mw[ct][c]);
-    float Lsum = 0.0f;
-    for (int c = 0; c < nch; ++c) {
-      const float mc = sm.mw[ct][c];
-      const float cs = mc == -INFINITY ? 0.0f : expf(mc - M);
-      Lsum += sm.ml[ct][c] * cs;
-      sm.mw[ct][c] = cs;
-    }
-    sm.mL[ct] = Lsum;
-  }
-  consumer_sync();
   for (int w = ct; w < a.H * HD / 8; w += MK_CW * 32) {
     const int hq = (8 * w) / HD, e0 = 8 * w - hq * HD;
     const int kvh = hq / g, r = hq - kvh * g;
-    const float* base = a.part + ((size_t)kvh * MK_MAXCH * MK_ROWS + r) * PS + MK_PAD + e0;
+    const float* base = a.part + ((size_t)kvh * MK_MAXCH * MK_ROWS + r) * PS;
+    float M = -INFINITY, Lsum = 0.0f;
     float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    int c = 0;
-    for (; c + 4 <= nch; c += 4) {  // four chunks' loads in flight together
-      float4 p[4][2];
+    for (int c0 = 0; c0 < nch; c0 += 2) {
+      float2 ml[2];
+      float4 p0[2], p1[2];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float4* q = reinterpret_cast<const float4*>(base + (size_t)(c + k) * MK_ROWS * PS);
-        p[k][0] = __ldcg(q);
-        p[k][1] = __ldcg(q + 1);
+      for (int k = 0; k < 2; ++k) {
+        if (c0 + k < nch) {
+          const float* pc = base + (size_t)(c0 + k) * MK_ROWS * PS;
+          ml[k] = __ldcg(reinterpret_cast<const float2*>(pc));
+          p0[k] = __ldcg(reinterpret_cast<const float4*>(pc + MK_PAD + e0));
+          p1[k] = __ldcg(reinterpret_cast<const float4*>(pc + MK_PAD + e0) + 1);
+        }
       }
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float cs = sm.mw[hq][c + k];
-        v[0] += cs * p[k][0].x; v[1] += cs * p[k][0].y; v[2] += cs * p[k][0].z; v[3] += cs * p[k][0].w;
-        v[4] += cs * p[k][1].x; v[5] += cs * p[k][1].y; v[6] += cs * p[k][1].z; v[7] += cs * p[k][1].w;
+      for (int k = 0; k < 2; ++k) {
+        if (c0 + k < nch && ml[k].x != -INFINITY) {
+          if (ml[k].x > M) {  // rescale what was merged so far to the new maximum
+            const float rs = M == -INFINITY ? 0.0f : expf(M - ml[k].x);
+            Lsum *= rs;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) v[b] *= rs;
+            M = ml[k].x;
+          }
+          const float cs = expf(ml[k].x - M);
+          Lsum += ml[k].y * cs;
+          v[0] += cs * p0[k].x; v[1] += cs * p0[k].y; v[2] += cs * p0[k].z; v[3] += cs * p0[k].w;
+          v[4] += cs * p1[k].x; v[5] += cs * p1[k].y; v[6] += cs * p1[k].z; v[7] += cs * p1[k].w;
+        }
       }
     }
-    for (; c < nch; ++c) {
-      const float cs = sm.mw[hq][c];
-      const float4* q = reinterpret_cast<const float4*>(base + (size_t)c * MK_ROWS * PS);
-      const float4 p0 = __ldcg(q), p1 = __ldcg(q + 1);
-      v[0] += cs * p0.x; v[1] += cs * p0.y; v[2] += cs * p0.z; v[3] += cs * p0.w;
-      v[4] += cs * p1.x; v[5] += cs * p1.y; v[6] += cs * p1.z; v[7] += cs * p1.w;
-    }
-    const float inv = sm.mL[hq];
 #pragma unroll
-    for (int b = 0; b < 8; ++b) v[b] = v[b] / inv;
+    for (int b = 0; b < 8; ++b) v[b] = v[b] / Lsum;
     stage_word(sm, w, v);
   }
 }
@@ -425,7 +408,6 @@ __device__ bool consume_stage(const MkArgs& a, MkSmem& sm, int st, int layer, un
   const ProjGeo gp = geo(a, st);
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int mrow[1] = {0};
   const int upi = gp.NU / gp.KS;
   const int nitems = gp.RT * gp.KS;
   const int nmine = nitems > (int)blockIdx.x ? (nitems - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -434,7 +416,7 @@ __device__ bool consume_stage(const MkArgs& a, MkSmem& sm, int st, int layer, un
     for (int j = 0; j < nb; ++j) {
       const int it = blockIdx.x + (b0 + j) * gridDim.x;
       const int ks = it % gp.KS;
-      float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (int u = ks * upi; u < (ks + 1) * upi; ++u, ++seq) {
         const int slot = seq % MK_NSLOT;
         if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, kWaitLimitNs)) {
@@ -448,11 +430,11 @@ __device__ bool consume_stage(const MkArgs& a, MkSmem& sm, int st, int layer, un
         const float sa = __half2float(sc[g * 8 + w]), sb = __half2float(sc[(g + 8) * 8 + w]);
         __syncwarp();
         if (lane == 0) mbar_arrive_cnt(&sm.empty[slot], 1);
-        mma_tile<1, true, true>(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, mrow, u * 128 + w * 16 + 4 * t, acc);
+        mma_tile_hl(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, g, u * 128 + w * 16 + 4 * t, acc);
       }
-      if (t == 0) {
-        sm.red[j][w][g] = acc[0][0];
-        sm.red[j][w][g + 8] = acc[0][2];
+      if (t == 0) {  // columns 0 / 1: the x_hi / x_lo products of rows g and g + 8
+        sm.red[j][w][g] = acc[0] + acc[1];
+        sm.red[j][w][g + 8] = acc[2] + acc[3];
       }
     }
     consumer_sync();
@@ -479,13 +461,12 @@ __device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq) {
   const ProjGeo gp = geo(a, ST_PER_LAYER);
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int mrow[1] = {0};
   unsigned long long best = 0ull;
   const int ntile = gp.RT > (int)blockIdx.x ? (gp.RT - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   for (int b0 = 0; b0 < ntile; b0 += MK_TB) {
     const int nb = min(MK_TB, ntile - b0);
     for (int j = 0; j < nb; ++j) {
-      float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (int u = 0; u < gp.NU; ++u, ++seq) {
         const int slot = seq % MK_NSLOT;
         if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, kWaitLimitNs)) {
@@ -499,11 +480,11 @@ __device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq) {
         const float sa = __half2float(sc[g * 8 + w]), sb = __half2float(sc[(g + 8) * 8 + w]);
         __syncwarp();
         if (lane == 0) mbar_arrive_cnt(&sm.empty[slot], 1);
-        mma_tile<1, true, true>(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, mrow, u * 128 + w * 16 + 4 * t, acc);
+        mma_tile_hl(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, g, u * 128 + w * 16 + 4 * t, acc);
       }
-      if (t == 0) {
-        sm.red[j][w][g] = acc[0][0];
-        sm.red[j][w][g + 8] = acc[0][2];
+      if (t == 0) {  // columns 0 / 1: the x_hi / x_lo products of rows g and g + 8
+        sm.red[j][w][g] = acc[0] + acc[1];
+        sm.red[j][w][g + 8] = acc[2] + acc[3];
       }
     }
     consumer_sync();
@@ -552,10 +533,10 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
   const size_t row_stride = (size_t)a.Hkv * HD;
   const int k0 = ch * MK_KCHUNK, k1 = min(k0 + MK_KCHUNK, ctx);
   const int jbase = k0 + 32 * w, j = jbase + lane;
-  for (int i = ct; i < HD; i += MK_CW * 32) sm.att_q[0][i] = __ldcg(a.q + ((size_t)kvh * g + r) * HD + i);
-  consumer_sync();
-  // one round of loads for the warp's 32 keys: this lane's 4 elements of every V row (8 bytes per
-  // key) and the first half of this lane's K row; the second K half follows
+  // one round of loads: the query row (one element per thread, to shared memory), this lane's 4
+  // elements of every V row of the warp's 32 keys (8 bytes per key) and the first half of this
+  // lane's K row; the second K half follows
+  const float qv = ct < HD ? __ldcg(a.q + ((size_t)kvh * g + r) * HD + ct) : 0.0f;
   const int jc = min(j, k1 - 1);
   uint2 vv[32];
 #pragma unroll
@@ -563,13 +544,19 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
     const int key = min(jbase + jj, k1 - 1);
     vv[jj] = __ldcg(reinterpret_cast<const uint2*>(vc + (size_t)key * row_stride + (size_t)kvh * HD + lane * EPL));
   }
-  float d = 0.0f;
   const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t)jc * row_stride + (size_t)kvh * HD);
+  uint4 kr[KU4 / 2];
+#pragma unroll
+  for (int u = 0; u < KU4 / 2; ++u) kr[u] = __ldcg(kp + u);
+  if (ct < HD) sm.att_q[0][ct] = qv;
+  consumer_sync();
+  float d = 0.0f;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
-    uint4 kr[KU4 / 2];
+    if (half == 1) {
 #pragma unroll
-    for (int u = 0; u < KU4 / 2; ++u) kr[u] = __ldcg(kp + half * (KU4 / 2) + u);
+      for (int u = 0; u < KU4 / 2; ++u) kr[u] = __ldcg(kp + KU4 / 2 + u);
+    }
 #pragma unroll
     for (int u = 0; u < KU4 / 2; ++u) {
       const __half2* h2 = reinterpret_cast<const __half2*>(&kr[u]);

@@ -263,43 +263,79 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnArgs a) {
 }
 
 // grid (H, ceil(C / 4)), block 128: warp w handles query row 4 * blockIdx.y + w of head blockIdx.x.
+// Keys go in blocks of 32: lane j scores key kb + j against the whole query row (read from shared
+// memory as broadcasts), one max and one sum reduction per block update the online softmax, then
+// P.V with lanes owning head elements (hd / 32 each) over the block's V rows, loaded together.
 template <int EPL>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
-  constexpr int HD = EPL * 32;
+  constexpr int HD = EPL * 32, KU4 = HD / 8;
+  __shared__ float s_q[4][HD];
   const int h = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.y * 4 + warp;
   griddep_launch_dependents();
   griddep_wait();
-  if (c >= a.C) return;
+  if (c >= a.C) return;  // whole warp; no block-wide barrier below
   const int g = a.H / a.Hkv, kvh = h / g;
   const int start = *a.pos0;
   const int nk = min(a.L, start + c + 1);
-  float q[EPL], o[EPL];
-  const float* qp = a.q + ((size_t)c * a.H + h) * HD + lane * EPL;
+  const float* qp = a.q + ((size_t)c * a.H + h) * HD;
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) {
-    q[e] = qp[e];
-    o[e] = 0.0f;
-  }
+  for (int e = 0; e < EPL; ++e) s_q[warp][lane * EPL + e] = qp[lane * EPL + e];
+  __syncwarp();
+  float o[EPL];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e) o[e] = 0.0f;
   float m = -INFINITY, l = 0.0f;
   const size_t kv_stride = (size_t)a.Hkv * HD;
-  const __half* kb = a.k_cache + (size_t)kvh * HD + lane * EPL;
-  const __half* vb = a.v_cache + (size_t)kvh * HD + lane * EPL;
-#pragma unroll 4
-  for (int j = 0; j < nk; ++j) {
-    float kv[EPL], vv[EPL];
-    load_half_vec<EPL>(kb + (size_t)j * kv_stride, kv);
-    load_half_vec<EPL>(vb + (size_t)j * kv_stride, vv);
+  const __half* kbase = a.k_cache + (size_t)kvh * HD;
+  const __half* vbase = a.v_cache + (size_t)kvh * HD + lane * EPL;
+  for (int kb = 0; kb < nk; kb += 32) {
+    const int j = kb + lane;
+    const bool valid = j < nk;
+    // this lane's key row and the block's V slices of this lane's elements, in one round
+    const uint4* kp = reinterpret_cast<const uint4*>(kbase + (size_t)min(j, nk - 1) * kv_stride);
+    uint4 kr[KU4];
+#pragma unroll
+    for (int u = 0; u < KU4; ++u) kr[u] = kp[u];
+    // V slices kept as packed fp16 (EPL halves per key) until used
+    __half vv[32][EPL];
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) {
+      const __half* vp = vbase + (size_t)min(kb + jj, nk - 1) * kv_stride;
+      if constexpr (EPL == 4) {
+        *reinterpret_cast<uint2*>(vv[jj]) = *reinterpret_cast<const uint2*>(vp);
+      } else if constexpr (EPL == 2) {
+        *reinterpret_cast<uint32_t*>(vv[jj]) = *reinterpret_cast<const uint32_t*>(vp);
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) vv[jj][e] = vp[e];
+      }
+    }
     float d = 0.0f;
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) d = fmaf(q[e], kv[e], d);
-    d = warp_sum(d) * a.scale;
-    const float mn = fmaxf(m, d);
-    const float cs = expf(m - mn), p = expf(d - mn);
-    l = l * cs + p;
+    for (int u = 0; u < KU4; ++u) {
+      const __half2* h2 = reinterpret_cast<const __half2*>(&kr[u]);
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) o[e] = o[e] * cs + p * vv[e];
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __half22float2(h2[t]);
+        d = fmaf(s_q[warp][8 * u + 2 * t], f.x, d);
+        d = fmaf(s_q[warp][8 * u + 2 * t + 1], f.y, d);
+      }
+    }
+    const float sc = valid ? d * a.scale : -INFINITY;
+    const float mn = fmaxf(m, warp_max(sc));  // lane 0's key is always visible: mn is finite
+    const float p = valid ? expf(sc - mn) : 0.0f;
+    const float cs = m == -INFINITY ? 0.0f : expf(m - mn);
+    l = l * cs + warp_sum(p);
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) o[e] *= cs;
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, p, jj);  // 0 for keys past nk
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) o[e] = fmaf(pj, __half2float(vv[jj][e]), o[e]);
+    }
     m = mn;
   }
   float* op = a.out + ((size_t)c * a.H + h) * HD + lane * EPL;

@@ -116,4 +116,29 @@ __device__ __forceinline__ void mma_tile(const uint4& wa, const uint4& wb, float
   }
 }
 
+
+// M = 1 with fp32 x: x_hi and x_lo as the first two columns of the MMA's B operand (lanes of group
+// g = 0 supply x_hi, g = 1 x_lo, the other columns are zero), so each m16n8k16 yields both halves'
+// products -- half the MMAs of mma_tile<1, true, *>. Lanes with t == 0 end up holding, for rows g
+// and g + 8, acc[0] / acc[2] (hi part) and acc[1] / acc[3] (lo part); the row's value is their sum.
+__device__ __forceinline__ void mma_tile_hl(const uint4& wa, const uint4& wb, float sa, float sb, const uint4* xs_hi,
+                                            const uint4* xs_lo, int g, int wbase, float (&acc)[4]) {
+  float part[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+  const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
+  const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+  const uint4* xs = g == 0 ? xs_hi : xs_lo;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t A[4], B[4];
+    dequant_word(wav[q], A);
+    dequant_word(wbv[q], B);
+    const uint4 xv = g < 2 ? xs[xswz(wbase + q)] : make_uint4(0u, 0u, 0u, 0u);
+    mma_16816(part[0], A[0], B[0], A[1], B[1], xv.x, xv.y);
+    mma_16816(part[1], A[2], B[2], A[3], B[3], xv.z, xv.w);
+  }
+  acc[0] = fmaf(sa, part[0][0] + part[1][0], acc[0]);
+  acc[1] = fmaf(sa, part[0][1] + part[1][1], acc[1]);
+  acc[2] = fmaf(sb, part[0][2] + part[1][2], acc[2]);
+  acc[3] = fmaf(sb, part[0][3] + part[1][3], acc[3]);
+}
 }  // namespace q4b
