@@ -403,7 +403,7 @@ def run_decode(args, rank, world, local, dist_mod):
     pos = [PROMPT_LEN + i for i in range(steps)]
     bytes_tok = statistics.mean(decode_bytes_per_token(cfg, p, world) for p in pos)
     achieved = bytes_tok * value / 1e9
-    persistent = world == 1 and os.environ.get("Q4B_PERSISTENT", "0") == "1"
+    persistent = world == 1 and os.environ.get("Q4B_PERSISTENT", "1") != "0"
     # persistent decode: one cooperative kernel per token (plus a 8-byte counter reset); else per layer
     # q|k|v, attention, o, gate|up, down, and embedding + final norm + lm_head (+ TP collectives)
     launches = 1 if persistent else 2 + 5 * cfg["num_hidden_layers"] + (

@@ -734,11 +734,11 @@ static bool mk_shapes_ok(const Model& m) {
          m.H * m.hd <= MK_MAXK && m.V % 16 == 0 && m.cfg.max_ctx <= MK_MAXCH * MK_KCHUNK;
 }
 
-// Q4B_PERSISTENT=1 selects the persistent kernel for decode, anything else the per-projection
-// kernels (read on every step)
+// The persistent kernel is the decode path where its shapes allow; Q4B_PERSISTENT=0 selects the
+// per-projection kernels instead (read on every step)
 static bool persistent_enabled() {
   const char* e = std::getenv("Q4B_PERSISTENT");
-  return e && e[0] == '1';
+  return !(e && e[0] == '0');
 }
 
 // Tensor maps and the layer table on the device; needs every weight set and no stream capture.

@@ -1,8 +1,8 @@
 """The persistent decode step (one cooperative launch per token, csrc/decode_mk.cu) against the
 per-projection kernels and the CPU oracle: same greedy tokens, logits within 1e-3 of max|logit|
 (the reference's tolerance, scripts/debug/op_test.py:75), and the same tokens through the runner's
-captured CUDA graphs. Q4B_PERSISTENT=1 selects the persistent step, anything else the per-projection
-path."""
+captured CUDA graphs. Q4B_PERSISTENT=0 selects the per-projection path (the persistent step is the
+default where its shapes allow)."""
 
 import os
 
