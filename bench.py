@@ -403,11 +403,13 @@ def run_decode(args, rank, world, local, dist_mod):
     pos = [PROMPT_LEN + i for i in range(steps)]
     bytes_tok = statistics.mean(decode_bytes_per_token(cfg, p, world) for p in pos)
     achieved = bytes_tok * value / 1e9
-    persistent = world == 1 and os.environ.get("Q4B_PERSISTENT", "1") != "0"
+    persistent = bool(q4b.lib().q4b_model_decode_path(model.native()))
     # persistent decode: one cooperative kernel per token (plus a 8-byte counter reset); else per layer
     # q|k|v, attention, o, gate|up, down, and embedding + final norm + lm_head (+ TP collectives)
     launches = 1 if persistent else 2 + 5 * cfg["num_hidden_layers"] + (
         0 if world == 1 else 2 * cfg["num_hidden_layers"] + 1)
+    # (with tp the persistent step pushes o / down partial sums and argmax keys to the peers' memory
+    # inside the kernel: no collective launches)
     line = {
         "metric": METRIC_DECODE, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": round(decode_ms / steps, 4), "higher_is_better": True,

@@ -190,6 +190,10 @@ int q4b_model_set_head(q4b_model* model, const q4b_qmat* embed, const float* ln_
 int q4b_model_step(q4b_model* model, const int32_t* tokens, int n_tokens, int start, int last, int L,
                    int32_t* next_token, float* logits, q4b_stream_t stream);
 void q4b_model_destroy(q4b_model* model);
+/* Which kernel runs single-token decode steps: 1 = the persistent step (one cooperative launch per
+ * token, tables built on the first decode step), 0 = one kernel per projection. No reference
+ * counterpart (a diagnostic of this library's decode path). */
+int q4b_model_decode_path(const q4b_model* model);
 
 /* ---- tensor parallelism (one process per GPU, NCCL loaded at run time) ---------------------- */
 

@@ -51,6 +51,7 @@ constexpr int MK_MAXCH = 64;                   // attention chunks (contexts up 
 constexpr int MK_ROWS = 4;                     // query rows per KV head (GQA group) at most
 constexpr int MK_TB = 8;                       // tiles of one stage per batched epilogue
 constexpr int MK_MAXKS = 3;                    // K splits of the o / down projections
+constexpr int MK_MAXTP = 8;                    // tensor-parallel ranks
 constexpr int MK_MAXD = 4096;                  // hidden size: at most two staged words per thread
 constexpr int MK_PAD = 4;                      // partial row: m, l and two pad floats before o (16-B aligned)
 
@@ -79,11 +80,20 @@ struct MkArgs {
   int32_t* token_log;
   float* logits;
   float* hb;     // [2][D] residual stream, ping-pong: QKV staging writes hb[1], WGU staging hb[0]
-  float* psum;   // [MK_MAXKS][D] K-split partial sums of the o / down projections
+  float* psum;   // [2][tp * MK_MAXKS][D] partial sums of the o (buffer 0) / down (buffer 1) projections
   float* q;      // [H * hd]
   float* a;      // [I]
   float* part;   // attention partials [Hkv][MK_MAXCH][MK_ROWS][hd + 4]: m, l, -, -, o[hd]
-  unsigned* sync;  // [0] stage arrivals, [1] abort
+  unsigned* sync;  // [0] local stage arrivals, [1] abort, [2] arrivals of all ranks, [3] lm keys, [4] epoch
+  // tensor parallelism: this rank of tp; the peers' psum / sync / key buffers (peer memory mapped
+  // into this process; index rank = this GPU's own)
+  int tp, rank, Vfull;
+  float* peer_psum[MK_MAXTP];
+  unsigned* peer_sync[MK_MAXTP];
+  unsigned long long* peer_keys[MK_MAXTP];
+  unsigned long long* keys;  // [tp] this rank's copy of every rank's best argmax key
+  // limit of every wait: 1 s on one GPU; longer with peers, whose launches may start later
+  unsigned long long wait_ns;
 };
 
 struct MkSmem {
@@ -136,7 +146,7 @@ __device__ bool stage_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
         sm.abort_flag = 1;
         break;
       }
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > a.wait_ns) {
         atomicExch(&a.sync[1], 1u);
         sm.abort_flag = 1;
         break;
@@ -152,6 +162,49 @@ __device__ void stage_arrive(const MkArgs& a) {
   if (threadIdx.x == 32) {
     __threadfence();
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync) : "memory");
+  }
+}
+
+// Barrier over every CTA of every rank (after the row-split o / down projections, whose partial sums
+// go to the peers): each CTA adds 1 to every rank's counter after a system-scope fence, then waits
+// for its own counter. The counter is never reset (peers may add to it before this rank's step has
+// started), so targets count from the step's epoch.
+__device__ bool global_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
+  if (threadIdx.x == 32) {
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+      unsigned v;
+      if (a.tp > 1)
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 2) : "memory");
+      else
+        v = ld_acquire(a.sync + 2);
+      if ((int)(v - target) >= 0) break;
+      __nanosleep(32);
+      if (ld_acquire(&a.sync[1])) {
+        sm.abort_flag = 1;
+        break;
+      }
+      if (globaltimer_ns() - t0 > a.wait_ns) {
+        for (int r = 0; r < a.tp; ++r) atomicExch_system(a.peer_sync[r] + 1, 1u);
+        sm.abort_flag = 1;
+        break;
+      }
+    }
+  }
+  consumer_sync();
+  return !sm.abort_flag;
+}
+__device__ void global_arrive(const MkArgs& a) {
+  consumer_sync();
+  if (threadIdx.x == 32) {
+    if (a.tp > 1) {
+      __threadfence_system();
+      for (int r = 0; r < a.tp; ++r)
+        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.peer_sync[r] + 2) : "memory");
+    } else {
+      __threadfence();
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync + 2) : "memory");
+    }
   }
 }
 
@@ -172,9 +225,15 @@ __host__ __device__ __forceinline__ int k_splits(int nu) {
 __device__ __forceinline__ ProjGeo geo(const MkArgs& a, int st) {
   switch (st) {
     case ST_QKV: return {a.D, (a.H + 2 * a.Hkv) * a.hd / 16, a.D / MK_UK, true, 1};
-    case ST_WO: return {a.H * a.hd, a.D / 16, a.H * a.hd / MK_UK, false, k_splits(a.H * a.hd / MK_UK)};
+    case ST_WO: {
+      const int nu = (a.H * a.hd + MK_UK - 1) / MK_UK;  // a TP shard may end inside a unit: zero-filled
+      return {a.H * a.hd, a.D / 16, nu, false, k_splits(nu)};
+    }
     case ST_WGU: return {a.D, a.I / 8, a.D / MK_UK, true, 1};
-    case ST_WDOWN: return {a.I, a.D / 16, a.I / MK_UK, false, k_splits(a.I / MK_UK)};
+    case ST_WDOWN: {
+      const int nu = (a.I + MK_UK - 1) / MK_UK;
+      return {a.I, a.D / 16, nu, false, k_splits(nu)};
+    }
     default: return {a.D, a.V / 16, a.D / MK_UK, false, 1};  // lm_head
   }
 }
@@ -196,7 +255,7 @@ __device__ bool produce_stage(const MkArgs& a, MkSmem& sm, const MkProj& pj, int
     const int rt = it / gp.KS, ks = it - rt * gp.KS;
     for (int u = ks * upi; u < (ks + 1) * upi; ++u, ++seq) {
       const int slot = seq % MK_NSLOT, round = seq / MK_NSLOT;
-      if (round > 0 && !mbar_wait_bounded(&sm.empty[slot], (round - 1) & 1, kWaitLimitNs)) return false;
+      if (round > 0 && !mbar_wait_bounded(&sm.empty[slot], (round - 1) & 1, a.wait_ns)) return false;
       if (sm.abort_flag) return false;
       uint8_t* dst = sm.ring[slot];
       mbar_arrive_expect_tx(&sm.full[slot], MK_SLOT);
@@ -232,10 +291,10 @@ __device__ __forceinline__ void stage_word(MkSmem& sm, int w, const float (&v)[8
 // (QEmbedding.lookup, llama_q4.py:106-119); later it is h + the K-split partial sums of the o / down
 // projection (added in split order).
 __device__ __forceinline__ void norm_src(const MkArgs& a, int w, bool embed, int token, const float* hsrc,
-                                         int nparts, float (&v)[8]) {
+                                         const float* psrc, int nparts, float (&v)[8]) {
   if (embed) {
     const int words = a.D / 8;
-    const bool ok = token >= 0 && token < a.V;
+    const bool ok = token >= 0 && token < a.Vfull;
     const int32_t word = ok ? a.emb_qw[(size_t)token * words + w] : 0;
     const float s = ok ? __half2float(a.emb_s[(size_t)token * (a.D / 128) + (8 * w) / 128]) : 0.0f;
 #pragma unroll
@@ -243,22 +302,25 @@ __device__ __forceinline__ void norm_src(const MkArgs& a, int w, bool embed, int
   } else {
     const float4 p0 = __ldcg(reinterpret_cast<const float4*>(hsrc + 8 * w));
     const float4 p1 = __ldcg(reinterpret_cast<const float4*>(hsrc + 8 * w) + 1);
-    float4 q0[MK_MAXKS], q1[MK_MAXKS];
-#pragma unroll
-    for (int k = 0; k < MK_MAXKS; ++k) {
-      if (k < nparts) {
-        q0[k] = __ldcg(reinterpret_cast<const float4*>(a.psum + (size_t)k * a.D + 8 * w));
-        q1[k] = __ldcg(reinterpret_cast<const float4*>(a.psum + (size_t)k * a.D + 8 * w) + 1);
-      }
-    }
     v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
     v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
     float d[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int r = 0; r < a.tp; ++r) {  // every rank's partials, rank order then split order
+      const float* pr = psrc + (size_t)r * MK_MAXKS * a.D + 8 * w;
+      float4 q0[MK_MAXKS], q1[MK_MAXKS];
 #pragma unroll
-    for (int k = 0; k < MK_MAXKS; ++k) {
-      if (k < nparts) {
-        d[0] += q0[k].x; d[1] += q0[k].y; d[2] += q0[k].z; d[3] += q0[k].w;
-        d[4] += q1[k].x; d[5] += q1[k].y; d[6] += q1[k].z; d[7] += q1[k].w;
+      for (int k = 0; k < MK_MAXKS; ++k) {
+        if (k < nparts) {
+          q0[k] = __ldcg(reinterpret_cast<const float4*>(pr + (size_t)k * a.D));
+          q1[k] = __ldcg(reinterpret_cast<const float4*>(pr + (size_t)k * a.D) + 1);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < MK_MAXKS; ++k) {
+        if (k < nparts) {
+          d[0] += q0[k].x; d[1] += q0[k].y; d[2] += q0[k].z; d[3] += q0[k].w;
+          d[4] += q1[k].x; d[5] += q1[k].y; d[6] += q1[k].z; d[7] += q1[k].w;
+        }
       }
     }
 #pragma unroll
@@ -269,7 +331,7 @@ __device__ __forceinline__ void norm_src(const MkArgs& a, int w, bool embed, int
 // x = rmsnorm(h) * w (rms_norm, llama_q4.py:141-142). With hdst the updated residual stream is also
 // written (each word by one CTA) to the other ping-pong buffer.
 __device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float* lnw, bool embed, int token, const float* hsrc,
-                           int nparts, float* hdst) {
+                           const float* psrc, int nparts, float* hdst) {
   const int ct = threadIdx.x - 32;
   const int words = a.D / 8;
   // one round of loads: this thread's (at most two) words of h (+ partials) and of the norm weight
@@ -279,7 +341,7 @@ __device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float* lnw, bool e
   for (int i = 0; i < 2; ++i) {
     const int w = ct + i * (MK_CW * 32);
     if (w < words) {
-      norm_src(a, w, embed, token, hsrc, nparts, v[i]);
+      norm_src(a, w, embed, token, hsrc, psrc, nparts, v[i]);
       const float4 w0 = *reinterpret_cast<const float4*>(lnw + 8 * w);
       const float4 w1 = *reinterpret_cast<const float4*>(lnw + 8 * w + 4);
       lw[i][0] = w0.x; lw[i][1] = w0.y; lw[i][2] = w0.z; lw[i][3] = w0.w;
@@ -394,10 +456,14 @@ __device__ void pair_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, in
     }
   } else if (st == ST_WGU) {
     a.a[rt * 8 + s] = silu(v0) * v1;
-  } else {  // WO / WDOWN: this K split's partial sums (added to h by the next norm's staging)
-    float* p = a.psum + (size_t)ks * a.D + rt * 16;
-    p[s] = v0;
-    p[s + 8] = v1;
+  } else {  // WO / WDOWN: this rank's K-split partial sums, pushed to every rank (added to h there by
+            // the next norm's staging, in rank and split order)
+    const size_t off = ((size_t)(st == ST_WDOWN) * a.tp * MK_MAXKS + (size_t)a.rank * MK_MAXKS + ks) * a.D + rt * 16;
+    for (int r = 0; r < a.tp; ++r) {
+      float* p = a.peer_psum[r] + off;
+      p[s] = v0;
+      p[s + 8] = v1;
+    }
   }
 }
 
@@ -419,7 +485,7 @@ __device__ bool consume_stage(const MkArgs& a, MkSmem& sm, int st, int layer, un
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (int u = ks * upi; u < (ks + 1) * upi; ++u, ++seq) {
         const int slot = seq % MK_NSLOT;
-        if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, kWaitLimitNs)) {
+        if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, a.wait_ns)) {
           sm.abort_flag = 1;
           return false;
         }
@@ -457,7 +523,7 @@ __device__ bool consume_stage(const MkArgs& a, MkSmem& sm, int st, int layer, un
 // lm_head: the same split of K over the warps as consume_stage, each batch of tiles finished with
 // logits (optional) and greedy argmax keys; the CTA's best key goes to the step state, the last CTA
 // publishes the token (first maximum on ties, like torch.argmax).
-__device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq) {
+__device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq, unsigned epoch) {
   const ProjGeo gp = geo(a, ST_PER_LAYER);
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -469,7 +535,7 @@ __device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq) {
       float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (int u = 0; u < gp.NU; ++u, ++seq) {
         const int slot = seq % MK_NSLOT;
-        if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, kWaitLimitNs)) {
+        if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, a.wait_ns)) {
           sm.abort_flag = 1;
           return false;
         }
@@ -495,7 +561,7 @@ __device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq) {
       for (int k = 0; k < MK_CW; ++k) v += sm.red[j][k][sl];
       const int row = (blockIdx.x + (b0 + j) * gridDim.x) * 16 + sl;
       if (a.logits) a.logits[row] = v;
-      best = max(best, argmax_key(v, (unsigned)row));
+      best = max(best, argmax_key(v, (unsigned)(a.rank * a.V + row)));
     }
     consumer_sync();
   }
@@ -511,9 +577,30 @@ __device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq) {
     sm.last = atomicAdd(&a.state->counter, 1u) == gridDim.x - 1;
     if (sm.last) {
       __threadfence();
-      const unsigned long long bb = atomicExch(&a.state->best, 0ull);
+      unsigned long long bb = atomicExch(&a.state->best, 0ull);
       a.state->counter = 0u;
+      if (a.tp > 1) {
+        // every rank's best key to every rank, then the largest (vocab rows are split by rank)
+        for (int r = 0; r < a.tp; ++r) a.peer_keys[r][a.rank] = bb;
+        __threadfence_system();
+        for (int r = 0; r < a.tp; ++r)
+          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.peer_sync[r] + 3) : "memory");
+        const unsigned target = (epoch + 1) * (unsigned)a.tp;  // epoch-based: never reset
+        const uint64_t t0 = globaltimer_ns();
+        for (;;) {
+          unsigned v;
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 3) : "memory");
+          if ((int)(v - target) >= 0) break;
+          if (globaltimer_ns() - t0 > a.wait_ns) {
+            a.state->status = 1;
+            break;
+          }
+        }
+        bb = 0ull;
+        for (int r = 0; r < a.tp; ++r) bb = max(bb, *(volatile unsigned long long*)&a.keys[r]);
+      }
       publish_token(a.state, a.token_log, (int32_t)argmax_index(bb));
+      a.sync[4] += 1u;  // this rank's step epoch (every rank runs every step)
     }
   }
   return true;
@@ -630,6 +717,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
   __syncthreads();
   const int pos = a.state->start;
   const int token = *a.token;
+  const unsigned epoch = *(volatile unsigned*)&a.sync[4];
   const int ctx = min(a.L, pos + 1);
   const int nch = (ctx + MK_KCHUNK - 1) / MK_KCHUNK;
 
@@ -660,19 +748,26 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
       sm.rope_c[e] = a.rope_cos[(size_t)pos * a.hd + e];
       sm.rope_s[e] = a.rope_sin[(size_t)pos * a.hd + e];
     }
+    // x past a shard's K meets zero-filled weights and scales: keep it finite
+    for (int e = ct; e < MK_XROW; e += MK_CW * 32) sm.xs_hi[e] = sm.xs_lo[e] = make_uint4(0, 0, 0, 0);
     consumer_sync();
   }
   unsigned seq = 0;
   unsigned stage = 0;
   const unsigned n = gridDim.x;
   const int nwo = geo(a, ST_WO).KS, nwd = geo(a, ST_WDOWN).KS;  // partial sums the norms add
+  const float* pwo = a.psum;                                      // o partials of every rank
+  const float* pwd = a.psum + (size_t)a.tp * MK_MAXKS * a.D;      // down partials of every rank
+  // global (all ranks) barrier count before this step, from the epoch: two per layer
+  const unsigned gbase = epoch * (unsigned)(2 * a.n_layers) * n * (unsigned)a.tp;
+  unsigned gstage = 0;
   bool ok = true;
   for (int l = 0; l < a.n_layers && ok; ++l) {
     const q4b_layer_weights& Lw = a.layers[l];
-    // QKV
-    ok = stage == 0 || stage_wait(a, sm, stage * n);
+    // QKV (after the previous layer's down projection: every rank's partials)
+    ok = l == 0 || global_wait(a, sm, gbase + gstage * n * a.tp);
     if (!ok) break;
-    stage_norm(a, sm, Lw.ln_in, l == 0, token, a.hb, nwd, a.hb + a.D);
+    stage_norm(a, sm, Lw.ln_in, l == 0, token, a.hb, pwd, nwd, a.hb + a.D);
     consumer_sync();
     ok = consume_stage(a, sm, ST_QKV, l, seq, pos);
     stage_arrive(a);
@@ -693,12 +788,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     stage_attn_merge(a, sm, nch);
     consumer_sync();
     ok = consume_stage(a, sm, ST_WO, l, seq, pos);
-    stage_arrive(a);
-    ++stage;
+    global_arrive(a);
+    ++gstage;
     if (!ok) break;
-    // WGU
-    if (!(ok = stage_wait(a, sm, stage * n))) break;
-    stage_norm(a, sm, Lw.ln_post, false, token, a.hb + a.D, nwo, a.hb);
+    // WGU (after every rank's o partials)
+    if (!(ok = global_wait(a, sm, gbase + gstage * n * a.tp))) break;
+    stage_norm(a, sm, Lw.ln_post, false, token, a.hb + a.D, pwo, nwo, a.hb);
     consumer_sync();
     ok = consume_stage(a, sm, ST_WGU, l, seq, pos);
     stage_arrive(a);
@@ -709,13 +804,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     stage_plain(a, sm, a.a, a.I);
     consumer_sync();
     ok = consume_stage(a, sm, ST_WDOWN, l, seq, pos);
-    stage_arrive(a);
-    ++stage;
+    global_arrive(a);
+    ++gstage;
   }
-  if (ok && (ok = stage_wait(a, sm, stage * n))) {
-    stage_norm(a, sm, a.ln_f, false, token, a.hb, nwd, nullptr);
+  if (ok && (ok = global_wait(a, sm, gbase + gstage * n * a.tp))) {
+    stage_norm(a, sm, a.ln_f, false, token, a.hb, pwd, nwd, nullptr);
     consumer_sync();
-    ok = consume_lm(a, sm, seq);
+    ok = consume_lm(a, sm, seq, epoch);
   }
   if (!ok && threadIdx.x == 32) {
     atomicExch(&a.sync[1], 1u);
@@ -727,11 +822,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
 
 // ---- host ----------------------------------------------------------------------------------------
 
+// Shapes of this rank's shard the kernel takes (H, Hkv, I, V are per rank; an o / down shard may end
+// inside a 1024-k unit, whose rest the TMA zero-fills).
 static bool mk_shapes_ok(const Model& m) {
-  return m.cfg.tp_size == 1 && m.hd == MK_HD && m.H % m.Hkv == 0 && m.H / m.Hkv <= MK_ROWS && m.H <= 32 &&
-         m.D <= MK_MAXD &&
-         m.D % MK_UK == 0 && (m.H * m.hd) % MK_UK == 0 && m.I % MK_UK == 0 && m.I <= MK_MAXK && m.D <= MK_MAXK &&
-         m.H * m.hd <= MK_MAXK && m.V % 16 == 0 && m.cfg.max_ctx <= MK_MAXCH * MK_KCHUNK;
+  return m.cfg.tp_size <= MK_MAXTP && (m.cfg.tp_size == 1 || m.comm) && m.hd == MK_HD && m.H % m.Hkv == 0 &&
+         m.H / m.Hkv <= MK_ROWS && m.H <= 32 && m.D <= MK_MAXD && m.D % MK_UK == 0 && (m.H * m.hd) % 128 == 0 &&
+         m.I % 128 == 0 && m.I <= MK_MAXK && m.H * m.hd <= MK_MAXK && m.V % 16 == 0 &&
+         m.cfg.max_ctx <= MK_MAXCH * MK_KCHUNK;
 }
 
 // The persistent kernel is the decode path where its shapes allow; Q4B_PERSISTENT=0 selects the
@@ -753,25 +850,56 @@ int Model::mk_prepare() {
       return set_error(Q4B_EUNSUPPORTED, "persistent decode: group 128 only");
   if (embed.group != 128) return set_error(Q4B_EUNSUPPORTED, "persistent decode: group 128 only");
   std::vector<MkProj> proj(layers.size() * 4 + 1);
-  auto mk = [](MkProj& p, const q4b_qmat& w, bool paired) {
+  mk_scale_pad.resize(proj.size(), nullptr);
+  // scales: fp16 [n, k/G]; the int32 tensor-map helper describes a row as k/G/2 int32 pairs (the box
+  // is 8 groups = 4 pairs = 16 bytes). A tensor map's row stride is a multiple of 16 bytes, so a
+  // shard whose scale rows are not (a tensor-parallel o / down shard: k/G = 12 or 6 or 3) is read
+  // from a copy with rows padded by zero scales to a multiple of 8 groups.
+  auto mk = [&](size_t i, const q4b_qmat& w, bool paired) {
+    MkProj& p = proj[i];
     int r = make_tmap_i32(&p.w, w.qweight, w.k / 8, w.n, w.k / 8, MK_UK / 8, paired ? 8 : 16);
     if (r) return r;
-    // scales: fp16 [n, k/G] as 16-bit elements: the int32 helper is for 4-byte elements, so describe
-    // the scale rows as [n, k/G/2] int32 pairs (the box is 8 groups = 4 pairs = 16 bytes)
-    return make_tmap_i32(&p.s, w.scales, w.k / w.group / 2, w.n, w.k / w.group / 2, 4, paired ? 8 : 16);
+    const int groups = w.k / w.group;
+    if (groups % 8 == 0) return make_tmap_i32(&p.s, w.scales, groups / 2, w.n, groups / 2, 4, paired ? 8 : 16);
+    const int padded = (groups + 7) / 8 * 8;
+    if (!mk_scale_pad[i] && (r = alloc(&mk_scale_pad[i], sizeof(__half) * (size_t)w.n * padded, true))) return r;
+    cudaError_t e = cudaMemcpy2D(mk_scale_pad[i], sizeof(__half) * padded, w.scales, sizeof(__half) * groups,
+                                 sizeof(__half) * groups, w.n, cudaMemcpyDeviceToDevice);
+    if (e != cudaSuccess) return set_error(Q4B_ECUDA, "persistent decode: scale copy: %s", cudaGetErrorString(e));
+    return make_tmap_i32(&p.s, mk_scale_pad[i], (groups + 1) / 2, w.n, padded / 2, 4, paired ? 8 : 16);
   };
   for (size_t l = 0; l < layers.size(); ++l) {
-    if ((rc = mk(proj[4 * l + 0], layers[l].wqkv, true))) return rc;
-    if ((rc = mk(proj[4 * l + 1], layers[l].wo, false))) return rc;
-    if ((rc = mk(proj[4 * l + 2], layers[l].wgu, true))) return rc;
-    if ((rc = mk(proj[4 * l + 3], layers[l].wdown, false))) return rc;
+    if ((rc = mk(4 * l + 0, layers[l].wqkv, true))) return rc;
+    if ((rc = mk(4 * l + 1, layers[l].wo, false))) return rc;
+    if ((rc = mk(4 * l + 2, layers[l].wgu, true))) return rc;
+    if ((rc = mk(4 * l + 3, layers[l].wdown, false))) return rc;
   }
-  if ((rc = mk(proj[4 * layers.size()], embed, false))) return rc;
+  q4b_qmat head = embed;  // this rank's vocab rows of the tied table
+  head.qweight = embed.qweight + (size_t)cfg.tp_rank * V * (D / 8);
+  head.scales = embed.scales + (size_t)cfg.tp_rank * V * (D / embed.group);
+  head.n = V;
+  if ((rc = mk(4 * layers.size(), head, false))) return rc;
   if (!mk_proj && (rc = alloc(&mk_proj, sizeof(MkProj) * proj.size(), false))) return rc;
   if (!mk_layers && (rc = alloc(&mk_layers, sizeof(q4b_layer_weights) * layers.size(), false))) return rc;
   if (!mk_part && (rc = alloc((void**)&mk_part, sizeof(float) * Hkv * MK_MAXCH * MK_ROWS * (hd + MK_PAD), true))) return rc;
-  if (!mk_sync && (rc = alloc((void**)&mk_sync, 2 * sizeof(unsigned), true))) return rc;
-  if (!mk_h && (rc = alloc((void**)&mk_h, sizeof(float) * (2 + MK_MAXKS) * D, true))) return rc;
+  const int t = cfg.tp_size;
+  // sync words [0, 8) and the argmax keys at byte 64; residual ping-pong + every rank's partials
+  if (!mk_sync && (rc = alloc((void**)&mk_sync, 256, true))) return rc;
+  if (!mk_h && (rc = alloc((void**)&mk_h, sizeof(float) * (2 + 2 * (size_t)t * MK_MAXKS) * D, true))) return rc;
+  if ((int)mk_peer_h.size() != t || (int)mk_peer_sync.size() != t) {  // once: the buffers live as long as the model
+    mk_peer_h.assign(t, nullptr);
+    mk_peer_sync.assign(t, nullptr);
+    mk_peer_h[cfg.tp_rank] = mk_h;
+    mk_peer_sync[cfg.tp_rank] = mk_sync;
+    if (t > 1) {  // every peer's buffers mapped into this process (NVLink peer memory)
+      if ((rc = tp_map_peers(mk_h, reinterpret_cast<void**>(mk_peer_h.data()))) ||
+          (rc = tp_map_peers(mk_sync, reinterpret_cast<void**>(mk_peer_sync.data())))) {
+        mk_peer_h.clear();
+        mk_peer_sync.clear();
+        return rc;
+      }
+    }
+  }
   cudaError_t e = cudaMemcpy(mk_proj, proj.data(), sizeof(MkProj) * proj.size(), cudaMemcpyHostToDevice);
   if (e == cudaSuccess)
     e = cudaMemcpy(mk_layers, layers.data(), sizeof(q4b_layer_weights) * layers.size(), cudaMemcpyHostToDevice);
@@ -784,7 +912,6 @@ int Model::mk_prepare() {
   if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, decode_step_kernel, MK_THREADS, smem);
   if (e != cudaSuccess || per < 1)
     return set_error(Q4B_EUNSUPPORTED, "persistent decode: kernel does not fit an SM (%s)", cudaGetErrorString(e));
-  if (D / 16 > 2 * sms) return set_error(Q4B_EUNSUPPORTED, "persistent decode: more than two o / down tiles per SM");
   mk_ctas = sms;
   mk_ready = true;
   return Q4B_OK;
@@ -829,6 +956,16 @@ int Model::mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_
   a.logits = logits;
   a.hb = mk_h;
   a.psum = mk_h + 2 * D;
+  a.tp = cfg.tp_size;
+  a.rank = cfg.tp_rank;
+  a.Vfull = cfg.vocab;
+  for (int r = 0; r < cfg.tp_size; ++r) {
+    a.peer_psum[r] = mk_peer_h[r] + 2 * D;
+    a.peer_sync[r] = mk_peer_sync[r];
+    a.peer_keys[r] = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(mk_peer_sync[r]) + 64);
+  }
+  a.keys = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(mk_sync) + 64);
+  a.wait_ns = cfg.tp_size > 1 ? 5 * kWaitLimitNs : kWaitLimitNs;
   a.q = q;
   a.a = this->a;
   a.part = mk_part;

@@ -312,6 +312,11 @@ extern "C" int q4b_model_step(q4b_model* model, const int32_t* tokens, int n_tok
 
 extern "C" void q4b_model_destroy(q4b_model* model) { delete reinterpret_cast<Model*>(model); }
 
+extern "C" int q4b_model_decode_path(const q4b_model* model) {
+  const Model* m = reinterpret_cast<const Model*>(model);
+  return m && m->mk_ready ? 1 : 0;
+}
+
 extern "C" int q4b_device_status(int reset) {
   const unsigned v = linear_status(reset != 0) | gemm_status(reset != 0);
   return v ? Q4B_ETIMEOUT : Q4B_OK;

@@ -31,7 +31,12 @@ struct Model {
   void* mk_layers = nullptr;
   float* mk_part = nullptr;
   unsigned* mk_sync = nullptr;
-  float* mk_h = nullptr;  // residual ping-pong [2][D] + K-split partials [4][D]
+  float* mk_h = nullptr;  // residual ping-pong [2][D] + every rank's o / down partials [2][tp][3][D]
+  std::vector<float*> mk_peer_h;        // per rank: its mk_h mapped here (own rank: mk_h)
+  std::vector<unsigned*> mk_peer_sync;  // per rank: its mk_sync mapped here
+  std::vector<void*> mk_mapped;         // peer mappings to close
+  std::vector<void*> mk_scale_pad;      // per projection: scale rows padded to 16 bytes (or null)
+  int tp_map_peers(void* local, void** peers);
   int mk_ctas = 0;
   bool mk_ready = false;
   int mk_prepare();

@@ -13,6 +13,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "model.h"
 
@@ -90,7 +91,55 @@ int Model::tp_finish_argmax(int32_t* token_log, cudaStream_t st) {
   return check_launch("argmax_gather");
 }
 
+// Maps every rank's `local` allocation (a cudaMalloc base pointer of the same size on each rank)
+// into this process: the IPC handles are all-gathered over the communicator, every peer's handle is
+// opened with peer access, and peers[rank] receives each rank's mapped pointer (peers[own rank] is
+// left as the caller set it). Collective: every rank calls it in the same order.
+int Model::tp_map_peers(void* local, void** peers) {
+  if (!comm) return set_error(Q4B_ESTATE, "model: tensor parallelism needs q4b_model_attach_tp");
+  const int t = cfg.tp_size;
+  cudaIpcMemHandle_t own;
+  cudaError_t e = cudaIpcGetMemHandle(&own, local);
+  if (e != cudaSuccess) return set_error(Q4B_ECUDA, "tp_map_peers: cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  std::vector<cudaIpcMemHandle_t> all(t);
+  unsigned char* dbuf = nullptr;
+  cudaStream_t st = nullptr;
+  e = cudaMalloc(&dbuf, sizeof(cudaIpcMemHandle_t) * (t + 1));
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMemcpy(dbuf, &own, sizeof(own), cudaMemcpyHostToDevice);
+  int rc = Q4B_OK;
+  if (e != cudaSuccess) {
+    rc = set_error(Q4B_ECUDA, "tp_map_peers: staging: %s", cudaGetErrorString(e));
+  } else {
+    rc = nccl_err(nccl()->all_gather(dbuf, dbuf + sizeof(own), sizeof(own), ncclUint8,
+                                     reinterpret_cast<ncclComm_t>(comm), st),
+                  "allgather(ipc handles)");
+    if (!rc) e = cudaStreamSynchronize(st);
+    if (!rc && e == cudaSuccess) e = cudaMemcpy(all.data(), dbuf + sizeof(own), sizeof(own) * t, cudaMemcpyDeviceToHost);
+    if (!rc && e != cudaSuccess) rc = set_error(Q4B_ECUDA, "tp_map_peers: gather: %s", cudaGetErrorString(e));
+  }
+  if (st) cudaStreamDestroy(st);
+  if (dbuf) cudaFree(dbuf);
+  for (int r = 0; r < t && !rc; ++r) {
+    if (r == cfg.tp_rank) continue;
+    void* p = nullptr;
+    e = cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      rc = set_error(Q4B_ECUDA, "tp_map_peers: cudaIpcOpenMemHandle(rank %d): %s", r, cudaGetErrorString(e));
+      break;
+    }
+    mk_mapped.push_back(p);
+    peers[r] = p;
+  }
+  return rc;
+}
+
 void Model::tp_release() {
+  for (void* p : mk_mapped) cudaIpcCloseMemHandle(p);
+  mk_mapped.clear();
+  mk_peer_h.clear();
+  mk_peer_sync.clear();
+  mk_ready = false;
   if (comm && nccl()) nccl()->comm_destroy(reinterpret_cast<ncclComm_t>(comm));
   comm = nullptr;
 }

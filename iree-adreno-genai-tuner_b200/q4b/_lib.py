@@ -96,6 +96,7 @@ SIGNATURES = {
     "q4b_model_set_head": (c_int, [c_void_p, ctypes.POINTER(QMat), c_void_p, c_void_p, c_void_p]),
     "q4b_model_step": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "q4b_model_destroy": (None, [c_void_p]),
+    "q4b_model_decode_path": (c_int, [c_void_p]),
     "q4b_device_status": (c_int, [c_int]),
     "q4b_tp_unique_id": (c_int, [c_void_p, c_int]),
     "q4b_model_attach_tp": (c_int, [c_void_p, c_void_p, c_int]),

@@ -3,6 +3,7 @@ reference's greedy tokens under both schedules, with graphs on/off and the synch
 Needs >= 2 GPUs (skipped otherwise)."""
 
 import json
+import os
 import pathlib
 import socket
 import subprocess
@@ -22,16 +23,35 @@ def _port():
         return s.getsockname()[1]
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tp2_tiny_ref_tokens():
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr",
-           "127.0.0.1", "--master-port", str(_port()), str(HERE / "tp_gpu_worker.py")]
-    r = subprocess.run(cmd, capture_output=True, text=True, timeout=600,
-                       env={**__import__("os").environ, "NCCL_NVLS_ENABLE": "0"})
+def _run(world, **env):
+    cmd = ["timeout", "-k", "60", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           str(HERE / "tp_gpu_worker.py")]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=700,
+                       env={**os.environ, "NCCL_NVLS_ENABLE": "0", **env})
     line = [ln for ln in r.stdout.splitlines() if ln.startswith("TP_RESULT ")]
     assert r.returncode == 0 and line, r.stderr[-3000:]
-    out = json.loads(line[0][len("TP_RESULT "):])
+    return json.loads(line[0][len("TP_RESULT "):])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_tiny_ref_tokens():
+    out = _run(2)
     z = np.load(HERE / "golden" / "model_tiny_ref.npz")
     for key, toks in out.items():
         schedule = key.split("_")[0]
         assert toks == z[f"{schedule}_tokens"].tolist(), key
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_persistent_decode():
+    """The persistent step over 2 GPUs (partial sums pushed to peer memory, one launch per token per
+    GPU) against the per-projection tp path and the single-GPU model."""
+    out = _run(2, Q4B_TP_MODE="persistent")
+    assert any("decode_step_kernel" in k for k in out["kernels"]), out["kernels"]
+    assert not any("q4_gemv" in k for k in out["kernels"]), out["kernels"]
+    assert out["status"] == 0
+    assert out["tokens_on"] == out["tokens_off"] == out["tokens_single"]
+    assert out["diff_on_off"] <= 1e-3 * out["scale"]
+    assert out["diff_single"] <= 1e-3 * out["scale"]
+    assert out["graphs_on"] == out["graphs_off"]

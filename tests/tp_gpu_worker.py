@@ -1,6 +1,7 @@
-"""One rank of the tensor-parallel GPU parity check (launched by tests/test_tp_gpu.py under
-torch.distributed.run): builds the reference's tiny KAT model (HF random init, seed 0) sharded
-over the ranks, runs the llm_runner.c schedule, and rank 0 prints the tokens as JSON."""
+"""One rank of the tensor-parallel GPU parity checks (launched by tests/test_tp_gpu.py under
+torch.distributed.run). Default: builds the reference's tiny KAT model (HF random init, seed 0)
+sharded over the ranks, runs the llm_runner.c schedule, and rank 0 prints the tokens as JSON.
+Q4B_TP_MODE=persistent: the persistent decode step sharded over the ranks (see persistent_main)."""
 
 import json
 import os
@@ -17,11 +18,95 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 
+# the persistent decode step's smallest shape (head_dim 128, D a multiple of 1024); the o / down
+# shards of 2 ranks (K 512 and 1024) cover a partial 1024-k unit and the padded scale rows
+PCFG = dict(hidden_size=1024, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2, head_dim=128,
+            intermediate_size=2048, vocab_size=4096, rms_norm_eps=1e-5, rope_theta=500000.0,
+            max_position_embeddings=4096, tie_word_embeddings=True, hidden_act="silu", attention_bias=False,
+            initializer_range=0.2)
+PROMPT, STEPS = 40, 12
+
+
+def _persistent_decode(model, persistent, gather):
+    """Prefill (per-projection path), then STEPS decode steps: (tokens, full-vocab logits per step)."""
+    os.environ["Q4B_PERSISTENT"] = "1" if persistent else "0"
+    caches = model.new_caches()
+    p = np.random.default_rng(7).integers(0, PCFG["vocab_size"], PROMPT).astype(np.int32)
+    dev = caches[0].device
+    nxt, _ = model.step(torch.from_numpy(p).reshape(1, -1), torch.tensor([0]), torch.tensor([PROMPT - 1]), caches, 64)
+    toks, logits = [int(nxt)], []
+    for i in range(STEPS):
+        pos = PROMPT + i
+        L = 64 if pos < 64 else 128
+        nxt, lg = model.step(nxt.reshape(1, 1), torch.tensor([pos]), torch.tensor([0]), caches, L)
+        toks.append(int(nxt))
+        logits.append(gather(lg.to(dev)).cpu().numpy()[0])
+    return toks, np.stack(logits)
+
+
+def persistent_main(rank, world, dev):
+    """tp=world persistent decode (peer-memory partial sums, one launch per token) against the
+    per-projection tp path (NCCL) and, on rank 0, the single-GPU model: tokens equal, logits within
+    1e-3 of max|logit|; the runner's graphs give the same tokens with the persistent step on / off."""
+    import q4b
+    from q4b import _lib
+
+    def gather(lg):
+        parts = [torch.empty_like(lg) for _ in range(world)]
+        dist.all_gather(parts, lg.contiguous())
+        return torch.cat(parts, dim=1)
+
+    sd = q4b.SyntheticStateDict(PCFG, seed=5)
+    model = q4b.LlamaQ4(None, group=128, max_ctx=1024, vocab_chunk=PCFG["vocab_size"], sd=sd, cfg=PCFG,
+                        max_chunk=64, tp_rank=rank, tp_size=world, device=dev)
+    model.attach_tp()
+    t_on, l_on = _persistent_decode(model, True, gather)
+    kernels = _one_step_kernels(model)
+    t_off, l_off = _persistent_decode(model, False, gather)
+    status = int(_lib.lib().q4b_device_status(1))
+    prompt = np.random.default_rng(7).integers(0, PCFG["vocab_size"], PROMPT).tolist()
+    graphs = {}
+    for on in (True, False):
+        os.environ["Q4B_PERSISTENT"] = "1" if on else "0"
+        r = q4b.Runner(model, 16, [64, 128, 256], "bucketed", graphs=True)
+        graphs[on], _ = r.generate(prompt, 24)
+        del r
+    out = dict(tokens_on=t_on, tokens_off=t_off, graphs_on=graphs[True], graphs_off=graphs[False],
+               diff_on_off=float(np.abs(l_on - l_off).max()), scale=float(max(1.0, np.abs(l_off).max())),
+               status=status, kernels=sorted(kernels))
+    if rank == 0:
+        single = q4b.LlamaQ4(None, group=128, max_ctx=1024, vocab_chunk=PCFG["vocab_size"], sd=sd, cfg=PCFG,
+                             max_chunk=64, device=dev)
+        t1, l1 = _persistent_decode(single, True, lambda x: x)
+        out.update(tokens_single=t1, diff_single=float(np.abs(l_on - l1).max()))
+    return out
+
+
+def _one_step_kernels(model):
+    from torch.profiler import ProfilerActivity, profile
+    os.environ["Q4B_PERSISTENT"] = "1"
+    caches = model.new_caches()
+    model.step(torch.tensor([[3]], dtype=torch.int32), torch.tensor([5]), torch.tensor([0]), caches, 64)
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        model.step(torch.tensor([[3]], dtype=torch.int32), torch.tensor([6]), torch.tensor([0]), caches, 64)
+        torch.cuda.synchronize()
+    return {e.name for e in prof.events() if e.device_type.name == "CUDA"}
+
+
 def main():
     rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    if os.environ.get("Q4B_TP_MODE") == "persistent":
+        out = persistent_main(rank, world, dev)
+        torch.cuda.synchronize()
+        dist.barrier()
+        if rank == 0:
+            print("TP_RESULT " + json.dumps(out), flush=True)
+        dist.destroy_process_group()
+        return
     import golden_inputs as gi
     import q4b
     from transformers import LlamaConfig, LlamaForCausalLM
