@@ -113,16 +113,22 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 // Wait for phase `parity` of the barrier, giving up after `limit_ns`; false on timeout.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// The timer is read only once the phase is not complete at the first try (the common case in a
+// streaming loop is a ready slot).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
-    uint32_t done;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    if (done) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     if (globaltimer_ns() - t0 > limit_ns) return false;
   }
 }

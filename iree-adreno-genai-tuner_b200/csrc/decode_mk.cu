@@ -51,7 +51,8 @@ constexpr int MK_MAXCH = 64;                   // attention chunks (contexts up 
 constexpr int MK_ROWS = 4;                     // query rows per KV head (GQA group) at most
 constexpr int MK_TB = 8;                       // tiles of one stage per batched epilogue
 constexpr int MK_MAXKS = 3;                    // K splits of the o / down projections
-constexpr int MK_MAXTP = 8;                    // tensor-parallel ranks
+constexpr int MK_MAXTP = 8;
+constexpr int MK_MAXL = 128;                   // layers                    // tensor-parallel ranks
 constexpr int MK_MAXD = 4096;                  // hidden size: at most two staged words per thread
 constexpr int MK_PAD = 4;                      // partial row: m, l and two pad floats before o (16-B aligned)
 
@@ -84,7 +85,9 @@ struct MkArgs {
   float* q;      // [H * hd]
   float* a;      // [I]
   float* part;   // attention partials [Hkv][MK_MAXCH][MK_ROWS][hd + 4]: m, l, -, -, o[hd]
-  unsigned* sync;  // [0] local stage arrivals, [1] abort, [2] arrivals of all ranks, [3] lm keys, [4] epoch
+  // [0] local stage arrivals, [1] abort, [2] local arrivals at cross-rank barriers (these three are
+  // zeroed per launch); [3] cross-rank barrier count, [4] lm key arrivals, [5] step epoch (never reset)
+  unsigned* sync;
   // tensor parallelism: this rank of tp; the peers' psum / sync / key buffers (peer memory mapped
   // into this process; index rank = this GPU's own)
   int tp, rank, Vfull;
@@ -108,6 +111,12 @@ struct MkSmem {
   float att_m[MK_CW][MK_ROWS], att_l[MK_CW][MK_ROWS];
   float att_cs[MK_CW][MK_ROWS];
   unsigned long long best[MK_CW];
+  // per layer: KV cache and norm weight pointers (read once at kernel start, not chased through
+  // the layer table in global memory at every use)
+  __half* kcache[MK_MAXL];
+  __half* vcache[MK_MAXL];
+  const float* ln_in[MK_MAXL];
+  const float* ln_post[MK_MAXL];
   uint64_t full[MK_NSLOT], empty[MK_NSLOT];
   int abort_flag;
   int last;
@@ -140,9 +149,12 @@ __device__ float consumer_sum(float v, float* scratch) {
 __device__ bool stage_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
   if (threadIdx.x == 32) {
     const uint64_t t0 = globaltimer_ns();
-    while (ld_acquire(&a.sync[0]) < target) {
-      __nanosleep(32);
-      if (ld_acquire(&a.sync[1])) {
+    for (;;) {
+      // sync[0] (arrivals) and sync[1] (abort) in one acquire load
+      unsigned long long both;
+      asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(both) : "l"(a.sync) : "memory");
+      if ((unsigned)both >= target) break;
+      if (both >> 32) {
         sm.abort_flag = 1;
         break;
       }
@@ -159,27 +171,28 @@ __device__ bool stage_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
 // Stage-end arrival: all consumer writes of this stage happen before the gpu-scope release.
 __device__ void stage_arrive(const MkArgs& a) {
   consumer_sync();
-  if (threadIdx.x == 32) {
-    __threadfence();
+  if (threadIdx.x == 32)  // release: cumulative over the CTA's writes ordered by the barrier above
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync) : "memory");
-  }
 }
 
 // Barrier over every CTA of every rank (after the row-split o / down projections, whose partial sums
-// go to the peers): each CTA adds 1 to every rank's counter after a system-scope fence, then waits
-// for its own counter. The counter is never reset (peers may add to it before this rank's step has
-// started), so targets count from the step's epoch.
+// go to the peers). One GPU: every CTA adds 1 to the counter sync[3] and waits for n more per
+// barrier. Several: every CTA makes its pushes visible system-wide and adds 1 to this rank's local
+// count sync[2]; the CTA that completes it adds 1 to every rank's sync[3], so each barrier adds tp
+// there (one NVLink atomic per rank pair instead of one per CTA). sync[3] is never reset (peers may
+// add to it before this rank's step has started), so targets count from the step's epoch.
 __device__ bool global_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
   if (threadIdx.x == 32) {
     const uint64_t t0 = globaltimer_ns();
+    unsigned polls = 0;
     for (;;) {
       unsigned v;
       if (a.tp > 1)
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 2) : "memory");
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 3) : "memory");
       else
-        v = ld_acquire(a.sync + 2);
+        v = ld_acquire(a.sync + 3);
       if ((int)(v - target) >= 0) break;
-      __nanosleep(32);
+      if ((++polls & 31) != 0) continue;  // the abort word and the clock every 32 polls
       if (ld_acquire(&a.sync[1])) {
         sm.abort_flag = 1;
         break;
@@ -194,16 +207,19 @@ __device__ bool global_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
   consumer_sync();
   return !sm.abort_flag;
 }
-__device__ void global_arrive(const MkArgs& a) {
+// gstage: global barriers this launch has passed before this one
+__device__ void global_arrive(const MkArgs& a, unsigned gstage) {
   consumer_sync();
   if (threadIdx.x == 32) {
     if (a.tp > 1) {
       __threadfence_system();
-      for (int r = 0; r < a.tp; ++r)
-        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.peer_sync[r] + 2) : "memory");
+      unsigned old;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.sync + 2) : "memory");
+      if (old == (gstage + 1) * gridDim.x - 1)
+        for (int r = 0; r < a.tp; ++r)
+          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.peer_sync[r] + 3) : "memory");
     } else {
-      __threadfence();
-      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync + 2) : "memory");
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync + 3) : "memory");
     }
   }
 }
@@ -251,6 +267,7 @@ __device__ bool produce_stage(const MkArgs& a, MkSmem& sm, const MkProj& pj, int
   tma_prefetch_map(&pj.w);
   tma_prefetch_map(&pj.s);
   const int upi = gp.NU / gp.KS;  // units per item
+  const uint64_t pol = l2_policy_evict_first();  // weights are read once per token
   for (int it = blockIdx.x; it < gp.RT * gp.KS; it += gridDim.x) {
     const int rt = it / gp.KS, ks = it - rt * gp.KS;
     for (int u = ks * upi; u < (ks + 1) * upi; ++u, ++seq) {
@@ -261,15 +278,29 @@ __device__ bool produce_stage(const MkArgs& a, MkSmem& sm, const MkProj& pj, int
       mbar_arrive_expect_tx(&sm.full[slot], MK_SLOT);
       if (gp.paired) {
         const int r0 = pair_row(a, st, rt, 0), r1 = pair_row(a, st, rt, 1);
-        tma_load_2d(dst, &pj.w, u * (MK_UK / 8), r0, &sm.full[slot]);
-        tma_load_2d(dst + MK_WBYTES / 2, &pj.w, u * (MK_UK / 8), r1, &sm.full[slot]);
-        tma_load_2d(dst + MK_WBYTES, &pj.s, u * 4, r0, &sm.full[slot]);
-        tma_load_2d(dst + MK_WBYTES + 128, &pj.s, u * 4, r1, &sm.full[slot]);
+        tma_load_2d_hint(dst, &pj.w, u * (MK_UK / 8), r0, &sm.full[slot], pol);
+        tma_load_2d_hint(dst + MK_WBYTES / 2, &pj.w, u * (MK_UK / 8), r1, &sm.full[slot], pol);
+        tma_load_2d_hint(dst + MK_WBYTES, &pj.s, u * 4, r0, &sm.full[slot], pol);
+        tma_load_2d_hint(dst + MK_WBYTES + 128, &pj.s, u * 4, r1, &sm.full[slot], pol);
       } else {
-        tma_load_2d(dst, &pj.w, u * (MK_UK / 8), rt * 16, &sm.full[slot]);
-        tma_load_2d(dst + MK_WBYTES, &pj.s, u * 4, rt * 16, &sm.full[slot]);
+        tma_load_2d_hint(dst, &pj.w, u * (MK_UK / 8), rt * 16, &sm.full[slot], pol);
+        tma_load_2d_hint(dst + MK_WBYTES, &pj.s, u * 4, rt * 16, &sm.full[slot], pol);
       }
     }
+  }
+  return true;
+}
+
+// The o projection's weights are requested once the layer's attention stage is over: attention is a
+// few dependent KV-cache loads per item, and a weight stream requested at the same moment (a full
+// ring on every SM) queues ahead of them in HBM. The o weights (a sixth of a layer) then stream in
+// while the attention output is merged.
+__device__ bool producer_gate(const MkArgs& a, MkSmem& sm, unsigned target) {
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire(&a.sync[0]) < target) {
+    __nanosleep(64);
+    if (sm.abort_flag || ld_acquire(&a.sync[1])) return false;
+    if (globaltimer_ns() - t0 > a.wait_ns) return false;
   }
   return true;
 }
@@ -330,22 +361,37 @@ __device__ __forceinline__ void norm_src(const MkArgs& a, int w, bool embed, int
 
 // x = rmsnorm(h) * w (rms_norm, llama_q4.py:141-142). With hdst the updated residual stream is also
 // written (each word by one CTA) to the other ping-pong buffer.
-__device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float* lnw, bool embed, int token, const float* hsrc,
-                           const float* psrc, int nparts, float* hdst) {
+// This thread's (at most two) words of a norm weight: loaded before the stage's barrier wait.
+__device__ __forceinline__ void norm_weights(const MkArgs& a, const float* lnw, float (&lw)[2][8]) {
   const int ct = threadIdx.x - 32;
-  const int words = a.D / 8;
-  // one round of loads: this thread's (at most two) words of h (+ partials) and of the norm weight
-  float v[2][8], lw[2][8];
-  float ss = 0.0f;
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int w = ct + i * (MK_CW * 32);
-    if (w < words) {
-      norm_src(a, w, embed, token, hsrc, psrc, nparts, v[i]);
+    if (w < a.D / 8) {
       const float4 w0 = *reinterpret_cast<const float4*>(lnw + 8 * w);
       const float4 w1 = *reinterpret_cast<const float4*>(lnw + 8 * w + 4);
       lw[i][0] = w0.x; lw[i][1] = w0.y; lw[i][2] = w0.z; lw[i][3] = w0.w;
       lw[i][4] = w1.x; lw[i][5] = w1.y; lw[i][6] = w1.z; lw[i][7] = w1.w;
+    }
+  }
+}
+
+__device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float (&lw)[2][8], bool embed, int token,
+                           const float* hsrc, const float* psrc, int nparts, float* hdst) {
+  const int ct = threadIdx.x - 32;
+  const int words = a.D / 8;
+  // one round of loads: this thread's (at most two) words of h (+ partials)
+  float v[2][8];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {  // every load before any store (the stores may alias nothing read,
+    const int w = ct + i * (MK_CW * 32);  // but the compiler cannot know)
+    if (w < words) norm_src(a, w, embed, token, hsrc, psrc, nparts, v[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int w = ct + i * (MK_CW * 32);
+    if (w < words) {
 #pragma unroll
       for (int b = 0; b < 8; ++b) ss += v[i][b] * v[i][b];
       if (hdst && w % (int)gridDim.x == (int)blockIdx.x) {
@@ -436,7 +482,6 @@ __device__ void pair_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, in
   if (st == ST_QKV) {
     const int per = a.hd / 16, head = rt / per, jj = rt - head * per;
     const int e1 = jj * 8 + s, e2 = a.hd / 2 + jj * 8 + s;
-    const q4b_layer_weights& Lw = a.layers[layer];
     if (head < a.H + a.Hkv) {
       // q * cos + rotate_half(q) * sin, rotate_half(x) = cat(-x[h:], x[:h]) (llama_q4.py:195-221)
       const float o1 = __fadd_rn(__fmul_rn(v0, sm.rope_c[e1]), __fmul_rn(-v1, sm.rope_s[e1]));
@@ -445,12 +490,12 @@ __device__ void pair_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, in
         a.q[head * a.hd + e1] = o1;
         a.q[head * a.hd + e2] = o2;
       } else {
-        __half* kc = reinterpret_cast<__half*>(Lw.k_cache) + ((size_t)pos * a.Hkv + (head - a.H)) * a.hd;
+        __half* kc = sm.kcache[layer] + ((size_t)pos * a.Hkv + (head - a.H)) * a.hd;
         kc[e1] = __float2half_rn(o1);
         kc[e2] = __float2half_rn(o2);
       }
     } else {
-      __half* vc = reinterpret_cast<__half*>(Lw.v_cache) + ((size_t)pos * a.Hkv + (head - a.H - a.Hkv)) * a.hd;
+      __half* vc = sm.vcache[layer] + ((size_t)pos * a.Hkv + (head - a.H - a.Hkv)) * a.hd;
       vc[e1] = __float2half_rn(v0);
       vc[e2] = __float2half_rn(v1);
     }
@@ -584,12 +629,12 @@ __device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq, unsigned 
         for (int r = 0; r < a.tp; ++r) a.peer_keys[r][a.rank] = bb;
         __threadfence_system();
         for (int r = 0; r < a.tp; ++r)
-          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.peer_sync[r] + 3) : "memory");
+          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.peer_sync[r] + 4) : "memory");
         const unsigned target = (epoch + 1) * (unsigned)a.tp;  // epoch-based: never reset
         const uint64_t t0 = globaltimer_ns();
         for (;;) {
           unsigned v;
-          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 3) : "memory");
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 4) : "memory");
           if ((int)(v - target) >= 0) break;
           if (globaltimer_ns() - t0 > a.wait_ns) {
             a.state->status = 1;
@@ -600,11 +645,12 @@ __device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq, unsigned 
         for (int r = 0; r < a.tp; ++r) bb = max(bb, *(volatile unsigned long long*)&a.keys[r]);
       }
       publish_token(a.state, a.token_log, (int32_t)argmax_index(bb));
-      a.sync[4] += 1u;  // this rank's step epoch (every rank runs every step)
+      a.sync[5] += 1u;  // this rank's step epoch (every rank runs every step)
     }
   }
   return true;
 }
+
 
 // Attention item (query row r of KV head kvh's group, keys [256 ch, 256 ch + 256) of ctx): the
 // chunk's (max, sum, weighted V) for that row -- the online-softmax pieces of attn_decode_kernel.
@@ -614,9 +660,8 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
   constexpr int HD = MK_HD, EPL = HD / 32, KU4 = HD / 8;
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
   const int g = a.H / a.Hkv;
-  const q4b_layer_weights& Lw = a.layers[layer];
-  const __half* kc = reinterpret_cast<const __half*>(Lw.k_cache);
-  const __half* vc = reinterpret_cast<const __half*>(Lw.v_cache);
+  const __half* kc = sm.kcache[layer];
+  const __half* vc = sm.vcache[layer];
   const size_t row_stride = (size_t)a.Hkv * HD;
   const int k0 = ch * MK_KCHUNK, k1 = min(k0 + MK_KCHUNK, ctx);
   const int jbase = k0 + 32 * w, j = jbase + lane;
@@ -717,7 +762,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
   __syncthreads();
   const int pos = a.state->start;
   const int token = *a.token;
-  const unsigned epoch = *(volatile unsigned*)&a.sync[4];
+  const unsigned epoch = *(volatile unsigned*)&a.sync[5];
   const int ctx = min(a.L, pos + 1);
   const int nch = (ctx + MK_KCHUNK - 1) / MK_KCHUNK;
 
@@ -726,13 +771,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     unsigned seq = 0;
     if (lane == 0) {
       bool ok = true;
-      for (int l = 0; l < a.n_layers && ok; ++l) {
-        ok = ok && produce_stage(a, sm, a.proj[4 * l + 0], ST_QKV, seq);
-        ok = ok && produce_stage(a, sm, a.proj[4 * l + 1], ST_WO, seq);
-        ok = ok && produce_stage(a, sm, a.proj[4 * l + 2], ST_WGU, seq);
-        ok = ok && produce_stage(a, sm, a.proj[4 * l + 3], ST_WDOWN, seq);
+      // projections in consumption order: per layer q|k|v, o, gate|up, down; then the lm_head
+      const int nproj = 4 * a.n_layers + 1;
+      const auto kind = [&](int i) {
+        constexpr int per_layer[4] = {ST_QKV, ST_WO, ST_WGU, ST_WDOWN};
+        return i == 4 * a.n_layers ? (int)ST_PER_LAYER : per_layer[i & 3];
+      };
+      for (int i = 0; i < nproj && ok; ++i) {
+        // local stage arrivals: q|k|v, attention, gate|up per layer (n CTAs each)
+        if (kind(i) == ST_WO) ok = producer_gate(a, sm, (3u * (i >> 2) + 2u) * gridDim.x);
+        ok = ok && produce_stage(a, sm, a.proj[i], kind(i), seq);
       }
-      ok = ok && produce_stage(a, sm, a.proj[4 * a.n_layers], ST_PER_LAYER, seq);
       if (!ok) {
         atomicExch(&a.sync[1], 1u);
         sm.abort_flag = 1;
@@ -748,6 +797,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
       sm.rope_c[e] = a.rope_cos[(size_t)pos * a.hd + e];
       sm.rope_s[e] = a.rope_sin[(size_t)pos * a.hd + e];
     }
+    for (int l = ct; l < a.n_layers; l += MK_CW * 32) {
+      sm.kcache[l] = reinterpret_cast<__half*>(a.layers[l].k_cache);
+      sm.vcache[l] = reinterpret_cast<__half*>(a.layers[l].v_cache);
+      sm.ln_in[l] = a.layers[l].ln_in;
+      sm.ln_post[l] = a.layers[l].ln_post;
+    }
     // x past a shard's K meets zero-filled weights and scales: keep it finite
     for (int e = ct; e < MK_XROW; e += MK_CW * 32) sm.xs_hi[e] = sm.xs_lo[e] = make_uint4(0, 0, 0, 0);
     consumer_sync();
@@ -758,16 +813,19 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
   const int nwo = geo(a, ST_WO).KS, nwd = geo(a, ST_WDOWN).KS;  // partial sums the norms add
   const float* pwo = a.psum;                                      // o partials of every rank
   const float* pwd = a.psum + (size_t)a.tp * MK_MAXKS * a.D;      // down partials of every rank
-  // global (all ranks) barrier count before this step, from the epoch: two per layer
-  const unsigned gbase = epoch * (unsigned)(2 * a.n_layers) * n * (unsigned)a.tp;
+  // global (all ranks) barrier count before this step, from the epoch: two barriers per layer, each
+  // adding n (one GPU) or tp (one per rank)
+  const unsigned gunit = a.tp > 1 ? (unsigned)a.tp : n;
+  const unsigned gbase = epoch * (unsigned)(2 * a.n_layers) * gunit;
   unsigned gstage = 0;
   bool ok = true;
+  float lw[2][8];  // the next norm's weights
   for (int l = 0; l < a.n_layers && ok; ++l) {
-    const q4b_layer_weights& Lw = a.layers[l];
     // QKV (after the previous layer's down projection: every rank's partials)
-    ok = l == 0 || global_wait(a, sm, gbase + gstage * n * a.tp);
+    norm_weights(a, sm.ln_in[l], lw);
+    ok = l == 0 || global_wait(a, sm, gbase + gstage * gunit);
     if (!ok) break;
-    stage_norm(a, sm, Lw.ln_in, l == 0, token, a.hb, pwd, nwd, a.hb + a.D);
+    stage_norm(a, sm, lw, l == 0, token, a.hb, pwd, nwd, a.hb + a.D);
     consumer_sync();
     ok = consume_stage(a, sm, ST_QKV, l, seq, pos);
     stage_arrive(a);
@@ -788,12 +846,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     stage_attn_merge(a, sm, nch);
     consumer_sync();
     ok = consume_stage(a, sm, ST_WO, l, seq, pos);
-    global_arrive(a);
+    global_arrive(a, gstage);
     ++gstage;
     if (!ok) break;
     // WGU (after every rank's o partials)
-    if (!(ok = global_wait(a, sm, gbase + gstage * n * a.tp))) break;
-    stage_norm(a, sm, Lw.ln_post, false, token, a.hb + a.D, pwo, nwo, a.hb);
+    norm_weights(a, sm.ln_post[l], lw);
+    if (!(ok = global_wait(a, sm, gbase + gstage * gunit))) break;
+    stage_norm(a, sm, lw, false, token, a.hb + a.D, pwo, nwo, a.hb);
     consumer_sync();
     ok = consume_stage(a, sm, ST_WGU, l, seq, pos);
     stage_arrive(a);
@@ -804,11 +863,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     stage_plain(a, sm, a.a, a.I);
     consumer_sync();
     ok = consume_stage(a, sm, ST_WDOWN, l, seq, pos);
-    global_arrive(a);
+    global_arrive(a, gstage);
     ++gstage;
   }
-  if (ok && (ok = global_wait(a, sm, gbase + gstage * n * a.tp))) {
-    stage_norm(a, sm, a.ln_f, false, token, a.hb, pwd, nwd, nullptr);
+  if (ok) norm_weights(a, a.ln_f, lw);
+  if (ok && (ok = global_wait(a, sm, gbase + gstage * gunit))) {
+    stage_norm(a, sm, lw, false, token, a.hb, pwd, nwd, nullptr);
     consumer_sync();
     ok = consume_lm(a, sm, seq, epoch);
   }
@@ -825,7 +885,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
 // Shapes of this rank's shard the kernel takes (H, Hkv, I, V are per rank; an o / down shard may end
 // inside a 1024-k unit, whose rest the TMA zero-fills).
 static bool mk_shapes_ok(const Model& m) {
-  return m.cfg.tp_size <= MK_MAXTP && (m.cfg.tp_size == 1 || m.comm) && m.hd == MK_HD && m.H % m.Hkv == 0 &&
+  return m.cfg.tp_size <= MK_MAXTP && (int)m.layers.size() <= MK_MAXL && (m.cfg.tp_size == 1 || m.comm) && m.hd == MK_HD && m.H % m.Hkv == 0 &&
          m.H / m.Hkv <= MK_ROWS && m.H <= 32 && m.D <= MK_MAXD && m.D % MK_UK == 0 && (m.H * m.hd) % 128 == 0 &&
          m.I % 128 == 0 && m.I <= MK_MAXK && m.H * m.hd <= MK_MAXK && m.V % 16 == 0 &&
          m.cfg.max_ctx <= MK_MAXCH * MK_KCHUNK;
@@ -930,7 +990,7 @@ bool Model::mk_usable(int C, cudaStream_t st) {
 }
 
 int Model::mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_log, cudaStream_t st) {
-  cudaError_t e = cudaMemsetAsync(mk_sync, 0, 2 * sizeof(unsigned), st);
+  cudaError_t e = cudaMemsetAsync(mk_sync, 0, 3 * sizeof(unsigned), st);
   if (e != cudaSuccess) return set_error(Q4B_ECUDA, "persistent decode: reset: %s", cudaGetErrorString(e));
   MkArgs a = {};
   a.proj = reinterpret_cast<const MkProj*>(mk_proj);
