@@ -8,7 +8,7 @@
 // waiting for activations), while eight consumer warps follow through the dependency chain:
 //
 //   per layer  QKV  (RMSNorm of h fused into the x staging; RoPE + fp16 KV-cache write epilogue)
-//              ATTN (split-key GQA over the cache: (KV head, 256-key chunk) items)
+//              ATTN (split-key GQA over the cache: (query row, 128-key chunk) items)
 //              WO   (merge of the attention partials fused into the x staging; h += o Wo^T)
 //              WGU  (RMSNorm; SwiGLU epilogue into a)
 //              WDOWN (h += a Wdown^T)
@@ -46,8 +46,8 @@ constexpr int MK_MAXK = 8192;
 constexpr int MK_XROW = MK_MAXK / 8 + 4;       // staged x: uint4 per row (+64 B, as kernel 1)
 constexpr int MK_HD = 128;
 static_assert(MK_HD <= MK_CW * 32, "one query element per consumer thread");
-constexpr int MK_KCHUNK = 256;                 // keys per attention item (8 warps x 32)
-constexpr int MK_MAXCH = 64;                   // attention chunks (contexts up to 16384)
+constexpr int MK_KCHUNK = 128;                 // keys per attention item (8 warps x 16)
+constexpr int MK_MAXCH = 128;                  // attention chunks (contexts up to 16384)
 constexpr int MK_ROWS = 4;                     // query rows per KV head (GQA group) at most
 constexpr int MK_TB = 8;                       // tiles of one stage per batched epilogue
 constexpr int MK_MAXKS = 3;                    // K splits of the o / down projections
@@ -85,6 +85,8 @@ struct MkArgs {
   float* q;      // [H * hd]
   float* a;      // [I]
   float* part;   // attention partials [Hkv][MK_MAXCH][MK_ROWS][hd + 4]: m, l, -, -, o[hd]
+  unsigned* rowcnt;  // [H] chunks of each query row done in this layer (the last one merges)
+  float* attn_out;   // [H * hd] the attention output (the o projection's x)
   // [0] local stage arrivals, [1] abort, [2] local arrivals at cross-rank barriers (these three are
   // zeroed per launch); [3] cross-rank barrier count, [4] lm key arrivals, [5] step epoch (never reset)
   unsigned* sync;
@@ -120,6 +122,7 @@ struct MkSmem {
   uint64_t full[MK_NSLOT], empty[MK_NSLOT];
   int abort_flag;
   int last;
+  int att_last;
 };
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
@@ -426,53 +429,6 @@ __device__ void stage_plain(const MkArgs& a, MkSmem& sm, const float* src, int K
   }
 }
 
-// x = attention output o [H * hd]: the chunk partials of every head merged (max, sum, weighted V),
-// online over the chunks; the (max, sum) pair and the 8 elements of each chunk are loaded together,
-// four chunks per round (one round up to 1024 keys).
-__device__ void stage_attn_merge(const MkArgs& a, MkSmem& sm, int nch) {
-  const int ct = threadIdx.x - 32;
-  const int g = a.H / a.Hkv, HD = a.hd;
-  const size_t PS = HD + MK_PAD;
-  for (int w = ct; w < a.H * HD / 8; w += MK_CW * 32) {
-    const int hq = (8 * w) / HD, e0 = 8 * w - hq * HD;
-    const int kvh = hq / g, r = hq - kvh * g;
-    const float* base = a.part + ((size_t)kvh * MK_MAXCH * MK_ROWS + r) * PS;
-    float M = -INFINITY, Lsum = 0.0f;
-    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int c0 = 0; c0 < nch; c0 += 2) {
-      float2 ml[2];
-      float4 p0[2], p1[2];
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        if (c0 + k < nch) {
-          const float* pc = base + (size_t)(c0 + k) * MK_ROWS * PS;
-          ml[k] = __ldcg(reinterpret_cast<const float2*>(pc));
-          p0[k] = __ldcg(reinterpret_cast<const float4*>(pc + MK_PAD + e0));
-          p1[k] = __ldcg(reinterpret_cast<const float4*>(pc + MK_PAD + e0) + 1);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        if (c0 + k < nch && ml[k].x != -INFINITY) {
-          if (ml[k].x > M) {  // rescale what was merged so far to the new maximum
-            const float rs = M == -INFINITY ? 0.0f : expf(M - ml[k].x);
-            Lsum *= rs;
-#pragma unroll
-            for (int b = 0; b < 8; ++b) v[b] *= rs;
-            M = ml[k].x;
-          }
-          const float cs = expf(ml[k].x - M);
-          Lsum += ml[k].y * cs;
-          v[0] += cs * p0[k].x; v[1] += cs * p0[k].y; v[2] += cs * p0[k].z; v[3] += cs * p0[k].w;
-          v[4] += cs * p1[k].x; v[5] += cs * p1[k].y; v[6] += cs * p1[k].z; v[7] += cs * p1[k].w;
-        }
-      }
-    }
-#pragma unroll
-    for (int b = 0; b < 8; ++b) v[b] = v[b] / Lsum;
-    stage_word(sm, w, v);
-  }
-}
 
 // ---- consumers: projections ------------------------------------------------------------------
 
@@ -652,65 +608,60 @@ __device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq, unsigned 
 }
 
 
-// Attention item (query row r of KV head kvh's group, keys [256 ch, 256 ch + 256) of ctx): the
+// Attention item (query row r of KV head kvh's group, keys [128 ch, 128 ch + 128) of ctx): the
 // chunk's (max, sum, weighted V) for that row -- the online-softmax pieces of attn_decode_kernel.
 // One row per item spreads a layer's attention over three times as many CTAs as one item per KV
 // head (the rows of a group share K and V, which L2 serves again).
-__device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int ch, int r, int ctx) {
-  constexpr int HD = MK_HD, EPL = HD / 32, KU4 = HD / 8;
+__device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int ch, int r, int ctx, int nch) {
+  constexpr int HD = MK_HD, EPL = HD / 32, KW = MK_KCHUNK / MK_CW;  // KW keys per warp (16)
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
+  const int kk = lane >> 1, hh = lane & 1;  // scores: two lanes per key, alternate 16-byte pieces
   const int g = a.H / a.Hkv;
   const __half* kc = sm.kcache[layer];
   const __half* vc = sm.vcache[layer];
   const size_t row_stride = (size_t)a.Hkv * HD;
   const int k0 = ch * MK_KCHUNK, k1 = min(k0 + MK_KCHUNK, ctx);
-  const int jbase = k0 + 32 * w, j = jbase + lane;
-  // one round of loads: the query row (one element per thread, to shared memory), this lane's 4
-  // elements of every V row of the warp's 32 keys (8 bytes per key) and the first half of this
-  // lane's K row; the second K half follows
+  const int jbase = k0 + KW * w, j = jbase + kk;
+  // one round of loads: the query row (one element per thread, to shared memory), this lane's
+  // 4 elements of every V row of the warp's keys (8 bytes per key) and its half of its key's K row
+  // (pieces 2i + hh of 16 bytes, so a load instruction reads 32 contiguous bytes of 16 rows)
   const float qv = ct < HD ? __ldcg(a.q + ((size_t)kvh * g + r) * HD + ct) : 0.0f;
-  const int jc = min(j, k1 - 1);
-  uint2 vv[32];
+  uint2 vv[KW];
 #pragma unroll
-  for (int jj = 0; jj < 32; ++jj) {
+  for (int jj = 0; jj < KW; ++jj) {
     const int key = min(jbase + jj, k1 - 1);
     vv[jj] = __ldcg(reinterpret_cast<const uint2*>(vc + (size_t)key * row_stride + (size_t)kvh * HD + lane * EPL));
   }
-  const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t)jc * row_stride + (size_t)kvh * HD);
-  uint4 kr[KU4 / 2];
+  const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t)min(j, k1 - 1) * row_stride + (size_t)kvh * HD);
+  uint4 kr[HD / 16];
 #pragma unroll
-  for (int u = 0; u < KU4 / 2; ++u) kr[u] = __ldcg(kp + u);
+  for (int i = 0; i < HD / 16; ++i) kr[i] = __ldcg(kp + 2 * i + hh);
   if (ct < HD) sm.att_q[0][ct] = qv;
   consumer_sync();
-  float d = 0.0f;
+  float d0 = 0.0f, d1 = 0.0f;
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
-    if (half == 1) {
+  for (int i = 0; i < HD / 16; ++i) {
+    const __half2* h2 = reinterpret_cast<const __half2*>(&kr[i]);
+    const float* qp = &sm.att_q[0][8 * (2 * i + hh)];
 #pragma unroll
-      for (int u = 0; u < KU4 / 2; ++u) kr[u] = __ldcg(kp + KU4 / 2 + u);
-    }
-#pragma unroll
-    for (int u = 0; u < KU4 / 2; ++u) {
-      const __half2* h2 = reinterpret_cast<const __half2*>(&kr[u]);
-#pragma unroll
-      for (int tt = 0; tt < 4; ++tt) {
-        const float2 f = __half22float2(h2[tt]);
-        const int e = 8 * (half * (KU4 / 2) + u) + 2 * tt;
-        d = fmaf(sm.att_q[0][e], f.x, d);
-        d = fmaf(sm.att_q[0][e + 1], f.y, d);
-      }
+    for (int tt = 0; tt < 4; ++tt) {
+      const float2 f = __half22float2(h2[tt]);
+      d0 = fmaf(qp[2 * tt], f.x, d0);
+      d1 = fmaf(qp[2 * tt + 1], f.y, d1);
     }
   }
+  float d = d0 + d1;
+  d += __shfl_xor_sync(0xffffffffu, d, 1);
   const float sc = j < k1 ? d * a.scale : -INFINITY;
-  const float m = warp_max(sc);
+  const float m = warp_max(sc);  // each key twice: the maximum is the same
   float o[EPL] = {0.0f, 0.0f, 0.0f, 0.0f};
   float lw = 0.0f;
   if (m != -INFINITY) {
-    const float p = expf(sc - m);  // 0 for keys past the context: their V slices are never used
-    lw = warp_sum(p);
+    const float p = expf(sc - m);  // 0 for keys past the chunk: their V slices are never used
+    lw = warp_sum(hh == 0 ? p : 0.0f);
 #pragma unroll
-    for (int jj = 0; jj < 32; ++jj) {
-      const float pj = __shfl_sync(0xffffffffu, p, jj);
+    for (int jj = 0; jj < KW; ++jj) {
+      const float pj = __shfl_sync(0xffffffffu, p, 2 * jj);
       const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj].x));
       const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj].y));
       o[0] = fmaf(pj, v0.x, o[0]);
@@ -745,6 +696,49 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
     for (int k = 0; k < MK_CW; ++k) v += sm.att_o[k][0][e] * sm.att_cs[k][0];
     part[MK_PAD + e] = v;
   }
+  // the CTA that completes a query row's chunks merges them (max, sum, weighted V, online over the
+  // chunks) into the attention output, so the o projection stages x with one plain round of loads
+  const int hq = kvh * g + r;
+  consumer_sync();
+  if (ct == 0) {
+    __threadfence();
+    sm.att_last = atomicAdd(&a.rowcnt[hq], 1u) == (unsigned)(nch - 1);
+  }
+  consumer_sync();
+  if (!sm.att_last) return;
+  __threadfence();
+  if (ct < HD) {
+    const float* base = a.part + ((size_t)kvh * MK_MAXCH * MK_ROWS + r) * (HD + MK_PAD);
+    float M = -INFINITY, L = 0.0f, v = 0.0f;
+    for (int c0 = 0; c0 < nch; c0 += 4) {
+      float2 ml[4];
+      float ov[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {  // one round of loads per four chunks
+        if (c0 + k < nch) {
+          const float* pc = base + (size_t)(c0 + k) * MK_ROWS * (HD + MK_PAD);
+          ml[k] = __ldcg(reinterpret_cast<const float2*>(pc));
+          ov[k] = __ldcg(pc + MK_PAD + ct);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (c0 + k < nch && ml[k].x != -INFINITY) {
+          if (ml[k].x > M) {  // rescale what was merged so far to the new maximum
+            const float rs = M == -INFINITY ? 0.0f : expf(M - ml[k].x);
+            L *= rs;
+            v *= rs;
+            M = ml[k].x;
+          }
+          const float cs = expf(ml[k].x - M);
+          L += ml[k].y * cs;
+          v += cs * ov[k];
+        }
+      }
+    }
+    a.attn_out[(size_t)hq * HD + ct] = v / L;
+  }
+  if (ct == 0) a.rowcnt[hq] = 0u;  // the next layer's items start after the next stage barrier
 }
 
 __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
@@ -803,6 +797,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
       sm.ln_in[l] = a.layers[l].ln_in;
       sm.ln_post[l] = a.layers[l].ln_post;
     }
+    if (blockIdx.x == 0)  // row counters of the attention merge (left non-zero only by an aborted launch)
+      for (int i = ct; i < a.H; i += MK_CW * 32) a.rowcnt[i] = 0u;
     // x past a shard's K meets zero-filled weights and scales: keep it finite
     for (int e = ct; e < MK_XROW; e += MK_CW * 32) sm.xs_hi[e] = sm.xs_lo[e] = make_uint4(0, 0, 0, 0);
     consumer_sync();
@@ -836,14 +832,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     const int g = a.H / a.Hkv;
     for (int it = blockIdx.x; it < a.H * nch; it += gridDim.x) {  // (query row, chunk) items
       const int hq = it / nch, ch = it - hq * nch;
-      attn_item(a, sm, l, hq / g, ch, hq % g, ctx);
+      attn_item(a, sm, l, hq / g, ch, hq % g, ctx, nch);
       consumer_sync();
     }
     stage_arrive(a);
     ++stage;
     // WO
     if (!(ok = stage_wait(a, sm, stage * n))) break;
-    stage_attn_merge(a, sm, nch);
+    stage_plain(a, sm, a.attn_out, a.H * a.hd);
     consumer_sync();
     ok = consume_stage(a, sm, ST_WO, l, seq, pos);
     global_arrive(a, gstage);
@@ -942,6 +938,8 @@ int Model::mk_prepare() {
   if (!mk_proj && (rc = alloc(&mk_proj, sizeof(MkProj) * proj.size(), false))) return rc;
   if (!mk_layers && (rc = alloc(&mk_layers, sizeof(q4b_layer_weights) * layers.size(), false))) return rc;
   if (!mk_part && (rc = alloc((void**)&mk_part, sizeof(float) * Hkv * MK_MAXCH * MK_ROWS * (hd + MK_PAD), true))) return rc;
+  if (!mk_rows && (rc = alloc((void**)&mk_rows, sizeof(unsigned) * H, true))) return rc;
+  if (!mk_attn && (rc = alloc((void**)&mk_attn, sizeof(float) * H * hd, true))) return rc;
   const int t = cfg.tp_size;
   // sync words [0, 8) and the argmax keys at byte 64; residual ping-pong + every rank's partials
   if (!mk_sync && (rc = alloc((void**)&mk_sync, 256, true))) return rc;
@@ -1029,6 +1027,8 @@ int Model::mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_
   a.q = q;
   a.a = this->a;
   a.part = mk_part;
+  a.rowcnt = mk_rows;
+  a.attn_out = mk_attn;
   a.sync = mk_sync;
   cudaLaunchConfig_t cfgl = {};
   cfgl.gridDim = dim3(mk_ctas);

@@ -31,6 +31,8 @@ struct Model {
   void* mk_layers = nullptr;
   float* mk_part = nullptr;
   unsigned* mk_sync = nullptr;
+  unsigned* mk_rows = nullptr;  // attention row counters [H]
+  float* mk_attn = nullptr;     // attention output [H * hd]
   float* mk_h = nullptr;  // residual ping-pong [2][D] + every rank's o / down partials [2][tp][3][D]
   std::vector<float*> mk_peer_h;        // per rank: its mk_h mapped here (own rank: mk_h)
   std::vector<unsigned*> mk_peer_sync;  // per rank: its mk_sync mapped here
