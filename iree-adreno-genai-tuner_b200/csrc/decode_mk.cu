@@ -87,8 +87,8 @@ struct MkArgs {
   float* part;   // attention partials [Hkv][MK_MAXCH][MK_ROWS][hd + 4]: m, l, -, -, o[hd]
   unsigned* rowcnt;  // [H] chunks of each query row done in this layer (the last one merges)
   float* attn_out;   // [H * hd] the attention output (the o projection's x)
-  // [0] local stage arrivals, [1] abort, [2] local arrivals at cross-rank barriers (these three are
-  // zeroed per launch); [3] cross-rank barrier count, [4] lm key arrivals, [5] step epoch (never reset)
+  // [0] local stage arrivals, [1] abort (both zeroed per launch); [4] lm key arrivals of every rank,
+  // [5] step epoch, [6] poison (an earlier step timed out) -- never reset by a launch
   unsigned* sync;
   // tensor parallelism: this rank of tp; the peers' psum / sync / key buffers (peer memory mapped
   // into this process; index rank = this GPU's own)
@@ -121,6 +121,7 @@ struct MkSmem {
   const float* ln_post[MK_MAXL];
   uint64_t full[MK_NSLOT], empty[MK_NSLOT];
   int abort_flag;
+  unsigned tagbase;  // epoch * n_layers: partial sums of layer l carry parity (tagbase + l) & 1
   int last;
   int att_last;
 };
@@ -148,6 +149,18 @@ __device__ float consumer_sum(float v, float* scratch) {
   return t;
 }
 
+// Abort of the step: every wait of every rank sees the flag; the model is poisoned (sync[6], never
+// reset by a launch): partial sums of the failed step may carry the tags the retry would accept, so
+// later launches do no work and report the failure until the host prepares the model again.
+__device__ void raise_abort(const MkArgs& a, MkSmem& sm) {
+  sm.abort_flag = 1;
+  for (int r = 0; r < a.tp; ++r) {
+    atomicExch_system(a.peer_sync[r] + 1, 1u);
+    atomicExch_system(a.peer_sync[r] + 6, 1u);
+  }
+  a.state->status = 1;
+}
+
 // Stage-start wait (first consumer thread spins, bounded; then the consumer warps sync).
 __device__ bool stage_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
   if (threadIdx.x == 32) {
@@ -162,8 +175,7 @@ __device__ bool stage_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
         break;
       }
       if (globaltimer_ns() - t0 > a.wait_ns) {
-        atomicExch(&a.sync[1], 1u);
-        sm.abort_flag = 1;
+        raise_abort(a, sm);
         break;
       }
     }
@@ -178,53 +190,33 @@ __device__ void stage_arrive(const MkArgs& a) {
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync) : "memory");
 }
 
-// Barrier over every CTA of every rank (after the row-split o / down projections, whose partial sums
-// go to the peers). One GPU: every CTA adds 1 to the counter sync[3] and waits for n more per
-// barrier. Several: every CTA makes its pushes visible system-wide and adds 1 to this rank's local
-// count sync[2]; the CTA that completes it adds 1 to every rank's sync[3], so each barrier adds tp
-// there (one NVLink atomic per rank pair instead of one per CTA). sync[3] is never reset (peers may
-// add to it before this rank's step has started), so targets count from the step's epoch.
-__device__ bool global_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
-  if (threadIdx.x == 32) {
-    const uint64_t t0 = globaltimer_ns();
-    unsigned polls = 0;
-    for (;;) {
-      unsigned v;
-      if (a.tp > 1)
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync + 3) : "memory");
-      else
-        v = ld_acquire(a.sync + 3);
-      if ((int)(v - target) >= 0) break;
-      if ((++polls & 31) != 0) continue;  // the abort word and the clock every 32 polls
-      if (ld_acquire(&a.sync[1])) {
-        sm.abort_flag = 1;
-        break;
-      }
-      if (globaltimer_ns() - t0 > a.wait_ns) {
-        for (int r = 0; r < a.tp; ++r) atomicExch_system(a.peer_sync[r] + 1, 1u);
-        sm.abort_flag = 1;
-        break;
-      }
-    }
-  }
-  consumer_sync();
-  return !sm.abort_flag;
+// The o / down partial sums carry their layer's parity in the lowest mantissa bit (one ulp, far
+// below the 1e-3 tolerance of the path): the next norm's staging polls the partials themselves until
+// every word it needs shows the parity of the layer it expects, on this GPU or pushed by a peer, so no
+// grid-wide (or cross-GPU) barrier separates a row-split projection from the next RMSNorm. A slot is
+// rewritten once per layer and every CTA reads every slot before it can write the next layer's value
+// (each needs all the previous partials first), so one bit tells the two candidates apart.
+__device__ __forceinline__ float tag_value(float v, unsigned tag) {
+  return __uint_as_float((__float_as_uint(v) & ~1u) | tag);
 }
-// gstage: global barriers this launch has passed before this one
-__device__ void global_arrive(const MkArgs& a, unsigned gstage) {
-  consumer_sync();
-  if (threadIdx.x == 32) {
-    if (a.tp > 1) {
-      __threadfence_system();
-      unsigned old;
-      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(a.sync + 2) : "memory");
-      if (old == (gstage + 1) * gridDim.x - 1)
-        for (int r = 0; r < a.tp; ++r)
-          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.peer_sync[r] + 3) : "memory");
-    } else {
-      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync + 3) : "memory");
-    }
-  }
+__device__ __forceinline__ bool tags_match(const float4& q, unsigned tag) {
+  return ((__float_as_uint(q.x) & __float_as_uint(q.y) & __float_as_uint(q.z) & __float_as_uint(q.w) & 1u) == tag) &&
+         (((__float_as_uint(q.x) | __float_as_uint(q.y) | __float_as_uint(q.z) | __float_as_uint(q.w)) & 1u) == tag);
+}
+// Loads that must see other SMs' (and, with peers, other GPUs') recent stores: L2, not L1.
+__device__ __forceinline__ float4 ld_fresh4(const float* p, bool sys) {
+  float4 v;
+  if (sys)
+    asm volatile("ld.relaxed.sys.global.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+  else
+    asm volatile("ld.relaxed.gpu.global.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
+  return v;
 }
 
 // Projection of a stage: rows per tile pairing and geometry.
@@ -324,8 +316,8 @@ __device__ __forceinline__ void stage_word(MkSmem& sm, int w, const float (&v)[8
 // The residual stream before a norm: the first layer's h is the embedding row of the token
 // (QEmbedding.lookup, llama_q4.py:106-119); later it is h + the K-split partial sums of the o / down
 // projection (added in split order).
-__device__ __forceinline__ void norm_src(const MkArgs& a, int w, bool embed, int token, const float* hsrc,
-                                         const float* psrc, int nparts, float (&v)[8]) {
+__device__ __forceinline__ bool norm_src(const MkArgs& a, int w, bool embed, int token, const float* hsrc,
+                                         const float* psrc, int nparts, unsigned tag, float (&v)[8]) {
   if (embed) {
     const int words = a.D / 8;
     const bool ok = token >= 0 && token < a.Vfull;
@@ -333,38 +325,40 @@ __device__ __forceinline__ void norm_src(const MkArgs& a, int w, bool embed, int
     const float s = ok ? __half2float(a.emb_s[(size_t)token * (a.D / 128) + (8 * w) / 128]) : 0.0f;
 #pragma unroll
     for (int b = 0; b < 8; ++b) v[b] = (float)(((word >> (4 * b)) & 15) - 8) * s;
-  } else {
-    const float4 p0 = __ldcg(reinterpret_cast<const float4*>(hsrc + 8 * w));
-    const float4 p1 = __ldcg(reinterpret_cast<const float4*>(hsrc + 8 * w) + 1);
-    v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
-    v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
-    float d[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int r = 0; r < a.tp; ++r) {  // every rank's partials, rank order then split order
-      const float* pr = psrc + (size_t)r * MK_MAXKS * a.D + 8 * w;
-      float4 q0[MK_MAXKS], q1[MK_MAXKS];
+    return true;
+  }
+  const float4 p0 = __ldcg(reinterpret_cast<const float4*>(hsrc + 8 * w));
+  const float4 p1 = __ldcg(reinterpret_cast<const float4*>(hsrc + 8 * w) + 1);
+  v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+  v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+  float d[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  bool fresh = true;
+  const bool sys = a.tp > 1;
+  for (int r = 0; r < a.tp; ++r) {  // every rank's partials, rank order then split order
+    const float* pr = psrc + (size_t)r * MK_MAXKS * a.D + 8 * w;
+    float4 q0[MK_MAXKS], q1[MK_MAXKS];
 #pragma unroll
-      for (int k = 0; k < MK_MAXKS; ++k) {
-        if (k < nparts) {
-          q0[k] = __ldcg(reinterpret_cast<const float4*>(pr + (size_t)k * a.D));
-          q1[k] = __ldcg(reinterpret_cast<const float4*>(pr + (size_t)k * a.D) + 1);
-        }
-      }
-#pragma unroll
-      for (int k = 0; k < MK_MAXKS; ++k) {
-        if (k < nparts) {
-          d[0] += q0[k].x; d[1] += q0[k].y; d[2] += q0[k].z; d[3] += q0[k].w;
-          d[4] += q1[k].x; d[5] += q1[k].y; d[6] += q1[k].z; d[7] += q1[k].w;
-        }
+    for (int k = 0; k < MK_MAXKS; ++k) {
+      if (k < nparts) {
+        q0[k] = ld_fresh4(pr + (size_t)k * a.D, sys);
+        q1[k] = ld_fresh4(pr + (size_t)k * a.D + 4, sys);
       }
     }
 #pragma unroll
-    for (int b = 0; b < 8; ++b) v[b] += d[b];
+    for (int k = 0; k < MK_MAXKS; ++k) {
+      if (k < nparts) {
+        fresh = fresh && tags_match(q0[k], tag) && tags_match(q1[k], tag);
+        d[0] += q0[k].x; d[1] += q0[k].y; d[2] += q0[k].z; d[3] += q0[k].w;
+        d[4] += q1[k].x; d[5] += q1[k].y; d[6] += q1[k].z; d[7] += q1[k].w;
+      }
+    }
   }
+#pragma unroll
+  for (int b = 0; b < 8; ++b) v[b] += d[b];
+  return fresh;
 }
 
-// x = rmsnorm(h) * w (rms_norm, llama_q4.py:141-142). With hdst the updated residual stream is also
-// written (each word by one CTA) to the other ping-pong buffer.
-// This thread's (at most two) words of a norm weight: loaded before the stage's barrier wait.
+// This thread's (at most two) words of a norm weight: loaded before the stage's data arrives.
 __device__ __forceinline__ void norm_weights(const MkArgs& a, const float* lnw, float (&lw)[2][8]) {
   const int ct = threadIdx.x - 32;
 #pragma unroll
@@ -379,17 +373,29 @@ __device__ __forceinline__ void norm_weights(const MkArgs& a, const float* lnw, 
   }
 }
 
+// x = rmsnorm(h + partials) * w (rms_norm, llama_q4.py:141-142). With hdst the updated residual
+// stream is also written (each word by one CTA) to the other ping-pong buffer. Each thread reloads
+// its words until their partial sums carry the expected tag (bounded; a timeout aborts the step).
 __device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float (&lw)[2][8], bool embed, int token,
-                           const float* hsrc, const float* psrc, int nparts, float* hdst) {
+                           const float* hsrc, const float* psrc, int nparts, unsigned tag, float* hdst) {
   const int ct = threadIdx.x - 32;
   const int words = a.D / 8;
-  // one round of loads: this thread's (at most two) words of h (+ partials)
   float v[2][8];
   float ss = 0.0f;
+  uint64_t t0 = 0;
+  for (int tries = 0;; ++tries) {
+    bool fresh = true;
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {  // every load before any store (the stores may alias nothing read,
-    const int w = ct + i * (MK_CW * 32);  // but the compiler cannot know)
-    if (w < words) norm_src(a, w, embed, token, hsrc, psrc, nparts, v[i]);
+    for (int i = 0; i < 2; ++i) {  // one round: every load before any store
+      const int w = ct + i * (MK_CW * 32);
+      if (w < words) fresh = norm_src(a, w, embed, token, hsrc, psrc, nparts, tag, v[i]) && fresh;
+    }
+    if (fresh) break;
+    if (tries == 0) t0 = globaltimer_ns();
+    if (globaltimer_ns() - t0 > a.wait_ns || *(volatile unsigned*)&a.sync[1]) {
+      raise_abort(a, sm);
+      break;
+    }
   }
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
@@ -460,10 +466,11 @@ __device__ void pair_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, in
   } else {  // WO / WDOWN: this rank's K-split partial sums, pushed to every rank (added to h there by
             // the next norm's staging, in rank and split order)
     const size_t off = ((size_t)(st == ST_WDOWN) * a.tp * MK_MAXKS + (size_t)a.rank * MK_MAXKS + ks) * a.D + rt * 16;
+    const unsigned tag = (sm.tagbase + (unsigned)layer) & 1u;
     for (int r = 0; r < a.tp; ++r) {
       float* p = a.peer_psum[r] + off;
-      p[s] = v0;
-      p[s + 8] = v1;
+      p[s] = tag_value(v0, tag);
+      p[s + 8] = tag_value(v1, tag);
     }
   }
 }
@@ -750,7 +757,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
       mbar_init(&sm.full[i], 1);
       mbar_init(&sm.empty[i], MK_CW);
     }
-    sm.abort_flag = 0;
+    // a poisoned model (an earlier step of it timed out) does no work and reports the failure again
+    sm.abort_flag = *(volatile unsigned*)&a.sync[6] ? 1 : 0;
+    if (sm.abort_flag) a.state->status = 1;
+    sm.tagbase = *(volatile unsigned*)&a.sync[5] * (unsigned)a.n_layers;  // tag parity of layer 0
     fence_mbar_init();
   }
   __syncthreads();
@@ -776,10 +786,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
         if (kind(i) == ST_WO) ok = producer_gate(a, sm, (3u * (i >> 2) + 2u) * gridDim.x);
         ok = ok && produce_stage(a, sm, a.proj[i], kind(i), seq);
       }
-      if (!ok) {
-        atomicExch(&a.sync[1], 1u);
-        sm.abort_flag = 1;
-      }
+      if (!ok) raise_abort(a, sm);
     }
     __syncwarp();
     return;
@@ -809,19 +816,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
   const int nwo = geo(a, ST_WO).KS, nwd = geo(a, ST_WDOWN).KS;  // partial sums the norms add
   const float* pwo = a.psum;                                      // o partials of every rank
   const float* pwd = a.psum + (size_t)a.tp * MK_MAXKS * a.D;      // down partials of every rank
-  // global (all ranks) barrier count before this step, from the epoch: two barriers per layer, each
-  // adding n (one GPU) or tp (one per rank)
-  const unsigned gunit = a.tp > 1 ? (unsigned)a.tp : n;
-  const unsigned gbase = epoch * (unsigned)(2 * a.n_layers) * gunit;
-  unsigned gstage = 0;
-  bool ok = true;
+  bool ok = !sm.abort_flag;  // a poisoned model (an earlier step timed out) does no work
   float lw[2][8];  // the next norm's weights
   for (int l = 0; l < a.n_layers && ok; ++l) {
-    // QKV (after the previous layer's down projection: every rank's partials)
+    // QKV (x from the previous layer's down partials of every rank, tagged with that layer's parity)
     norm_weights(a, sm.ln_in[l], lw);
-    ok = l == 0 || global_wait(a, sm, gbase + gstage * gunit);
-    if (!ok) break;
-    stage_norm(a, sm, lw, l == 0, token, a.hb, pwd, nwd, a.hb + a.D);
+    stage_norm(a, sm, lw, l == 0, token, a.hb, pwd, nwd, (sm.tagbase + l + 1) & 1u, a.hb + a.D);
     consumer_sync();
     ok = consume_stage(a, sm, ST_QKV, l, seq, pos);
     stage_arrive(a);
@@ -842,13 +842,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     stage_plain(a, sm, a.attn_out, a.H * a.hd);
     consumer_sync();
     ok = consume_stage(a, sm, ST_WO, l, seq, pos);
-    global_arrive(a, gstage);
-    ++gstage;
-    if (!ok) break;
-    // WGU (after every rank's o partials)
+    if (!ok || sm.abort_flag) break;
+    // WGU (x from every rank's o partials of this layer)
     norm_weights(a, sm.ln_post[l], lw);
-    if (!(ok = global_wait(a, sm, gbase + gstage * gunit))) break;
-    stage_norm(a, sm, lw, false, token, a.hb + a.D, pwo, nwo, a.hb);
+    stage_norm(a, sm, lw, false, token, a.hb + a.D, pwo, nwo, (sm.tagbase + l) & 1u, a.hb);
     consumer_sync();
     ok = consume_stage(a, sm, ST_WGU, l, seq, pos);
     stage_arrive(a);
@@ -858,20 +855,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     if (!(ok = stage_wait(a, sm, stage * n))) break;
     stage_plain(a, sm, a.a, a.I);
     consumer_sync();
-    ok = consume_stage(a, sm, ST_WDOWN, l, seq, pos);
-    global_arrive(a, gstage);
-    ++gstage;
+    ok = consume_stage(a, sm, ST_WDOWN, l, seq, pos) && !sm.abort_flag;
   }
-  if (ok) norm_weights(a, a.ln_f, lw);
-  if (ok && (ok = global_wait(a, sm, gbase + gstage * gunit))) {
-    stage_norm(a, sm, lw, false, token, a.hb, pwd, nwd, nullptr);
+  if (ok) {
+    norm_weights(a, a.ln_f, lw);
+    stage_norm(a, sm, lw, false, token, a.hb, pwd, nwd, (sm.tagbase + a.n_layers + 1) & 1u, nullptr);
     consumer_sync();
-    ok = consume_lm(a, sm, seq, epoch);
+    ok = !sm.abort_flag && consume_lm(a, sm, seq, epoch);
   }
-  if (!ok && threadIdx.x == 32) {
-    atomicExch(&a.sync[1], 1u);
-    a.state->status = 1;
-  }
+  if (!ok && threadIdx.x == 32) raise_abort(a, sm);
 }
 
 }  // namespace
@@ -943,7 +935,23 @@ int Model::mk_prepare() {
   const int t = cfg.tp_size;
   // sync words [0, 8) and the argmax keys at byte 64; residual ping-pong + every rank's partials
   if (!mk_sync && (rc = alloc((void**)&mk_sync, 256, true))) return rc;
-  if (!mk_h && (rc = alloc((void**)&mk_h, sizeof(float) * (2 + 2 * (size_t)t * MK_MAXKS) * D, true))) return rc;
+  const size_t psum_bytes = sizeof(float) * 2 * (size_t)t * MK_MAXKS * D;
+  if (!mk_h) {
+    if ((rc = alloc((void**)&mk_h, sizeof(float) * 2 * D + psum_bytes, true))) return rc;
+    // partial-sum tags: layer 0 of epoch 0 expects parity 0, so every slot starts with parity 1
+    if (cudaMemset(mk_h + 2 * D, 0x01, psum_bytes) != cudaSuccess) return set_error(Q4B_ECUDA, "persistent decode: init");
+  }
+  if (t == 1) {  // a poisoned model (a step timed out) is cleared: slots get the parity the next layer 0 does not expect
+    unsigned w[8];
+    if (cudaMemcpy(w, mk_sync, sizeof(w), cudaMemcpyDeviceToHost) != cudaSuccess)
+      return set_error(Q4B_ECUDA, "persistent decode: state read");
+    if (w[6]) {
+      const int p0 = (int)((w[5] * (unsigned)layers.size()) & 1u);
+      if (cudaMemset(mk_h + 2 * D, p0 ? 0x00 : 0x01, psum_bytes) != cudaSuccess ||
+          cudaMemset(mk_sync + 6, 0, sizeof(unsigned)) != cudaSuccess)
+        return set_error(Q4B_ECUDA, "persistent decode: reset");
+    }
+  }
   if ((int)mk_peer_h.size() != t || (int)mk_peer_sync.size() != t) {  // once: the buffers live as long as the model
     mk_peer_h.assign(t, nullptr);
     mk_peer_sync.assign(t, nullptr);
@@ -988,7 +996,7 @@ bool Model::mk_usable(int C, cudaStream_t st) {
 }
 
 int Model::mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_log, cudaStream_t st) {
-  cudaError_t e = cudaMemsetAsync(mk_sync, 0, 3 * sizeof(unsigned), st);
+  cudaError_t e = cudaMemsetAsync(mk_sync, 0, 2 * sizeof(unsigned), st);
   if (e != cudaSuccess) return set_error(Q4B_ECUDA, "persistent decode: reset: %s", cudaGetErrorString(e));
   MkArgs a = {};
   a.proj = reinterpret_cast<const MkProj*>(mk_proj);
