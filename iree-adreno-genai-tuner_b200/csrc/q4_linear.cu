@@ -1188,16 +1188,36 @@ static int plan_tc(int M, int K, int G, bool xf32, const q4b_linear_cfg* cfg, Pl
   if (T && T != 4 && T != 8) return set_error(Q4B_EINVAL, "q4_linear: kernel 5 takes tiles 4 or 8 (64 or 128 rows)");
   const int NG = K / G;
   pl.tiles_m = (M + 127) / 128;
-  pl.bn = T ? T * 16 : 128;
-  if (!T && (long long)pl.tiles_m * ((pl.RT + 7) / 8) < 100) pl.bn = 64;  // few tiles: narrower ones
-  pl.tiles_n = (pl.RT + pl.bn / 16 - 1) / (pl.bn / 16);
-  const long long tiles = (long long)pl.tiles_m * pl.tiles_n;
   int S = cfg && cfg->split ? cfg->split : 0;
   if (S < 0 || S > NG) return set_error(Q4B_EINVAL, "q4_linear: split must be in [1, %d] (scale groups)", NG);
-  if (!S) {
-    S = 1;
-    while (tiles * S < 148 && NG / (S * 2) >= 2) S *= 2;
+  {
+    // A 64-k stage costs about one loaded L2 round trip (~1.1 us) for its x tile whatever the tile
+    // width, so the time is ~ waves x stages per CTA, plus the split-K partial tiles written and read
+    // back (at ~5 TB/s): wide tiles (half the x re-reads) and a split that fills one wave of the
+    // 148 SMs usually win.
+    double best = 1e30;
+    int best_bn = T ? T * 16 : 128, best_s = 1;
+    for (int bn = 128; bn >= 64; bn -= 64) {
+      if (T && bn != T * 16) continue;  // the configuration fixes the tile width
+      const long long tl = (long long)pl.tiles_m * ((pl.RT + bn / 16 - 1) / (bn / 16));
+      for (int s = 1; s <= NG && s <= 64; ++s) {
+        if (S && s != S) continue;
+        if ((NG + s - 1) / s > K5_MAX_GROUPS || (s > 1 && tl > kMaxCounters)) continue;
+        const long long waves = (tl * s + 147) / 148;
+        const double reduce = s > 1 ? 2.0 * s * (double)tl * K5_BM * bn * 4 / 5e12 / 1.1e-6 : 0.0;
+        const double cost = (double)waves * ((NG + s - 1) / s) * (G / K5_BK) + reduce;
+        if (cost < best - 1e-9) {
+          best = cost;
+          best_bn = bn;
+          best_s = s;
+        }
+      }
+    }
+    pl.bn = best_bn;
+    if (!S) S = best_s;
   }
+  pl.tiles_n = (pl.RT + pl.bn / 16 - 1) / (pl.bn / 16);
+  const long long tiles = (long long)pl.tiles_m * pl.tiles_n;
   while ((NG + S - 1) / S > K5_MAX_GROUPS) ++S;
   if (S > 1 && tiles > kMaxCounters)
     return set_error(Q4B_EUNSUPPORTED, "q4_linear: split-K limited to %d tiles", kMaxCounters);

@@ -84,6 +84,27 @@ def test_linear_workspace_plan(L):
     assert L.q4b_q4_linear_workspace(1, 5120, 3072, 128, 0, ctypes.byref(cfg)) == 0
 
 
+def test_prefill_gemm_plan(L):
+    """Kernel 5 (prefill, M > 32) plans: every configuration form plans without a fault, and the
+    default for the 3B prefill shapes picks the wide tile and a split that fills one wave."""
+    from q4b import _lib
+    KB = 65536  # the split-K counters
+    x2 = lambda m, k: ((m * k * 2 + 255) // 256) * 256  # noqa: E731  (x hi + x lo)
+
+    def ws(m, n, k, epi=0, **cfg):
+        c = _lib.LinearCfg(**cfg) if cfg else None
+        return L.q4b_q4_linear_workspace(m, n, k, 128, epi, ctypes.byref(c) if c else None)
+
+    for cfg in (dict(kernel=5), dict(kernel=5, tiles=4), dict(kernel=5, tiles=8), dict(kernel=5, split=3),
+                dict(kernel=5, tiles=4, split=5), dict(kernel=5, tiles=8, split=1)):
+        for m, n, k in ((128, 5120, 3072), (64, 384, 3072), (33, 3072, 8192), (128, 16384, 3072)):
+            assert ws(m, n, k, **cfg) >= KB, (cfg, m, n, k)
+    # 3B o projection at a 128-row chunk: 24 tiles of 128 rows x 6 splits = 144 CTAs
+    assert ws(128, 3072, 3072) == KB + 2 * x2(128, 3072) + 6 * 24 * 128 * 128 * 4
+    # gate|up (16384 rows): 128 wide tiles already fill a wave, no split
+    assert ws(128, 16384, 3072, epi=2) == KB + 2 * x2(128, 3072)
+
+
 def test_no_cpu_fallback_without_gpu():
     """The product ops refuse CPU tensors instead of computing on the host."""
     import torch
