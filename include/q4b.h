@@ -194,6 +194,11 @@ void q4b_model_destroy(q4b_model* model);
  * token, tables built on the first decode step), 0 = one kernel per projection. No reference
  * counterpart (a diagnostic of this library's decode path). */
 int q4b_model_decode_path(const q4b_model* model);
+/* Testing the failure path without a device fault: marks the model's persistent decode step as
+ * failed, exactly as a bounded device wait that gave up does. Later decode steps do no work, the
+ * runner returns Q4B_ETIMEOUT, until the model is prepared again (q4b_model_set_head or
+ * q4b_model_set_layer; single GPU). No reference counterpart. */
+int q4b_model_fail_decode(q4b_model* model);
 
 /* ---- tensor parallelism (one process per GPU, NCCL loaded at run time) ---------------------- */
 

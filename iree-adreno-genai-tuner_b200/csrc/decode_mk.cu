@@ -983,6 +983,19 @@ int Model::mk_prepare() {
   return Q4B_OK;
 }
 
+// Marks the persistent step failed, as a timed-out wait does (sync[6]): the failure path without a
+// device fault. Single-GPU models are cleared by preparing them again.
+int Model::mk_poison() {
+  if (!mk_ready) {
+    const int rc = mk_prepare();
+    if (rc) return rc;
+  }
+  const unsigned one = 1u;
+  if (cudaMemcpy(mk_sync + 6, &one, sizeof(one), cudaMemcpyHostToDevice) != cudaSuccess)
+    return set_error(Q4B_ECUDA, "persistent decode: poison");
+  return Q4B_OK;
+}
+
 bool Model::mk_usable(int C, cudaStream_t st) {
   if (C != 1 || !persistent_enabled() || !mk_shapes_ok(*this)) return false;
   if (mk_ready) return true;

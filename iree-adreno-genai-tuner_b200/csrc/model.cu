@@ -312,6 +312,13 @@ extern "C" int q4b_model_step(q4b_model* model, const int32_t* tokens, int n_tok
 
 extern "C" void q4b_model_destroy(q4b_model* model) { delete reinterpret_cast<Model*>(model); }
 
+extern "C" int q4b_model_fail_decode(q4b_model* model) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m) return set_error(Q4B_EINVAL, "model_fail_decode: null model");
+  if (!m->mk_usable(1, nullptr)) return set_error(Q4B_EUNSUPPORTED, "model_fail_decode: no persistent decode step");
+  return m->mk_poison();
+}
+
 extern "C" int q4b_model_decode_path(const q4b_model* model) {
   const Model* m = reinterpret_cast<const Model*>(model);
   return m && m->mk_ready ? 1 : 0;

@@ -42,6 +42,7 @@ struct Model {
   int mk_ctas = 0;
   bool mk_ready = false;
   int mk_prepare();
+  int mk_poison();
   bool mk_usable(int C, cudaStream_t st);
   int mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_log, cudaStream_t st);
   // tensor parallelism (tp.cu)

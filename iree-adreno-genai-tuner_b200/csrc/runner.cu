@@ -154,6 +154,9 @@ int Runner::generate(const int32_t* prompt, int n, int max_new, const int32_t* s
   // reference); graphs are captured on first use here, outside the timed region
   const auto t_warm0 = clk::now();
   if (cudaStreamSynchronize(stream) != cudaSuccess) return set_error(Q4B_ECUDA, "runner: stream");
+  // a failure recorded by an earlier request is not this one's (a poisoned persistent step sets it again)
+  if (cudaMemset(&model->state->status, 0, sizeof(int32_t)) != cudaSuccess)
+    return set_error(Q4B_ECUDA, "runner: state reset");
   slot = 0;
   memset(h_tokens, 0, sizeof(int32_t) * C);
   const DecodeState* zero_state = new_state();
@@ -251,6 +254,10 @@ int Runner::generate(const int32_t* prompt, int n, int max_new, const int32_t* s
     }
     if (cudaStreamSynchronize(stream) != cudaSuccess)
       return set_error(Q4B_ECUDA, "runner: decode: %s", cudaGetErrorString(cudaGetLastError()));
+    int32_t dstat = 0;  // the persistent decode step records a bounded wait that gave up here
+    if (cudaMemcpy(&dstat, &model->state->status, sizeof(dstat), cudaMemcpyDeviceToHost) != cudaSuccess)
+      return set_error(Q4B_ECUDA, "runner: state read");
+    if (dstat) return set_error(Q4B_ETIMEOUT, "runner: a decode step gave up a bounded device wait");
     if (!opts.sync_every_step) {
       DecodeState fin;
       if (cudaMemcpy(&fin, model->state, sizeof(DecodeState), cudaMemcpyDeviceToHost) != cudaSuccess ||

@@ -128,6 +128,31 @@ def test_persistent_through_runner_graphs(model):
     assert outs[True] == outs[False]
 
 
+def test_persistent_failure_is_reported_and_cleared(model):
+    """The failure path without a device fault: a step marked failed (as a bounded wait that gave up
+    marks it) does no work, the runner reports Q4B_ETIMEOUT, and preparing the model again (here by
+    setting its head again) clears it -- the same tokens as before the failure."""
+    import ctypes
+
+    import q4b
+    from q4b import _lib
+    m, _ = model
+    L = _lib.lib()
+    with _Persistent(True):
+        r = q4b.Runner(m, 16, [64, 128, 256], "bucketed", graphs=True)
+        ref, _ = r.generate(_prompt().tolist(), 8)
+        _lib.check(L.q4b_model_fail_decode(m.native()), "model_fail_decode")
+        with pytest.raises(_lib.Q4BError) as err:
+            r.generate(_prompt().tolist(), 8)
+        assert err.value.code == _lib.Q4B_ETIMEOUT
+        head = m._qmat(m.embed)
+        _lib.check(L.q4b_model_set_head(m.native(), ctypes.byref(head), m.ln_f.data_ptr(), m.cos.data_ptr(),
+                                        m.sin.data_ptr()), "model_set_head")
+        again, _ = r.generate(_prompt().tolist(), 8)
+    assert again == ref
+    assert L.q4b_device_status(1) == 0
+
+
 def _state_keys():
     ks = ["model.embed_tokens.weight", "model.norm.weight"]
     for i in range(CFG["num_hidden_layers"]):
