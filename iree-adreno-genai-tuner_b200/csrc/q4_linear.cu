@@ -1109,11 +1109,18 @@ static int plan_reg(int M, int K, bool xf32, const q4b_linear_cfg* cfg, Plan& pl
   int W = cfg && cfg->warps ? cfg->warps : 0;
   int T = cfg && cfg->tiles ? cfg->tiles : 0;
   int S = cfg && cfg->split ? cfg->split : 0;
-  if (!W && !T && !S && pl.MT <= 2 && KT <= 64) {
+  if (!W && !T && !S && pl.MT == 1 && KT <= 64) {
     // decode: up to 8 warps cover all of K with a few 128-k tiles in flight per warp and tile
     // row, no split-K, so the post-wait path is x staging + MMAs + one shared-memory reduction
     W = std::min(8, KT);
     T = round_up_tiles(pl.MT, (KT + W - 1) / W);
+  } else if (!W && !T && !S && pl.MT >= 2) {
+    // 9..32 rows: the staged x grows with the rows, so split K until a CTA holds at most 8 tiles
+    // (one per warp): a small slice of x per CTA and many CTAs per SM (measured 1.1-4x faster on
+    // the 3B projections than all of K in one CTA)
+    W = std::min(8, KT);
+    T = 1;
+    S = (KT + W - 1) / W;
   }
   if (!T) T = pl.MT == 1 ? 2 : 1;
   if (!W) {
