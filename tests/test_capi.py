@@ -105,6 +105,17 @@ def test_prefill_gemm_plan(L):
     assert ws(128, 16384, 3072, epi=2) == KB + 2 * x2(128, 3072)
 
 
+def test_small_m_gemv_plan_splits_k(L):
+    """9..32 rows: the GEMV splits K so a CTA stages at most 8 k-tiles of x (8 splits of the 64
+    tiles of K = 8192 at 16 rows); up to 8 rows K stays whole (no workspace)."""
+    counters = 65536
+    assert L.q4b_q4_linear_workspace(4, 3072, 8192, 128, 0, None) == 0
+    ws = L.q4b_q4_linear_workspace(16, 3072, 8192, 128, 0, None)
+    assert ws == counters + 8 * 16 * (3072 // 16) * 16 * 4
+    ws = L.q4b_q4_linear_workspace(16, 5120, 3072, 128, 0, None)  # 24 tiles: 3 splits
+    assert ws == counters + 3 * 16 * (5120 // 16) * 16 * 4
+
+
 def test_no_cpu_fallback_without_gpu():
     """The product ops refuse CPU tensors instead of computing on the host."""
     import torch
