@@ -773,7 +773,6 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
   const int NG = p.K / p.G, SPG = p.G / K5_BK;
   const int g0 = (int)((long long)z * NG / p.nsplit), g1 = (int)((long long)(z + 1) * NG / p.nsplit);
   const int NGL = g1 - g0, NS = NGL * SPG;
-  const int KW = p.K / 8;
   __half* s_sc = reinterpret_cast<__half*>(smem + L::SC_OFF);
 
   if (threadIdx.x == 0) {
