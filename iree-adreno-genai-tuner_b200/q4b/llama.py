@@ -60,10 +60,45 @@ class LazySafetensors:
         return k in self.where
 
 
+_MASK32 = 0xFFFFFFFF
+
+
+def _mul32(x, c: int):
+    """(x * c) mod 2^32 for int64 tensors x in [0, 2^32), without any int64 product above 2^49."""
+    return (x * (c & 0xFFFF) + (((x * (c >> 16)) & 0xFFFF) << 16)) & _MASK32
+
+
+def hash_normal(key: int, n: int, std: float, device, chunk: int = 1 << 26):
+    """n seeded values with mean 0 and standard deviation `std`, identical bit for bit on any device.
+
+    Element i hashes the 32-bit counter (i * 0x9E3779B1 + key) with an integer avalanche mix
+    (xorshift-multiply rounds, constants 0x7feb352d and 0x846ca68b); the sum of the hash's four bytes
+    is an Irwin-Hall(4) variate on 0..1020 (mean 510, variance 4 (256^2 - 1) / 12), which one fp32
+    multiply scales to the requested deviation. Integer arithmetic and one correctly rounded fp32
+    multiply give the same bits on a CPU and a GPU, so a checker on the host regenerates exactly the
+    weights a GPU run used."""
+    import math
+    out = torch.empty(n, dtype=torch.float32, device=device)
+    scale = torch.tensor(std / math.sqrt(4 * (256 * 256 - 1) / 12.0), dtype=torch.float32, device=device)
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        x = torch.arange(s, e, dtype=torch.int64, device=device)
+        x = (x * 0x9E3779B1 + (key & _MASK32)) & _MASK32
+        x = x ^ (x >> 16)
+        x = _mul32(x, 0x7FEB352D)
+        x = x ^ (x >> 15)
+        x = _mul32(x, 0x846CA68B)
+        x = x ^ (x >> 16)
+        b = (x & 255) + ((x >> 8) & 255) + ((x >> 16) & 255) + (x >> 24)
+        out[s:e] = (b - 510).to(torch.float32) * scale
+    return out
+
+
 class SyntheticStateDict:
-    """Seeded random-init Llama weights generated per tensor on the GPU (HF init: N(0, std) for
-    projections and the embedding, ones for the norms), so a 3B-shaped model never exists in fp32
-    all at once."""
+    """Seeded random-init Llama weights generated per tensor name (HF init: mean 0, deviation
+    `initializer_range` for projections and the embedding, ones for the norms), so a 3B-shaped model
+    never exists in fp32 all at once. The values come from hash_normal, so the same (cfg, seed) gives
+    the same weights on the GPU and on the host (where the reference's own code can be run on them)."""
 
     def __init__(self, cfg: dict, seed: int = 0, std: float | None = None, device="cuda"):
         self.cfg, self.seed, self.device = cfg, seed, torch.device(device)
@@ -90,9 +125,8 @@ class SyntheticStateDict:
         shp = self._shape(k)
         if len(shp) == 1:
             return torch.ones(shp, device=self.device)
-        g = torch.Generator(device=self.device)
-        g.manual_seed((zlib.crc32(k.encode()) & 0x7FFFFFFF) ^ self.seed)
-        return torch.randn(shp, device=self.device, generator=g) * self.std
+        key = (zlib.crc32(k.encode()) ^ (self.seed * 0x85EBCA6B)) & _MASK32
+        return hash_normal(key, shp[0] * shp[1], self.std, self.device).reshape(shp)
 
     def __contains__(self, k):
         try:
