@@ -45,10 +45,15 @@ enum { Q4B_F32 = 0, Q4B_F16 = 1 };
  *               y[m, i] = silu(gate_i . x_m) * (up_i . x_m)   (llama_q4.py:235-236)           */
 enum { Q4B_EPI_STORE = 0, Q4B_EPI_ACCUMULATE = 1, Q4B_EPI_SWIGLU = 2 };
 
-/* Kernel selection for q4b_q4_linear (NULL = tuned default).
- *   kernel: 0 = auto, 1 = tensor-core dequant GEMV (needs G % 128 == 0, M <= 64), 2 = generic SIMT
- *   warps (1..8), tiles (128-k tiles per warp kept in flight: 1, 2 or 4), split (k splits, >= 1):
- *   0 = choose automatically.                                                                  */
+/* Kernel selection for q4b_q4_linear (NULL = tuned default; all fields 0 = choose automatically).
+ *   kernel 1  tensor-core dequant GEMV, weights in registers (G % 128 == 0, M <= 64): warps (1..8),
+ *             tiles (128-k tiles per warp in flight: 1, 2, 3, 4, 6, 8), split (k splits, >= 1)
+ *   kernel 2  generic SIMT (any G % 8 == 0)
+ *   kernel 3  GEMV with the weight tile staged by bulk copies (M <= 16): warps, split
+ *   kernel 4  persistent GEMV, one CTA per SM, whole-row-tile ring (M == 1, G == 128): warps (1..24)
+ *   kernel 5  tcgen05 int4-weight GEMM for many rows (prefill): tiles (4 or 8 row tiles of 16), split
+ *   kernel 6  persistent bulk-copy ring GEMV (M <= 8, G == 128, K % 1024 == 0; the decode default):
+ *             tiles = resident CTAs per SM (1 or 2), split = 1 keeps each row tile in one CTA   */
 typedef struct q4b_linear_cfg {
   int kernel;
   int warps;
@@ -89,6 +94,10 @@ size_t q4b_q4_linear_workspace(int m, int n, int k, int group, int epilogue, con
 int q4b_q4_linear(const int32_t* qweight, const uint16_t* scales, int group, const void* x, int x_dtype,
                   void* y, int y_dtype, int m, int n, int k, int epilogue, const q4b_linear_cfg* cfg,
                   void* workspace, size_t workspace_bytes, q4b_stream_t stream);
+
+/* The kernel (1..6, see q4b_linear_cfg) q4b_q4_linear runs for this problem with 16-byte aligned
+ * pointers and the workspace q4b_q4_linear_workspace asks for; or a negative Q4B_E* code. */
+int q4b_q4_linear_kernel(int m, int n, int k, int group, int epilogue, int x_dtype, const q4b_linear_cfg* cfg);
 
 /* Allocation-free variant of q4b_q4_linear (no counterpart in the reference). For callers that
  * cannot allocate device memory themselves: hosts that reach this library only through a plain C

@@ -348,15 +348,9 @@ int attn_decode_chunks(int L) { return (L + kChunk - 1) / kChunk; }
 template <int HD, int ROWS>
 static cudaError_t launch_decode_hd(const AttnArgs& a, dim3 grid, cudaStream_t st) {
   const size_t smem = (size_t)(kChunk / 32) * ROWS * HD * sizeof(float);
-  static unsigned long long done = 0;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(done >> (dev & 63) & 1ull)) {
-    const cudaError_t e =
-        cudaFuncSetAttribute(attn_decode_kernel<HD, ROWS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    done |= 1ull << (dev & 63);
-  }
+  static std::atomic<unsigned long long> done;
+  const cudaError_t e = set_max_dynamic_smem(attn_decode_kernel<HD, ROWS>, (int)smem, done);
+  if (e != cudaSuccess) return e;
   return launch_pdl(attn_decode_kernel<HD, ROWS>, grid, dim3(256), smem, st, a);
 }
 

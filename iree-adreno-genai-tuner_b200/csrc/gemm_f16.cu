@@ -358,14 +358,9 @@ template <int BN, bool A_MN, bool B_MN>
 cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, const GemmPlan& pl,
                       cudaStream_t st) {
   auto kern = gemm_f16_tc<BN, A_MN, B_MN>;
-  static unsigned long long done = 0;  // per device: the smem attribute is set once
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(done >> (dev & 63) & 1ull)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemBudget + 1024);
-    if (e != cudaSuccess) return e;
-    done |= 1ull << (dev & 63);
-  }
+  static std::atomic<unsigned long long> done;  // per device: the smem attribute is set once
+  const cudaError_t e = set_max_dynamic_smem(kern, kGemmSmemBudget + 1024, done);
+  if (e != cudaSuccess) return e;
   return launch_pdl(kern, dim3(pl.tiles_m, pl.tiles_n, pl.split), dim3(128), pl.smem, st, ta, tb, a, pl.stages);
 }
 

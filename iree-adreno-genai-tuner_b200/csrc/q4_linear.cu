@@ -25,6 +25,7 @@
 // Split-K partials go to a workspace; the last CTA of a row tile (arrival counter) sums them in
 // split order, so results are deterministic.
 #include <algorithm>
+#include <atomic>
 
 #include "linear.h"
 #include "q4dev.cuh"
@@ -69,6 +70,11 @@ struct LinArgs {
   int index_offset;
   int finalize;
   int RT;  // row tiles of the whole problem (the argmax epilogue counts finished tiles)
+  // kernel 6 (ring GEMV)
+  int ring_slots;   // stages in the shared-memory ring
+  int kc;           // stages per row tile (K / 1024)
+  int split_units;  // 1: CTAs take equal runs of stages, row tiles cut between CTAs meet in ws
+  int red_off;      // byte offset of the cross-warp reduction slots in dynamic shared memory
 };
 
 // status word of this file's kernels (bounded waits that gave up), read by linear_status()
@@ -146,8 +152,8 @@ __device__ __forceinline__ float x_value(const LinArgs& p, const float* rs, int 
 // Stage x[:, kt0*128 : kt0*128 + nwords*8) as permuted fp16 pairs (hi, and lo for fp32 x).
 template <bool XF32>
 __device__ __forceinline__ void stage_x(const LinArgs& p, const float* rs, uint4* xs_hi, uint4* xs_lo, int rstride,
-                                        int kt0, int nwords) {
-  for (int i = threadIdx.x; i < p.M * nwords; i += blockDim.x) {
+                                        int kt0, int nwords, int tid, int nth) {
+  for (int i = tid; i < p.M * nwords; i += nth) {
     const int m = i / nwords, w = i - m * nwords;
     const int k0 = kt0 * TILE_K + 8 * w;
     const size_t kb = (size_t)x_row(p, m) * p.K + k0;
@@ -185,9 +191,20 @@ __device__ __forceinline__ void stage_x(const LinArgs& p, const float* rs, uint4
   }
 }
 
+template <bool XF32>
+__device__ __forceinline__ void stage_x(const LinArgs& p, const float* rs, uint4* xs_hi, uint4* xs_lo, int rstride,
+                                        int kt0, int nwords) {
+  stage_x<XF32>(p, rs, xs_hi, xs_lo, rstride, kt0, nwords, (int)threadIdx.x, (int)blockDim.x);
+}
+
 // Epilogue of one finished tile: fin[m * fs + s] holds the fp32 dot product of slot s, batch row m
 // (fs = 16, or 17 where a padded stride avoids shared-memory bank conflicts when it is written).
+// WARP: the calling warp alone does the work (lanes 0..31); else the whole CTA. The argmax form is
+// CTA-only.
+template <bool WARP = false>
 __device__ void epilogue_tile(const LinArgs& p, const float* fin, int rt, int* s_flag, int fs = 16) {
+  const int tid = WARP ? (int)(threadIdx.x & 31) : (int)threadIdx.x;
+  const int nth = WARP ? 32 : (int)blockDim.x;
   const int items = p.M * 16;
   if (p.epi == EPI_ARGMAX) {  // m == 1
     if (threadIdx.x < 16) {
@@ -215,7 +232,7 @@ __device__ void epilogue_tile(const LinArgs& p, const float* fin, int rt, int* s
   if (p.epi == EPI_ROPE_KV) {
     const int per = p.hd / 16;
     const int head = rt / per, j = rt - head * per;
-    for (int i = threadIdx.x; i < p.M * 8; i += blockDim.x) {
+    for (int i = tid; i < p.M * 8; i += nth) {
       const int m = i >> 3, s = i & 7;
       const int e1 = j * 8 + s, e2 = p.hd / 2 + j * 8 + s;
       const float x1 = fin[m * fs + s], x2 = fin[m * fs + s + 8];
@@ -243,7 +260,7 @@ __device__ void epilogue_tile(const LinArgs& p, const float* fin, int rt, int* s
     }
     return;
   }
-  for (int i = threadIdx.x; i < items; i += blockDim.x) {
+  for (int i = tid; i < items; i += nth) {
     const int m = i >> 4, s = i & 15;
     if (p.epi == EPI_SWIGLU) {
       const int col = rt * 8 + s;
@@ -425,12 +442,12 @@ __global__ void __launch_bounds__(256) q4_gemv_tma(LinArgs p) {
   stage_x<XF32>(p, s_rs, xs_hi, xs_lo, rstride, kt0, ntile * 16);
   __syncthreads();  // also publishes the initialised barrier to every thread
 
-  // 3) weights landed? (bounded: a copy that never completes sets a status bit instead of hanging)
+  // 3) weights landed? (bounded: a copy that never completes sets a status bit instead of hanging;
+  // the CTA then skips its MMAs but still arrives on the split-K counter, so the workspace counters
+  // return to zero, and waits once more for the copy before exiting)
   const bool ok = mbar_wait_bounded(&bar, 0, kWaitLimitNs);
-  if (__syncthreads_or(!ok)) {
-    if (threadIdx.x == 0) atomicOr(&g_linear_status, kStatusTimeout);
-    return;
-  }
+  const bool failed = __syncthreads_or(!ok);
+  if (failed && threadIdx.x == 0) atomicOr(&g_linear_status, kStatusTimeout);
 
   // 4) MMAs from shared memory
   float acc[MT][4];
@@ -441,7 +458,7 @@ __global__ void __launch_bounds__(256) q4_gemv_tma(LinArgs p) {
   for (int nt = 0; nt < MT; ++nt) mrow[nt] = min(nt * 8 + g, p.M - 1) * rstride;
   const unsigned char* swa = sw + g * p.wstride + t * 16;
   const unsigned char* swb = sw + (g + 8) * p.wstride + t * 16;
-  for (int kl = warp; kl < ntile; kl += W) {
+  for (int kl = failed ? ntile : warp; kl < ntile; kl += W) {
     const int grp = ((kt0 + kl) * TILE_K) / p.G;
     const float sa = __half2float(ss[g * KG + grp]);
     const float sb = __half2float(ss[(g + 8) * KG + grp]);
@@ -450,6 +467,7 @@ __global__ void __launch_bounds__(256) q4_gemv_tma(LinArgs p) {
     mma_tile<MT, XF32, false>(wa, wb, sa, sb, xs_hi, xs_lo, mrow, kl * 16 + 4 * t, acc);
   }
   finish_tile<MT>(p, acc, reinterpret_cast<float*>(smem_raw + p.x_off), &s_flag, rt, sp);
+  if (failed && threadIdx.x == 0) mbar_wait_bounded(&bar, 0, kWaitLimitNs);
 }
 
 // ---- kernel 4: persistent, weights streamed through a TMA ring ---------------------------------
@@ -537,8 +555,14 @@ __global__ void __launch_bounds__(768) q4_gemv_stream(LinArgs p) {
     }
     const bool ok = mbar_wait_bounded(&full[slot], (uint32_t)((i / kStreamRing) & 1), kWaitLimitNs);
     if (__syncthreads_or(!ok)) {
-      if (threadIdx.x == 0) atomicOr(&g_linear_status, kStatusTimeout);
-      return;
+      // a copy did not land: stop consuming, let the copies in flight (stages i .. i + ring - 1)
+      // finish before the CTA exits, and still fold into the argmax counter below so it completes
+      if (threadIdx.x == 0) {
+        atomicOr(&g_linear_status, kStatusTimeout);
+        for (int j = i; j < i + kStreamRing && j < nstages; ++j)
+          mbar_wait_bounded(&full[j % kStreamRing], (uint32_t)((j / kStreamRing) & 1), kWaitLimitNs);
+      }
+      break;
     }
     const unsigned char* sw = ring_w + slot * SWB + t * 16;
     const __half* ss = ring_s + slot * (SSB / 2);
@@ -587,6 +611,259 @@ __global__ void __launch_bounds__(768) q4_gemv_stream(LinArgs p) {
   }
   if (p.epi == EPI_ARGMAX && threadIdx.x == 0) {
     atomicMax(&p.state->best, best);
+    __threadfence();
+    if (p.finalize && atomicAdd(&p.state->counter, 1u) == gridDim.x - 1) {
+      __threadfence();
+      const unsigned long long b = atomicExch(&p.state->best, 0ull);
+      p.state->counter = 0u;
+      publish_token(p.state, p.token_log, (int32_t)argmax_index(b));
+    }
+  }
+}
+
+// ---- kernel 6: persistent bulk-copy ring GEMV ----------------------------------------------------
+//
+// Decode shapes: M <= 8 rows of x, G == 128, K % 1024 == 0, no fused norm. One CTA per SM, or two
+// (then the next kernel on the stream is resident beside this one and fills its own ring while this
+// one finishes), each with 8 consumer warps and 1 producer warp.
+//  - A stage is one row tile's 16 rows x 1024 k. One producer lane per row issues a 512-byte bulk
+//    copy into a row padded to 576 B (rows g and g + 1 of a quad read land on different bank halves),
+//    16 more lanes copy the rows' 8 fp16 scales; all complete on the slot's `full` mbarrier. The
+//    producer refills a slot when the 8 consumer warps have arrived on its `empty` mbarrier. It never
+//    waits for the previous kernel (the weights are not that kernel's output), so the ring fills
+//    while the previous kernel runs; only the consumers wait (griddepcontrol) before staging x.
+//  - Consumer warp w takes 128-k tile w of every stage (the LOP3 dequant + mma.sync math of kernels
+//    1 and 3) and keeps a row tile's sums in registers across its stages. At a row tile's last stage
+//    of this CTA every warp writes its 16 x M sums into the slot's reduction area; the last warp to
+//    arrive (a shared counter) adds the 8 in warp order and runs the epilogue, then releases the slot.
+//  - CTAs take equal runs of the RT x K/1024 stages. A row tile cut between CTAs is finished by the
+//    last of them through the split-K workspace (partials added in CTA order): deterministic results.
+//  - Every wait is bounded. A wait that gives up sets the status bit and the abort flag; the warps
+//    then finish their loops without waiting (all counters still arrive, so the workspace is left
+//    clean) and the producer waits for its copies in flight before the CTA exits.
+constexpr int kRingSK = 1024;
+constexpr int kRingCW = kRingSK / TILE_K;  // consumer warps: one 128-k tile of each stage
+constexpr int kRingThreads = (kRingCW + 1) * 32;
+constexpr int kRingRowPitch = kRingSK / 2 + 64;
+constexpr int kRingWBytes = 16 * kRingRowPitch;
+constexpr int kRingSlotBytes = kRingWBytes + 16 * 16;  // + 16 rows x 8 fp16 scales
+constexpr uint32_t kRingTx = 16 * (kRingSK / 2) + 16 * 16;
+constexpr int kRingMaxSlots = 24;
+
+// the CTA whose run of stages [c U / G, (c + 1) U / G) contains stage u
+__device__ __forceinline__ int ring_cta_of(long long u, long long U, int G) {
+  return (int)(((u + 1) * G + U - 1) / U) - 1;
+}
+
+// One warp finishes row tile rt: the 8 warps' sums (red [kRingCW][M*16]) in warp order, the
+// cross-CTA partials if the tile was cut, then the epilogue (argmax keys fold into *s_best).
+__device__ void ring_finish(const LinArgs& p, const float* red, float* fin, int rt, long long U,
+                            unsigned long long* s_best, int lane) {
+  const int items = p.M * 16;
+  for (int i = lane; i < items; i += 32) {
+    float v = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kRingCW; ++w) v += red[w * items + i];
+    fin[i] = v;
+  }
+  __syncwarp();
+  if (p.split_units) {
+    const long long ua = (long long)rt * p.kc;
+    const int c0 = ring_cta_of(ua, U, gridDim.x), c1 = ring_cta_of(ua + p.kc - 1, U, gridDim.x);
+    if (c1 > c0) {
+      float* part = p.ws + (size_t)rt * p.kc * items;
+      for (int i = lane; i < items; i += 32) part[((int)blockIdx.x - c0) * items + i] = fin[i];
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) last = atomicAdd(&p.counters[rt], 1u) == (unsigned)(c1 - c0);
+      if (!__shfl_sync(0xffffffffu, last, 0)) return;
+      __threadfence();
+      for (int i = lane; i < items; i += 32) {
+        float v = 0.0f;
+        for (int q = 0; q <= c1 - c0; ++q) v += __ldcg(part + q * items + i);
+        fin[i] = v;
+      }
+      if (lane == 0) p.counters[rt] = 0u;
+      __syncwarp();
+    }
+  }
+  if (p.epi == EPI_ARGMAX) {  // m == 1
+    unsigned long long key = 0ull;
+    if (lane < 16) {
+      const int row = rt * 16 + lane;
+      if (row < p.N) {
+        if (p.logits) p.logits[row] = fin[lane];
+        key = argmax_key(fin[lane], (unsigned)(p.index_offset + row));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+    if (lane == 0) atomicMax(s_best, key);
+    return;
+  }
+  epilogue_tile<true>(p, fin, rt, nullptr);
+}
+
+template <bool XF32, bool HL>
+__global__ void __launch_bounds__(kRingThreads, 2) q4_gemv_ring(LinArgs p) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ __align__(8) uint64_t full[kRingMaxSlots];
+  __shared__ __align__(8) uint64_t empty[kRingMaxSlots];
+  __shared__ int cnt[kRingMaxSlots];
+  __shared__ float s_fin[kRingCW][8 * 16];
+  __shared__ unsigned long long s_best;
+  __shared__ volatile int s_abort;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int S = p.ring_slots, KC = p.kc, nct = gridDim.x, c = blockIdx.x;
+  const long long U = (long long)p.RT * KC;
+  long long u0, u1;
+  if (p.split_units) {
+    u0 = (long long)c * U / nct;
+    u1 = (long long)(c + 1) * U / nct;
+  } else {
+    u0 = (long long)c * p.RT / nct * KC;
+    u1 = (long long)(c + 1) * p.RT / nct * KC;
+  }
+  const int n = (int)(u1 - u0);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kRingCW);
+      cnt[s] = 0;
+    }
+    s_best = 0ull;
+    s_abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  griddep_launch_dependents();
+  int issued = 0;  // producer: stages whose copies were issued
+
+  if (warp == kRingCW) {
+    // ---- producer warp ----
+    const uint64_t pol = l2_policy_evict_first();
+    const unsigned char* q8 = reinterpret_cast<const unsigned char*>(p.qw);
+    const int KG = p.K / 128;
+    const int r = lane & 15;
+    for (int i = 0; i < n; ++i) {
+      const int slot = i % S;
+      if (i >= S) {
+        int ok = 1;
+        if (lane == 0)
+          ok = !s_abort && mbar_wait_bounded(&empty[slot], (uint32_t)(((i / S) - 1) & 1), kWaitLimitNs) &&
+               !s_abort;
+        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+          if (lane == 0) {
+            atomicOr(&g_linear_status, kStatusTimeout);
+            s_abort = 1;
+          }
+          break;
+        }
+      }
+      const long long u = u0 + i;
+      const int rt = (int)(u / KC), kc = (int)(u - (long long)rt * KC);
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], kRingTx);
+      __syncwarp();
+      const int row = tile_row(p, rt, r);
+      unsigned char* sl = smem_raw + (size_t)slot * kRingSlotBytes;
+      if (lane < 16)
+        bulk_g2s_hint(sl + r * kRingRowPitch, q8 + (size_t)row * (p.K / 2) + (size_t)kc * (kRingSK / 2), kRingSK / 2,
+                      &full[slot], pol);
+      else
+        bulk_g2s_hint(sl + kRingWBytes + r * 16, p.scales + (size_t)row * KG + kc * 8, 16, &full[slot], pol);
+      issued = i + 1;
+    }
+  } else {
+    // ---- consumer warps ----
+    const int g = lane >> 2, t = lane & 3;
+    griddep_wait();
+    const int rstride = p.K / 8 + 4;
+    uint4* xs_hi = reinterpret_cast<uint4*>(smem_raw + p.x_off);
+    uint4* xs_lo = xs_hi + (size_t)p.M * rstride;
+    stage_x<XF32>(p, nullptr, xs_hi, xs_lo, rstride, 0, p.K / 8, (int)threadIdx.x, kRingCW * 32);
+    named_bar_sync(1, kRingCW * 32);
+    float* red = reinterpret_cast<float*>(smem_raw + p.red_off);  // [S][kRingCW][M * 16]
+    const int items = p.M * 16;
+    float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
+    float hl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    int mrow[1];
+    mrow[0] = min(g, p.M - 1) * rstride;
+    for (int i = 0; i < n; ++i) {
+      const int slot = i % S;
+      const long long u = u0 + i;
+      const int rt = (int)(u / KC), kc = (int)(u - (long long)rt * KC);
+      const bool last = kc == KC - 1 || i == n - 1;
+      int ok = !s_abort;
+      if (ok) ok = mbar_wait_bounded(&full[slot], (uint32_t)((i / S) & 1), kWaitLimitNs);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok && lane == 0) {
+        atomicOr(&g_linear_status, kStatusTimeout);
+        s_abort = 1;
+      }
+      uint4 wa = make_uint4(0u, 0u, 0u, 0u), wb = wa;
+      float sa = 0.0f, sb = 0.0f;
+      if (ok) {
+        const unsigned char* sl = smem_raw + (size_t)slot * kRingSlotBytes;
+        wa = *reinterpret_cast<const uint4*>(sl + g * kRingRowPitch + warp * 64 + t * 16);
+        wb = *reinterpret_cast<const uint4*>(sl + (g + 8) * kRingRowPitch + warp * 64 + t * 16);
+        const __half* ss = reinterpret_cast<const __half*>(sl + kRingWBytes);
+        sa = __half2float(ss[g * 8 + warp]);
+        sb = __half2float(ss[(g + 8) * 8 + warp]);
+      }
+      if (!last) {  // registers hold this warp's share: the slot may be refilled
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+      const int wbase = (kc * kRingCW + warp) * 16 + 4 * t;
+      if constexpr (HL)
+        mma_tile_hl(wa, wb, sa, sb, xs_hi, xs_lo, g, wbase, hl);
+      else
+        mma_tile<1, XF32, false>(wa, wb, sa, sb, xs_hi, xs_lo, mrow, wbase, acc);
+      if (last) {
+        float* rw = red + ((size_t)slot * kRingCW + warp) * items;
+        if constexpr (HL) {
+          if (t == 0) {
+            rw[g] = hl[0] + hl[1];
+            rw[g + 8] = hl[2] + hl[3];
+          }
+          hl[0] = hl[1] = hl[2] = hl[3] = 0.0f;
+        } else {
+          const int m0 = 2 * t;
+          if (m0 < p.M) {
+            rw[m0 * 16 + g] = acc[0][0];
+            rw[m0 * 16 + g + 8] = acc[0][2];
+          }
+          if (m0 + 1 < p.M) {
+            rw[(m0 + 1) * 16 + g] = acc[0][1];
+            rw[(m0 + 1) * 16 + g + 8] = acc[0][3];
+          }
+          acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.0f;
+        }
+        __syncwarp();
+        int prev = 0;
+        if (lane == 0) {
+          __threadfence_block();
+          prev = atomicAdd(&cnt[slot], 1);
+        }
+        if (__shfl_sync(0xffffffffu, prev, 0) == kRingCW - 1) {
+          __threadfence_block();
+          ring_finish(p, red + (size_t)slot * kRingCW * items, s_fin[warp], rt, U, &s_best, lane);
+          if (lane == 0) cnt[slot] = 0;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == kRingCW && lane == 0 && s_abort) {
+    // copies still in flight land in this CTA's shared memory: wait for them before exiting
+    for (int i = max(0, issued - S); i < issued; ++i)
+      mbar_wait_bounded(&full[i % S], (uint32_t)((i / S) & 1), kWaitLimitNs);
+  }
+  if (p.epi == EPI_ARGMAX && threadIdx.x == 0) {
+    atomicMax(&p.state->best, s_best);
     __threadfence();
     if (p.finalize && atomicAdd(&p.state->counter, 1u) == gridDim.x - 1) {
       __threadfence();
@@ -750,10 +1027,6 @@ __device__ __forceinline__ void k5_col(const LinArgs& p, int RTS, int c, int& rt
   }
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 template <int BN, bool XF32>
 __global__ void __launch_bounds__(K5_THREADS, 1)
     q4_gemm_tc(const __grid_constant__ CUtensorMap txh, const __grid_constant__ CUtensorMap txl,
@@ -763,9 +1036,10 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t raw_full[K5_RAW], raw_empty[K5_RAW], x_full[K5_XS], x_empty[K5_XS], deq_full[K5_DS],
-      deq_empty[K5_DS], acc_full[2], acc_free[2];
+      deq_empty[K5_DS], acc_full[2], acc_free[2], mma_done;
   __shared__ uint32_t s_tmem;
   __shared__ int s_fail, s_flag;
+  __shared__ int s_raw_n, s_x_n, s_mma_n;  // stages issued by each producer (drained on failure)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * K5_BM;
   const int rt0 = blockIdx.y * RTS;
@@ -792,7 +1066,9 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_free[i], 8);
     }
+    mbar_init(&mma_done, 1);
     s_fail = 0;
+    s_raw_n = s_x_n = s_mma_n = 0;
     fence_mbar_init();
   }
   if (warp == 13) tmem_alloc(&s_tmem, 2 * BN);
@@ -816,6 +1092,7 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
         const int j = g0 * SPG + i;
         uint8_t* dst = smem + L::RAW_OFF + rs * L::RAW_BYTES;
         for (int b = 0; b < nb; ++b) tma_load_2d(dst + b * rpb * 32, &tw, j * 8, k5_run_row(p, rt0, RTS, b), &raw_full[rs]);
+        s_raw_n = i + 1;
       }
     }
     __syncwarp();
@@ -834,6 +1111,7 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
         mbar_arrive_expect_tx(&x_full[xs], XF32 ? L::XSTAGE : L::X_BYTES);
         tma_load_2d(dst, &txh, kx, m0, &x_full[xs]);
         if constexpr (XF32) tma_load_2d(dst + L::X_BYTES, &txl, kx, m0, &x_full[xs]);
+        s_x_n = i + 1;
       }
     }
     __syncwarp();
@@ -903,6 +1181,7 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
         tc_commit(&x_empty[xs]);
         tc_commit(&deq_empty[ds]);
         if (kg == SPG - 1) tc_commit(&acc_full[b]);
+        s_mma_n = i + 1;
       }
     }
     __syncwarp();
@@ -938,12 +1217,35 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (s_fail) {
+    // a wait gave up: let this CTA's MMAs and copies in flight finish (bounded) before the TMEM
+    // is freed and the CTA exits
+    if (warp == 13 && lane == 0 && s_mma_n > 0) {
+      tc_commit(&mma_done);
+      mbar_wait_bounded(&mma_done, 0, kWaitLimitNs);
+    }
+    if (threadIdx.x == 0) {
+      for (int i = max(0, s_raw_n - K5_RAW); i < s_raw_n; ++i)
+        mbar_wait_bounded(&raw_full[i % K5_RAW], (uint32_t)((i / K5_RAW) & 1), kWaitLimitNs);
+      for (int i = max(0, s_x_n - K5_XS); i < s_x_n; ++i)
+        mbar_wait_bounded(&x_full[i % K5_XS], (uint32_t)((i / K5_XS) & 1), kWaitLimitNs);
+    }
+    __syncthreads();
+  }
   if (warp == 13) {
     tc_fence_after();
     tmem_dealloc(tmem, 2 * BN);
   }
   if (s_fail) {
-    if (threadIdx.x == 0) atomicOr(&g_linear_status, kStatusTimeout);
+    if (threadIdx.x == 0) {
+      atomicOr(&g_linear_status, kStatusTimeout);
+      // still arrive on the split-K counter (the tile's result is void, but the counter must end
+      // at zero for the next call that uses this workspace): the last arrival resets it
+      if (p.nsplit > 1) {
+        const size_t tile = (size_t)blockIdx.x * gridDim.y + blockIdx.y;
+        if (atomicAdd(&p.counters[tile], 1u) == (unsigned)(p.nsplit - 1)) p.counters[tile] = 0u;
+      }
+    }
     griddep_launch_dependents();
     return;
   }
@@ -1037,6 +1339,7 @@ struct Plan {
   bool ilp = false;                        // kernel 1: two accumulator chains
   int RT = 0;  // row tiles (grid.x)
   int wstride = 0, x_off = 0;
+  int ring_slots = 0, occ = 1, split_units = 0, red_off = 0;  // kernel 6
   size_t smem = 0;
   size_t ws_bytes = 0;
 };
@@ -1236,6 +1539,43 @@ static int plan_tc(int M, int K, int G, bool xf32, const q4b_linear_cfg* cfg, Pl
   return Q4B_OK;
 }
 
+// kernel 6: ring depth from the shared memory left beside the staged x and the reduction slots;
+// two CTAs per SM when that still leaves >= 6 stages, else one
+constexpr size_t kRingSmem2 = 108 * 1024;  // dynamic bytes per CTA with two resident per SM
+constexpr size_t kRingSmem1 = 200 * 1024;
+static bool ring_ok(int M, int K, int G, int epi, bool norm) {
+  return M <= 8 && G == 128 && K % kRingSK == 0 && !norm && (epi != EPI_ARGMAX || M == 1);
+}
+static size_t ring_xbytes(int M, int K, bool xf32) { return (size_t)M * (K / 8 + 4) * 16 * (xf32 ? 2 : 1); }
+static bool ring_layout(Plan& pl, int M, int K, bool xf32, int occ) {
+  const size_t xb = align_up(ring_xbytes(M, K, xf32), 128);
+  const size_t per = kRingSlotBytes + (size_t)kRingCW * M * 16 * 4;
+  const size_t budget = occ == 2 ? kRingSmem2 : kRingSmem1;
+  const long long slots = xb < budget ? (long long)((budget - xb) / per) : 0;
+  pl.ring_slots = (int)std::min<long long>(slots, kRingMaxSlots);
+  pl.occ = occ;
+  pl.x_off = pl.ring_slots * kRingSlotBytes;
+  pl.red_off = (int)(pl.x_off + xb);
+  pl.smem = pl.red_off + (size_t)pl.ring_slots * kRingCW * M * 16 * 4;
+  return pl.ring_slots >= (occ == 2 ? 6 : 3);
+}
+static size_t ring_ws(const Plan& pl, int M, int K) {
+  return kCounterBytes + align_up((size_t)pl.RT * (K / kRingSK) * M * 16 * 4, 256);
+}
+static int plan_ring(int M, int K, bool xf32, const q4b_linear_cfg* cfg, Plan& pl) {
+  pl.kernel = 6;
+  const int occ = cfg && cfg->tiles ? cfg->tiles : 0;
+  if (occ < 0 || occ > 2) return set_error(Q4B_EINVAL, "q4_linear: kernel 6 takes tiles = 1 or 2 CTAs per SM");
+  const bool ok =
+      occ ? ring_layout(pl, M, K, xf32, occ) : (ring_layout(pl, M, K, xf32, 2) || ring_layout(pl, M, K, xf32, 1));
+  if (!ok) return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 6 ring does not fit beside x (m=%d k=%d)", M, K);
+  pl.nsplit = 1;
+  pl.kps = K / TILE_K;
+  pl.split_units = !(cfg && cfg->split == 1) && pl.RT <= kMaxCounters;
+  pl.ws_bytes = pl.split_units ? ring_ws(pl, M, K) : 0;
+  return Q4B_OK;
+}
+
 static bool stream_ok(int M, int K, int G, bool norm) {
   (void)norm;
   return M == 1 && G == 128 && K % 1024 == 0 && K <= 8192;
@@ -1267,6 +1607,14 @@ static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, bool norm
     if (pl.MT > 2) return set_error(Q4B_EUNSUPPORTED, "q4_linear: TMA kernel needs m <= 16");
     return plan_tma(M, K, G, xf32, cfg, pl);
   }
+  if (want == 6) {
+    if (!ring_ok(M, K, G, epi, norm))
+      return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 6 needs m <= 8, group 128, k %% 1024 == 0, no fused norm");
+    return plan_ring(M, K, xf32, cfg, pl);
+  }
+  const bool tuned = !cfg || (!cfg->warps && !cfg->tiles && !cfg->split);
+  if (want == 0 && tuned && ring_ok(M, K, G, epi, norm) && plan_ring(M, K, xf32, nullptr, pl) == Q4B_OK)
+    return Q4B_OK;
   if (want == 4) {
     if (!stream_ok(M, K, G, norm))
       return set_error(Q4B_EUNSUPPORTED, "q4_linear: streaming kernel needs m == 1, group 128, k %% 1024 == 0, k <= 8192");
@@ -1278,26 +1626,34 @@ static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, bool norm
 }
 
 template <typename Kern>
-static cudaError_t set_smem_attr(Kern kern, unsigned long long& done) {
+static cudaError_t set_smem_attr(Kern kern, std::atomic<unsigned long long>& done, int bytes = (int)kMaxSmem) {
+  return set_max_dynamic_smem(kern, bytes, done);
+}
+
+// SMs of the current device (cached per device ordinal)
+static int num_sms() {
+  static std::atomic<int> cache[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (done >> (dev & 63) & 1ull) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
-  if (e == cudaSuccess) done |= 1ull << (dev & 63);
-  return e;
+  int v = cache[dev & 63].load(std::memory_order_relaxed);
+  if (!v) {
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev & 63].store(v, std::memory_order_relaxed);
+  }
+  return v;
 }
 
 template <int MT, bool XF32, int T>
 static cudaError_t launch_reg_t(const Plan& pl, const LinArgs& a, cudaStream_t st) {
   if constexpr (MT == 1 && (T == 3 || T == 8)) {  // the decode shapes: few-CTA launches take the ILP form
     if (pl.ilp) {
-      static unsigned long long done_ilp = 0;
+      static std::atomic<unsigned long long> done_ilp;
       cudaError_t e = set_smem_attr(q4_gemv_reg<MT, XF32, T, true>, done_ilp);
       if (e != cudaSuccess) return e;
       return launch_pdl(q4_gemv_reg<MT, XF32, T, true>, dim3(pl.RT, pl.nsplit), dim3(pl.W * 32), pl.smem, st, a);
     }
   }
-  static unsigned long long done = 0;
+  static std::atomic<unsigned long long> done;
   cudaError_t e = set_smem_attr(q4_gemv_reg<MT, XF32, T>, done);
   if (e != cudaSuccess) return e;
   return launch_pdl(q4_gemv_reg<MT, XF32, T>, dim3(pl.RT, pl.nsplit), dim3(pl.W * 32), pl.smem, st, a);
@@ -1332,7 +1688,7 @@ static cudaError_t launch_reg(const Plan& pl, const LinArgs& a, cudaStream_t st)
 
 template <int MT, bool XF32>
 static cudaError_t launch_tma_t(const Plan& pl, const LinArgs& a, cudaStream_t st) {
-  static unsigned long long done = 0;
+  static std::atomic<unsigned long long> done;
   cudaError_t e = set_smem_attr(q4_gemv_tma<MT, XF32>, done);
   if (e != cudaSuccess) return e;
   return launch_pdl(q4_gemv_tma<MT, XF32>, dim3(pl.RT, pl.nsplit), dim3(pl.W * 32), pl.smem, st, a);
@@ -1402,6 +1758,19 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
     if (forced) return set_error(Q4B_EINVAL, "q4_linear: qweight, x and ln_w must be 16-byte aligned");
     simt_plan(op, pl);
   }
+  if (pl.kernel == 6 && !aligned(op.scales, 16)) {  // scale rows arrive by bulk copies
+    if (forced) return set_error(Q4B_EINVAL, "q4_linear: kernel 6 needs 16-byte aligned scales");
+    Plan alt;
+    q4b_linear_cfg k1 = {1, 0, 0, 0};
+    if (plan_linear(op.m, op.n, op.k, op.group, op.epi, xf32, op.ln_w != nullptr, &k1, alt) == Q4B_OK)
+      pl = alt;
+    else
+      simt_plan(op, pl);
+  }
+  if (pl.kernel == 6 && pl.split_units && (pl.ws_bytes > op.ws_bytes || !op.ws || !aligned(op.ws, 16))) {
+    pl.split_units = 0;  // whole row tiles per CTA: no workspace needed
+    pl.ws_bytes = 0;
+  }
   if (pl.kernel == 5 && !tc_rope_ok(op.epi, op.head_dim, pl.bn)) {
     if (forced) return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 5 RoPE tiles need head_dim / 16 and the tile to nest");
     simt_plan(op, pl);
@@ -1468,10 +1837,14 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
   a.index_offset = op.index_offset;
   a.finalize = op.finalize;
   a.RT = pl.RT;
-  if (pl.kernel != 2 && pl.kernel != 5 && pl.nsplit > 1) {
+  if ((pl.kernel != 2 && pl.kernel != 5 && pl.nsplit > 1) || (pl.kernel == 6 && pl.split_units)) {
     a.counters = reinterpret_cast<unsigned*>(op.ws);
     a.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(op.ws) + kCounterBytes);
   }
+  a.ring_slots = pl.ring_slots;
+  a.kc = op.k / kRingSK;
+  a.split_units = pl.split_units;
+  a.red_off = pl.red_off;
   cudaError_t e;
   if (pl.kernel == 5) {
     char* w = reinterpret_cast<char*>(op.ws);
@@ -1491,16 +1864,11 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
     e = xf32 ? launch_pdl(q4_xsplit<true>, dim3(pgrid), dim3(256), 0, st, a, xh, xl)
              : launch_pdl(q4_xsplit<false>, dim3(pgrid), dim3(256), 0, st, a, xh, xl);
     if (e == cudaSuccess) {
-      static unsigned long long d[4] = {0, 0, 0, 0};
+      static std::atomic<unsigned long long> d[4];
       const dim3 grid(pl.tiles_m, pl.tiles_n, pl.nsplit);
-      auto go = [&](auto kern, unsigned long long& done) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (!(done >> (dev & 63) & 1ull)) {
-          cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem);
-          if (r != cudaSuccess) return r;
-          done |= 1ull << (dev & 63);
-        }
+      auto go = [&](auto kern, std::atomic<unsigned long long>& done) {
+        const cudaError_t r = set_smem_attr(kern, done, (int)pl.smem);
+        if (r != cudaSuccess) return r;
         return launch_pdl(kern, grid, dim3(K5_THREADS), pl.smem, st, th, tl, tw, a);
       };
       if (pl.bn == 128)
@@ -1508,8 +1876,16 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
       else
         e = xf32 ? go(q4_gemm_tc<64, true>, d[2]) : go(q4_gemm_tc<64, false>, d[3]);
     }
+  } else if (pl.kernel == 6) {
+    static std::atomic<unsigned long long> d[3];
+    const bool hl = xf32 && op.m == 1;
+    auto kern = hl ? q4_gemv_ring<true, true> : xf32 ? q4_gemv_ring<true, false> : q4_gemv_ring<false, false>;
+    e = set_smem_attr(kern, d[hl ? 0 : xf32 ? 1 : 2]);
+    const long long units = pl.split_units ? (long long)pl.RT * a.kc : pl.RT;
+    const int grid = (int)std::min<long long>(units, (long long)num_sms() * pl.occ);
+    if (e == cudaSuccess) e = launch_pdl(kern, dim3(grid), dim3(kRingThreads), pl.smem, st, a);
   } else if (pl.kernel == 4) {
-    static unsigned long long d0 = 0, d1 = 0;
+    static std::atomic<unsigned long long> d0, d1;
     e = xf32 ? set_smem_attr(q4_gemv_stream<true>, d1) : set_smem_attr(q4_gemv_stream<false>, d0);
     const int grid = std::min(pl.RT, kStreamCtas);
     if (e == cudaSuccess)
@@ -1520,7 +1896,7 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
   } else if (pl.kernel == 1) {
     e = xf32 ? launch_reg<true>(pl, a, st) : launch_reg<false>(pl, a, st);
   } else {
-    static unsigned long long d0 = 0, d1 = 0;
+    static std::atomic<unsigned long long> d0, d1;
     e = xf32 ? set_smem_attr(q4_linear_simt<true>, d1) : set_smem_attr(q4_linear_simt<false>, d0);
     if (e == cudaSuccess)
       e = xf32 ? launch_pdl(q4_linear_simt<true>, dim3(pl.RT), dim3(256), pl.smem, st, a)
@@ -1577,6 +1953,17 @@ extern "C" size_t q4b_q4_linear_workspace(int m, int n, int k, int group, int ep
   static const int dummy[4] = {0, 0, 0, 0};  // never dereferenced: planning only
   return linear_workspace(public_op(dummy, reinterpret_cast<const uint16_t*>(dummy), group, dummy, Q4B_F32,
                                     const_cast<int*>(dummy), Q4B_F32, m, n, k, epilogue, cfg, nullptr, 0));
+}
+
+extern "C" int q4b_q4_linear_kernel(int m, int n, int k, int group, int epilogue, int x_dtype,
+                                    const q4b_linear_cfg* cfg) {
+  static const int dummy[4] = {0, 0, 0, 0};  // never dereferenced: planning only
+  int rc = validate_linear(dummy, reinterpret_cast<const uint16_t*>(dummy), group, dummy, x_dtype,
+                           const_cast<int*>(dummy), Q4B_F32, m, n, k, epilogue);
+  if (rc) return rc;
+  Plan pl;
+  if ((rc = plan_linear(m, n, k, group, epilogue, x_dtype == Q4B_F32, false, cfg, pl))) return rc;
+  return pl.kernel;
 }
 
 extern "C" int q4b_q4_linear(const int32_t* qweight, const uint16_t* scales, int group, const void* x, int x_dtype,

@@ -95,7 +95,8 @@ CFGS = [dict(kernel=2), dict(kernel=1, warps=1, tiles=1), dict(kernel=1, warps=2
         dict(kernel=1, warps=4, tiles=2), dict(kernel=1, warps=4, tiles=1, split=6), dict(kernel=1, warps=8, tiles=3),
         dict(kernel=1, warps=6, tiles=4, split=1), dict(kernel=1, warps=3, tiles=3), dict(kernel=3),
         dict(kernel=3, warps=8), dict(kernel=3, split=3), dict(kernel=3, warps=2, split=5), dict(kernel=3, warps=1), dict(kernel=4),
-        dict(kernel=4, warps=8), dict(kernel=4, warps=24), dict(kernel=4, warps=3)]
+        dict(kernel=4, warps=8), dict(kernel=4, warps=24), dict(kernel=4, warps=3), dict(kernel=6),
+        dict(kernel=6, tiles=1), dict(kernel=6, split=1)]
 
 
 @pytest.mark.parametrize("cfg", CFGS, ids=[str(c) for c in CFGS])
@@ -117,6 +118,9 @@ def test_linear_config_space(dev, cfg):
             except q4b.Q4BError as e:  # a fixed configuration the planner rejects for this shape
                 if "streaming" in str(e):  # kernel 4: m == 1, group 128, k % 1024 == 0
                     assert M > 1 or K % 1024
+                    continue
+                if "kernel 6" in str(e):  # m <= 8, k % 1024 == 0, x staged whole beside the ring
+                    assert M > 8 or K % 1024 or "does not fit" in str(e), str(e)
                     continue
                 assert any(w in str(e) for w in ("shared memory", "tiles one of", "m <= 16", "leaves")), str(e)
                 continue
@@ -283,3 +287,85 @@ def test_tcgen05_gemm_is_deterministic_and_leaves_counters_zero(dev):
     assert torch.equal(y1, y2)
     ws = ops.WORKSPACE.bufs[(dev.index, torch.cuda.current_stream().cuda_stream)]
     assert int(ws[:65536].view(torch.int32).abs().sum()) == 0
+
+
+# ---- kernel 6: the persistent bulk-copy ring GEMV (decode rows) ---------------------------------
+K6_CASES = [(5120, 3072, 1), (3072, 8192, 1), (37, 1024, 1), (1000, 3072, 1), (200, 2048, 3), (1000, 8192, 4),
+            (520, 1024, 8), (16384, 3072, 2), (40000, 3072, 1)]
+K6_CFGS = [None, dict(kernel=6, tiles=1), dict(kernel=6, tiles=2), dict(kernel=6, split=1),
+           dict(kernel=6, tiles=1, split=1)]
+
+
+@pytest.mark.parametrize("cfg", K6_CFGS, ids=[str(c) for c in K6_CFGS])
+def test_ring_gemv_kernel(dev, cfg):
+    """Stages of 16 rows x 1024 k through a bulk-copy ring, row tiles cut between CTAs finished in
+    the workspace: every shape and configuration against the oracle (fp32 and fp16 x), the SwiGLU
+    and accumulate epilogues, bit-identical repeats, and counters back at zero."""
+    import q4b
+    from q4b import _lib, ops
+    for (N, K, M) in K6_CASES:
+        qw, s = gi.synthetic_q4(N, K, 128, seed=N + K + M)
+        x = np.random.default_rng(M + K).standard_normal((M, K)).astype(np.float32)
+        ref32 = O.q4_linear(qw, s, 128, x)
+        ref16 = O.q4_linear(qw, s, 128, x.astype(np.float16).astype(np.float32))
+        qwt, st = torch.from_numpy(qw).to(dev), torch.from_numpy(s).to(dev)
+        for xdt, ref in ((torch.float32, ref32), (torch.float16, ref16)):
+            xt = torch.from_numpy(x).to(dev).to(xdt)
+            try:
+                y = q4b.q4_linear(xt, qwt, st, 128, out=poisoned((M, N), torch.float32, dev), cfg=cfg)
+            except q4b.Q4BError as e:  # x too large to stage whole beside a ring at this occupancy
+                assert cfg and "does not fit" in str(e), str(e)
+                continue
+            assert O.rel_err(y.cpu().numpy(), ref) <= TOL, (N, K, M, xdt, cfg)
+            y2 = q4b.q4_linear(xt, qwt, st, 128, out=poisoned((M, N), torch.float32, dev), cfg=cfg)
+            assert torch.equal(y, y2), (N, K, M, cfg)
+        xt = torch.from_numpy(x).to(dev)
+        try:
+            if N % 2 == 0:
+                I = N // 2
+                y = q4b.q4_linear(xt, qwt, st, 128, epilogue="swiglu", out=poisoned((M, I), torch.float32, dev),
+                                  cfg=cfg)
+                sw = (O.silu(ref32[:, :I]) * ref32[:, I:]).astype(np.float32)
+                assert O.rel_err(y.cpu().numpy(), sw) <= TOL, ("swiglu", N, K, M, cfg)
+            h0 = np.random.default_rng(N).standard_normal((M, N)).astype(np.float32)
+            h = torch.from_numpy(h0).to(dev)
+            q4b.q4_linear(xt, qwt, st, 128, epilogue="accumulate", out=h, cfg=cfg)
+            assert O.rel_err(h.cpu().numpy(), h0 + ref32) <= TOL, ("accumulate", N, K, M, cfg)
+            hh = torch.from_numpy(h0).to(dev).half()
+            q4b.q4_linear(xt, qwt, st, 128, epilogue="accumulate", out=hh, cfg=cfg)
+            ref_h = h0.astype(np.float16).astype(np.float32) + ref32
+            assert O.rel_err(hh.float().cpu().numpy(), ref_h) <= TOL, ("accumulate fp16", N, K, M, cfg)
+        except q4b.Q4BError as e:
+            assert cfg and "does not fit" in str(e), str(e)
+    torch.cuda.synchronize()
+    ws = ops.WORKSPACE.bufs[(dev.index, torch.cuda.current_stream().cuda_stream)]
+    assert int(ws[:65536].view(torch.int32).abs().sum()) == 0
+    assert _lib.lib().q4b_device_status(1) == 0
+
+
+def test_ring_gemv_is_the_decode_default(dev):
+    """The planner sends the decode projections (m <= 8, group 128, K % 1024 == 0) to kernel 6."""
+    import q4b
+    L = q4b.lib()
+    for (n, k, m) in [(5120, 3072, 1), (3072, 3072, 1), (16384, 3072, 1), (3072, 8192, 1), (128256, 3072, 1),
+                      (5120, 3072, 8)]:
+        assert L.q4b_q4_linear_kernel(m, n, k, 128, 0, 1, None) == 6, (n, k, m)
+
+
+def test_ring_gemv_without_workspace(dev):
+    """Called through the C ABI with no workspace, kernel 6 keeps every row tile inside one CTA."""
+    import ctypes
+
+    import q4b
+    from q4b import _lib
+    N, K = 5120, 3072
+    qw, s = gi.synthetic_q4(N, K, 128, seed=21)
+    x = np.random.default_rng(3).standard_normal((1, K)).astype(np.float32)
+    qwt, st, xt = torch.from_numpy(qw).to(dev), torch.from_numpy(s).to(dev), torch.from_numpy(x).to(dev)
+    y = poisoned((1, N), torch.float32, dev)
+    rc = q4b.lib().q4b_q4_linear(qwt.data_ptr(), st.data_ptr(), 128, xt.data_ptr(), 0, y.data_ptr(), 0, 1, N, K, 0,
+                                 None, None, 0, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 0, q4b.lib().q4b_last_error()
+    torch.cuda.synchronize()
+    assert O.rel_err(y.cpu().numpy(), O.q4_linear(qw, s, 128, x)) <= TOL
+    assert _lib.lib().q4b_device_status(1) == 0
