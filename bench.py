@@ -1,6 +1,7 @@
 """Benchmark of the int4 Llama hot path on B200 (one process per GPU; torchrun for N > 1).
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemv|decode] [--impl ours|reference]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|gemv|sweep|profile]
+                  [--impl ours|reference]
 
 Prints ONE JSON line (rank 0). Workloads:
   decode  (default) BASELINE config 4: Llama-3.2-3B-shape LlamaQ4 (28 layers, hidden 3072, 24 heads,
@@ -9,12 +10,17 @@ Prints ONE JSON line (rank 0). Workloads:
           then greedy decode with KV buckets {256, ..., 4096} through the native runner (one CUDA
           graph per bucket). One step = one decode token; --steps K times K decode tokens (K + 1
           generated, the first from the prefill) after --warmup W untimed generate calls. At N > 1
-          the model is tensor-parallel over N GPUs (strong scaling). value = decode tokens/s.
+          the model is tensor-parallel over N GPUs (strong scaling). value = decode tokens/s. The
+          line carries BASELINE config 1 as its `gemv_5120x3072` object (value, roofline, e2e and
+          CPU baseline of its own).
   gemv    BASELINE config 1: int4 GEMV y[5120] = dequant(W)[5120, 3072] . x[3072], group 128, fp16 x/y.
-          One step = 32 back-to-back calls over 32 distinct weight copies (260 MB > 126 MB L2), each
-          a separate kernel launch captured in one CUDA graph (programmatic dependent launch lets a
+          One step = back-to-back calls over 33 distinct weight copies (> 2x the 126 MB L2), each a
+          separate kernel launch captured in one CUDA graph (programmatic dependent launch lets a
           call's weight stream start while the previous call finishes). value = weight+scale+x+y
           bytes moved per second, summed over ranks (replicas: the GEMV does not shard).
+  sweep   BASELINE config 5: every 3B projection and the lm_head at M in {1, 4, 16, 64} (--shapes,
+          --m), each row timed like config 1; value = aggregate GB/s, with one entry per row.
+  profile a short fixed launch sequence for profilers (--layers, --prefill, --ctx, --bucket).
 --impl reference times the CPU restatement of the reference path (oracle port) on the host cores of
 rank 0; other ranks exit without work.
 """
@@ -198,114 +204,47 @@ def cpu_gemv_baseline(budget_s=12.0):
 # ---------------------------------------------------------------------------------------------
 
 def run_gemv(args, rank, world, local, dist_mod):
-    import numpy as np
+    """BASELINE config 1 as its own line: value = weight + scale + x + y bytes per second of the
+    chained calls, summed over ranks (replicas: a 5120 x 3072 GEMV is one GPU's work)."""
     import torch
-
-    import q4b
-    from q4b import ops
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    g = torch.Generator(device=dev)
-    g.manual_seed(1234 + rank)
-    # synthetic inputs of BASELINE config 1: uniform nibbles packed 8 per int32, |N(0,0.02)| fp16 scales
-    qws = [torch.randint(-2**31, 2**31 - 1, (GEMV_N, GEMV_K // 8), dtype=torch.int32, device=dev, generator=g)
-           for _ in range(GEMV_COPIES)]
-    scs = [(torch.randn(GEMV_N, GEMV_K // GEMV_G, device=dev, generator=g) * 0.02).abs().half()
-           for _ in range(GEMV_COPIES)]
-    x = torch.randn(1, GEMV_K, device=dev, generator=g).half()
-    ys = [torch.empty(1, GEMV_N, dtype=torch.float16, device=dev) for _ in range(GEMV_COPIES)]
-    stream = torch.cuda.Stream(device=dev)
     cfg = json.loads(args.gemv_cfg) if args.gemv_cfg else None
-
-    def one_pass():
-        for i in range(GEMV_COPIES):
-            ops.q4_linear(x, qws[i], scs[i], GEMV_G, out=ys[i], cfg=cfg)
-
-    with torch.cuda.stream(stream):
-        one_pass()  # allocates the workspace outside the capture
-    stream.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        graph.capture_begin()
-        one_pass()
-        graph.capture_end()
-    stream.synchronize()
-    for _ in range(args.warmup):
-        with torch.cuda.stream(stream):
-            graph.replay()
-    stream.synchronize()
     if dist_mod:
         dist_mod.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
-        with torch.cuda.stream(stream):
-            ev0.record(stream)
-            for _ in range(args.steps):
-                graph.replay()
-            ev1.record(stream)
-        ev1.synchronize()
-    ms = ev0.elapsed_time(ev1)
-    if dist_mod:
-        dist_mod.barrier()
-    torch.cuda.synchronize()
-    ms_max = max_over_ranks(ms, dist_mod)
-    ms_step = ms_max / args.steps
-    per_call_s = ms_step / 1e3 / GEMV_COPIES
-    value = world * GEMV_COPIES * GEMV_BYTES / (ms_step / 1e3) / 1e9
-
-    # correctness spot check of the last pass against the CPU oracle restatement (rank 0, copy 0)
+        per_call, copies, qws, scs, x, ys = chain_measure(dev, GEMV_N, GEMV_K, 1, args.steps, args.warmup, cfg=cfg,
+                                                          seed=1234 + rank)
+    per_call = max_over_ranks(per_call, dist_mod)
+    ms_step = per_call * copies * 1e3
+    value = world * GEMV_BYTES / per_call / 1e9
     check = None
-    if rank == 0:
+    if rank == 0:  # parity spot check of the last pass against the CPU restatement (copy 0)
         from oracle import q4_oracle as O
-        y0 = ys[0].float().cpu().numpy()
         ref = O.q4_linear(qws[0].cpu().numpy(), scs[0].cpu().numpy(), GEMV_G, x.float().cpu().numpy())
-        check = O.rel_err(y0, ref)
-
-    # end to end through the public API: pinned host x -> QLinear.forward -> pinned host y, per call
-    ql = q4b.QLinear.from_packed(qws[0], scs[0], GEMV_G)
-    xh = x.cpu().pin_memory()
-    yh = torch.empty(1, GEMV_N, dtype=torch.float16).pin_memory()
-    e2e_steps = max(args.steps, 50)
-    for i in range(5):
-        xd = xh.to(dev, non_blocking=True)
-        yh.copy_(ql(xd), non_blocking=True)
-    torch.cuda.synchronize()
-    if dist_mod:
-        dist_mod.barrier()
-    t0 = time.perf_counter()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(e2e_steps):
-        xd = xh.to(dev, non_blocking=True)
-        yh.copy_(ql(xd), non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-    e1.record()
-    e1.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, dist_mod)
-    wall_ms = (time.perf_counter() - t0) * 1e3 / e2e_steps
-
+        check = O.rel_err(ys[0].float().cpu().numpy(), ref)
+    e2e_ms = max_over_ranks(gemv_e2e(dev, qws[0], scs[0], x, max(args.steps, 50)), dist_mod)
     if rank != 0:
         return None
     pk = peaks()
-    traffic = profile_traffic("q4_gemv_mma_5120x3072")
+    k = kernel_of(1, GEMV_N, GEMV_K, cfg)
     line = {
         "metric": METRIC_GEMV, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int4 weights, fp16 x/y, fp32 accumulate", "data": "synthetic",
         "config": {"workload": "int4 GEMV 5120x3072 group 128 M=1 (BASELINE config 1)",
-                   "calls_per_step": GEMV_COPIES, "l2": f"inputs larger than L2: {GEMV_COPIES} distinct weight "
+                   "calls_per_step": copies, "l2": f"inputs larger than L2: {copies} distinct weight "
                    f"copies x {GEMV_BYTES / 1e6:.2f} MB", "parallelism": f"replicas x{world}",
-                   "launch": "CUDA graph of separate launches with programmatic dependent launch"},
-        "roofline": {"bound": "hbm", "achieved": round(GEMV_BYTES / per_call_s / 1e9, 1), "peak": pk["hbm_gbs"],
-                     "unit": "GB/s", "frac": round(GEMV_BYTES / per_call_s / 1e9 / pk["hbm_gbs"], 4),
-                     "traffic": traffic, "peak_source": pk["source"], "kernel": "q4_gemv_mma",
+                   "launch": "CUDA graph of separate launches with programmatic dependent launch", "cfg": cfg},
+        "roofline": {"bound": "hbm", "achieved": round(GEMV_BYTES / per_call / 1e9, 1), "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(GEMV_BYTES / per_call / 1e9 / pk["hbm_gbs"], 4),
+                     "traffic": profile_traffic("q4_gemv_ring_5120x3072") if k == 6 else None,
+                     "peak_source": pk["source"], "kernel": f"q4_linear kernel {k}",
                      "algorithmic_bytes_per_launch": GEMV_BYTES},
         "e2e": {"value": round(world * GEMV_BYTES / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
-                "h2d_bytes_per_step": GEMV_K * 2, "d2h_bytes_per_step": GEMV_N * 2,
-                "ms_per_call": round(e2e_ms, 4), "wall_ms_per_call": round(wall_ms, 4),
+                "h2d_bytes_per_step": GEMV_K * 2, "d2h_bytes_per_step": GEMV_N * 2, "ms_per_call": round(e2e_ms, 4),
                 "path": "q4b.QLinear.forward per call with pinned-host x in and y out, synchronised"},
-        "gpu_launches": args.steps * GEMV_COPIES,
+        "gpu_launches": args.steps * copies,
         "clocks": clk.summary(),
         "parity_rel_err": check,
     }
@@ -396,7 +335,7 @@ def run_decode(args, rank, world, local, dist_mod):
     same = toks_e2e == toks
     gemv = None
     if world == 1 and not args.no_gemv:
-        gemv = gemv_measure(dev, steps=50, warmup=5)
+        gemv = gemv_measure(dev, steps=50, warmup=5, cpu=not args.no_cpu_baseline)
     if rank != 0:
         return None
     pk = peaks()
@@ -443,27 +382,60 @@ def run_decode(args, rank, world, local, dist_mod):
     return line
 
 
-def gemv_measure(dev, steps=50, warmup=5):
-    """BASELINE config 1 inside the decode run: GB/s of 32 chained launches over distinct weights."""
+L2_BYTES = 126 * 2**20
+SWEEP_SHAPES = {"qkv": (5120, 3072), "o": (3072, 3072), "gu": (16384, 3072), "down": (3072, 8192),
+                "lm": (128256, 3072)}
+
+
+def linear_bytes(n, k, m, g=128):
+    """Algorithmic bytes of one q4_linear call: int4 weights + fp16 scales + fp16 x and y."""
+    return n * k // 2 + 2 * n * (k // g) + 2 * m * k + 2 * m * n
+
+
+def kernel_of(m, n, k, cfg=None, x_f16=True):
+    """The kernel number the library's planner picks (include/q4b.h, q4b_q4_linear_kernel)."""
+    import ctypes
+
+    import q4b
+    from q4b import _lib
+    c = _lib.LinearCfg(**cfg) if cfg else None
+    return int(q4b.lib().q4b_q4_linear_kernel(m, n, k, 128, 0, 1 if x_f16 else 0, ctypes.byref(c) if c else None))
+
+
+def chain_measure(dev, n, k, m, steps, warmup, cfg=None, seed=99):
+    """Seconds per q4_linear call over distinct weight copies (together more than twice the 126 MB
+    L2, so every call streams its weights from HBM), each call a separate launch, all captured in
+    one CUDA graph (programmatic dependent launch lets a call's weight stream start while the
+    previous call finishes). Returns (seconds per call, copies, weights, scales, x, outputs)."""
+    import math
+
     import torch
 
+    import q4b
     from q4b import ops
+    wbytes = n * k // 2 + 2 * n * (k // 128)
+    copies = max(1, math.ceil(2 * L2_BYTES / wbytes))
     g = torch.Generator(device=dev)
-    g.manual_seed(99)
-    qws = [torch.randint(-2**31, 2**31 - 1, (GEMV_N, GEMV_K // 8), dtype=torch.int32, device=dev, generator=g)
-           for _ in range(GEMV_COPIES)]
-    scs = [(torch.randn(GEMV_N, GEMV_K // GEMV_G, device=dev, generator=g) * 0.02).abs().half()
-           for _ in range(GEMV_COPIES)]
-    x = torch.randn(1, GEMV_K, device=dev, generator=g).half()
-    ys = [torch.empty(1, GEMV_N, dtype=torch.float16, device=dev) for _ in range(GEMV_COPIES)]
+    g.manual_seed(seed)
+    # BASELINE config 1's inputs: uniform nibbles packed 8 per int32, |N(0, 0.02)| fp16 scales, fp16 x
+    qws = [torch.randint(-2**31, 2**31 - 1, (n, k // 8), dtype=torch.int32, device=dev, generator=g)
+           for _ in range(copies)]
+    scs = [(torch.randn(n, k // 128, device=dev, generator=g) * 0.02).abs().half() for _ in range(copies)]
+    x = torch.randn(m, k, device=dev, generator=g).half()
+    ys = [torch.empty(m, n, dtype=torch.float16, device=dev) for _ in range(copies)]
     stream = torch.cuda.Stream(device=dev)
+
+    def one_pass():
+        for i in range(copies):
+            ops.q4_linear(x, qws[i], scs[i], 128, out=ys[i], cfg=cfg)
+
     with torch.cuda.stream(stream):
-        for i in range(GEMV_COPIES):
-            ops.q4_linear(x, qws[i], scs[i], GEMV_G, out=ys[i])
-        graph = torch.cuda.CUDAGraph()
+        one_pass()  # allocates the workspace outside the capture
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
         graph.capture_begin()
-        for i in range(GEMV_COPIES):
-            ops.q4_linear(x, qws[i], scs[i], GEMV_G, out=ys[i])
+        one_pass()
         graph.capture_end()
         for _ in range(warmup):
             graph.replay()
@@ -475,12 +447,128 @@ def gemv_measure(dev, steps=50, warmup=5):
             graph.replay()
         e1.record(stream)
     e1.synchronize()
-    per_call = e0.elapsed_time(e1) / 1e3 / (steps * GEMV_COPIES)
+    if q4b.lib().q4b_device_status(1) != 0:
+        raise RuntimeError("q4b: a bounded device wait gave up during the measurement")
+    per_call = e0.elapsed_time(e1) / 1e3 / (steps * copies)
+    del graph
+    return per_call, copies, qws, scs, x, ys
+
+
+def gemv_e2e(dev, qw, sc, x, steps):
+    """Config 1 end to end through the public API: pinned host x -> QLinear.forward -> pinned host
+    y, synchronised after every call (ms per call)."""
+    import torch
+
+    import q4b
+    ql = q4b.QLinear.from_packed(qw, sc, GEMV_G)
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(1, GEMV_N, dtype=torch.float16).pin_memory()
+    for _ in range(5):
+        yh.copy_(ql(xh.to(dev, non_blocking=True)), non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        yh.copy_(ql(xh.to(dev, non_blocking=True)), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e1.record()
+    e1.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def gemv_measure(dev, steps=50, warmup=5, cpu=True):
+    """BASELINE config 1 inside the decode run: its own value, roofline, e2e and CPU baseline."""
+    from oracle import q4_oracle as O
+    per_call, copies, qws, scs, x, ys = chain_measure(dev, GEMV_N, GEMV_K, 1, steps, warmup)
+    ref = O.q4_linear(qws[0].cpu().numpy(), scs[0].cpu().numpy(), GEMV_G, x.float().cpu().numpy())
+    err = O.rel_err(ys[0].float().cpu().numpy(), ref)
+    e2e_ms = gemv_e2e(dev, qws[0], scs[0], x, max(steps, 50))
     pk = peaks()
     gbs = GEMV_BYTES / per_call / 1e9
-    return {"metric": METRIC_GEMV, "value": round(gbs, 1), "unit": "GB/s", "us_per_call": round(per_call * 1e6, 3),
-            "frac": round(gbs / pk["hbm_gbs"], 4), "peak": pk["hbm_gbs"], "calls": steps * GEMV_COPIES,
-            "l2": f"{GEMV_COPIES} distinct weight copies (260 MB > L2)"}
+    k = kernel_of(1, GEMV_N, GEMV_K)
+    out = {"metric": METRIC_GEMV, "value": round(gbs, 1), "unit": "GB/s", "us_per_call": round(per_call * 1e6, 3),
+           "kernel": f"q4_linear kernel {k}", "calls": steps * copies,
+           "l2": f"{copies} distinct weight copies ({copies * GEMV_BYTES / 1e6:.0f} MB > L2)",
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                        "frac": round(gbs / pk["hbm_gbs"], 4), "peak_source": pk["source"],
+                        "traffic": profile_traffic("q4_gemv_ring_5120x3072") if k == 6 else None,
+                        "algorithmic_bytes_per_launch": GEMV_BYTES},
+           "e2e": {"value": round(GEMV_BYTES / (e2e_ms / 1e3) / 1e9, 2), "unit": "GB/s",
+                   "h2d_bytes_per_step": GEMV_K * 2, "d2h_bytes_per_step": GEMV_N * 2, "ms_per_call": round(e2e_ms, 4),
+                   "path": "q4b.QLinear.forward per call with pinned-host x in and y out, synchronised"},
+           "parity_rel_err": err}
+    if cpu:
+        out["cpu_baseline"] = cpu_gemv_baseline()
+    return out
+
+
+def run_sweep(args, rank, world, local, dist_mod):
+    """every 3B projection (and the lm_head) at M in {1, 4, 16, 64}, each timed as
+    a chain over distinct weight copies, against the HBM roofline; one GPU per rank (replicas)."""
+    import torch
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pk = peaks()
+    rows, tot_b, tot_s = [], 0, 0.0
+    shapes = args.shapes or list(SWEEP_SHAPES)
+    cfg = json.loads(args.gemv_cfg) if args.gemv_cfg else None
+    for name in shapes:
+        n, k = SWEEP_SHAPES[name]
+        for m in args.m:
+            per_call, copies, *_ = chain_measure(dev, n, k, m, args.steps, args.warmup, cfg=cfg)
+            b = linear_bytes(n, k, m)
+            gbs = b / per_call / 1e9
+            rows.append({"shape": name, "N": n, "K": k, "M": m, "bytes": b, "us_per_call": round(per_call * 1e6, 3),
+                         "GB_s": round(gbs, 1), "frac": round(gbs / pk["hbm_gbs"], 4), "weight_copies": copies,
+                         "kernel": kernel_of(m, n, k, cfg)})
+            tot_b += b
+            tot_s += per_call
+            torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    value = world * tot_b / tot_s / 1e9
+    return {"metric": "int4 projection sweep GB/s (3B shapes x M)", "value": round(value, 1), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, fp16 x/y, fp32 accumulate",
+            "data": "synthetic", "config": {"workload": "batched int4 projection sweep (BASELINE config 5)",
+                                            "parallelism": f"replicas x{world}", "cfg": cfg,
+                                            "l2": "each row: distinct weight copies > 2x L2"},
+            "roofline": {"bound": "hbm", "peak": pk["hbm_gbs"], "unit": "GB/s", "peak_source": pk["source"],
+                         "achieved": round(tot_b / tot_s / 1e9, 1),
+                         "frac": round(tot_b / tot_s / 1e9 / pk["hbm_gbs"], 4), "traffic": None},
+            "rows": rows, "gpu_launches": sum(r["weight_copies"] for r in rows) * args.steps}
+
+
+def run_profile(args, rank, world, local, dist_mod):
+    """A short fixed launch sequence for profilers: a 3B-shaped model with --layers layers, an optional
+    --prefill C chunk at position 0, then --steps single-token decode steps at position --ctx."""
+    import torch
+
+    import q4b
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = dict(q4b.SYNTHETIC["3b"], num_hidden_layers=args.layers)
+    model = q4b.LlamaQ4(None, group=128, max_ctx=max(args.bucket, args.ctx + args.steps + 1),
+                        sd=q4b.SyntheticStateDict(cfg, device=dev), cfg=cfg, max_chunk=max(8, args.prefill),
+                        device=dev)
+    caches = model.new_caches()
+    if args.prefill:
+        toks = torch.arange(args.prefill, dtype=torch.int32).reshape(1, -1) * 7 + 3
+        model.step(toks, torch.tensor([0]), torch.tensor([args.prefill - 1]), caches, max(args.bucket, args.prefill))
+    tok = torch.tensor([[17]], dtype=torch.int32)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        nxt, _ = model.step(tok, torch.tensor([args.ctx + i]), torch.tensor([0]), caches, args.bucket)
+        tok = nxt.reshape(1, 1)
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    return {"metric": "profile sequence (3B shape)", "value": round(ms / args.steps, 4), "unit": "ms/step",
+            "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": 0,
+            "config": {"workload": "profile", "layers": args.layers, "ctx": args.ctx, "bucket": args.bucket,
+                       "prefill": args.prefill}, "last_token": int(tok)}
 
 
 def run_reference(args, rank, world):
@@ -515,16 +603,22 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="decode: tokens (255); gemv: graph replays (200)")
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "sweep", "profile"])
+    ap.add_argument("--shapes", nargs="*", default=None, help="sweep: subset of " + " ".join(SWEEP_SHAPES))
+    ap.add_argument("--m", nargs="*", type=int, default=[1, 4, 16, 64], help="sweep: rows of x")
+    ap.add_argument("--layers", type=int, default=1, help="profile: layers of the 3B-shaped model")
+    ap.add_argument("--ctx", type=int, default=128, help="profile: position of the first decode step")
+    ap.add_argument("--bucket", type=int, default=256, help="profile: KV bucket of the decode steps")
+    ap.add_argument("--prefill", type=int, default=0, help="profile: rows of one prefill chunk run first")
     ap.add_argument("--no-gemv", action="store_true", help="decode: skip the config-1 GEMV sub-measurement")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gemv-cfg", default=None, help='JSON q4b_linear_cfg, e.g. {"warps":4,"tiles":2}')
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    if args.warmup < 3:
+    if args.warmup < 3 and args.workload != "profile":
         args.warmup = 3
     if args.steps is None:
-        args.steps = 255 if args.workload == "decode" else 200
+        args.steps = {"decode": 255, "gemv": 200, "sweep": 20, "profile": 3}[args.workload]
     rank, world, local = dist_env()
     if args.impl == "reference":
         line = run_reference(args, rank, world)
@@ -533,7 +627,8 @@ def main():
         return
     dist_mod = init_dist(world, local)
     try:
-        line = (run_decode if args.workload == "decode" else run_gemv)(args, rank, world, local, dist_mod)
+        run = {"decode": run_decode, "gemv": run_gemv, "sweep": run_sweep, "profile": run_profile}[args.workload]
+        line = run(args, rank, world, local, dist_mod)
     finally:
         if dist_mod:
             dist_mod.barrier()

@@ -1,4 +1,4 @@
-"""The roofline arithmetic of bench.py and q4b.sweep on the CPU: the algorithmic bytes each bench
+"""The roofline arithmetic of bench.py on the CPU: the algorithmic bytes each bench
 line divides by the measured time, and the traffic figures it reads from profiles/."""
 
 import pathlib
@@ -10,7 +10,6 @@ sys.path.insert(0, str(ROOT / "iree-adreno-genai-tuner_b200"))
 
 import bench  # noqa: E402
 import q4b  # noqa: E402
-from q4b import sweep  # noqa: E402
 
 
 def test_decode_bytes_per_token_3b():
@@ -25,7 +24,7 @@ def test_decode_bytes_per_token_3b():
 
 def test_gemv_config1_bytes():
     assert bench.GEMV_BYTES == 8_126_464  # qweight + scales + x + y of the 5120 x 3072 GEMV
-    assert sweep.algorithmic_bytes(5120, 3072, 1) == bench.GEMV_BYTES
+    assert bench.linear_bytes(5120, 3072, 1) == bench.GEMV_BYTES
 
 
 def test_profile_traffic_lines():
