@@ -7,9 +7,9 @@ gemm/cost_model.py:1-198 of the reference).
                       plus split-K partial traffic; + reduction and launch overheads. Peaks come
                       from MEASURED_PEAKS.json when present (driver-measured copy GB/s and dense
                       bf16 TFLOP/s), else the pool's earlier measurement.
-  Learned             gradient-boosted trees on schedule + shape features (including the analytic
-                      estimate) -> log(us), trained online on every measurement across shapes;
-                      used once it has enough samples, the analytic estimate ranks until then.
+  ResidualModel       the analytic estimate corrected by a ridge regression of log(measured /
+                      analytic) on schedule + shape features, refitted after every batch of
+                      measurements and shared across shapes.
 """
 
 from __future__ import annotations
@@ -95,34 +95,47 @@ def features(s, sc: Schedule) -> np.ndarray:
     return np.array([float(x) for x in f])
 
 
-class Learned:
-    """Online gradient-boosted regressor on log(us); falls back to the analytic model."""
+class ResidualModel:
+    """Analytic estimate times a learned correction: log(us) = log(analytic_us) + w . z(features),
+    where z standardises the features over the measurements seen so far and w is a ridge
+    regression of the log residuals (closed form, numpy). With no measurements w = 0 and the
+    prediction is the analytic estimate; the ridge penalty shrinks the correction towards zero
+    while measurements are few, so the model moves away from the analytic ranking only as far as
+    the data supports. One instance is shared across shapes: the features are shape-relative, so
+    residuals measured on one shape correct the ranking on the next."""
 
-    def __init__(self, min_samples: int = 24):
-        self.X, self.y = [], []
-        self.model = None
-        self.min_samples = min_samples
+    def __init__(self, ridge: float = 4.0):
+        self.ridge = ridge
+        self.rows, self.resid = [], []
+        self.w = None
+        self.mu = self.sd = None
 
     def add(self, s, sc: Schedule, us: float):
-        self.X.append(features(s, sc))
-        self.y.append(math.log(us))
+        self.rows.append(features(s, sc))
+        self.resid.append(math.log(us) - math.log(analytic_us(s, sc)))
 
     def fit(self):
-        if len(self.y) < self.min_samples:
-            self.model = None
+        if not self.rows:
+            self.w = None
             return
-        from sklearn.ensemble import HistGradientBoostingRegressor
-        self.model = HistGradientBoostingRegressor(max_iter=200, learning_rate=0.08, max_leaf_nodes=15,
-                                                   min_samples_leaf=4, l2_regularization=0.1, random_state=0)
-        self.model.fit(np.array(self.X), np.array(self.y))
+        X = np.stack(self.rows)
+        self.mu = X.mean(0)
+        self.sd = X.std(0)
+        self.sd[self.sd < 1e-9] = 1.0
+        Z = np.hstack([np.ones((len(X), 1)), (X - self.mu) / self.sd])
+        r = np.asarray(self.resid)
+        A = Z.T @ Z + self.ridge * np.eye(Z.shape[1])
+        self.w = np.linalg.solve(A, Z.T @ r)
+
+    def correction(self, s, sc: Schedule) -> float:
+        if self.w is None:
+            return 0.0
+        z = np.concatenate([[1.0], (features(s, sc) - self.mu) / self.sd])
+        return float(z @ self.w)
 
     def predict_us(self, s, scheds) -> np.ndarray:
-        if not scheds:
-            return np.array([])
-        if self.model is None:
-            return np.array([analytic_us(s, sc) for sc in scheds])
-        return np.exp(self.model.predict(np.array([features(s, sc) for sc in scheds])))
+        return np.array([analytic_us(s, sc) * math.exp(self.correction(s, sc)) for sc in scheds])
 
     @property
     def kind(self) -> str:
-        return "learned" if self.model is not None else "analytic"
+        return "analytic" if self.w is None else f"analytic+residual({len(self.rows)})"

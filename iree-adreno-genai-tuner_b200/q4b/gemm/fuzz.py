@@ -13,7 +13,7 @@ import pathlib
 import random
 
 from .schedule import Schedule, default_schedule
-from .search import Log, measure, random_sched
+from .search import Recorder, admissible, run_candidates
 from .shapes import BY_ID, REF_SHAPES, make_data
 from .verifier import library_accepts, verify
 
@@ -22,16 +22,10 @@ FIXED = [Schedule(kernel=2), Schedule(kernel=1, bn=64, stages=2, split=1), Sched
 
 
 def pick_schedules(s, n, rng):
-    picks, seen = [], set()
-    tries = 0
-    while len(picks) < n and tries < 50 * n:
-        tries += 1
-        sc = random_sched(s, rng)
-        if sc.key() in seen:
-            continue
-        seen.add(sc.key())
-        if verify(s, sc).ok and library_accepts(s, sc):
-            picks.append(sc)
+    """n admissible schedules drawn at random, plus the corners and the library default."""
+    pool, _ = admissible(s)
+    picks = rng.sample(pool, min(n, len(pool)))
+    seen = {sc.key() for sc in picks}
     for sc in FIXED + [default_schedule(s)]:
         if sc.key() not in seen and verify(s, sc).ok and library_accepts(s, sc):
             seen.add(sc.key())
@@ -44,13 +38,13 @@ def run(shapes, per_shape, out, tag, seed=7, **hkw):
     data = out / "data"
     log_dir = out / tag
     log_dir.mkdir(parents=True, exist_ok=True)
-    log, rng, tot = Log(log_dir / "log.jsonl"), random.Random(seed), collections.Counter()
+    rec, rng, tot = Recorder(log_dir / "log.jsonl"), random.Random(seed), collections.Counter()
     failures = []
     for s in shapes:
         if not (data / s.id / "meta.txt").exists():
             make_data(s, data / s.id)
         picks = pick_schedules(s, per_shape, rng)
-        res = measure(s, picks, data, log_dir, tag, log, dict(method="fuzz", round=0, model="none"), **hkw)
+        res = run_candidates(s, picks, data, log_dir, tag, rec, "fuzz", **hkw)
         ok = sum(1 for sc in picks if res.get(sc.key()))
         tot["ok"] += ok
         tot["n"] += len(picks)

@@ -1,151 +1,178 @@
-"""Schedule search for q4b_gemm_f16: propose -> verify -> rank (cost model) -> measure the top k
-through the harness -> learn (the CUDA counterpart of gemm/search.py:1-275 of the reference).
+"""Schedule search for q4b_gemm_f16 (the CUDA counterpart of the reference's gemm/search.py:148-215
+propose -> verify -> rank -> measure -> refit loop).
 
-  python -m q4b.gemm.search --shapes B1 B2 --budget 48 --batch 12 --method model random --tag run1
+  python -m q4b.gemm.search --shapes B1 B2 --budget 48 --batch 12 --method ranked random --tag run1
 
-method=model   evolutionary search: each round pools random schedules plus mutations / crossovers of
-               the best measured ones, keeps the verifier-approved ones the library also accepts,
-               ranks them with the cost model, measures the top `batch` (25% exploration picks) in
-               one harness call, refits the model.
-method=random  the same GPU budget spent on verifier-approved schedules in random order.
-Every candidate's verdict, prediction and measurement goes to <out>/<tag>/log.jsonl; the best
-schedule per shape goes to <out>/<tag>/best.json ({shape id: candidate string}).
+The CUDA schedule space of one shape is small (tile width x ring depth x k split, a few hundred
+points), so it is enumerated whole and filtered once by the verifier and by the library's own
+plan check; the search then spends its GPU budget in batches over that admissible set:
+
+  ranked  each batch is the unmeasured schedules the cost model predicts fastest, except that a
+          quarter of it goes to the best-predicted schedule of each tile width neither measured
+          nor in the batch yet (the strata the model knows least about); after each batch the
+          residual model is refitted on every measurement so far (all shapes) and the remainder
+          re-ranked.
+  random  the same budget on admissible schedules in a seeded random order (the control).
+
+Every measurement and every batch summary is one JSON object in <out>/<tag>/log.jsonl (see
+Recorder); the fastest correct schedule per shape goes to <out>/<tag>/best.json as
+{shape id: {"candidate", "us", "tflops"}}.
 """
 
 from __future__ import annotations
 
 import argparse
-import collections
-import dataclasses
+import itertools
 import json
 import pathlib
 import random
 import time
+import zlib
+
+import numpy as np
 
 from . import harness
-from .cost_model import Learned
+from .cost_model import ResidualModel
 from .schedule import Schedule, default_schedule, domains
 from .shapes import BY_ID, SHAPES, make_data
 from .verifier import library_accepts, verify
 
 
-def random_sched(s, rng):
+def space(s):
+    """Every tcgen05 schedule the domains of shape s name (unverified), one per distinct kernel."""
     d = domains(s)
-    return Schedule(kernel=1, bn=rng.choice(d["bn"]), stages=rng.choice(d["stages"]), split=rng.choice(d["split"]))
-
-
-def mutate(s, sc, rng):
-    d = domains(s)
-    k = dataclasses.asdict(sc)
-    for name in rng.sample(list(d), rng.choice([1, 1, 2])):
-        k[name] = rng.choice(d[name])
-    k["kernel"] = 1
-    return Schedule(**k)
-
-
-def crossover(a, b, rng):
-    ka, kb = dataclasses.asdict(a), dataclasses.asdict(b)
-    return Schedule(**{n: (ka if rng.random() < 0.5 else kb)[n] for n in ka})
-
-
-class Log:
-    def __init__(self, path):
-        self.f = open(path, "a")
-
-    def write(self, **kw):
-        self.f.write(json.dumps(kw) + "\n")
-        self.f.flush()
-
-
-def measure(s, scheds, data_dir, out_dir, tag, log, meta, metric="us", **hkw):
-    """Run a batch through the harness. Returns {key: time or None}."""
-    cands, by_name = [], {}
-    for i, sc in enumerate(scheds):
-        name = f"{s.id}_{tag}_{i}"
-        cands.append({"name": name, "shape_dir": str(data_dir / s.id), "candidate": sc.candidate()})
-        by_name[name] = sc
-    res = harness.run_batch(cands, out_dir, f"{s.id}_{tag}", **hkw) if cands else {}
-    out = {}
-    for name, sc in by_name.items():
-        r = res.get(name, {"ok": False, "error": "missing"})
-        good = bool(r.get("ok")) and r.get("us") is not None
-        out[sc.key()] = r[metric] if good else None
-        log.write(**meta, shape=s.id, sched=dataclasses.asdict(sc), stage="gpu", ok=good, us=r.get("us"),
-                  us_min=r.get("us_min"), err=r.get("err"), error=r.get("error"),
-                  tflops=(s.flops / (r["us"] * 1e6)) if good else None)
+    out, keys = [], set()
+    for bn, st, sp in itertools.product(d["bn"], d["stages"], d["split"]):
+        sc = Schedule(kernel=1, bn=bn, stages=st, split=sp)
+        if sc.key() not in keys:
+            keys.add(sc.key())
+            out.append(sc)
     return out
 
 
-def tune(s, method, budget, batch, model, data_dir, out_dir, log, seed=0, pool=400, init=None, **hkw):
-    rng = random.Random(seed * 1000 + int(s.id[1:]) + (0 if method == "model" else 7))
-    measured = dict(init or {})  # key -> (sched, us or None)
-    budget += len(measured)
-    rejected = collections.Counter()
-    round_i = 0
-    while len(measured) < budget:
-        props = [random_sched(s, rng) for _ in range(pool)]
-        if method == "model":
-            good = sorted(((us, sc) for sc, us in measured.values() if us), key=lambda t: t[0])[:8]
-            for _ in range(pool if good else 0):
-                p = rng.choice(good)[1]
-                props.append(mutate(s, p, rng) if rng.random() < 0.75 else crossover(p, rng.choice(good)[1], rng))
-        seen, valid = set(measured), []
-        for sc in props:
-            k = sc.key()
-            if k in seen:
-                continue
-            seen.add(k)
-            v = verify(s, sc)
-            if v.ok and not library_accepts(s, sc):
-                v.ok, v.reasons = False, ["library-rejects"]
-            if v.ok:
-                valid.append(sc)
-            else:
-                rejected.update(v.reasons)
-        if not valid:
-            break
-        take = min(batch, budget - len(measured))
-        meta = dict(method=method, round=round_i, model=model.kind if method == "model" else "none")
-        if method == "random":
-            rng.shuffle(valid)
-            pick, preds = valid[:take], [None] * min(take, len(valid))
+def admissible(s):
+    """(schedules the verifier passes and the library plans, {reason: count} of the rest)."""
+    ok, why = [], {}
+    for sc in space(s):
+        v = verify(s, sc)
+        reasons = list(v.reasons) if not v.ok else ([] if library_accepts(s, sc) else ["library-rejects"])
+        if reasons:
+            for r in reasons:
+                why[r] = why.get(r, 0) + 1
         else:
-            preds_all = model.predict_us(s, valid)
-            order = sorted(range(len(valid)), key=lambda i: preds_all[i])
-            n_exploit = max(1, int(take * 0.75))
-            exploit = [valid[i] for i in order[:n_exploit]]
-            rest = [valid[i] for i in order[n_exploit:]]
-            pick = exploit + rng.sample(rest, min(len(rest), take - n_exploit))
-            idx = {sc.key(): i for i, sc in enumerate(valid)}
-            preds = [float(preds_all[idx[sc.key()]]) for sc in pick]
+            ok.append(sc)
+    return ok, why
+
+
+class Recorder:
+    """Append-only JSON-lines record of a search: {"t": seconds since start, "event": ..., ...}."""
+
+    def __init__(self, path):
+        self.path = pathlib.Path(path)
+        self.t0 = time.time()
+
+    def __call__(self, event: str, **fields):
+        with self.path.open("a") as f:
+            f.write(json.dumps({"t": round(time.time() - self.t0, 3), "event": event, **fields}) + "\n")
+
+
+def run_candidates(s, scheds, data_dir, out_dir, tag, rec, strategy, round_i=0, predicted=None, **hkw):
+    """Measure schedules of shape s in one harness process. Returns {schedule key: us or None};
+    a wrong result, a launch error or a lost device counts as None."""
+    names = [f"{s.id}_{tag}_{i}" for i in range(len(scheds))]
+    cands = [{"name": n, "shape_dir": str(pathlib.Path(data_dir) / s.id), "candidate": sc.candidate()}
+             for n, sc in zip(names, scheds)]
+    results = harness.run_batch(cands, out_dir, f"{s.id}_{tag}", **hkw) if cands else {}
+    out = {}
+    for i, (n, sc) in enumerate(zip(names, scheds)):
+        r = results.get(n, {"ok": False, "error": "no result"})
+        good = bool(r.get("ok")) and r.get("us") is not None
+        status = "ok" if good else ("wrong" if r.get("err") is not None and not r.get("ok") else "failed")
+        out[sc.key()] = float(r["us"]) if good else None
+        rec("measurement", shape=s.id, strategy=strategy, round=round_i, schedule=sc.candidate(),
+            predicted_us=None if predicted is None else round(float(predicted[i]), 3),
+            us=r.get("us"), us_min=r.get("us_min"), rel_err=r.get("err"), status=status, error=r.get("error"),
+            tflops=round(s.flops / (r["us"] * 1e6), 2) if good else None)
+    return out
+
+
+def rank_corr(a, b):
+    """Spearman correlation of two equal-length sequences (ties broken by position)."""
+    if len(a) < 3:
+        return None
+    ra = np.argsort(np.argsort(np.asarray(a, dtype=float)))
+    rb = np.argsort(np.argsort(np.asarray(b, dtype=float)))
+    if ra.std() == 0 or rb.std() == 0:
+        return None
+    return float(np.corrcoef(ra, rb)[0, 1])
+
+
+def pick_ranked(pool, pred, take, measured_bn):
+    """take schedules from pool: the best predicted, except that a quarter of the batch (at least
+    one) goes to the best-predicted schedule of each tile width that is neither measured yet nor
+    already in the batch, strata taken in order of their best prediction."""
+    order = sorted(range(len(pool)), key=lambda i: pred[i])
+    quota = max(1, take // 4)
+    chosen = order[: max(0, take - quota)]
+    covered = measured_bn | {pool[i].bn for i in chosen}
+    for i in order:  # stratum leaders: first (best-predicted) schedule of each uncovered width
+        if len(chosen) >= take:
+            break
+        if pool[i].bn not in covered:
+            covered.add(pool[i].bn)
+            chosen.append(i)
+    for i in order:  # fill the rest of the batch by prediction
+        if len(chosen) >= take:
+            break
+        if i not in chosen:
+            chosen.append(i)
+    return chosen
+
+
+def tune(s, strategy, budget, batch, model, data_dir, out_dir, rec, seed=0, **hkw):
+    """Spend `budget` measurements of shape s with `strategy`. Returns {key: (schedule, us or None)}."""
+    pool, rejected = admissible(s)
+    rng = random.Random(zlib.crc32(f"{s.id}/{strategy}/{seed}".encode()))
+    if strategy == "random":
+        rng.shuffle(pool)
+    done = {}
+    round_i = 0
+    while len(done) < budget and pool:
+        take = min(batch, budget - len(done), len(pool))
+        if strategy == "random":
+            idx = list(range(take))
+            pred = None
+        else:
+            pred_all = model.predict_us(s, pool)
+            idx = pick_ranked(pool, pred_all, take, {sc.bn for sc, _ in done.values()})
+            pred = [pred_all[i] for i in idx]
+        scheds = [pool[i] for i in idx]
         t0 = time.time()
-        res = measure(s, pick, data_dir, out_dir, f"{method}{round_i}", log, meta, **hkw)
-        for sc in pick:
-            us = res.get(sc.key())
-            measured[sc.key()] = (sc, us)
-            if us:
-                model.add(s, sc, us)
-        pairs = [(pr, res.get(sc.key())) for sc, pr in zip(pick, preds) if pr and res.get(sc.key())]
-        rho = None
-        if len(pairs) >= 5 and len({p for p, _ in pairs}) > 1 and len({m for _, m in pairs}) > 1:
-            from scipy.stats import spearmanr
-            rho = float(spearmanr([p for p, _ in pairs], [m for _, m in pairs]).correlation)
+        res = run_candidates(s, scheds, data_dir, out_dir, f"{strategy}{round_i}", rec, strategy, round_i, pred, **hkw)
+        for sc in scheds:
+            done[sc.key()] = (sc, res.get(sc.key()))
+            if res.get(sc.key()):
+                model.add(s, sc, res[sc.key()])
+        taken = set(idx)
+        pool = [sc for j, sc in enumerate(pool) if j not in taken]
         model.fit()
-        best = min((us for _, us in measured.values() if us), default=None)
-        log.write(kind="round", shape=s.id, method=method, round=round_i, n=len(measured), best_us=best, rho=rho,
-                  valid=len(valid), proposed=len(props), gpu_s=round(time.time() - t0, 1), model=meta["model"],
-                  rejected=dict(rejected))
-        print(f"  {s.id} {method:6s} round {round_i}: measured {len(measured):3d}  best "
-              f"{best and s.flops / (best * 1e6):8.1f} TFLOP/s  rank-rho {rho if rho is None else round(rho, 2)}  "
-              f"[{meta['model']}] valid {len(valid)}/{len(props)}", flush=True)
+        ok = [(p, res[sc.key()]) for sc, p in zip(scheds, pred or [None] * len(scheds)) if res.get(sc.key()) and p]
+        best = min((us for _, us in done.values() if us), default=None)
+        corr = rank_corr([p for p, _ in ok], [m for _, m in ok]) if ok else None
+        rec("round", shape=s.id, strategy=strategy, round=round_i, measured=len(done), remaining=len(pool),
+            best_us=best, best_tflops=round(s.flops / (best * 1e6), 2) if best else None, rank_corr=corr,
+            model=model.kind, rejected=rejected, gpu_s=round(time.time() - t0, 1))
+        print(f"  {s.id} {strategy:6s} batch {round_i}: {len(done):3d} measured, best "
+              f"{(s.flops / (best * 1e6)) if best else 0:8.1f} TFLOP/s, rank corr "
+              f"{'-' if corr is None else f'{corr:.2f}'} [{model.kind}]", flush=True)
         round_i += 1
-    return measured, rejected
+    return done
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--shapes", nargs="+", default=[s.id for s in SHAPES])
-    ap.add_argument("--method", nargs="+", default=["model", "random"])
+    ap.add_argument("--method", nargs="+", default=["ranked", "random"], choices=["ranked", "random"])
     ap.add_argument("--budget", type=int, default=48)
     ap.add_argument("--batch", type=int, default=12)
     ap.add_argument("--tag", default="run1")
@@ -157,8 +184,8 @@ def main(argv=None):
     out = pathlib.Path(a.out) / a.tag
     out.mkdir(parents=True, exist_ok=True)
     data = pathlib.Path(a.out) / "data"
-    log = Log(out / "log.jsonl")
-    model = Learned()  # shared across shapes: knowledge transfers from earlier shapes
+    rec = Recorder(out / "log.jsonl")
+    model = ResidualModel()  # one model for every shape: residuals transfer through the features
     hkw = dict(target_ms=a.target_ms, reps=a.reps, cold=a.cold)
     best = {}
     for sid in a.shapes:
@@ -166,19 +193,19 @@ def main(argv=None):
         if not (data / s.id / "meta.txt").exists():
             make_data(s, data / s.id)
         print(f"== {s.id} {s.name} M={s.M} N={s.N} K={s.K} {s.layout}", flush=True)
-        base = measure(s, [Schedule(kernel=2), default_schedule(s)], data, out, "baseline", log,
-                       dict(method="baseline", round=0, model="none"), **hkw)
-        for sc in (Schedule(kernel=2), default_schedule(s)):
+        anchors = [Schedule(kernel=2), default_schedule(s)]
+        base = run_candidates(s, anchors, data, out, "anchor", rec, "anchor", **hkw)
+        seen = {sc.key(): (sc, base.get(sc.key())) for sc in anchors}
+        for sc in anchors:
             us = base.get(sc.key())
             print(f"  {sc.short():24s}: {us and s.flops / (us * 1e6):8.1f} TFLOP/s ({us} us)", flush=True)
-        results = {sc.key(): (sc, base.get(sc.key())) for sc in (Schedule(kernel=2), default_schedule(s))}
         for m in a.method:
-            measured, _ = tune(s, m, a.budget, a.batch, model, data, out, log, **hkw)
-            results.update(measured)
-        top = min(((us, sc) for sc, us in results.values() if us), key=lambda t: t[0], default=None)
-        if top:
-            best[s.id] = {"candidate": top[1].candidate(), "us": top[0], "tflops": s.flops / (top[0] * 1e6)}
-            print(f"  best {top[1].short()}: {best[s.id]['tflops']:.1f} TFLOP/s ({top[0]:.2f} us)", flush=True)
+            seen.update(tune(s, m, a.budget, a.batch, model, data, out, rec, **hkw))
+        fastest = min(((us, sc) for sc, us in seen.values() if us), key=lambda t: t[0], default=None)
+        if fastest:
+            us, sc = fastest
+            best[s.id] = {"candidate": sc.candidate(), "us": us, "tflops": s.flops / (us * 1e6)}
+            print(f"  best {sc.short()}: {best[s.id]['tflops']:.1f} TFLOP/s ({us:.2f} us)", flush=True)
     (out / "best.json").write_text(json.dumps(best, indent=1) + "\n")
     return 0
 
