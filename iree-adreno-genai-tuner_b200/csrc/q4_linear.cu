@@ -621,111 +621,184 @@ __global__ void __launch_bounds__(768) q4_gemv_stream(LinArgs p) {
   }
 }
 
-// ---- kernel 6: persistent bulk-copy ring GEMV ----------------------------------------------------
+// ---- kernel 6: persistent ring GEMV ------------------------------------------------------------
 //
-// Decode shapes: M <= 8 rows of x, G == 128, K % 1024 == 0, no fused norm. One CTA per SM, or two
-// (then the next kernel on the stream is resident beside this one and fills its own ring while this
-// one finishes), each with 8 consumer warps and 1 producer warp.
-//  - A stage is one row tile's 16 rows x 1024 k. One producer lane per row issues a 512-byte bulk
-//    copy into a row padded to 576 B (rows g and g + 1 of a quad read land on different bank halves),
-//    16 more lanes copy the rows' 8 fp16 scales; all complete on the slot's `full` mbarrier. The
-//    producer refills a slot when the 8 consumer warps have arrived on its `empty` mbarrier. It never
-//    waits for the previous kernel (the weights are not that kernel's output), so the ring fills
-//    while the previous kernel runs; only the consumers wait (griddepcontrol) before staging x.
-//  - Consumer warp w takes 128-k tile w of every stage (the LOP3 dequant + mma.sync math of kernels
-//    1 and 3) and keeps a row tile's sums in registers across its stages. At a row tile's last stage
-//    of this CTA every warp writes its 16 x M sums into the slot's reduction area; the last warp to
-//    arrive (a shared counter) adds the 8 in warp order and runs the epilogue, then releases the slot.
-//  - CTAs take equal runs of the RT x K/1024 stages. A row tile cut between CTAs is finished by the
-//    last of them through the split-K workspace (partials added in CTA order): deterministic results.
+// Decode shapes: M <= 8 rows of x, G == 128, K % 1024 == 0, no fused norm. One CTA per SM (cfg
+// tiles = 2: two) with 8 consumer warps and 1 producer warp, sized so that one CTA of the next
+// kernel on the stream still fits beside it: that kernel starts under programmatic dependent launch
+// and fills its own ring while this one finishes.
+//  - A stage is a row pair (two row tiles, 32 rows) x 1024 k: one 2-D TMA box of {128 int32 words,
+//    32 rows} of int4 and one of {8 fp16 scales, 32 rows} (SwiGLU and RoPE tiles, whose rows come
+//    in runs of 8, take four 8-row boxes of each), 16896 bytes completing on the slot's `full`
+//    mbarrier. Few large copies per stage keep the copy engine's per-copy cost off the critical
+//    path. The producer refills a slot once the 8 consumer warps have arrived on its `empty`
+//    mbarrier. It never waits for the previous kernel (the weights are not that kernel's output);
+//    only the consumers wait (griddepcontrol) before staging x.
+//  - Consumer warp w takes 128-k tile w of both row tiles of every stage: two independent tiles per
+//    barrier wait, sharing one set of x fragments (the LOP3 dequant + mma.sync math of kernels 1 and
+//    3), and keeps the row pair's sums in registers across its stages. Loop indices advance by
+//    increments (no divisions in the stream loop). At a row pair's last stage of this CTA every warp
+//    writes its sums into the slot's reduction area; the last warp to arrive (a shared counter) adds
+//    the 8 in warp order and runs the epilogue, then releases the slot.
+//  - CTAs take equal runs of the NRP x K/1024 stages (NRP row pairs). A row pair cut between CTAs
+//    is finished by the last of them through the split-K workspace (partials added in CTA order):
+//    deterministic results.
 //  - Every wait is bounded. A wait that gives up sets the status bit and the abort flag; the warps
 //    then finish their loops without waiting (all counters still arrive, so the workspace is left
 //    clean) and the producer waits for its copies in flight before the CTA exits.
 constexpr int kRingSK = 1024;
 constexpr int kRingCW = kRingSK / TILE_K;  // consumer warps: one 128-k tile of each stage
 constexpr int kRingThreads = (kRingCW + 1) * 32;
-constexpr int kRingRowPitch = kRingSK / 2 + 64;
-constexpr int kRingWBytes = 16 * kRingRowPitch;
-constexpr int kRingSlotBytes = kRingWBytes + 16 * 16;  // + 16 rows x 8 fp16 scales
-constexpr uint32_t kRingTx = 16 * (kRingSK / 2) + 16 * 16;
-constexpr int kRingMaxSlots = 24;
+constexpr int kRingRowPitch = kRingSK / 2;  // a TMA box lands rows densely
+constexpr int kRingWBytes = 32 * kRingRowPitch;
+constexpr int kRingSlotBytes = kRingWBytes + 32 * 16;  // + 32 rows x 8 fp16 scales (16896, 128-B multiple)
+constexpr uint32_t kRingTx = kRingSlotBytes;
+constexpr int kRingMaxSlots = 16;
 
 // the CTA whose run of stages [c U / G, (c + 1) U / G) contains stage u
 __device__ __forceinline__ int ring_cta_of(long long u, long long U, int G) {
   return (int)(((u + 1) * G + U - 1) / U) - 1;
 }
 
-// One warp finishes row tile rt: the 8 warps' sums (red [kRingCW][M*16]) in warp order, the
-// cross-CTA partials if the tile was cut, then the epilogue (argmax keys fold into *s_best).
-__device__ void ring_finish(const LinArgs& p, const float* red, float* fin, int rt, long long U,
+// first weight row of run `half` (slots 0..7 or 8..15) of a SwiGLU / RoPE row tile
+__device__ __forceinline__ int ring_run_row(const LinArgs& p, int rt, int half) {
+  if (p.epi == EPI_SWIGLU) return half * p.n_out + rt * 8;
+  const int per = p.hd / 16;
+  const int head = rt / per, j = rt - head * per;
+  return head * p.hd + half * (p.hd / 2) + j * 8;
+}
+
+// x row 0 (after the row select) for the int8 tile form (mma_tile_i8): per 128-k group, terms
+// m = 0..2 as {even, odd} byte words at xq[m * qstride + word] (qstride = K/8 + 8 uint2, so the three
+// terms' rows fall on different bank halves) and xg[group] = {X_a, X_b, X_c, sx}. Warp w of nw
+// stages groups w, w + nw, ...; lane l holds k = 4l .. 4l + 3 of the group.
+template <bool XF32>
+__device__ void stage_x_i8(const LinArgs& p, uint2* xq, int4* xg, int qstride, int warp, int lane, int nw) {
+  const int NG = p.K / 128;
+  const size_t base = (size_t)x_row(p, 0) * p.K;
+  for (int grp = warp; grp < NG; grp += nw) {
+    const int k0 = grp * 128 + 4 * lane;
+    float v[4];
+    if constexpr (XF32) {
+      const float4 f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.x) + base + k0);
+      v[0] = f.x, v[1] = f.y, v[2] = f.z, v[3] = f.w;
+    } else {
+      const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(p.x) + base + k0);
+      const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+      const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+      v[0] = f0.x, v[1] = f0.y, v[2] = f1.x, v[3] = f1.y;
+    }
+    const float am = warp_max(fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
+    const float sx = am > 0.0f ? am / 127.0f : 1.0f;
+    int q[3][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float u = v[i] / sx;
+      const float a = fminf(fmaxf(rintf(u), -127.0f), 127.0f);
+      const float r = (u - a) * 254.0f;
+      const float b = fminf(fmaxf(rintf(r), -127.0f), 127.0f);
+      const float c = fminf(fmaxf(rintf((r - b) * 254.0f), -127.0f), 127.0f);
+      q[0][i] = (int)a, q[1][i] = (int)b, q[2][i] = (int)c;
+    }
+    int X[3];
+#pragma unroll
+    for (int m = 0; m < 3; ++m) {
+      int sum = q[m][0] + q[m][1] + q[m][2] + q[m][3];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      X[m] = sum;
+      // k % 8 = 4 (lane & 1) + i: even bytes hold k % 8 = 0, 2, 4, 6, odd bytes 1, 3, 5, 7
+      const uint32_t ev = (q[m][0] & 0xFF) | ((q[m][2] & 0xFF) << 8);
+      const uint32_t od = (q[m][1] & 0xFF) | ((q[m][3] & 0xFF) << 8);
+      const uint32_t mine = ev | (od << 16);
+      const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 1);
+      if (!(lane & 1))
+        xq[(size_t)m * qstride + grp * 16 + (lane >> 1)] =
+            make_uint2((mine & 0xFFFFu) | (other << 16), (mine >> 16) | (other & 0xFFFF0000u));
+    }
+    if (lane == 0) xg[grp] = make_int4(X[0], X[1], X[2], __float_as_int(sx));
+  }
+}
+
+// One warp finishes row pair rp: per row tile the 8 warps' sums (red [kRingCW][2][M*16]) in warp
+// order, the cross-CTA partials if the pair was cut, then the epilogue (argmax keys fold into
+// *s_best).
+__device__ void ring_finish(const LinArgs& p, const float* red, float* fin, int rp, long long U,
                             unsigned long long* s_best, int lane) {
   const int items = p.M * 16;
-  for (int i = lane; i < items; i += 32) {
+  for (int i = lane; i < 2 * items; i += 32) {
     float v = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kRingCW; ++w) v += red[w * items + i];
+    for (int w = 0; w < kRingCW; ++w) v += red[w * 2 * items + i];
     fin[i] = v;
   }
   __syncwarp();
   if (p.split_units) {
-    const long long ua = (long long)rt * p.kc;
+    const long long ua = (long long)rp * p.kc;
     const int c0 = ring_cta_of(ua, U, gridDim.x), c1 = ring_cta_of(ua + p.kc - 1, U, gridDim.x);
     if (c1 > c0) {
-      float* part = p.ws + (size_t)rt * p.kc * items;
-      for (int i = lane; i < items; i += 32) part[((int)blockIdx.x - c0) * items + i] = fin[i];
+      float* part = p.ws + (size_t)rp * p.kc * 2 * items;
+      for (int i = lane; i < 2 * items; i += 32) part[((int)blockIdx.x - c0) * 2 * items + i] = fin[i];
       __threadfence();
       __syncwarp();
       int last = 0;
-      if (lane == 0) last = atomicAdd(&p.counters[rt], 1u) == (unsigned)(c1 - c0);
+      if (lane == 0) last = atomicAdd(&p.counters[rp], 1u) == (unsigned)(c1 - c0);
       if (!__shfl_sync(0xffffffffu, last, 0)) return;
       __threadfence();
-      for (int i = lane; i < items; i += 32) {
+      for (int i = lane; i < 2 * items; i += 32) {
         float v = 0.0f;
-        for (int q = 0; q <= c1 - c0; ++q) v += __ldcg(part + q * items + i);
+        for (int q = 0; q <= c1 - c0; ++q) v += __ldcg(part + q * 2 * items + i);
         fin[i] = v;
       }
-      if (lane == 0) p.counters[rt] = 0u;
+      if (lane == 0) p.counters[rp] = 0u;
       __syncwarp();
     }
   }
-  if (p.epi == EPI_ARGMAX) {  // m == 1
-    unsigned long long key = 0ull;
-    if (lane < 16) {
-      const int row = rt * 16 + lane;
-      if (row < p.N) {
-        if (p.logits) p.logits[row] = fin[lane];
-        key = argmax_key(fin[lane], (unsigned)(p.index_offset + row));
+  for (int j = 0; j < 2; ++j) {
+    const int rt = 2 * rp + j;
+    if (rt >= p.RT) break;
+    const float* f = fin + j * items;
+    if (p.epi == EPI_ARGMAX) {  // m == 1
+      unsigned long long key = 0ull;
+      if (lane < 16) {
+        const int row = rt * 16 + lane;
+        if (row < p.N) {
+          if (p.logits) p.logits[row] = f[lane];
+          key = argmax_key(f[lane], (unsigned)(p.index_offset + row));
+        }
       }
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
-    if (lane == 0) atomicMax(s_best, key);
-    return;
+      for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+      if (lane == 0) atomicMax(s_best, key);
+    } else {
+      epilogue_tile<true>(p, f, rt, nullptr);
+    }
   }
-  epilogue_tile<true>(p, fin, rt, nullptr);
 }
 
-template <bool XF32, bool HL>
-__global__ void __launch_bounds__(kRingThreads, 2) q4_gemv_ring(LinArgs p) {
+template <bool XF32, bool M1>
+__global__ void __launch_bounds__(kRingThreads, 2)
+    q4_gemv_ring(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ts, LinArgs p) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t full[kRingMaxSlots];
   __shared__ __align__(8) uint64_t empty[kRingMaxSlots];
   __shared__ int cnt[kRingMaxSlots];
-  __shared__ float s_fin[kRingCW][8 * 16];
   __shared__ unsigned long long s_best;
   __shared__ volatile int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = p.ring_slots, KC = p.kc, nct = gridDim.x, c = blockIdx.x;
-  const long long U = (long long)p.RT * KC;
+  const int NRP = (p.RT + 1) / 2;
+  const long long U = (long long)NRP * KC;
   long long u0, u1;
   if (p.split_units) {
     u0 = (long long)c * U / nct;
     u1 = (long long)(c + 1) * U / nct;
   } else {
-    u0 = (long long)c * p.RT / nct * KC;
-    u1 = (long long)(c + 1) * p.RT / nct * KC;
+    u0 = (long long)c * NRP / nct * KC;
+    u1 = (long long)(c + 1) * NRP / nct * KC;
   }
   const int n = (int)(u1 - u0);
+  const int rp0 = (int)(u0 / KC), kc0 = (int)(u0 - (long long)rp0 * KC);
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -741,39 +814,45 @@ __global__ void __launch_bounds__(kRingThreads, 2) q4_gemv_ring(LinArgs p) {
   int issued = 0;  // producer: stages whose copies were issued
 
   if (warp == kRingCW) {
-    // ---- producer warp ----
+    // ---- producer warp (lane 0 issues) ----
     const uint64_t pol = l2_policy_evict_first();
-    const unsigned char* q8 = reinterpret_cast<const unsigned char*>(p.qw);
-    const int KG = p.K / 128;
-    const int r = lane & 15;
-    for (int i = 0; i < n; ++i) {
-      const int slot = i % S;
-      if (i >= S) {
-        int ok = 1;
-        if (lane == 0)
-          ok = !s_abort && mbar_wait_bounded(&empty[slot], (uint32_t)(((i / S) - 1) & 1), kWaitLimitNs) &&
-               !s_abort;
-        if (!__shfl_sync(0xffffffffu, ok, 0)) {
-          if (lane == 0) {
-            atomicOr(&g_linear_status, kStatusTimeout);
-            s_abort = 1;
-          }
+    const bool paired = p.epi == EPI_SWIGLU || p.epi == EPI_ROPE_KV;
+    if (lane == 0) {
+      tma_prefetch_map(&tw);
+      tma_prefetch_map(&ts);
+      int rp = rp0, kc = kc0, slot = 0;
+      uint32_t ph = 0;  // parity of the empty phase a refill waits for
+      for (int i = 0; i < n; ++i) {
+        if (i >= S && !(!s_abort && mbar_wait_bounded(&empty[slot], ph, kWaitLimitNs) && !s_abort)) {
+          atomicOr(&g_linear_status, kStatusTimeout);
+          s_abort = 1;
           break;
         }
+        unsigned char* sl = smem_raw + (size_t)slot * kRingSlotBytes;
+        mbar_arrive_expect_tx(&full[slot], kRingTx);
+        if (paired) {
+          for (int j = 0; j < 2; ++j)
+            for (int h = 0; h < 2; ++h) {
+              const int row = ring_run_row(p, 2 * rp + j, h);
+              tma_load_2d_hint(sl + (16 * j + 8 * h) * kRingRowPitch, &tw, kc * (kRingSK / 8), row, &full[slot], pol);
+              tma_load_2d_hint(sl + kRingWBytes + (16 * j + 8 * h) * 16, &ts, kc * 4, row, &full[slot], pol);
+            }
+        } else {
+          tma_load_2d_hint(sl, &tw, kc * (kRingSK / 8), rp * 32, &full[slot], pol);
+          tma_load_2d_hint(sl + kRingWBytes, &ts, kc * 4, rp * 32, &full[slot], pol);
+        }
+        issued = i + 1;
+        if (++kc == KC) {
+          kc = 0;
+          ++rp;
+        }
+        if (++slot == S) {
+          slot = 0;
+          if (i >= S) ph ^= 1u;  // refills of round r wait for the consumers' phase r - 1
+        }
       }
-      const long long u = u0 + i;
-      const int rt = (int)(u / KC), kc = (int)(u - (long long)rt * KC);
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], kRingTx);
-      __syncwarp();
-      const int row = tile_row(p, rt, r);
-      unsigned char* sl = smem_raw + (size_t)slot * kRingSlotBytes;
-      if (lane < 16)
-        bulk_g2s_hint(sl + r * kRingRowPitch, q8 + (size_t)row * (p.K / 2) + (size_t)kc * (kRingSK / 2), kRingSK / 2,
-                      &full[slot], pol);
-      else
-        bulk_g2s_hint(sl + kRingWBytes + r * 16, p.scales + (size_t)row * KG + kc * 8, 16, &full[slot], pol);
-      issued = i + 1;
     }
+    __syncwarp();
   } else {
     // ---- consumer warps ----
     const int g = lane >> 2, t = lane & 3;
@@ -781,64 +860,100 @@ __global__ void __launch_bounds__(kRingThreads, 2) q4_gemv_ring(LinArgs p) {
     const int rstride = p.K / 8 + 4;
     uint4* xs_hi = reinterpret_cast<uint4*>(smem_raw + p.x_off);
     uint4* xs_lo = xs_hi + (size_t)p.M * rstride;
-    stage_x<XF32>(p, nullptr, xs_hi, xs_lo, rstride, 0, p.K / 8, (int)threadIdx.x, kRingCW * 32);
+    const int qstride = p.K / 8 + 8;  // M1: int8 x terms
+    uint2* xq = reinterpret_cast<uint2*>(smem_raw + p.x_off);
+    int4* xg = reinterpret_cast<int4*>(xq + 3 * (size_t)qstride);
+    if constexpr (M1)
+      stage_x_i8<XF32>(p, xq, xg, qstride, warp, lane, kRingCW);
+    else
+      stage_x<XF32>(p, nullptr, xs_hi, xs_lo, rstride, 0, p.K / 8, (int)threadIdx.x, kRingCW * 32);
     named_bar_sync(1, kRingCW * 32);
-    float* red = reinterpret_cast<float*>(smem_raw + p.red_off);  // [S][kRingCW][M * 16]
+    float* red = reinterpret_cast<float*>(smem_raw + p.red_off);  // [S][kRingCW][2][M * 16]
     const int items = p.M * 16;
-    float acc[1][4] = {{0.0f, 0.0f, 0.0f, 0.0f}};
-    float hl[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float acc[2][1][4];
+    float hl[2][2];  // M1: rows g and g + 8 of both row tiles (lanes t == 0)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[j][0][e] = 0.0f;
+      hl[j][0] = hl[j][1] = 0.0f;
+    }
     int mrow[1];
     mrow[0] = min(g, p.M - 1) * rstride;
+    int rp = rp0, kc = kc0, slot = 0;
+    uint32_t ph = 0;
     for (int i = 0; i < n; ++i) {
-      const int slot = i % S;
-      const long long u = u0 + i;
-      const int rt = (int)(u / KC), kc = (int)(u - (long long)rt * KC);
       const bool last = kc == KC - 1 || i == n - 1;
       int ok = !s_abort;
-      if (ok) ok = mbar_wait_bounded(&full[slot], (uint32_t)((i / S) & 1), kWaitLimitNs);
+      if (ok) ok = mbar_wait_bounded(&full[slot], ph, kWaitLimitNs);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok && lane == 0) {
         atomicOr(&g_linear_status, kStatusTimeout);
         s_abort = 1;
       }
-      uint4 wa = make_uint4(0u, 0u, 0u, 0u), wb = wa;
-      float sa = 0.0f, sb = 0.0f;
-      if (ok) {
-        const unsigned char* sl = smem_raw + (size_t)slot * kRingSlotBytes;
-        wa = *reinterpret_cast<const uint4*>(sl + g * kRingRowPitch + warp * 64 + t * 16);
-        wb = *reinterpret_cast<const uint4*>(sl + (g + 8) * kRingRowPitch + warp * 64 + t * 16);
-        const __half* ss = reinterpret_cast<const __half*>(sl + kRingWBytes);
-        sa = __half2float(ss[g * 8 + warp]);
-        sb = __half2float(ss[(g + 8) * 8 + warp]);
+      uint4 w[2][2];
+      float sc[2][2];
+      const unsigned char* sl = smem_raw + (size_t)slot * kRingSlotBytes;
+      const __half* ss = reinterpret_cast<const __half*>(sl + kRingWBytes);
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        if (ok) {
+          w[j][0] = *reinterpret_cast<const uint4*>(sl + (16 * j + g) * kRingRowPitch + warp * 64 + t * 16);
+          w[j][1] = *reinterpret_cast<const uint4*>(sl + (16 * j + g + 8) * kRingRowPitch + warp * 64 + t * 16);
+          sc[j][0] = __half2float(ss[(16 * j + g) * 8 + warp]);
+          sc[j][1] = __half2float(ss[(16 * j + g + 8) * 8 + warp]);
+        } else {
+          w[j][0] = w[j][1] = make_uint4(0u, 0u, 0u, 0u);
+          sc[j][0] = sc[j][1] = 0.0f;
+        }
       }
       if (!last) {  // registers hold this warp's share: the slot may be refilled
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
       }
-      const int wbase = (kc * kRingCW + warp) * 16 + 4 * t;
-      if constexpr (HL)
-        mma_tile_hl(wa, wb, sa, sb, xs_hi, xs_lo, g, wbase, hl);
-      else
-        mma_tile<1, XF32, false>(wa, wb, sa, sb, xs_hi, xs_lo, mrow, wbase, acc);
-      if (last) {
-        float* rw = red + ((size_t)slot * kRingCW + warp) * items;
-        if constexpr (HL) {
-          if (t == 0) {
-            rw[g] = hl[0] + hl[1];
-            rw[g + 8] = hl[2] + hl[3];
-          }
-          hl[0] = hl[1] = hl[2] = hl[3] = 0.0f;
+      const int ktile = kc * kRingCW + warp;  // 128-k tile = scale group
+      if constexpr (M1) {
+        uint2 xv[4];
+        if (g < 3) {
+          const uint4* src = reinterpret_cast<const uint4*>(xq + (size_t)g * qstride + ktile * 16 + 4 * t);
+          const uint4 lo = src[0], hi = src[1];
+          xv[0] = make_uint2(lo.x, lo.y), xv[1] = make_uint2(lo.z, lo.w);
+          xv[2] = make_uint2(hi.x, hi.y), xv[3] = make_uint2(hi.z, hi.w);
         } else {
-          const int m0 = 2 * t;
-          if (m0 < p.M) {
-            rw[m0 * 16 + g] = acc[0][0];
-            rw[m0 * 16 + g + 8] = acc[0][2];
+          xv[0] = xv[1] = xv[2] = xv[3] = make_uint2(0u, 0u);
+        }
+        const int4 xgv = xg[ktile];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) mma_tile_i8(w[j][0], w[j][1], sc[j][0], sc[j][1], xv, xgv, hl[j]);
+      } else {
+        const int wbase = ktile * 16 + 4 * t;
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+          mma_tile<1, XF32, true>(w[j][0], w[j][1], sc[j][0], sc[j][1], xs_hi, xs_lo, mrow, wbase, acc[j]);
+      }
+      if (last) {
+        float* rw = red + ((size_t)slot * kRingCW + warp) * 2 * items;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          float* r = rw + j * items;
+          if constexpr (M1) {
+            if (t == 0) {
+              r[g] = hl[j][0];
+              r[g + 8] = hl[j][1];
+            }
+            hl[j][0] = hl[j][1] = 0.0f;
+          } else {
+            const int m0 = 2 * t;
+            if (m0 < p.M) {
+              r[m0 * 16 + g] = acc[j][0][0];
+              r[m0 * 16 + g + 8] = acc[j][0][2];
+            }
+            if (m0 + 1 < p.M) {
+              r[(m0 + 1) * 16 + g] = acc[j][0][1];
+              r[(m0 + 1) * 16 + g + 8] = acc[j][0][3];
+            }
+            acc[j][0][0] = acc[j][0][1] = acc[j][0][2] = acc[j][0][3] = 0.0f;
           }
-          if (m0 + 1 < p.M) {
-            rw[(m0 + 1) * 16 + g] = acc[0][1];
-            rw[(m0 + 1) * 16 + g + 8] = acc[0][3];
-          }
-          acc[0][0] = acc[0][1] = acc[0][2] = acc[0][3] = 0.0f;
         }
         __syncwarp();
         int prev = 0;
@@ -848,11 +963,21 @@ __global__ void __launch_bounds__(kRingThreads, 2) q4_gemv_ring(LinArgs p) {
         }
         if (__shfl_sync(0xffffffffu, prev, 0) == kRingCW - 1) {
           __threadfence_block();
-          ring_finish(p, red + (size_t)slot * kRingCW * items, s_fin[warp], rt, U, &s_best, lane);
+          // the sums land in this warp's own reduction row (each lane overwrites only what it read)
+          float* rs = red + (size_t)slot * kRingCW * 2 * items;
+          ring_finish(p, rs, rs + (size_t)warp * 2 * items, rp, U, &s_best, lane);
           if (lane == 0) cnt[slot] = 0;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
+      }
+      if (++kc == KC) {
+        kc = 0;
+        ++rp;
+      }
+      if (++slot == S) {
+        slot = 0;
+        ph ^= 1u;
       }
     }
   }
@@ -1539,39 +1664,55 @@ static int plan_tc(int M, int K, int G, bool xf32, const q4b_linear_cfg* cfg, Pl
   return Q4B_OK;
 }
 
-// kernel 6: ring depth from the shared memory left beside the staged x and the reduction slots;
-// two CTAs per SM when that still leaves >= 6 stages, else one
-constexpr size_t kRingSmem2 = 108 * 1024;  // dynamic bytes per CTA with two resident per SM
-constexpr size_t kRingSmem1 = 200 * 1024;
+// kernel 6: ring depth from the shared memory left beside the staged x and the reduction slots.
+// Residency modes (cfg->tiles; 0 = automatic):
+//   1  one CTA per SM, sized so that one CTA of the next kernel on the stream fits beside it: that
+//      kernel starts under programmatic dependent launch and fills its own ring while this one runs
+//      (chains of small projections)
+//   2  two CTAs per SM filling it (twice the consumer warps and bytes in flight; large problems)
+//   3  one CTA per SM with the whole shared memory (x too large to stage beside a deep ring)
+constexpr size_t kRingSmemHalf = 104 * 1024;   // dynamic bytes of one of two CTAs on an SM
+constexpr size_t kRingSmemAlone = 200 * 1024;  // dynamic bytes of a CTA alone on an SM
+constexpr size_t kRingLargeBytes = 64u << 20;  // weights above this: mode 2 by default
 static bool ring_ok(int M, int K, int G, int epi, bool norm) {
   return M <= 8 && G == 128 && K % kRingSK == 0 && !norm && (epi != EPI_ARGMAX || M == 1);
 }
-static size_t ring_xbytes(int M, int K, bool xf32) { return (size_t)M * (K / 8 + 4) * 16 * (xf32 ? 2 : 1); }
-static bool ring_layout(Plan& pl, int M, int K, bool xf32, int occ) {
+// staged x: one row as int8 terms (three rows of K/8 + 8 uint2, plus a 16-byte record per group), or
+// up to 8 rows as fp16 (hi, and lo for fp32 x)
+static size_t ring_xbytes(int M, int K, bool xf32) {
+  if (M == 1) return (size_t)3 * (K / 8 + 8) * 8 + (size_t)(K / 128) * 16;
+  return (size_t)M * (K / 8 + 4) * 16 * (xf32 ? 2 : 1);
+}
+static bool ring_layout(Plan& pl, int M, int K, bool xf32, int mode) {
   const size_t xb = align_up(ring_xbytes(M, K, xf32), 128);
-  const size_t per = kRingSlotBytes + (size_t)kRingCW * M * 16 * 4;
-  const size_t budget = occ == 2 ? kRingSmem2 : kRingSmem1;
+  const size_t per = kRingSlotBytes + (size_t)kRingCW * 2 * M * 16 * 4;
+  const size_t budget = mode == 3 ? kRingSmemAlone : kRingSmemHalf;
   const long long slots = xb < budget ? (long long)((budget - xb) / per) : 0;
   pl.ring_slots = (int)std::min<long long>(slots, kRingMaxSlots);
-  pl.occ = occ;
+  pl.occ = mode == 2 ? 2 : 1;
   pl.x_off = pl.ring_slots * kRingSlotBytes;
   pl.red_off = (int)(pl.x_off + xb);
-  pl.smem = pl.red_off + (size_t)pl.ring_slots * kRingCW * M * 16 * 4;
-  return pl.ring_slots >= (occ == 2 ? 6 : 3);
+  pl.smem = pl.red_off + (size_t)pl.ring_slots * kRingCW * 2 * M * 16 * 4;
+  return pl.ring_slots >= (mode == 3 ? 3 : 4);
 }
 static size_t ring_ws(const Plan& pl, int M, int K) {
-  return kCounterBytes + align_up((size_t)pl.RT * (K / kRingSK) * M * 16 * 4, 256);
+  return kCounterBytes + align_up((size_t)((pl.RT + 1) / 2) * (K / kRingSK) * 2 * M * 16 * 4, 256);
 }
-static int plan_ring(int M, int K, bool xf32, const q4b_linear_cfg* cfg, Plan& pl) {
+static int plan_ring(int M, int N, int K, bool xf32, const q4b_linear_cfg* cfg, Plan& pl) {
   pl.kernel = 6;
-  const int occ = cfg && cfg->tiles ? cfg->tiles : 0;
-  if (occ < 0 || occ > 2) return set_error(Q4B_EINVAL, "q4_linear: kernel 6 takes tiles = 1 or 2 CTAs per SM");
-  const bool ok =
-      occ ? ring_layout(pl, M, K, xf32, occ) : (ring_layout(pl, M, K, xf32, 2) || ring_layout(pl, M, K, xf32, 1));
+  const int mode = cfg && cfg->tiles ? cfg->tiles : 0;
+  if (mode < 0 || mode > 3) return set_error(Q4B_EINVAL, "q4_linear: kernel 6 takes tiles = 1, 2 or 3 (residency mode)");
+  bool ok;
+  if (mode) {
+    ok = ring_layout(pl, M, K, xf32, mode);
+  } else {
+    const size_t wbytes = (size_t)N * K / 2;
+    ok = ring_layout(pl, M, K, xf32, wbytes > kRingLargeBytes ? 2 : 1) || ring_layout(pl, M, K, xf32, 3);
+  }
   if (!ok) return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 6 ring does not fit beside x (m=%d k=%d)", M, K);
   pl.nsplit = 1;
   pl.kps = K / TILE_K;
-  pl.split_units = !(cfg && cfg->split == 1) && pl.RT <= kMaxCounters;
+  pl.split_units = !(cfg && cfg->split == 1) && (pl.RT + 1) / 2 <= kMaxCounters;
   pl.ws_bytes = pl.split_units ? ring_ws(pl, M, K) : 0;
   return Q4B_OK;
 }
@@ -1610,10 +1751,10 @@ static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, bool norm
   if (want == 6) {
     if (!ring_ok(M, K, G, epi, norm))
       return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 6 needs m <= 8, group 128, k %% 1024 == 0, no fused norm");
-    return plan_ring(M, K, xf32, cfg, pl);
+    return plan_ring(M, N, K, xf32, cfg, pl);
   }
   const bool tuned = !cfg || (!cfg->warps && !cfg->tiles && !cfg->split);
-  if (want == 0 && tuned && ring_ok(M, K, G, epi, norm) && plan_ring(M, K, xf32, nullptr, pl) == Q4B_OK)
+  if (want == 0 && tuned && ring_ok(M, K, G, epi, norm) && plan_ring(M, N, K, xf32, nullptr, pl) == Q4B_OK)
     return Q4B_OK;
   if (want == 4) {
     if (!stream_ok(M, K, G, norm))
@@ -1877,13 +2018,22 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
         e = xf32 ? go(q4_gemm_tc<64, true>, d[2]) : go(q4_gemm_tc<64, false>, d[3]);
     }
   } else if (pl.kernel == 6) {
-    static std::atomic<unsigned long long> d[3];
-    const bool hl = xf32 && op.m == 1;
-    auto kern = hl ? q4_gemv_ring<true, true> : xf32 ? q4_gemv_ring<true, false> : q4_gemv_ring<false, false>;
-    e = set_smem_attr(kern, d[hl ? 0 : xf32 ? 1 : 2]);
-    const long long units = pl.split_units ? (long long)pl.RT * a.kc : pl.RT;
+    static std::atomic<unsigned long long> d[4];
+    const bool m1 = op.m == 1;
+    auto kern = m1 ? (xf32 ? q4_gemv_ring<true, true> : q4_gemv_ring<false, true>)
+                   : (xf32 ? q4_gemv_ring<true, false> : q4_gemv_ring<false, false>);
+    // weights as int32 [n, k/8] in boxes of {128 words, 32 rows}, scales as int32 pairs [n, k/256]
+    // in boxes of {4 words, 32 rows} (8-row boxes for SwiGLU / RoPE tiles); rows past n read zero
+    const uint32_t box_rows = (op.epi == EPI_SWIGLU || op.epi == EPI_ROPE_KV) ? 8 : 32;
+    CUtensorMap tw, ts;
+    int rc2 = make_tmap_i32(&tw, op.qw, op.k / 8, op.n, op.k / 8, kRingSK / 8, box_rows);
+    if (!rc2) rc2 = make_tmap_i32(&ts, op.scales, op.k / 256, op.n, op.k / 256, 4, box_rows);
+    if (rc2) return rc2;
+    e = set_smem_attr(kern, d[(m1 ? 0 : 2) + (xf32 ? 0 : 1)]);
+    const long long pairs = (pl.RT + 1) / 2;
+    const long long units = pl.split_units ? pairs * a.kc : pairs;
     const int grid = (int)std::min<long long>(units, (long long)num_sms() * pl.occ);
-    if (e == cudaSuccess) e = launch_pdl(kern, dim3(grid), dim3(kRingThreads), pl.smem, st, a);
+    if (e == cudaSuccess) e = launch_pdl(kern, dim3(grid), dim3(kRingThreads), pl.smem, st, tw, ts, a);
   } else if (pl.kernel == 4) {
     static std::atomic<unsigned long long> d0, d1;
     e = xf32 ? set_smem_attr(q4_gemv_stream<true>, d1) : set_smem_attr(q4_gemv_stream<false>, d0);

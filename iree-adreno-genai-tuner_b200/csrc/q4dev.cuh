@@ -141,4 +141,50 @@ __device__ __forceinline__ void mma_tile_hl(const uint4& wa, const uint4& wb, fl
   acc[2] = fmaf(sb, part[0][2] + part[1][2], acc[2]);
   acc[3] = fmaf(sb, part[0][3] + part[1][3], acc[3]);
 }
+// ---- int8 tensor-core form for one x row --------------------------------------------------------
+//
+// x row staged per 128-k group as three int8 terms, x ~= sx * (a + b / 254 + c / 254^2) with
+// sx = max|x| / 127 over the group (a, b, c in [-127, 127]; the residual is at most
+// 0.5 * sx / 254^2, about 6e-8 of the group's largest |x|). The weights enter the MMA as their
+// stored biased nibbles (0..15, unsigned bytes) and the zero point comes back exactly as an integer:
+// sum_k (nib - 8) q_k = sum_k nib q_k - 8 X with X = sum_k q_k of the group.
+constexpr float kI8Step = 1.0f / 254.0f;
+constexpr float kI8Step2 = kI8Step * kI8Step;
+
+__device__ __forceinline__ void mma_k32_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                             uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// One 128-k tile (one scale group) of rows g and g + 8 against the staged int8 x terms. wa / wb: the
+// lane's 4 words of rows g / g + 8 (words 4t .. 4t + 3 of the tile); xv[q]: {even, odd} bytes of
+// word 4t + q for term g (lanes g >= 3 pass zeros); xg = {X_a, X_b, X_c, sx} of the group. MMA q
+// covers words 4t + q: k-slots 4t + i hold nibble 2i (even bytes), k-slots 16 + 4t + i nibble 2i + 1.
+// Two integer accumulator chains (q even / odd) are added exactly. Columns of the result: 0 = term
+// a, 1 = term b (lanes t == 0), 2 = term c (lanes t == 1, fetched by a shuffle). Adds s * sx * the
+// group's dot product to acc[0] (row g) and acc[1] (row g + 8) on lanes t == 0.
+__device__ __forceinline__ void mma_tile_i8(const uint4& wa, const uint4& wb, float sa, float sb, const uint2 (&xv)[4],
+                                            const int4& xg, float (&acc)[2]) {
+  int d[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+  const uint32_t wav[4] = {wa.x, wa.y, wa.z, wa.w};
+  const uint32_t wbv[4] = {wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t a0 = wav[q] & 0x0F0F0F0Fu, a2 = (wav[q] >> 4) & 0x0F0F0F0Fu;
+    const uint32_t a1 = wbv[q] & 0x0F0F0F0Fu, a3 = (wbv[q] >> 4) & 0x0F0F0F0Fu;
+    mma_k32_u8s8(d[q & 1], a0, a1, a2, a3, xv[q].x, xv[q].y);
+  }
+  const int s0 = d[0][0] + d[1][0], s1 = d[0][1] + d[1][1];
+  const int s2 = d[0][2] + d[1][2], s3 = d[0][3] + d[1][3];
+  const int c_g = __shfl_down_sync(0xffffffffu, s0, 1);   // term c of row g (lane t + 1)
+  const int c_g8 = __shfl_down_sync(0xffffffffu, s2, 1);  // term c of row g + 8
+  const float sx = __int_as_float(xg.w);
+  const float vg = (float)(s0 - 8 * xg.x) + (float)(s1 - 8 * xg.y) * kI8Step + (float)(c_g - 8 * xg.z) * kI8Step2;
+  const float vg8 = (float)(s2 - 8 * xg.x) + (float)(s3 - 8 * xg.y) * kI8Step + (float)(c_g8 - 8 * xg.z) * kI8Step2;
+  acc[0] = fmaf(sa * sx, vg, acc[0]);
+  acc[1] = fmaf(sb * sx, vg8, acc[1]);
+}
 }  // namespace q4b

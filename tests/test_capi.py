@@ -133,7 +133,7 @@ def test_linear_kernel_choice(L):
     assert L.q4b_q4_linear_kernel(1, 256, 688, 16, 0, F32, None) == 2
     cfg = _lib.LinearCfg(kernel=1, warps=8, tiles=3, split=1)
     assert L.q4b_q4_linear_kernel(1, 5120, 3072, 128, 0, F16, ctypes.byref(cfg)) == 1
-    bad = _lib.LinearCfg(kernel=6, tiles=3)
+    bad = _lib.LinearCfg(kernel=6, tiles=4)
     assert L.q4b_q4_linear_kernel(1, 5120, 3072, 128, 0, F16, ctypes.byref(bad)) == _lib.Q4B_EINVAL
     assert L.q4b_q4_linear_kernel(0, 5120, 3072, 128, 0, F16, None) == _lib.Q4B_EINVAL
 

@@ -292,7 +292,7 @@ def test_tcgen05_gemm_is_deterministic_and_leaves_counters_zero(dev):
 # ---- kernel 6: the persistent bulk-copy ring GEMV (decode rows) ---------------------------------
 K6_CASES = [(5120, 3072, 1), (3072, 8192, 1), (37, 1024, 1), (1000, 3072, 1), (200, 2048, 3), (1000, 8192, 4),
             (520, 1024, 8), (16384, 3072, 2), (40000, 3072, 1)]
-K6_CFGS = [None, dict(kernel=6, tiles=1), dict(kernel=6, tiles=2), dict(kernel=6, split=1),
+K6_CFGS = [None, dict(kernel=6, tiles=1), dict(kernel=6, tiles=2), dict(kernel=6, tiles=3), dict(kernel=6, split=1),
            dict(kernel=6, tiles=1, split=1)]
 
 
