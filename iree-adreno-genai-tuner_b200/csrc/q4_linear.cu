@@ -635,11 +635,12 @@ __global__ void __launch_bounds__(768) q4_gemv_stream(LinArgs p) {
 //    mbarrier. It never waits for the previous kernel (the weights are not that kernel's output);
 //    only the consumers wait (griddepcontrol) before staging x.
 //  - Consumer warp w takes 128-k tile w of both row tiles of every stage: two independent tiles per
-//    barrier wait, sharing one set of x fragments (the LOP3 dequant + mma.sync math of kernels 1 and
-//    3), and keeps the row pair's sums in registers across its stages. Loop indices advance by
-//    increments (no divisions in the stream loop). At a row pair's last stage of this CTA every warp
-//    writes its sums into the slot's reduction area; the last warp to arrive (a shared counter) adds
-//    the 8 in warp order and runs the epilogue, then releases the slot.
+//    barrier wait, sharing one set of x fragments, and keeps the row pair's sums in registers across
+//    its stages; it releases a ring slot as soon as its share is in registers. Loop indices advance
+//    by increments (no divisions in the stream loop). At a row pair's last stage of this CTA every
+//    consumer writes its sums into a reduction slot and arrives on that slot's `red_full`
+//    mbarrier; a separate epilogue warp adds the 8 in warp order, finishes the pair (cross-CTA
+//    partials, epilogue) and frees the slot (`red_free`), off the consumers' path.
 //  - CTAs take equal runs of the NRP x K/1024 stages (NRP row pairs). A row pair cut between CTAs
 //    is finished by the last of them through the split-K workspace (partials added in CTA order):
 //    deterministic results.
@@ -648,7 +649,8 @@ __global__ void __launch_bounds__(768) q4_gemv_stream(LinArgs p) {
 //    clean) and the producer waits for its copies in flight before the CTA exits.
 constexpr int kRingSK = 1024;
 constexpr int kRingCW = kRingSK / TILE_K;  // consumer warps: one 128-k tile of each stage
-constexpr int kRingThreads = (kRingCW + 1) * 32;
+constexpr int kRingThreads = (kRingCW + 2) * 32;  // + the producer warp and the epilogue warp
+constexpr int kRingRed = 4;  // reduction slots (row pairs between the consumers and the epilogue warp)
 constexpr int kRingRowPitch = kRingSK / 2;  // a TMA box lands rows densely
 constexpr int kRingWBytes = 32 * kRingRowPitch;
 constexpr int kRingSlotBytes = kRingWBytes + 32 * 16;  // + 32 rows x 8 fp16 scales (16896, 128-B multiple)
@@ -721,9 +723,9 @@ __device__ void stage_x_i8(const LinArgs& p, uint2* xq, int4* xg, int qstride, i
 }
 
 // One warp finishes row pair rp: per row tile the 8 warps' sums (red [kRingCW][2][M*16]) in warp
-// order, the cross-CTA partials if the pair was cut, then the epilogue (argmax keys fold into
-// *s_best).
-__device__ void ring_finish(const LinArgs& p, const float* red, float* fin, int rp, long long U,
+// order, the cross-CTA partials if the pair was cut (`cut`: this CTA holds only part of its stages;
+// only a CTA's first and last pair can be), then the epilogue (argmax keys fold into *s_best).
+__device__ void ring_finish(const LinArgs& p, const float* red, float* fin, int rp, long long U, bool cut,
                             unsigned long long* s_best, int lane) {
   const int items = p.M * 16;
   for (int i = lane; i < 2 * items; i += 32) {
@@ -733,7 +735,7 @@ __device__ void ring_finish(const LinArgs& p, const float* red, float* fin, int 
     fin[i] = v;
   }
   __syncwarp();
-  if (p.split_units) {
+  if (cut) {
     const long long ua = (long long)rp * p.kc;
     const int c0 = ring_cta_of(ua, U, gridDim.x), c1 = ring_cta_of(ua + p.kc - 1, U, gridDim.x);
     if (c1 > c0) {
@@ -782,7 +784,8 @@ __global__ void __launch_bounds__(kRingThreads, 2)
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ __align__(8) uint64_t full[kRingMaxSlots];
   __shared__ __align__(8) uint64_t empty[kRingMaxSlots];
-  __shared__ int cnt[kRingMaxSlots];
+  __shared__ __align__(8) uint64_t red_full[kRingRed];
+  __shared__ __align__(8) uint64_t red_free[kRingRed];
   __shared__ unsigned long long s_best;
   __shared__ volatile int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -803,7 +806,10 @@ __global__ void __launch_bounds__(kRingThreads, 2)
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kRingCW);
-      cnt[s] = 0;
+    }
+    for (int r = 0; r < kRingRed; ++r) {
+      mbar_init(&red_full[r], kRingCW);
+      mbar_init(&red_free[r], 1);
     }
     s_best = 0ull;
     s_abort = 0;
@@ -813,7 +819,29 @@ __global__ void __launch_bounds__(kRingThreads, 2)
   griddep_launch_dependents();
   int issued = 0;  // producer: stages whose copies were issued
 
-  if (warp == kRingCW) {
+  if (warp == kRingCW + 1) {
+    // ---- epilogue warp: finishes this CTA's row pairs in order ----
+    const int items = p.M * 16;
+    float* red = reinterpret_cast<float*>(smem_raw + p.red_off);  // [kRingRed][kRingCW][2][M * 16]
+    const int npairs = n > 0 ? (int)((u1 - 1) / KC) - rp0 + 1 : 0;
+    const bool last_cut = n > 0 && (u1 % KC) != 0;
+    for (int q = 0; q < npairs; ++q) {
+      const int r = q & (kRingRed - 1);
+      int ok = !s_abort;
+      if (ok) ok = mbar_wait_bounded(&red_full[r], (uint32_t)((q / kRingRed) & 1), kWaitLimitNs);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok && lane == 0) {
+        atomicOr(&g_linear_status, kStatusTimeout);
+        s_abort = 1;
+      }
+      // cut: the pair began in an earlier CTA, or this CTA's run ends before its last stage
+      const bool cut = p.split_units && ((q == 0 && kc0 != 0) || (q == npairs - 1 && last_cut));
+      float* rs = red + (size_t)r * kRingCW * 2 * items;
+      ring_finish(p, rs, rs, rp0 + q, U, cut, &s_best, lane);  // sums land in warp 0's row
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_free[r]);
+    }
+  } else if (warp == kRingCW) {
     // ---- producer warp (lane 0 issues) ----
     const uint64_t pol = l2_policy_evict_first();
     const bool paired = p.epi == EPI_SWIGLU || p.epi == EPI_ROPE_KV;
@@ -868,7 +896,7 @@ __global__ void __launch_bounds__(kRingThreads, 2)
     else
       stage_x<XF32>(p, nullptr, xs_hi, xs_lo, rstride, 0, p.K / 8, (int)threadIdx.x, kRingCW * 32);
     named_bar_sync(1, kRingCW * 32);
-    float* red = reinterpret_cast<float*>(smem_raw + p.red_off);  // [S][kRingCW][2][M * 16]
+    float* red = reinterpret_cast<float*>(smem_raw + p.red_off);  // [kRingRed][kRingCW][2][M * 16]
     const int items = p.M * 16;
     float acc[2][1][4];
     float hl[2][2];  // M1: rows g and g + 8 of both row tiles (lanes t == 0)
@@ -880,7 +908,7 @@ __global__ void __launch_bounds__(kRingThreads, 2)
     }
     int mrow[1];
     mrow[0] = min(g, p.M - 1) * rstride;
-    int rp = rp0, kc = kc0, slot = 0;
+    int rp = rp0, kc = kc0, slot = 0, q = 0;
     uint32_t ph = 0;
     for (int i = 0; i < n; ++i) {
       const bool last = kc == KC - 1 || i == n - 1;
@@ -907,10 +935,8 @@ __global__ void __launch_bounds__(kRingThreads, 2)
           sc[j][0] = sc[j][1] = 0.0f;
         }
       }
-      if (!last) {  // registers hold this warp's share: the slot may be refilled
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-      }
+      __syncwarp();  // registers hold this warp's share: the slot may be refilled
+      if (lane == 0) mbar_arrive(&empty[slot]);
       const int ktile = kc * kRingCW + warp;  // 128-k tile = scale group
       if constexpr (M1) {
         uint2 xv[4];
@@ -932,7 +958,18 @@ __global__ void __launch_bounds__(kRingThreads, 2)
           mma_tile<1, XF32, true>(w[j][0], w[j][1], sc[j][0], sc[j][1], xs_hi, xs_lo, mrow, wbase, acc[j]);
       }
       if (last) {
-        float* rw = red + ((size_t)slot * kRingCW + warp) * 2 * items;
+        // reduction slot of this CTA's q-th row pair; wait until the epilogue warp has read its
+        // previous use (pair q - kRingRed)
+        const int r = q & (kRingRed - 1);
+        if (q >= kRingRed) {
+          int fr = !s_abort;
+          if (fr) fr = mbar_wait_bounded(&red_free[r], (uint32_t)(((q / kRingRed) - 1) & 1), kWaitLimitNs);
+          if (!__all_sync(0xffffffffu, fr) && lane == 0) {
+            atomicOr(&g_linear_status, kStatusTimeout);
+            s_abort = 1;
+          }
+        }
+        float* rw = red + ((size_t)r * kRingCW + warp) * 2 * items;
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           float* r = rw + j * items;
@@ -956,20 +993,8 @@ __global__ void __launch_bounds__(kRingThreads, 2)
           }
         }
         __syncwarp();
-        int prev = 0;
-        if (lane == 0) {
-          __threadfence_block();
-          prev = atomicAdd(&cnt[slot], 1);
-        }
-        if (__shfl_sync(0xffffffffu, prev, 0) == kRingCW - 1) {
-          __threadfence_block();
-          // the sums land in this warp's own reduction row (each lane overwrites only what it read)
-          float* rs = red + (size_t)slot * kRingCW * 2 * items;
-          ring_finish(p, rs, rs + (size_t)warp * 2 * items, rp, U, &s_best, lane);
-          if (lane == 0) cnt[slot] = 0;
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
+        if (lane == 0) mbar_arrive(&red_full[r]);  // release: the epilogue warp's wait sees the sums
+        ++q;
       }
       if (++kc == KC) {
         kc = 0;
@@ -1685,14 +1710,14 @@ static size_t ring_xbytes(int M, int K, bool xf32) {
 }
 static bool ring_layout(Plan& pl, int M, int K, bool xf32, int mode) {
   const size_t xb = align_up(ring_xbytes(M, K, xf32), 128);
-  const size_t per = kRingSlotBytes + (size_t)kRingCW * 2 * M * 16 * 4;
   const size_t budget = mode == 3 ? kRingSmemAlone : kRingSmemHalf;
-  const long long slots = xb < budget ? (long long)((budget - xb) / per) : 0;
+  const size_t reds = (size_t)kRingRed * kRingCW * 2 * M * 16 * 4;  // reduction slots
+  const long long slots = xb + reds < budget ? (long long)((budget - xb - reds) / kRingSlotBytes) : 0;
   pl.ring_slots = (int)std::min<long long>(slots, kRingMaxSlots);
   pl.occ = mode == 2 ? 2 : 1;
   pl.x_off = pl.ring_slots * kRingSlotBytes;
   pl.red_off = (int)(pl.x_off + xb);
-  pl.smem = pl.red_off + (size_t)pl.ring_slots * kRingCW * 2 * M * 16 * 4;
+  pl.smem = pl.red_off + reds;
   return pl.ring_slots >= (mode == 3 ? 3 : 4);
 }
 static size_t ring_ws(const Plan& pl, int M, int K) {
