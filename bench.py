@@ -21,8 +21,8 @@ Prints ONE JSON line (rank 0). Workloads:
   sweep   BASELINE config 5: every 3B projection and the lm_head at M in {1, 4, 16, 64} (--shapes,
           --m), each row timed like config 1; value = aggregate GB/s, with one entry per row.
   profile a short fixed launch sequence for profilers (--layers, --prefill, --ctx, --bucket).
---impl reference times the CPU restatement of the reference path (oracle port) on the host cores of
-rank 0; other ranks exit without work.
+--impl reference times the CPU restatement of the reference path (oracle port: whole decode steps with
+the int4 GEMVs in C) on the host cores of rank 0; other ranks exit without work.
 """
 
 from __future__ import annotations
@@ -175,28 +175,28 @@ def sum_over_ranks(v, dist_mod):
 # CPU baseline (oracle port of the reference's QLinear dequant + linear, scripts/llm/llama_q4.py:72)
 # ---------------------------------------------------------------------------------------------
 
-def cpu_gemv_baseline(budget_s=12.0):
+def cpu_gemv_baseline(budget_s=8.0):
+    """BASELINE config 1 on the host cores: the C restatement of QLinear._gemv_fused
+    (oracle/q4_cpu.c) on the same synthetic 5120 x 3072 inputs, one thread per CPU."""
     import numpy as np
 
     import golden_inputs as gi
-    from oracle import q4_oracle as O
+    from oracle import q4_cpu as C
     qw, s, x = gi.gemv_inputs()
-    xf = x.astype(np.float32)[None]
+    xf = x.astype(np.float32)
+    C.gemv(qw, s, GEMV_G, xf)
     times = []
     t_end = time.perf_counter() + budget_s
-    while time.perf_counter() < t_end or len(times) < 3:
+    while time.perf_counter() < t_end or len(times) < 5:
         t0 = time.perf_counter()
-        W = O.dequantize_q4(qw, s, GEMV_G)
-        y = xf @ W.T
+        C.gemv(qw, s, GEMV_G, xf)
         times.append(time.perf_counter() - t0)
-        if len(times) >= 200:
+        if len(times) >= 2000:
             break
-    assert y.shape == (1, GEMV_N)
     med = statistics.median(times)
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    return {"value": GEMV_BYTES / med / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
-            "sample": f"{len(times)} calls of numpy dequantize_q4 + fp32 matmul on 5120x3072 g128 "
-                      f"(median {med * 1e3:.2f} ms/call; dequant single-threaded, BLAS on {cores} threads)"}
+    return {"value": GEMV_BYTES / med / 1e9, "unit": "GB/s", "cores": C.threads(), "kind": "port",
+            "sample": f"{len(times)} calls of the C restatement of the fused GEMV on 5120x3072 g128 "
+                      f"(median {med * 1e3:.3f} ms/call, {C.threads()} threads)"}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -253,44 +253,29 @@ def run_gemv(args, rank, world, local, dist_mod):
     return line
 
 
-def cpu_decode_baseline(budget_s=20.0):
-    """Oracle port of one 3B decode token on the host cores, from a bounded sample: the four
-    projections of one layer (numpy dequantize_q4 + fp32 matmul, the reference's eager QLinear
-    form), GQA attention over 640 cached positions, and 1/8 of the lm_head rows; scaled to 28 layers
-    and the full vocabulary."""
-    import numpy as np
-
-    import golden_inputs as gi
-    from oracle import q4_oracle as O
-    D, H, Hkv, hd, I, V, n_layers = 3072, 24, 8, 128, 8192, 128256, 28
-    mats = [gi.synthetic_q4(n, k, 128, seed=n + k) for n, k in
-            [((H + 2 * Hkv) * hd, D), (D, H * hd), (2 * I, D), (D, I)]]
-    head = gi.synthetic_q4(V // 8, D, 128, seed=7)
-    rng = np.random.default_rng(0)
-    kc = rng.standard_normal((640, Hkv, hd)).astype(np.float16)
-    vc = rng.standard_normal((640, Hkv, hd)).astype(np.float16)
-    q = rng.standard_normal((1, H, hd)).astype(np.float32)
-    t_layer, t_head, n = [], [], 0
-    t_end = time.perf_counter() + budget_s
-    while (time.perf_counter() < t_end and n < 5) or n < 2:
-        t0 = time.perf_counter()
-        for (qw, sc) in mats:
-            W = O.dequantize_q4(qw, sc, 128)
-            _ = rng.standard_normal((1, W.shape[1])).astype(np.float32) @ W.T
-        O.attention(q, kc, vc, np.array([639]), 640, Hkv)
-        t1 = time.perf_counter()
-        W = O.dequantize_q4(head[0], head[1], 128)
-        _ = rng.standard_normal((1, D)).astype(np.float32) @ W.T
-        t2 = time.perf_counter()
-        t_layer.append(t1 - t0)
-        t_head.append(t2 - t1)
-        n += 1
-    tok_s = 1.0 / (n_layers * statistics.median(t_layer) + 8 * statistics.median(t_head))
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    return {"value": tok_s, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{n} x (one layer's 4 projections via numpy dequantize_q4 + fp32 matmul, attention over 640 "
-                      f"cached positions, 1/8 of the lm_head rows), scaled to 28 layers + full vocab; layer "
-                      f"{statistics.median(t_layer) * 1e3:.0f} ms, lm_head/8 {statistics.median(t_head) * 1e3:.0f} ms"}
+def cpu_decode_baseline(steps=5, warmup=1, pos0=PROMPT_LEN, bucket=1024):
+    """The reference's decode step restated on the host cores (oracle/q4_cpu.py): whole 28-layer
+    Llama-3.2-3B-shape steps at the bench's positions (pos0, pos0 + 1, ...) and bucket, int4 GEMVs in
+    C on one thread per CPU (QLinear._gemv_fused), norm / RoPE / attention / SwiGLU in numpy. The KV
+    cache holds random fp16 values instead of the prompt's (the time does not depend on them)."""
+    import q4b
+    from oracle import q4_cpu as C
+    t0 = time.perf_counter()
+    m = C.DecodeModel(q4b.SYNTHETIC["3b"], max_ctx=bucket)
+    build_s = time.perf_counter() - t0
+    tok = 17
+    for i in range(warmup):
+        tok = m.step(tok, pos0 + i, bucket)
+    t0 = time.perf_counter()
+    for i in range(steps):
+        tok = m.step(tok, pos0 + warmup + i, bucket)
+    dt = time.perf_counter() - t0
+    return {"value": steps / dt, "unit": "tokens/s", "cores": C.threads(), "kind": "port",
+            "sample": f"{steps} whole decode steps (28 layers + lm_head) at positions {pos0 + warmup}.."
+                      f"{pos0 + warmup + steps - 1}, bucket {bucket}, after {warmup} warm-up; "
+                      f"{dt / steps * 1e3:.0f} ms/token; C int4 GEMVs on {C.threads()} threads + numpy "
+                      f"(model build {build_s:.1f} s, KV cache random)",
+            "same_config": True}
 
 
 def run_decode(args, rank, world, local, dist_mod):
@@ -378,7 +363,7 @@ def run_decode(args, rank, world, local, dist_mod):
     if gemv:
         line["gemv_5120x3072"] = gemv
     if not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_decode_baseline()
+        line["cpu_baseline"] = cpu_decode_baseline(steps=5, warmup=1)
     return line
 
 
@@ -576,12 +561,12 @@ def run_reference(args, rank, world):
     if rank != 0:
         return None
     if args.workload == "decode":
-        cb = cpu_decode_baseline(budget_s=30.0)
+        cb = cpu_decode_baseline(steps=args.steps, warmup=args.warmup)
         return {"metric": METRIC_DECODE, "value": round(cb["value"], 4), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
                 "vs_baseline": None, "dtype": "int4 weights, fp32 compute", "data": "synthetic", "impl": "reference",
                 "config": {"workload": "Llama-3.2-3B-shape LlamaQ4 batch-1 decode (BASELINE config 4)",
-                           "prompt": PROMPT_LEN, "chunk": CHUNK, "buckets": BUCKETS},
+                           "prompt": PROMPT_LEN, "chunk": CHUNK, "buckets": BUCKETS, "decode_bucket": 1024},
                 "cpu_baseline": cb,
                 "e2e": {"value": round(cb["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}

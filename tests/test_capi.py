@@ -71,9 +71,11 @@ def test_pack_rejects_bad_args_on_host(L):
 
 
 def test_linear_workspace_plan(L):
-    # decode 5120 x 3072, group 128, M = 1: the ring GEMV (kernel 6); row tiles cut between CTAs
-    # meet in the workspace (counters + one 16-float partial per (row tile, 1024-k stage))
-    assert L.q4b_q4_linear_workspace(1, 5120, 3072, 128, 0, None) == 65536 + 320 * 3 * 16 * 4
+    # decode 5120 x 3072, group 128, M = 1: all of K in one CTA of the register GEMV, no workspace
+    assert L.q4b_q4_linear_workspace(1, 5120, 3072, 128, 0, None) == 0
+    # the lm_head (197 MB of weights): the ring GEMV (kernel 6); row pairs cut between CTAs meet in
+    # the workspace (counters + one 32-float partial per (row pair, 1024-k stage))
+    assert L.q4b_q4_linear_workspace(1, 128256, 3072, 128, 0, None) == 65536 + 4008 * 3 * 32 * 4
     # 16 rows of x over K = 8192 do not fit one CTA's shared memory: split-K partials + counters
     ws = L.q4b_q4_linear_workspace(16, 3072, 8192, 128, 0, None)
     assert ws > 65536 and ws % 256 == 0
@@ -110,8 +112,7 @@ def test_small_m_gemv_plan_splits_k(L):
     """9..32 rows: the GEMV splits K so a CTA stages at most 8 k-tiles of x (8 splits of the 64
     tiles of K = 8192 at 16 rows); up to 8 rows K stays whole (no workspace)."""
     counters = 65536
-    # 4 rows: the ring GEMV (one CTA per SM, x staged whole), partials per (row tile, stage, row)
-    assert L.q4b_q4_linear_workspace(4, 3072, 8192, 128, 0, None) == counters + 192 * 8 * 4 * 16 * 4
+    assert L.q4b_q4_linear_workspace(4, 3072, 8192, 128, 0, None) == 0
     ws = L.q4b_q4_linear_workspace(16, 3072, 8192, 128, 0, None)
     assert ws == counters + 8 * 16 * (3072 // 16) * 16 * 4
     ws = L.q4b_q4_linear_workspace(16, 5120, 3072, 128, 0, None)  # 24 tiles: 3 splits
@@ -119,20 +120,23 @@ def test_small_m_gemv_plan_splits_k(L):
 
 
 def test_linear_kernel_choice(L):
-    """The planner's kernel for the reference's shapes: the ring GEMV for decode rows (m <= 8,
-    group 128, K % 1024 == 0), the register GEMV for 9..32 rows, tcgen05 for prefill chunks, SIMT for
-    groups that are not a multiple of 128; a fixed configuration is honoured."""
+    """The planner's kernel for the reference's shapes: the ring GEMV for decode rows over large
+    weights (the lm_head), the register GEMV for the layer projections and 9..32 rows, tcgen05 for
+    prefill chunks, SIMT for groups that are not a multiple of 128; a fixed configuration is
+    honoured."""
     from q4b import _lib
     F32, F16 = 0, 1
-    assert L.q4b_q4_linear_kernel(1, 5120, 3072, 128, 0, F16, None) == 6
-    assert L.q4b_q4_linear_kernel(8, 3072, 8192, 128, 1, F32, None) == 1  # x too large to stage whole
-    assert L.q4b_q4_linear_kernel(4, 16384, 3072, 128, 2, F32, None) == 6
+    assert L.q4b_q4_linear_kernel(1, 128256, 3072, 128, 0, F16, None) == 6
+    assert L.q4b_q4_linear_kernel(1, 64128, 3072, 128, 0, F32, None) == 6
+    assert L.q4b_q4_linear_kernel(1, 5120, 3072, 128, 0, F16, None) == 1
+    assert L.q4b_q4_linear_kernel(8, 3072, 8192, 128, 1, F32, None) == 1
+    assert L.q4b_q4_linear_kernel(4, 16384, 3072, 128, 2, F32, None) == 1
     assert L.q4b_q4_linear_kernel(1, 256, 256, 128, 0, F32, None) == 1  # K % 1024
     assert L.q4b_q4_linear_kernel(16, 3072, 8192, 128, 0, F32, None) == 1
     assert L.q4b_q4_linear_kernel(128, 5120, 3072, 128, 0, F32, None) == 5
     assert L.q4b_q4_linear_kernel(1, 256, 688, 16, 0, F32, None) == 2
-    cfg = _lib.LinearCfg(kernel=1, warps=8, tiles=3, split=1)
-    assert L.q4b_q4_linear_kernel(1, 5120, 3072, 128, 0, F16, ctypes.byref(cfg)) == 1
+    cfg = _lib.LinearCfg(kernel=6, tiles=1)
+    assert L.q4b_q4_linear_kernel(1, 5120, 3072, 128, 0, F16, ctypes.byref(cfg)) == 6
     bad = _lib.LinearCfg(kernel=6, tiles=4)
     assert L.q4b_q4_linear_kernel(1, 5120, 3072, 128, 0, F16, ctypes.byref(bad)) == _lib.Q4B_EINVAL
     assert L.q4b_q4_linear_kernel(0, 5120, 3072, 128, 0, F16, None) == _lib.Q4B_EINVAL

@@ -343,13 +343,19 @@ def test_ring_gemv_kernel(dev, cfg):
     assert _lib.lib().q4b_device_status(1) == 0
 
 
-def test_ring_gemv_is_the_decode_default(dev):
-    """The planner sends the decode projections (m <= 8, group 128, K % 1024 == 0) to kernel 6."""
+def test_ring_gemv_is_the_lm_head_default(dev):
+    """The planner sends large decode GEMVs (the lm_head and its tensor-parallel halves) to kernel 6
+    and checks the result on a full-vocabulary lm_head through the default path."""
     import q4b
     L = q4b.lib()
-    for (n, k, m) in [(5120, 3072, 1), (3072, 3072, 1), (16384, 3072, 1), (3072, 8192, 1), (128256, 3072, 1),
-                      (5120, 3072, 8)]:
+    for (n, k, m) in [(128256, 3072, 1), (64128, 3072, 1), (128256, 3072, 4)]:
         assert L.q4b_q4_linear_kernel(m, n, k, 128, 0, 1, None) == 6, (n, k, m)
+    N, K = 128256, 3072
+    qw, s = gi.synthetic_q4(N, K, 128, seed=5)
+    x = np.random.default_rng(8).standard_normal((1, K)).astype(np.float32)
+    y = q4b.q4_linear(torch.from_numpy(x).to(dev), torch.from_numpy(qw).to(dev), torch.from_numpy(s).to(dev), 128,
+                      out=poisoned((1, N), torch.float32, dev))
+    assert O.rel_err(y.cpu().numpy(), O.q4_linear(qw, s, 128, x)) <= TOL
 
 
 def test_ring_gemv_without_workspace(dev):
