@@ -52,8 +52,11 @@ enum { Q4B_EPI_STORE = 0, Q4B_EPI_ACCUMULATE = 1, Q4B_EPI_SWIGLU = 2 };
  *   kernel 3  GEMV with the weight tile staged by bulk copies (M <= 16): warps, split
  *   kernel 4  persistent GEMV, one CTA per SM, whole-row-tile ring (M == 1, G == 128): warps (1..24)
  *   kernel 5  tcgen05 int4-weight GEMM for many rows (prefill): tiles (4 or 8 row tiles of 16), split
- *   kernel 6  persistent bulk-copy ring GEMV (M <= 8, G == 128, K % 1024 == 0; the decode default):
- *             tiles = resident CTAs per SM (1 or 2), split = 1 keeps each row tile in one CTA   */
+ *   kernel 6  persistent TMA-ring GEMV (M <= 8, G == 128, K % 1024 == 0; the default for weights of
+ *             40 MB and more, e.g. the lm_head), int8 tensor-core math for one x row: tiles =
+ *             residency (1: one CTA per SM leaving room for the next kernel on the stream, 2: two
+ *             CTAs per SM, 3: one CTA with the whole shared memory), split = 1 keeps each row pair
+ *             in one CTA                                                                      */
 typedef struct q4b_linear_cfg {
   int kernel;
   int warps;

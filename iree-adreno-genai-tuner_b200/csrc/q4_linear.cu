@@ -1698,7 +1698,11 @@ static int plan_tc(int M, int K, int G, bool xf32, const q4b_linear_cfg* cfg, Pl
 //   3  one CTA per SM with the whole shared memory (x too large to stage beside a deep ring)
 constexpr size_t kRingSmemHalf = 104 * 1024;   // dynamic bytes of one of two CTAs on an SM
 constexpr size_t kRingSmemAlone = 200 * 1024;  // dynamic bytes of a CTA alone on an SM
-constexpr size_t kRingLargeBytes = 64u << 20;  // weights above this: mode 2 by default
+// The planner sends a GEMV to kernel 6 by default only when its weights exceed kRingMinBytes: below
+// that a launch is dominated by its fixed path (x staging, a few stages per CTA, the finish), where
+// kernel 1's many small CTAs with loads issued before the dependency wait do better (measured on the
+// 3B projections: 8-26 MB faster in kernel 1, the 197 MB lm_head 1.6x faster in kernel 6).
+constexpr size_t kRingMinBytes = 40u << 20;
 static bool ring_ok(int M, int K, int G, int epi, bool norm) {
   return M <= 8 && G == 128 && K % kRingSK == 0 && !norm && (epi != EPI_ARGMAX || M == 1);
 }
@@ -1731,8 +1735,8 @@ static int plan_ring(int M, int N, int K, bool xf32, const q4b_linear_cfg* cfg, 
   if (mode) {
     ok = ring_layout(pl, M, K, xf32, mode);
   } else {
-    const size_t wbytes = (size_t)N * K / 2;
-    ok = ring_layout(pl, M, K, xf32, wbytes > kRingLargeBytes ? 2 : 1) || ring_layout(pl, M, K, xf32, 3);
+    ok = ring_layout(pl, M, K, xf32, 2) || ring_layout(pl, M, K, xf32, 3);
+    (void)N;
   }
   if (!ok) return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 6 ring does not fit beside x (m=%d k=%d)", M, K);
   pl.nsplit = 1;
@@ -1779,7 +1783,8 @@ static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, bool norm
     return plan_ring(M, N, K, xf32, cfg, pl);
   }
   const bool tuned = !cfg || (!cfg->warps && !cfg->tiles && !cfg->split);
-  if (want == 0 && tuned && ring_ok(M, K, G, epi, norm) && plan_ring(M, N, K, xf32, nullptr, pl) == Q4B_OK)
+  if (want == 0 && tuned && ring_ok(M, K, G, epi, norm) && (size_t)N * K / 2 >= kRingMinBytes &&
+      plan_ring(M, N, K, xf32, nullptr, pl) == Q4B_OK)
     return Q4B_OK;
   if (want == 4) {
     if (!stream_ok(M, K, G, norm))
