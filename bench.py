@@ -318,9 +318,10 @@ def run_decode(args, rank, world, local, dist_mod):
     toks_e2e, rep_e2e = rs.generate(prompt, n_new)
     e2e_ms = max_over_ranks(rep_e2e["decode_wall_ms"], dist_mod)
     same = toks_e2e == toks
-    gemv = None
+    gemv = lm = None
     if world == 1 and not args.no_gemv:
         gemv = gemv_measure(dev, steps=50, warmup=5, cpu=not args.no_cpu_baseline)
+        lm = lm_head_measure(dev)
     if rank != 0:
         return None
     pk = peaks()
@@ -362,6 +363,8 @@ def run_decode(args, rank, world, local, dist_mod):
     }
     if gemv:
         line["gemv_5120x3072"] = gemv
+    if lm:
+        line["gemv_lm_head_128256x3072"] = lm
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_decode_baseline(steps=5, warmup=1)
     return line
@@ -485,6 +488,22 @@ def gemv_measure(dev, steps=50, warmup=5, cpu=True):
     if cpu:
         out["cpu_baseline"] = cpu_gemv_baseline()
     return out
+
+
+def lm_head_measure(dev, steps=20, warmup=3):
+    """The 3B lm_head as one GEMV launch (128256 x 3072, 197 MB of int4 + scales, M = 1): GB/s of
+    chained launches over two weight copies (> 2x L2) against the HBM roofline."""
+    n, k = 128256, 3072
+    per_call, copies, *_ = chain_measure(dev, n, k, 1, steps, warmup, seed=7)
+    b = linear_bytes(n, k, 1)
+    pk = peaks()
+    gbs = b / per_call / 1e9
+    return {"metric": "int4 GEMV HBM GB/s (128256x3072, one launch)", "value": round(gbs, 1), "unit": "GB/s",
+            "us_per_call": round(per_call * 1e6, 2), "kernel": f"q4_linear kernel {kernel_of(1, n, k)}",
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": round(gbs / pk["hbm_gbs"], 4), "peak_source": pk["source"],
+                         "traffic": profile_traffic("q4_gemv_ring_lm_head"), "algorithmic_bytes_per_launch": b},
+            "calls": steps * copies}
 
 
 def run_sweep(args, rank, world, local, dist_mod):
