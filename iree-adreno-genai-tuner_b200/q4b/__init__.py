@@ -3,11 +3,11 @@ scripts/llm/llama_q4.py (QLinear, QEmbedding, LlamaQ4) and runner/llm_runner.c (
 computed by hand-written CUDA in libq4b.so behind the C ABI of include/q4b.h."""
 
 from ._lib import LIB_PATH, GemmCfg, LinearCfg, Q4BError, lib
-from .llama import LlamaQ4, StepFn, SyntheticStateDict, group_for, rope_tables, shard_layer
+from .llama import LazySafetensors, LlamaQ4, StepFn, SyntheticStateDict, group_for, rope_tables, shard_layer
 from .ops import attention, dequantize_q4, embed_lookup, gemm_f16, q4_linear, quantize_q4, rmsnorm, unpack_q4
 from .qlinear import QEmbedding, QLinear
 from .runner import SYNTHETIC, Runner
 
 __all__ = ["LIB_PATH", "GemmCfg", "LinearCfg", "gemm_f16", "Q4BError", "lib", "quantize_q4", "unpack_q4", "dequantize_q4", "q4_linear",
-           "embed_lookup", "rmsnorm", "attention", "QLinear", "QEmbedding", "LlamaQ4", "StepFn", "SyntheticStateDict",
+           "embed_lookup", "rmsnorm", "attention", "QLinear", "QEmbedding", "LlamaQ4", "StepFn", "SyntheticStateDict", "LazySafetensors",
            "group_for", "rope_tables", "shard_layer", "Runner", "SYNTHETIC"]

@@ -1,8 +1,11 @@
 """Runner: the scheduler of runner/llm_runner.c over the native model (q4b_runner_* in libq4b.so).
 
-    python -m q4b.runner --prompt ids.txt [--max_new_tokens 32] [--chunk 128]
+    python -m q4b.runner [--prompt ids.txt] [--max_new_tokens 32] [--chunk 128]
         [--buckets 256,512,1024,2048,4096] [--schedule bucketed|max] [--stop_ids 1,2] [--warmup 1]
         (--model-dir DIR | --synthetic tiny|3b [--seed 0]) [--n_layers N] [--max_ctx 4096]
+
+--model-dir takes a Hugging Face checkpoint directory (quantised at load) or a q4b export
+(python -m q4b.export: packed weights + meta.json, whose prompt is the default).
 
 Flag names and the printed JSON object follow runner/llm_runner.c:35-45 and :249-262.
 """
@@ -69,7 +72,8 @@ def _parse_ints(s):
 def main(argv=None):
     from . import LlamaQ4, SyntheticStateDict
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--prompt", required=True, help="file with whitespace-separated prompt token ids")
+    ap.add_argument("--prompt", default=None, help="file with whitespace-separated prompt token ids "
+                    "(default: the prompt in the export's meta.json)")
     ap.add_argument("--max_new_tokens", type=int, default=32)
     ap.add_argument("--chunk", type=int, default=128)
     ap.add_argument("--buckets", default="256,512,1024,2048,4096")
@@ -83,8 +87,19 @@ def main(argv=None):
     ap.add_argument("--synthetic", choices=["tiny", "3b"], default=None)
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)
-    prompt = _parse_ints(pathlib.Path(a.prompt).read_text())
-    if a.model_dir:
+    meta = None
+    if a.model_dir and (a.model_dir / "meta.json").exists():  # a q4b export (q4b.export): packed weights
+        from . import export
+        meta = json.loads((a.model_dir / "meta.json").read_text())
+    if a.prompt:
+        prompt = _parse_ints(pathlib.Path(a.prompt).read_text())
+    elif meta and meta.get("prompt"):
+        prompt = [int(t) for t in meta["prompt"]]
+    else:
+        ap.error("--prompt is required (the model has no exported prompt)")
+    if meta:
+        model = export.load(a.model_dir, max_ctx=a.max_ctx, max_chunk=a.chunk)
+    elif a.model_dir:
         model = LlamaQ4(a.model_dir, group=a.group, max_ctx=a.max_ctx, n_layers=a.n_layers, max_chunk=a.chunk,
                         per_linear_group=True)
     else:
