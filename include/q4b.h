@@ -159,6 +159,31 @@ int q4b_attention(const float* q, const uint16_t* k_cache, const uint16_t* v_cac
                   int n_heads, int n_kv_heads, int head_dim, int L, float* out, void* workspace,
                   size_t workspace_bytes, q4b_stream_t stream);
 
+/* The same attention in its one-pass form for any row count (a prefill chunk, :208-232): no
+ * workspace; the causal mask and bucket as q4b_attention. */
+int q4b_prefill_attn(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* start,
+                     int n_rows, int n_heads, int n_kv_heads, int head_dim, int L, float* out, q4b_stream_t stream);
+
+/* The fused q|k|v projection of one layer (:204-223): rows = x [m, dim] fp32 @ wqkv^T (wqkv rows
+ * q heads | k heads | v heads, int4 [(n_heads + 2 n_kv_heads) head_dim, dim/8]), RoPE on q and k
+ * with the fp32 tables rope_cos / rope_sin [max_ctx, head_dim] at positions *start + r, q to
+ * q_out [m, n_heads, head_dim] fp32, k and v into the fp16 caches [max_ctx, n_kv_heads, head_dim]
+ * at rows *start + r (in place, :222-223). start is a device int32. Workspace as
+ * q4b_q4_linear's (zero-filled once). */
+size_t q4b_qkv_rope_kvwrite_workspace(int m, int dim, int n_heads, int n_kv_heads, int head_dim, int group);
+int q4b_qkv_rope_kvwrite(const int32_t* qweight, const uint16_t* scales, int group, const float* x, int m, int dim,
+                         int n_heads, int n_kv_heads, int head_dim, const float* rope_cos, const float* rope_sin,
+                         const int32_t* start, float* q_out, uint16_t* k_cache, uint16_t* v_cache, void* workspace,
+                         size_t workspace_bytes, q4b_stream_t stream);
+
+/* SwiGLU (:235-236): out[r, i] = silu(gate_up[r, i]) * gate_up[r, inter + i] (gate rows first,
+ * :152), fp32 [rows, 2 inter] -> [rows, inter]. */
+int q4b_silu_mul(const float* gate_up, int rows, int inter, float* out, q4b_stream_t stream);
+
+/* Greedy head (:238-239): *index (device int32) = the first index of the largest of logits[n]
+ * (torch.argmax's tie rule). */
+int q4b_argmax(const float* logits, int n, int32_t* index, q4b_stream_t stream);
+
 /* ---- LlamaQ4 model (scripts/llm/llama_q4.py:145-243) --------------------------------------- */
 
 typedef struct q4b_model_cfg {
@@ -219,6 +244,22 @@ int q4b_tp_unique_id(unsigned char* id, int id_bytes);
 /* Join the communicator of the model's tp_size ranks as tp_rank (collective across the ranks).
  * Afterwards each step all-reduces the wo / wdown partial outputs and gathers the per-rank argmax. */
 int q4b_model_attach_tp(q4b_model* model, const unsigned char* id, int id_bytes);
+
+/* Standalone collectives for a tensor-parallel caller outside the model (the reference runs on
+ * one device; these are the exchange steps of its column / row / vocabulary splits). */
+typedef struct q4b_tp q4b_tp;
+/* Join a communicator of `world` ranks as `rank` (collective; id from q4b_tp_unique_id). */
+int q4b_tp_init(int rank, int world, const unsigned char* id, int id_bytes, q4b_tp** out);
+void q4b_tp_destroy(q4b_tp* tp);
+/* In-place sum over the ranks of n elements (a row-split projection's partial outputs). */
+int q4b_tp_allreduce_f16(q4b_tp* tp, void* buf, size_t n, q4b_stream_t stream);
+int q4b_tp_allreduce_f32(q4b_tp* tp, float* buf, size_t n, q4b_stream_t stream);
+/* Greedy head over a vocabulary split: this rank's logits[n_local] are rows index_offset.. of
+ * the full vocabulary; *token (device int32, every rank) = the global first maximum. Workspace:
+ * q4b_tp_argmax_workspace(tp) bytes, 8-byte aligned. */
+size_t q4b_tp_argmax_workspace(const q4b_tp* tp);
+int q4b_tp_argmax_gather(q4b_tp* tp, const float* logits, int n_local, int index_offset, int32_t* token,
+                         void* workspace, size_t workspace_bytes, q4b_stream_t stream);
 
 /* ---- runner (runner/llm_runner.c) ---------------------------------------------------------- */
 

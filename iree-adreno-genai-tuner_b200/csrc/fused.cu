@@ -374,7 +374,7 @@ int attention_run(const AttnArgs& in, cudaStream_t st) {
   const int g = a.H / a.Hkv;
   if (a.H % a.Hkv || (a.head_dim != 32 && a.head_dim != 64 && a.head_dim != 128))
     return set_error(Q4B_EUNSUPPORTED, "attention: head_dim must be 32, 64 or 128 and H %% Hkv == 0");
-  const bool decode = a.C * g <= kMaxRows;
+  const bool decode = a.C * g <= kMaxRows && !a.force_prefill;
   if (decode && attn_decode_chunks(a.L) > kMaxChunks)
     return set_error(Q4B_EUNSUPPORTED, "attention: bucket %d above %d keys", a.L, kMaxChunks * kChunk);
   cudaError_t e;
@@ -457,5 +457,26 @@ extern "C" int q4b_attention(const float* q, const uint16_t* k_cache, const uint
   a.out = out;
   a.ws_base = workspace;
   a.ws_bytes = workspace_bytes;
+  return attention_run(a, as_stream(stream));
+}
+
+extern "C" int q4b_prefill_attn(const float* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* start,
+                                int n_rows, int n_heads, int n_kv_heads, int head_dim, int L, float* out,
+                                q4b_stream_t stream) {
+  if (!q || !k_cache || !v_cache || !start || !out || n_rows < 1 || L < 1)
+    return set_error(Q4B_EINVAL, "prefill_attn: bad arguments");
+  AttnArgs a = {};
+  a.q = q;
+  a.k_cache = reinterpret_cast<const __half*>(k_cache);
+  a.v_cache = reinterpret_cast<const __half*>(v_cache);
+  a.pos0 = start;
+  a.C = n_rows;
+  a.H = n_heads;
+  a.Hkv = n_kv_heads;
+  a.head_dim = head_dim;
+  a.L = L;
+  a.scale = (float)(1.0 / sqrt((double)head_dim));
+  a.out = out;
+  a.force_prefill = 1;
   return attention_run(a, as_stream(stream));
 }

@@ -17,6 +17,7 @@ struct AttnArgs {
   size_t ws_bytes;
   unsigned* counters;
   float* ws;
+  int force_prefill;      // 1: the one-pass form for any row count (no workspace)
 };
 
 constexpr size_t kCounterRegion = 4096;  // attention arrival counters (one per KV head)

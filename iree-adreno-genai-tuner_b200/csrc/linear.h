@@ -67,6 +67,10 @@ struct LinearOp {
 };
 
 int linear_run(const LinearOp& op, cudaStream_t st);
+// Greedy argmax of one row (first maximum): the key (orderable value, index) and / or the index
+// (idx_offset added: a vocabulary shard's first row). One CTA.
+int argmax_run(const float* v, int n, int idx_offset, unsigned long long* key_out, int32_t* index_out,
+               cudaStream_t st);
 size_t linear_workspace(const LinearOp& op);
 
 // Publish a greedy token into the step state (append to the log, stop ids, advance): the device

@@ -13,6 +13,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <new>
 #include <vector>
 
 #include "model.h"
@@ -175,4 +176,84 @@ extern "C" int q4b_model_attach_tp(q4b_model* model, const unsigned char* id, in
   m->comm = reinterpret_cast<ncclComm*>(c);
   if (!m->gather && (rc = m->alloc((void**)&m->gather, sizeof(unsigned long long) * m->cfg.tp_size, true))) return rc;
   return Q4B_OK;
+}
+
+// ---- standalone collectives (tensor-parallel callers outside the model) ---------------------------
+
+struct q4b_tp {
+  ncclComm_t comm = nullptr;
+  int rank = 0, world = 1;
+};
+
+namespace q4b {
+// token = index of the largest of n gathered keys (lowest index on equal values)
+__global__ void keys_max_kernel(const unsigned long long* keys, int n, int32_t* token) {
+  if (threadIdx.x != 0) return;
+  unsigned long long best = 0ull;
+  for (int i = 0; i < n; ++i) best = max(best, keys[i]);
+  *token = (int32_t)argmax_index(best);
+}
+}  // namespace q4b
+
+extern "C" int q4b_tp_init(int rank, int world, const unsigned char* id, int id_bytes, q4b_tp** out) {
+  if (!out || !id || id_bytes < (int)sizeof(ncclUniqueId) || world < 1 || rank < 0 || rank >= world)
+    return set_error(Q4B_EINVAL, "tp_init: bad arguments");
+  *out = nullptr;
+  const NcclApi* api = nccl();
+  if (!api) return set_error(Q4B_EUNSUPPORTED, "tp_init: libnccl.so.2 not found (set Q4B_NCCL_LIB)");
+  ncclUniqueId u;
+  memcpy(&u, id, sizeof(u));
+  ncclComm_t c = nullptr;
+  int rc = nccl_err(api->comm_init_rank(&c, world, u, rank), "ncclCommInitRank");
+  if (rc) return rc;
+  q4b_tp* t = new (std::nothrow) q4b_tp;
+  if (!t) {
+    api->comm_destroy(c);
+    return set_error(Q4B_ENOMEM, "tp_init: out of host memory");
+  }
+  t->comm = c;
+  t->rank = rank;
+  t->world = world;
+  *out = t;
+  return Q4B_OK;
+}
+
+extern "C" void q4b_tp_destroy(q4b_tp* tp) {
+  if (!tp) return;
+  if (tp->comm && nccl()) nccl()->comm_destroy(tp->comm);
+  delete tp;
+}
+
+static int tp_allreduce(q4b_tp* tp, void* buf, size_t n, ncclDataType_t t, const char* what, q4b_stream_t stream) {
+  if (!tp || !tp->comm || (!buf && n)) return set_error(Q4B_EINVAL, "%s: bad arguments", what);
+  if (!n) return Q4B_OK;
+  return nccl_err(nccl()->all_reduce(buf, buf, n, t, ncclSum, tp->comm, as_stream(stream)), what);
+}
+
+extern "C" int q4b_tp_allreduce_f16(q4b_tp* tp, void* buf, size_t n, q4b_stream_t stream) {
+  return tp_allreduce(tp, buf, n, ncclFloat16, "tp_allreduce_f16", stream);
+}
+
+extern "C" int q4b_tp_allreduce_f32(q4b_tp* tp, float* buf, size_t n, q4b_stream_t stream) {
+  return tp_allreduce(tp, buf, n, ncclFloat32, "tp_allreduce_f32", stream);
+}
+
+extern "C" size_t q4b_tp_argmax_workspace(const q4b_tp* tp) {
+  return tp ? sizeof(unsigned long long) * (size_t)(tp->world + 1) : 0;
+}
+
+extern "C" int q4b_tp_argmax_gather(q4b_tp* tp, const float* logits, int n_local, int index_offset, int32_t* token,
+                                    void* workspace, size_t workspace_bytes, q4b_stream_t stream) {
+  if (!tp || !tp->comm || !logits || !token || n_local < 1 || index_offset < 0)
+    return set_error(Q4B_EINVAL, "tp_argmax_gather: bad arguments");
+  if (!workspace || workspace_bytes < q4b_tp_argmax_workspace(tp) || !aligned(workspace, 8))
+    return set_error(Q4B_EINVAL, "tp_argmax_gather: workspace of %zu bytes needed", q4b_tp_argmax_workspace(tp));
+  cudaStream_t st = as_stream(stream);
+  auto* keys = reinterpret_cast<unsigned long long*>(workspace);
+  int rc = argmax_run(logits, n_local, index_offset, keys, nullptr, st);
+  if (rc) return rc;
+  rc = nccl_err(nccl()->all_gather(keys, keys + 1, 1, ncclUint64, tp->comm, st), "tp_argmax_gather allgather");
+  if (rc) return rc;
+  keys_max_kernel<<<1, 32, 0, st>>>(keys + 1, tp->world, token);
+  return check_launch("tp_argmax_gather");
 }

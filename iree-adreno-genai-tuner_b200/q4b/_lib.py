@@ -92,6 +92,20 @@ SIGNATURES = {
     "q4b_attention_workspace": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "q4b_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p,
                               c_void_p, c_size_t, c_void_p]),
+    "q4b_prefill_attn": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                                 c_void_p, c_void_p]),
+    "q4b_qkv_rope_kvwrite_workspace": (c_size_t, [c_int, c_int, c_int, c_int, c_int, c_int]),
+    "q4b_qkv_rope_kvwrite": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int,
+                                     c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                     c_void_p]),
+    "q4b_silu_mul": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "q4b_argmax": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
+    "q4b_tp_init": (c_int, [c_int, c_int, c_void_p, c_int, ctypes.POINTER(c_void_p)]),
+    "q4b_tp_destroy": (None, [c_void_p]),
+    "q4b_tp_allreduce_f16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "q4b_tp_allreduce_f32": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "q4b_tp_argmax_workspace": (c_size_t, [c_void_p]),
+    "q4b_tp_argmax_gather": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p, c_size_t, c_void_p]),
     "q4b_model_create": (c_int, [ctypes.POINTER(ModelCfg), ctypes.POINTER(c_void_p)]),
     "q4b_model_set_layer": (c_int, [c_void_p, c_int, ctypes.POINTER(LayerWeights)]),
     "q4b_model_set_head": (c_int, [c_void_p, ctypes.POINTER(QMat), c_void_p, c_void_p, c_void_p]),
