@@ -20,7 +20,10 @@ Prints ONE JSON line (rank 0). Workloads:
           bytes moved per second, summed over ranks (replicas: the GEMV does not shard).
   sweep   BASELINE config 5: every 3B projection and the lm_head at M in {1, 4, 16, 64} (--shapes,
           --m), each row timed like config 1; value = aggregate GB/s, with one entry per row.
-  profile a short fixed launch sequence for profilers (--layers, --prefill, --ctx, --bucket).
+  profile a short fixed launch sequence for profilers (--layers, --prefill, --pos, --bucket).
+  ctx     the context-length sweep of scripts/llm/bench.py + summarize.py: ctx 256 .. 4096 (prompt
+          = ctx - --new), schedules bucketed and max, --prompts seeded prompts each; one line with
+          the per-(schedule, ctx) medians and speed-ups.
 --impl reference times the CPU restatement of the reference path (oracle port: whole decode steps with
 the int4 GEMVs in C) on the host cores of rank 0; other ranks exit without work.
 """
@@ -506,6 +509,74 @@ def lm_head_measure(dev, steps=20, warmup=3):
             "calls": steps * copies}
 
 
+def summarize_ctx(records):
+    """scripts/llm/summarize.py:25-44: per (schedule, ctx) medians over the prompts (prefill tok/s,
+    TTFT, decode tok/s) and each row's speed-up over the first schedule at the same ctx."""
+    groups = {}
+    for r in records:
+        groups.setdefault((r["schedule"], r["ctx"]), []).append(r)
+    order = []
+    for r in records:
+        if r["schedule"] not in order:
+            order.append(r["schedule"])
+    rows = []
+    for (sched, ctx), rs in sorted(groups.items(), key=lambda kv: (order.index(kv[0][0]), kv[0][1])):
+        rows.append(dict(schedule=sched, ctx=ctx, n=len(rs),
+                         prefill_tok_s=round(statistics.median(r["prefill_tok_s"] for r in rs), 1),
+                         ttft_s=round(statistics.median(r["ttft_ms"] for r in rs) / 1e3, 4),
+                         decode_tok_s=round(statistics.median(r["decode_tok_s"] for r in rs), 2)))
+    base = {r["ctx"]: r for r in rows if r["schedule"] == order[0]}
+    for r in rows:
+        b = base.get(r["ctx"])
+        r["prefill_x"] = round(r["prefill_tok_s"] / b["prefill_tok_s"], 3) if b else None
+        r["decode_x"] = round(r["decode_tok_s"] / b["decode_tok_s"], 3) if b else None
+    return rows
+
+
+def run_ctx(args, rank, world, local, dist_mod):
+    """scripts/llm/bench.py:67-104 on the B200: for each context length (prompt = ctx - new tokens,
+    then `new` greedy tokens) and schedule, the runner's report on the 3B-shape model; the reference's
+    three prompt kinds (tokenised text) become three seeded random-id prompts (no tokenizer or corpus
+    here; the ids do not change the work). One JSON line with the summarize.py table."""
+    import numpy as np
+    import torch
+
+    import q4b
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = q4b.SYNTHETIC["3b"]
+    model = q4b.LlamaQ4(None, group=128, max_ctx=max(BUCKETS), sd=q4b.SyntheticStateDict(cfg, seed=0, device=dev),
+                        cfg=cfg, max_chunk=CHUNK, tp_rank=rank, tp_size=world, device=dev)
+    if world > 1:
+        model.attach_tp(dist_mod)
+    records = []
+    runners = {s: q4b.Runner(model, CHUNK, BUCKETS, s, graphs=True, warmup=1) for s in args.schedules}
+    for seed in range(args.prompts):
+        for ctx in args.ctx:
+            prompt = np.random.default_rng(100 + seed).integers(0, cfg["vocab_size"], ctx - args.new).tolist()
+            for sched in args.schedules:
+                toks, rep = runners[sched].generate(prompt, args.new)
+                records.append(dict(kind=f"seed{seed}", ctx=ctx, schedule=sched, prompt_tokens=rep["prompt_tokens"],
+                                    prefill_tok_s=rep["prefill_tok_s"], ttft_ms=rep["ttft_ms"],
+                                    decode_tok_s=rep["decode_tok_s"], new_tokens=len(toks)))
+    if rank != 0:
+        return None
+    rows = summarize_ctx(records)
+    dec = [r["decode_tok_s"] for r in rows if r["schedule"] == args.schedules[0]]
+    if args.out:
+        with open(args.out, "a") as f:
+            for r in records:
+                f.write(json.dumps(dict(r, tag=args.tag)) + "\n")
+    return {"metric": "3B-shape decode tokens/s across context lengths (median over prompts)",
+            "value": round(statistics.median(dec), 2), "unit": "tokens/s", "n_gpus": world, "steps": args.new,
+            "warmup": 1, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int4 weights, fp32 activations, fp16 KV cache", "data": "synthetic (seeded random prompt ids)",
+            "config": {"workload": "context-length sweep (scripts/llm/bench.py + summarize.py)", "ctx": args.ctx,
+                       "new": args.new, "prompts": args.prompts, "schedules": args.schedules, "chunk": CHUNK,
+                       "buckets": BUCKETS, "parallelism": f"tp{world}"},
+            "rows": rows}
+
+
 def run_sweep(args, rank, world, local, dist_mod):
     """every 3B projection (and the lm_head) at M in {1, 4, 16, 64}, each timed as
     a chain over distinct weight copies, against the HBM roofline; one GPU per rank (replicas)."""
@@ -545,14 +616,14 @@ def run_sweep(args, rank, world, local, dist_mod):
 
 def run_profile(args, rank, world, local, dist_mod):
     """A short fixed launch sequence for profilers: a 3B-shaped model with --layers layers, an optional
-    --prefill C chunk at position 0, then --steps single-token decode steps at position --ctx."""
+    --prefill C chunk at position 0, then --steps single-token decode steps at position --pos."""
     import torch
 
     import q4b
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     cfg = dict(q4b.SYNTHETIC["3b"], num_hidden_layers=args.layers)
-    model = q4b.LlamaQ4(None, group=128, max_ctx=max(args.bucket, args.ctx + args.steps + 1),
+    model = q4b.LlamaQ4(None, group=128, max_ctx=max(args.bucket, args.pos + args.steps + 1),
                         sd=q4b.SyntheticStateDict(cfg, device=dev), cfg=cfg, max_chunk=max(8, args.prefill),
                         device=dev)
     caches = model.new_caches()
@@ -564,14 +635,14 @@ def run_profile(args, rank, world, local, dist_mod):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for i in range(args.steps):
-        nxt, _ = model.step(tok, torch.tensor([args.ctx + i]), torch.tensor([0]), caches, args.bucket)
+        nxt, _ = model.step(tok, torch.tensor([args.pos + i]), torch.tensor([0]), caches, args.bucket)
         tok = nxt.reshape(1, 1)
     e1.record()
     e1.synchronize()
     ms = e0.elapsed_time(e1)
     return {"metric": "profile sequence (3B shape)", "value": round(ms / args.steps, 4), "unit": "ms/step",
             "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": 0,
-            "config": {"workload": "profile", "layers": args.layers, "ctx": args.ctx, "bucket": args.bucket,
+            "config": {"workload": "profile", "layers": args.layers, "pos": args.pos, "bucket": args.bucket,
                        "prefill": args.prefill}, "last_token": int(tok)}
 
 
@@ -607,11 +678,17 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="decode: tokens (255); gemv: graph replays (200)")
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "sweep", "profile"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "sweep", "profile", "ctx"])
+    ap.add_argument("--ctx", type=int, nargs="*", default=[256, 512, 1024, 2048, 4096], help="ctx: context lengths")
+    ap.add_argument("--new", type=int, default=64, help="ctx: generated tokens per run")
+    ap.add_argument("--prompts", type=int, default=3, help="ctx: prompts per context length")
+    ap.add_argument("--schedules", nargs="*", default=["bucketed", "max"], help="ctx: runner schedules")
+    ap.add_argument("--out", default=None, help="ctx: append every run's record (JSON lines) here")
+    ap.add_argument("--tag", default="run", help="ctx: tag of the records")
     ap.add_argument("--shapes", nargs="*", default=None, help="sweep: subset of " + " ".join(SWEEP_SHAPES))
     ap.add_argument("--m", nargs="*", type=int, default=[1, 4, 16, 64], help="sweep: rows of x")
     ap.add_argument("--layers", type=int, default=1, help="profile: layers of the 3B-shaped model")
-    ap.add_argument("--ctx", type=int, default=128, help="profile: position of the first decode step")
+    ap.add_argument("--pos", type=int, default=128, help="profile: position of the first decode step")
     ap.add_argument("--bucket", type=int, default=256, help="profile: KV bucket of the decode steps")
     ap.add_argument("--prefill", type=int, default=0, help="profile: rows of one prefill chunk run first")
     ap.add_argument("--no-gemv", action="store_true", help="decode: skip the config-1 GEMV sub-measurement")
@@ -622,7 +699,7 @@ def main():
     if args.warmup < 3 and args.workload != "profile":
         args.warmup = 3
     if args.steps is None:
-        args.steps = {"decode": 255, "gemv": 200, "sweep": 20, "profile": 3}[args.workload]
+        args.steps = {"decode": 255, "gemv": 200, "sweep": 20, "profile": 3, "ctx": 0}[args.workload]
     rank, world, local = dist_env()
     if args.impl == "reference":
         line = run_reference(args, rank, world)
@@ -631,7 +708,8 @@ def main():
         return
     dist_mod = init_dist(world, local)
     try:
-        run = {"decode": run_decode, "gemv": run_gemv, "sweep": run_sweep, "profile": run_profile}[args.workload]
+        run = {"decode": run_decode, "gemv": run_gemv, "sweep": run_sweep, "profile": run_profile,
+               "ctx": run_ctx}[args.workload]
         line = run(args, rank, world, local, dist_mod)
     finally:
         if dist_mod:
