@@ -21,6 +21,8 @@ Prints ONE JSON line (rank 0). Workloads:
   sweep   BASELINE config 5: every 3B projection and the lm_head at M in {1, 4, 16, 64} (--shapes,
           --m), each row timed like config 1; value = aggregate GB/s, with one entry per row.
   profile a short fixed launch sequence for profilers (--layers, --prefill, --pos, --bucket).
+  gemm    BASELINE config 2: the fp16 GEMM sweep (M in {128, 2048} x the 3B projections, plus the
+          M = 1 rows) through q4b_gemm_f16, TFLOP/s against min(tensor peak, AI x HBM).
   ctx     the context-length sweep of scripts/llm/bench.py + summarize.py: ctx 256 .. 4096 (prompt
           = ctx - --new), schedules bucketed and max, --prompts seeded prompts each; one line with
           the per-(schedule, ctx) medians and speed-ups.
@@ -577,6 +579,102 @@ def run_ctx(args, rank, world, local, dist_mod):
             "rows": rows}
 
 
+def run_gemm(args, rank, world, local, dist_mod):
+    """the fp16 GEMM sweep C = A B (row-major A [M, K], B [K, N], fp32
+    accumulate, fp16 C) on the 8 shapes M in {128, 2048} x the 3B projections plus the 4 M = 1 rows,
+    through q4b_gemm_f16's default plan. Per shape: mean time of back-to-back calls in a CUDA graph
+    over enough (A, B) copies that operands come from HBM (> 2x L2 where one call's bytes are below
+    it), TFLOP/s and the attainable roofline min(tensor peak, AI x HBM) (gemm/shapes.py flops and
+    min_bytes, BLOG-GEMM.md:109). value = the geometric mean of the 8 shapes' fractions of attainable."""
+    import math
+
+    import torch
+
+    from q4b import ops
+    from q4b.gemm.shapes import EXTRA, SHAPES
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pk = peaks()
+    rows = []
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    for s in SHAPES + EXTRA:
+        copies = max(1, math.ceil(2 * L2_BYTES / s.min_bytes)) if s.min_bytes < 2 * L2_BYTES else 1
+        A = [(torch.rand(s.M, s.K, device=dev, generator=g) * 2 - 1).half() for _ in range(copies)]
+        B = [(torch.rand(s.K, s.N, device=dev, generator=g) * 2 - 1).half() for _ in range(copies)]
+        C = [torch.empty(s.M, s.N, dtype=torch.float16, device=dev) for _ in range(copies)]
+        stream = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(stream):
+            for i in range(copies):
+                ops.gemm_f16(A[i], B[i], out=C[i])
+            graph = torch.cuda.CUDAGraph()
+            graph.capture_begin()
+            for i in range(copies):
+                ops.gemm_f16(A[i], B[i], out=C[i])
+            graph.capture_end()
+            for _ in range(args.warmup):
+                graph.replay()
+        stream.synchronize()
+        reps = max(1, args.steps)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+        e1.synchronize()
+        t = e0.elapsed_time(e1) / 1e3 / (reps * copies)
+        ref = A[0].float() @ B[0].float()
+        err = float((C[0].float() - ref).abs().max() / ref.abs().max())
+        tf = s.flops / t / 1e12
+        attainable = min(pk["bf16_tflops"], s.flops / s.min_bytes * pk["hbm_gbs"] / 1e3)
+        rows.append({"id": s.id, "shape": s.name, "M": s.M, "N": s.N, "K": s.K, "us": round(t * 1e6, 2),
+                     "TFLOP_s": round(tf, 1), "attainable_TFLOP_s": round(attainable, 1),
+                     "frac_attainable": round(tf / attainable, 4), "bound": "tensor" if attainable >= pk["bf16_tflops"]
+                     else "hbm", "rel_err": err, "copies": copies})
+        del graph, A, B, C
+        torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    main = [r for r in rows if r["M"] > 1]
+    gm = math.exp(sum(math.log(r["frac_attainable"]) for r in main) / len(main))
+    line = {"metric": "fp16 GEMM sweep, fraction of attainable (geomean, 8 shapes)", "value": round(gm, 4),
+            "unit": "fraction", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 in/out, fp32 accumulate",
+            "data": "synthetic U(-1, 1)",
+            "config": {"workload": "fp16 GEMM sweep (BASELINE config 2) + M=1 rows", "layout": "NN",
+                       "parallelism": f"replicas x{world}", "l2": "operand copies > 2x L2 per shape where needed"},
+            "roofline": {"bound": "tensor", "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "peak_source": pk["source"],
+                         "achieved": max(r["TFLOP_s"] for r in main),
+                         "frac": round(max(r["TFLOP_s"] for r in main) / pk["bf16_tflops"], 4), "traffic": None},
+            "rows": rows}
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_gemm_baseline()
+    return line
+
+
+def cpu_gemm_baseline(budget_s=10.0):
+    """The reference's Cref computation (gemm/shapes.py:62: A.float() @ B.float()) on the host cores
+    for the M = 128 x 5120 x 3072 shape, TFLOP/s."""
+    import torch
+    torch.manual_seed(0)
+    M, N, K = 128, 5120, 3072
+    a = torch.rand(M, K) * 2 - 1
+    b = torch.rand(K, N) * 2 - 1
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter()
+        _ = a.half().float() @ b.half().float()
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 200:
+            break
+    med = statistics.median(times)
+    return {"value": 2 * M * N * K / med / 1e12, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{len(times)} x torch CPU fp32 matmul of fp16-rounded U(-1,1) operands, 128x5120x3072 "
+                      f"(median {med * 1e3:.1f} ms)"}
+
+
 def run_sweep(args, rank, world, local, dist_mod):
     """every 3B projection (and the lm_head) at M in {1, 4, 16, 64}, each timed as
     a chain over distinct weight copies, against the HBM roofline; one GPU per rank (replicas)."""
@@ -678,7 +776,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="decode: tokens (255); gemv: graph replays (200)")
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "sweep", "profile", "ctx"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "sweep", "profile", "ctx", "gemm"])
     ap.add_argument("--ctx", type=int, nargs="*", default=[256, 512, 1024, 2048, 4096], help="ctx: context lengths")
     ap.add_argument("--new", type=int, default=64, help="ctx: generated tokens per run")
     ap.add_argument("--prompts", type=int, default=3, help="ctx: prompts per context length")
@@ -699,7 +797,7 @@ def main():
     if args.warmup < 3 and args.workload != "profile":
         args.warmup = 3
     if args.steps is None:
-        args.steps = {"decode": 255, "gemv": 200, "sweep": 20, "profile": 3, "ctx": 0}[args.workload]
+        args.steps = {"decode": 255, "gemv": 200, "sweep": 20, "profile": 3, "ctx": 0, "gemm": 20}[args.workload]
     rank, world, local = dist_env()
     if args.impl == "reference":
         line = run_reference(args, rank, world)
@@ -709,7 +807,7 @@ def main():
     dist_mod = init_dist(world, local)
     try:
         run = {"decode": run_decode, "gemv": run_gemv, "sweep": run_sweep, "profile": run_profile,
-               "ctx": run_ctx}[args.workload]
+               "ctx": run_ctx, "gemm": run_gemm}[args.workload]
         line = run(args, rank, world, local, dist_mod)
     finally:
         if dist_mod:
