@@ -77,15 +77,26 @@ def peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
-def profile_traffic(name):
-    """dram bytes per launch recorded from an ncu capture in profiles/<name>.txt ("traffic_bytes_per_launch: N")."""
+def profile_traffic(name, key="traffic_bytes_per_launch"):
+    """A figure recorded from an ncu capture in profiles/<name>.txt (a line "<key>: N"): by default the
+    dram bytes per launch."""
     p = ROOT / "profiles" / f"{name}.txt"
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
-            return float(line.split(":", 1)[1])
+        if line.startswith(key + ":"):
+            return float(line.split(":", 1)[1].split()[0])
     return None
+
+
+def decode_traffic(bytes_tok, world):
+    """roofline.traffic of the decode line: the 1-GPU capture's dram bytes per launch; at tp > 1 (no
+    capture per rank) the capture's traffic / algorithmic ratio times this GPU's algorithmic bytes."""
+    t = profile_traffic("decode_step_3b")
+    if t is None or world == 1:
+        return t
+    alg = profile_traffic("decode_step_3b", "algorithmic_bytes_per_launch")
+    return round(t / alg * bytes_tok) if alg else None
 
 
 class ClockSampler:
@@ -353,7 +364,9 @@ def run_decode(args, rank, world, local, dist_mod):
                    "decode_kernel": "persistent (one cooperative launch per token)" if persistent
                    else "per projection"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": profile_traffic("decode_step_3b"),
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": decode_traffic(bytes_tok, world),
+                     **({"traffic_note": "per GPU: the 1-GPU capture's traffic/algorithmic ratio x this GPU's "
+                                         "algorithmic bytes"} if world > 1 else {}),
                      "peak_source": pk["source"], "kernel": "decode_step_kernel" if persistent else "decode step (q4_gemv_* dominant)",
                      "algorithmic_bytes_per_token_per_gpu": round(bytes_tok)},
         "e2e": {"value": round(steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
@@ -738,10 +751,49 @@ def run_profile(args, rank, world, local, dist_mod):
     e1.record()
     e1.synchronize()
     ms = e0.elapsed_time(e1)
-    return {"metric": "profile sequence (3B shape)", "value": round(ms / args.steps, 4), "unit": "ms/step",
+    line = {"metric": "profile sequence (3B shape)", "value": round(ms / args.steps, 4), "unit": "ms/step",
             "higher_is_better": False, "n_gpus": 1, "steps": args.steps, "warmup": 0,
             "config": {"workload": "profile", "layers": args.layers, "pos": args.pos, "bucket": args.bucket,
                        "prefill": args.prefill}, "last_token": int(tok)}
+    if args.trace:  # one more step with the phase trace on (after the timed ones)
+        buf = model.decode_trace(True)
+        model.step(tok, torch.tensor([args.pos + args.steps]), torch.tensor([0]), caches, args.bucket)
+        torch.cuda.synchronize()
+        line["trace"] = trace_summary(buf.cpu().numpy(), args.layers)
+        model.decode_trace(False)
+    return line
+
+
+TRACE_PHASES = ("qkv", "attn", "o", "gate_up", "down")
+
+
+def trace_summary(ev, n_layers):
+    """Phase breakdown of one persistent decode step from its trace (q4b_model_set_trace layout),
+    in microseconds, averaged over the layers after the first: per phase `busy` = median over the
+    CTAs of (done - start), `lag` = median CTA start - the last CTA's end of the previous phase (the
+    synchronisation and x-staging latency), `span` = last end - first start."""
+    import numpy as np
+    ev = ev.astype(np.int64)
+    start = ev[:, 10 * n_layers + 2]
+    ev = ev[start > 0]
+    t0 = int(ev[:, 10 * n_layers + 2].min())
+    out = {p: {"busy": [], "lag": [], "span": []} for p in TRACE_PHASES}
+    for l in range(1, n_layers):
+        prev_end = ev[:, 10 * (l - 1) + 9].max()
+        for i, p in enumerate(TRACE_PHASES):
+            a, b = ev[:, 10 * l + 2 * i], ev[:, 10 * l + 2 * i + 1]
+            out[p]["busy"].append(float(np.median(b - a)))
+            out[p]["lag"].append(float(np.median(a) - prev_end))
+            out[p]["span"].append(float(b.max() - a.min()))
+            prev_end = b.max()
+    res = {p: {k: round(float(np.mean(v)) / 1e3, 3) for k, v in d.items()} for p, d in out.items()} if n_layers > 1 else {}
+    L = 10 * n_layers
+    res["lm_head"] = {"busy": round(float(np.median(ev[:, L + 1] - ev[:, L])) / 1e3, 3),
+                      "lag": round(float(np.median(ev[:, L]) - ev[:, L - 1].max()) / 1e3, 3)}
+    res["layer_us"] = round(float(ev[:, L - 1].max() - ev[:, 9].max()) / 1e3 / max(1, n_layers - 1), 3)
+    res["step_us"] = round(float(ev[:, L + 1].max() - t0) / 1e3, 3)
+    res["ctas"] = int(ev.shape[0])
+    return res
 
 
 def run_reference(args, rank, world):
@@ -789,6 +841,7 @@ def main():
     ap.add_argument("--pos", type=int, default=128, help="profile: position of the first decode step")
     ap.add_argument("--bucket", type=int, default=256, help="profile: KV bucket of the decode steps")
     ap.add_argument("--prefill", type=int, default=0, help="profile: rows of one prefill chunk run first")
+    ap.add_argument("--trace", action="store_true", help="profile: phase trace of one more decode step")
     ap.add_argument("--no-gemv", action="store_true", help="decode: skip the config-1 GEMV sub-measurement")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gemv-cfg", default=None, help='JSON q4b_linear_cfg, e.g. {"warps":4,"tiles":2}')

@@ -236,6 +236,14 @@ int q4b_model_decode_path(const q4b_model* model);
  * runner returns Q4B_ETIMEOUT, until the model is prepared again (q4b_model_set_head or
  * q4b_model_set_layer; single GPU). No reference counterpart. */
 int q4b_model_fail_decode(q4b_model* model);
+/* Phase trace of the persistent decode step (no reference counterpart; a profiling aid): with a
+ * device buffer of at least q4b_model_trace_events(model) uint64 set, every persistent step writes
+ * %globaltimer stamps (ns) per CTA: CTA c's row starts at c * (10 * n_layers + 4); per layer l the
+ * stamps 10 l + {0 q|k|v x staged, 1 q|k|v done, 2 attention start, 3 attention done, 4 o x staged,
+ * 5 o done, 6 gate|up x staged, 7 gate|up done, 8 down x staged, 9 down done}, then 10 n_layers +
+ * {0 lm_head x staged, 1 lm_head done, 2 consumers start}. NULL turns the trace off. */
+size_t q4b_model_trace_events(const q4b_model* model);
+int q4b_model_set_trace(q4b_model* model, unsigned long long* events, size_t n_events);
 
 /* ---- tensor parallelism (one process per GPU, NCCL loaded at run time) ---------------------- */
 

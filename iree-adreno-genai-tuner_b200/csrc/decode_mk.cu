@@ -99,7 +99,16 @@ struct MkArgs {
   unsigned long long* keys;  // [tp] this rank's copy of every rank's best argmax key
   // limit of every wait: 1 s on one GPU; longer with peers, whose launches may start later
   unsigned long long wait_ns;
+  // phase trace (null = off): per CTA mk_trace_stride(n_layers) %globaltimer stamps, see trace_ev
+  unsigned long long* trace;
 };
+
+// Trace events of a CTA: per layer l, 10 l + {0: q|k|v x staged, 1: q|k|v done, 2: attention start,
+// 3: attention done, 4: o x staged, 5: o done, 6: gate|up x staged, 7: gate|up done, 8: down x
+// staged, 9: down done}; then 10 L + {0: lm_head x staged, 1: lm_head done, 2: consumers start}.
+__device__ __forceinline__ void trace_ev(const MkArgs& a, int e) {
+  if (a.trace && threadIdx.x == 32) a.trace[(size_t)blockIdx.x * mk_trace_stride(a.n_layers) + e] = globaltimer_ns();
+}
 
 struct MkSmem {
   uint8_t ring[MK_NSLOT][MK_SLOT];
@@ -810,6 +819,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     for (int e = ct; e < MK_XROW; e += MK_CW * 32) sm.xs_hi[e] = sm.xs_lo[e] = make_uint4(0, 0, 0, 0);
     consumer_sync();
   }
+  trace_ev(a, 10 * a.n_layers + 2);
   unsigned seq = 0;
   unsigned stage = 0;
   const unsigned n = gridDim.x;
@@ -823,31 +833,39 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     norm_weights(a, sm.ln_in[l], lw);
     stage_norm(a, sm, lw, l == 0, token, a.hb, pwd, nwd, (sm.tagbase + l + 1) & 1u, a.hb + a.D);
     consumer_sync();
+    trace_ev(a, 10 * l + 0);
     ok = consume_stage(a, sm, ST_QKV, l, seq, pos);
+    trace_ev(a, 10 * l + 1);
     stage_arrive(a);
     ++stage;
     if (!ok) break;
     // attention
     if (!(ok = stage_wait(a, sm, stage * n))) break;
+    trace_ev(a, 10 * l + 2);
     const int g = a.H / a.Hkv;
     for (int it = blockIdx.x; it < a.H * nch; it += gridDim.x) {  // (query row, chunk) items
       const int hq = it / nch, ch = it - hq * nch;
       attn_item(a, sm, l, hq / g, ch, hq % g, ctx, nch);
       consumer_sync();
     }
+    trace_ev(a, 10 * l + 3);
     stage_arrive(a);
     ++stage;
     // WO
     if (!(ok = stage_wait(a, sm, stage * n))) break;
     stage_plain(a, sm, a.attn_out, a.H * a.hd);
     consumer_sync();
+    trace_ev(a, 10 * l + 4);
     ok = consume_stage(a, sm, ST_WO, l, seq, pos);
+    trace_ev(a, 10 * l + 5);
     if (!ok || sm.abort_flag) break;
     // WGU (x from every rank's o partials of this layer)
     norm_weights(a, sm.ln_post[l], lw);
     stage_norm(a, sm, lw, false, token, a.hb + a.D, pwo, nwo, (sm.tagbase + l) & 1u, a.hb);
     consumer_sync();
+    trace_ev(a, 10 * l + 6);
     ok = consume_stage(a, sm, ST_WGU, l, seq, pos);
+    trace_ev(a, 10 * l + 7);
     stage_arrive(a);
     ++stage;
     if (!ok) break;
@@ -855,13 +873,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     if (!(ok = stage_wait(a, sm, stage * n))) break;
     stage_plain(a, sm, a.a, a.I);
     consumer_sync();
+    trace_ev(a, 10 * l + 8);
     ok = consume_stage(a, sm, ST_WDOWN, l, seq, pos) && !sm.abort_flag;
+    trace_ev(a, 10 * l + 9);
   }
   if (ok) {
     norm_weights(a, a.ln_f, lw);
     stage_norm(a, sm, lw, false, token, a.hb, pwd, nwd, (sm.tagbase + a.n_layers + 1) & 1u, nullptr);
     consumer_sync();
+    trace_ev(a, 10 * a.n_layers + 0);
     ok = !sm.abort_flag && consume_lm(a, sm, seq, epoch);
+    trace_ev(a, 10 * a.n_layers + 1);
   }
   if (!ok && threadIdx.x == 32) raise_abort(a, sm);
 }
@@ -1051,6 +1073,7 @@ int Model::mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_
   a.rowcnt = mk_rows;
   a.attn_out = mk_attn;
   a.sync = mk_sync;
+  a.trace = mk_trace_cap >= (size_t)mk_ctas * mk_trace_stride(a.n_layers) ? mk_trace : nullptr;
   cudaLaunchConfig_t cfgl = {};
   cfgl.gridDim = dim3(mk_ctas);
   cfgl.blockDim = dim3(MK_THREADS);

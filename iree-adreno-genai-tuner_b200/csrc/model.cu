@@ -324,6 +324,25 @@ extern "C" int q4b_model_decode_path(const q4b_model* model) {
   return m && m->mk_ready ? 1 : 0;
 }
 
+extern "C" size_t q4b_model_trace_events(const q4b_model* model) {
+  const Model* m = reinterpret_cast<const Model*>(model);
+  if (!m) return 0;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 0;
+  return (size_t)sms * mk_trace_stride((int)m->layers.size());
+}
+
+extern "C" int q4b_model_set_trace(q4b_model* model, unsigned long long* events, size_t n_events) {
+  Model* m = reinterpret_cast<Model*>(model);
+  if (!m) return set_error(Q4B_EINVAL, "model_set_trace: null model");
+  if (events && (n_events < q4b_model_trace_events(model) || reinterpret_cast<uintptr_t>(events) % 8))
+    return set_error(Q4B_EINVAL, "model_set_trace: %zu events, 8-byte aligned, needed", q4b_model_trace_events(model));
+  m->mk_trace = events;
+  m->mk_trace_cap = events ? n_events : 0;
+  return Q4B_OK;
+}
+
 extern "C" int q4b_device_status(int reset) {
   const unsigned v = linear_status(reset != 0) | gemm_status(reset != 0);
   return v ? Q4B_ETIMEOUT : Q4B_OK;

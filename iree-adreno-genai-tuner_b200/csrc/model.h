@@ -9,6 +9,9 @@ struct ncclComm;
 
 namespace q4b {
 
+// Stamps per CTA of the persistent decode step's phase trace (10 per layer, then 4).
+__host__ __device__ inline int mk_trace_stride(int n_layers) { return 10 * n_layers + 4; }
+
 struct Model {
   q4b_model_cfg cfg{};
   int H = 0, Hkv = 0, I = 0, V = 0, D = 0, hd = 0;  // per-rank (sharded) sizes
@@ -40,6 +43,8 @@ struct Model {
   std::vector<void*> mk_scale_pad;      // per projection: scale rows padded to 16 bytes (or null)
   int tp_map_peers(void* local, void** peers);
   int mk_ctas = 0;
+  unsigned long long* mk_trace = nullptr;  // caller's phase-trace buffer (q4b_model_set_trace) or null
+  size_t mk_trace_cap = 0;
   bool mk_ready = false;
   int mk_prepare();
   int mk_poison();

@@ -112,6 +112,8 @@ SIGNATURES = {
     "q4b_model_step": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "q4b_model_destroy": (None, [c_void_p]),
     "q4b_model_decode_path": (c_int, [c_void_p]),
+    "q4b_model_trace_events": (c_size_t, [c_void_p]),
+    "q4b_model_set_trace": (c_int, [c_void_p, c_void_p, c_size_t]),
     "q4b_model_fail_decode": (c_int, [c_void_p]),
     "q4b_device_status": (c_int, [c_int]),
     "q4b_tp_unique_id": (c_int, [c_void_p, c_int]),

@@ -281,6 +281,24 @@ class LlamaQ4(nn.Module):
                                             self.sin.data_ptr()), "model_set_head")
         return self._handle
 
+    def decode_trace(self, on: bool = True):
+        """Turn the persistent decode step's phase trace on (returns the int64 device buffer the
+        steps fill: [CTAs, 10 * n_layers + 4] %globaltimer stamps, layout of q4b_model_set_trace) or
+        off (returns None)."""
+        L = _lib.lib()
+        h = self.native()
+        if not on:
+            _lib.check(L.q4b_model_set_trace(h, None, 0), "model_set_trace")
+            self._trace = None
+            return None
+        with torch.cuda.device(self.device):
+            n = int(L.q4b_model_trace_events(h))
+        stride = 10 * self.n_layers + 4
+        buf = torch.zeros(n // stride, stride, dtype=torch.int64, device=self.device)
+        _lib.check(L.q4b_model_set_trace(h, buf.data_ptr(), n), "model_set_trace")
+        self._trace = buf  # held while the native model may write it
+        return buf
+
     def attach_tp(self, dist_mod=None):
         """Join this model's NCCL communicator (tp_size ranks, one process per GPU): rank 0 makes
         the id and torch.distributed broadcasts it. Collective: every rank calls it."""

@@ -55,3 +55,30 @@ def test_tp2_persistent_decode():
     assert out["diff_on_off"] <= 1e-3 * out["scale"]
     assert out["diff_single"] <= 1e-3 * out["scale"]
     assert out["graphs_on"] == out["graphs_off"]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_persistent_decode_3b_shape(world):
+    """Two layers of the 3B shape over 2, 4 and 8 GPUs (one KV head per rank at 8; padded scale rows
+    of the o / down shards): the persistent step gives the single-GPU tokens, logits within 1e-3."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = _run(world, Q4B_TP_MODE="persistent", Q4B_TP_CFG="3b2")
+    assert any("decode_step_kernel" in k for k in out["kernels"]), out["kernels"]
+    assert out["status"] == 0
+    assert out["tokens_on"] == out["tokens_off"] == out["tokens_single"]
+    assert out["diff_on_off"] <= 1e-3 * out["scale"]
+    assert out["diff_single"] <= 1e-3 * out["scale"]
+    assert out["graphs_on"] == out["graphs_off"]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_collectives(world):
+    """q4b_tp_allreduce_f32 / _f16 sum the ranks' buffers; q4b_tp_argmax_gather finds the global
+    first maximum of a vocabulary-split logits row."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = _run(world, Q4B_TP_MODE="collectives")
+    assert out["f32_err"] <= 1e-5 * world
+    assert out["f16_err"] <= 2e-2 * world
+    assert out["token"] == out["want_token"]

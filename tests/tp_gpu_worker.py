@@ -25,13 +25,24 @@ PCFG = dict(hidden_size=1024, num_hidden_layers=2, num_attention_heads=8, num_ke
             max_position_embeddings=4096, tie_word_embeddings=True, hidden_act="silu", attention_bias=False,
             initializer_range=0.2)
 PROMPT, STEPS = 40, 12
+# Q4B_TP_CFG=3b2: two layers of the Llama-3.2-3B shape (24 heads, 8 KV heads: one KV head per rank
+# at 8 ranks; o / down shard scale rows of 12, 6 and 3 groups at 2, 4 and 8 ranks)
+CFGS = {"small": PCFG}
+
+
+def _cfg():
+    name = os.environ.get("Q4B_TP_CFG", "small")
+    if name == "3b2":
+        import q4b
+        return dict(q4b.SYNTHETIC["3b"], num_hidden_layers=2)
+    return CFGS[name]
 
 
 def _persistent_decode(model, persistent, gather):
     """Prefill (per-projection path), then STEPS decode steps: (tokens, full-vocab logits per step)."""
     os.environ["Q4B_PERSISTENT"] = "1" if persistent else "0"
     caches = model.new_caches()
-    p = np.random.default_rng(7).integers(0, PCFG["vocab_size"], PROMPT).astype(np.int32)
+    p = np.random.default_rng(7).integers(0, model.vocab, PROMPT).astype(np.int32)
     dev = caches[0].device
     nxt, _ = model.step(torch.from_numpy(p).reshape(1, -1), torch.tensor([0]), torch.tensor([PROMPT - 1]), caches, 64)
     toks, logits = [int(nxt)], []
@@ -56,15 +67,16 @@ def persistent_main(rank, world, dev):
         dist.all_gather(parts, lg.contiguous())
         return torch.cat(parts, dim=1)
 
-    sd = q4b.SyntheticStateDict(PCFG, seed=5)
-    model = q4b.LlamaQ4(None, group=128, max_ctx=1024, vocab_chunk=PCFG["vocab_size"], sd=sd, cfg=PCFG,
+    cfg = _cfg()
+    sd = q4b.SyntheticStateDict(cfg, seed=5, device=dev)
+    model = q4b.LlamaQ4(None, group=128, max_ctx=1024, vocab_chunk=cfg["vocab_size"], sd=sd, cfg=cfg,
                         max_chunk=64, tp_rank=rank, tp_size=world, device=dev)
     model.attach_tp()
     t_on, l_on = _persistent_decode(model, True, gather)
     kernels = _one_step_kernels(model)
     t_off, l_off = _persistent_decode(model, False, gather)
     status = int(_lib.lib().q4b_device_status(1))
-    prompt = np.random.default_rng(7).integers(0, PCFG["vocab_size"], PROMPT).tolist()
+    prompt = np.random.default_rng(7).integers(0, cfg["vocab_size"], PROMPT).tolist()
     graphs = {}
     for on in (True, False):
         os.environ["Q4B_PERSISTENT"] = "1" if on else "0"
@@ -75,10 +87,48 @@ def persistent_main(rank, world, dev):
                diff_on_off=float(np.abs(l_on - l_off).max()), scale=float(max(1.0, np.abs(l_off).max())),
                status=status, kernels=sorted(kernels))
     if rank == 0:
-        single = q4b.LlamaQ4(None, group=128, max_ctx=1024, vocab_chunk=PCFG["vocab_size"], sd=sd, cfg=PCFG,
+        single = q4b.LlamaQ4(None, group=128, max_ctx=1024, vocab_chunk=cfg["vocab_size"], sd=sd, cfg=cfg,
                              max_chunk=64, device=dev)
         t1, l1 = _persistent_decode(single, True, lambda x: x)
         out.update(tokens_single=t1, diff_single=float(np.abs(l_on - l1).max()))
+    return out
+
+
+def collectives_main(rank, world, dev):
+    """The standalone collectives of the C ABI across the ranks: fp32 / fp16 all-reduce sums and the
+    vocabulary-split argmax gather (every rank holds shard r of one global logits row)."""
+    import ctypes
+
+    import q4b
+    from q4b import _lib
+    L = q4b.lib()
+    uid = (ctypes.c_ubyte * 128)()
+    if rank == 0:
+        _lib.check(L.q4b_tp_unique_id(uid, 128), "tp_unique_id")
+    obj = [bytes(uid)]
+    dist.broadcast_object_list(obj, src=0)
+    uid = (ctypes.c_ubyte * 128).from_buffer_copy(obj[0])
+    tp = ctypes.c_void_p()
+    _lib.check(L.q4b_tp_init(rank, world, uid, 128, ctypes.byref(tp)), "tp_init")
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    g = torch.Generator().manual_seed(11)
+    parts = [torch.randn(4096, generator=g) for _ in range(world)]
+    x = parts[rank].to(dev)
+    _lib.check(L.q4b_tp_allreduce_f32(tp, x.data_ptr(), 4096, st), "allreduce f32")
+    h = parts[rank].half().to(dev)
+    _lib.check(L.q4b_tp_allreduce_f16(tp, h.data_ptr(), 4096, st), "allreduce f16")
+    V = 16032 * world
+    logits = torch.randn(V, generator=g)
+    shard = logits[rank * 16032:(rank + 1) * 16032].contiguous().to(dev)
+    ws = torch.zeros(L.q4b_tp_argmax_workspace(tp) // 8, dtype=torch.int64, device=dev)
+    tok = torch.empty(1, dtype=torch.int32, device=dev)
+    _lib.check(L.q4b_tp_argmax_gather(tp, shard.data_ptr(), 16032, rank * 16032, tok.data_ptr(), ws.data_ptr(),
+                                      ws.numel() * 8, st), "argmax_gather")
+    torch.cuda.synchronize()
+    want = torch.stack(parts).sum(0)
+    out = dict(f32_err=float((x.cpu() - want).abs().max()), f16_err=float((h.float().cpu() - want).abs().max()),
+               token=int(tok), want_token=int(torch.argmax(logits)))
+    L.q4b_tp_destroy(tp)
     return out
 
 
@@ -99,8 +149,9 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    if os.environ.get("Q4B_TP_MODE") == "persistent":
-        out = persistent_main(rank, world, dev)
+    mode = os.environ.get("Q4B_TP_MODE")
+    if mode in ("persistent", "collectives"):
+        out = (persistent_main if mode == "persistent" else collectives_main)(rank, world, dev)
         torch.cuda.synchronize()
         dist.barrier()
         if rank == 0:
