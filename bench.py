@@ -769,29 +769,32 @@ TRACE_PHASES = ("qkv", "attn", "o", "gate_up", "down")
 
 def trace_summary(ev, n_layers):
     """Phase breakdown of one persistent decode step from its trace (q4b_model_set_trace layout),
-    in microseconds, averaged over the layers after the first: per phase `busy` = median over the
-    CTAs of (done - start), `lag` = median CTA start - the last CTA's end of the previous phase (the
-    synchronisation and x-staging latency), `span` = last end - first start."""
+    in microseconds, averaged over the layers after the first. Per stage: `wait` = median CTA's
+    inputs-ready stamp - the last CTA's end of the previous stage (barrier / partial-sum latency),
+    `stage` = median (x staged - inputs ready), `busy` = median (done - x staged), `span` = last end -
+    first inputs-ready."""
     import numpy as np
     ev = ev.astype(np.int64)
-    start = ev[:, 10 * n_layers + 2]
-    ev = ev[start > 0]
-    t0 = int(ev[:, 10 * n_layers + 2].min())
-    out = {p: {"busy": [], "lag": [], "span": []} for p in TRACE_PHASES}
+    L = 15 * n_layers
+    ev = ev[ev[:, L + 3] > 0]
+    t0 = int(ev[:, L + 3].min())
+    keys = ("wait", "stage", "busy", "span")
+    out = {p: {k: [] for k in keys} for p in TRACE_PHASES}
     for l in range(1, n_layers):
-        prev_end = ev[:, 10 * (l - 1) + 9].max()
+        prev_end = ev[:, 15 * (l - 1) + 14].max()
         for i, p in enumerate(TRACE_PHASES):
-            a, b = ev[:, 10 * l + 2 * i], ev[:, 10 * l + 2 * i + 1]
-            out[p]["busy"].append(float(np.median(b - a)))
-            out[p]["lag"].append(float(np.median(a) - prev_end))
-            out[p]["span"].append(float(b.max() - a.min()))
-            prev_end = b.max()
+            r, x, d = (ev[:, 15 * l + 3 * i + j] for j in range(3))
+            out[p]["wait"].append(float(np.median(r) - prev_end))
+            out[p]["stage"].append(float(np.median(x - r)))
+            out[p]["busy"].append(float(np.median(d - x)))
+            out[p]["span"].append(float(d.max() - r.min()))
+            prev_end = d.max()
     res = {p: {k: round(float(np.mean(v)) / 1e3, 3) for k, v in d.items()} for p, d in out.items()} if n_layers > 1 else {}
-    L = 10 * n_layers
-    res["lm_head"] = {"busy": round(float(np.median(ev[:, L + 1] - ev[:, L])) / 1e3, 3),
-                      "lag": round(float(np.median(ev[:, L]) - ev[:, L - 1].max()) / 1e3, 3)}
-    res["layer_us"] = round(float(ev[:, L - 1].max() - ev[:, 9].max()) / 1e3 / max(1, n_layers - 1), 3)
-    res["step_us"] = round(float(ev[:, L + 1].max() - t0) / 1e3, 3)
+    res["lm_head"] = {"wait": round(float(np.median(ev[:, L]) - ev[:, L - 1].max()) / 1e3, 3),
+                      "stage": round(float(np.median(ev[:, L + 1] - ev[:, L])) / 1e3, 3),
+                      "busy": round(float(np.median(ev[:, L + 2] - ev[:, L + 1])) / 1e3, 3)}
+    res["layer_us"] = round(float(ev[:, L - 1].max() - ev[:, 14].max()) / 1e3 / max(1, n_layers - 1), 3)
+    res["step_us"] = round(float(ev[:, L + 2].max() - t0) / 1e3, 3)
     res["ctas"] = int(ev.shape[0])
     return res
 

@@ -112,7 +112,10 @@ int q4b_q4_linear_kernel(int m, int n, int k, int group, int epilogue, int x_dty
  * anything, when the problem needs more than 8 MiB of workspace. The first call on a device looks
  * up the array and zeroes its counters (synchronously); make that first call before any stream
  * capture. All calls share the one array: calls that overlap on the GPU (other streams, other host
- * threads) race, so order them on one stream. Never allocates (no cudaMalloc / cudaFree). */
+ * threads) race, so order them on one stream. Never allocates (no cudaMalloc / cudaFree). The
+ * array's address and the kernels' shared-memory attributes are looked up / set once per device for
+ * the life of the process: the entry point does not survive cudaDeviceReset (or any other teardown of
+ * the device's primary context) within the same process. */
 int q4b_q4_linear_noalloc(const int32_t* qweight, const uint16_t* scales, int group, const void* x, int x_dtype,
                           void* y, int y_dtype, int m, int n, int k, int epilogue, q4b_stream_t stream);
 
@@ -238,10 +241,10 @@ int q4b_model_decode_path(const q4b_model* model);
 int q4b_model_fail_decode(q4b_model* model);
 /* Phase trace of the persistent decode step (no reference counterpart; a profiling aid): with a
  * device buffer of at least q4b_model_trace_events(model) uint64 set, every persistent step writes
- * %globaltimer stamps (ns) per CTA: CTA c's row starts at c * (10 * n_layers + 4); per layer l the
- * stamps 10 l + {0 q|k|v x staged, 1 q|k|v done, 2 attention start, 3 attention done, 4 o x staged,
- * 5 o done, 6 gate|up x staged, 7 gate|up done, 8 down x staged, 9 down done}, then 10 n_layers +
- * {0 lm_head x staged, 1 lm_head done, 2 consumers start}. NULL turns the trace off. */
+ * %globaltimer stamps (ns) per CTA: CTA c's row starts at c * (15 * n_layers + 4); per layer l and
+ * stage s (0 q|k|v, 1 attention, 2 o, 3 gate|up, 4 down) the stamps 15 l + 3 s + {0 inputs ready
+ * (barrier passed or partial sums loaded), 1 x staged, 2 done}, then 15 n_layers + {0 lm_head inputs
+ * ready, 1 staged, 2 done, 3 consumers start}. NULL turns the trace off. */
 size_t q4b_model_trace_events(const q4b_model* model);
 int q4b_model_set_trace(q4b_model* model, unsigned long long* events, size_t n_events);
 

@@ -20,11 +20,24 @@
 // gives up raises an abort flag that every other wait also checks, the step reports Q4B_ETIMEOUT
 // through the state, and the kernel returns.
 //
-// The arithmetic per 128-k group is that of q4_linear.cu's kernel 1 (exact fp16 (nib - 8) by LOP3,
-// m16n8k16 with fp32 accumulation, x as fp16 hi + lo, one fmaf with the group scale), so decode
-// results match the per-projection path up to fp32 summation order.
+// The arithmetic per 128-k group: q|k|v, o and down as q4_linear.cu's kernel 1 (exact fp16 (nib - 8)
+// by LOP3, m16n8k16 with fp32 accumulation, x as fp16 hi + lo, one fmaf with the group scale);
+// gate|up and the lm_head as the int8 form of the ring GEMV (kernel 6: biased nibbles as unsigned
+// bytes in m16n8k32 MMAs against x as three int8 terms per group, zero point exact). The int8 form
+// streams ~1.5x faster per slot but quantising x costs warp reductions on a stage transition's
+// critical path, which pays off only for the two projections with the most weight bytes per staged x.
+// Results match the per-projection path within the x-term residual (~6e-8 of a group's largest |x|)
+// and fp32 summation order.
+//
+// Ring slots hold 32 weight rows x 1024 k (two 16-row MMA tiles per warp and slot): one 32-row TMA
+// box streams at about twice the rate of a 16-row one, and two tiles per warp give the consumers
+// two independent MMA chains. q|k|v items stay 16 rows (RoPE row pairs; 320 tiles balance over the
+// SMs far better than 160).
 #include <cuda.h>
 
+#include <algorithm>
+#include <cstddef>
+#include <cstdlib>
 #include <mutex>
 
 #include "fused.h"
@@ -39,18 +52,20 @@ namespace {
 constexpr int MK_CW = 8;                       // consumer warps
 constexpr int MK_THREADS = (MK_CW + 1) * 32;   // + one producer warp (warp 0)
 constexpr int MK_UK = 1024;                    // k per weight unit
-constexpr int MK_WBYTES = 16 * MK_UK / 2;      // 16 rows x 512 B of int4
-constexpr int MK_SLOT = MK_WBYTES + 16 * 16;   // + 16 rows x 8 fp16 scales = 8448 B (66 x 128)
-constexpr int MK_NSLOT = 16;
+constexpr int MK_SROWS = 32;                   // weight rows per ring slot
+constexpr int MK_WBYTES = MK_SROWS * MK_UK / 2;  // 32 rows x 512 B of int4
+constexpr int MK_SLOT = MK_WBYTES + MK_SROWS * 16;  // + 32 rows x 8 fp16 scales = 16896 B (132 x 128)
+constexpr int MK_NSLOT = 10;                   // ring slots allocated at most (Q4B_MK_SLOTS)
+constexpr int kMkDefaultSlots = 6;
 constexpr int MK_MAXK = 8192;
-constexpr int MK_XROW = MK_MAXK / 8 + 4;       // staged x: uint4 per row (+64 B, as kernel 1)
+constexpr int MK_XROW = MK_MAXK / 8 + 4;       // staged x: uint4 per 8-k word (+64 B, as kernel 1)
 constexpr int MK_HD = 128;
 static_assert(MK_HD <= MK_CW * 32, "one query element per consumer thread");
 constexpr int MK_KCHUNK = 128;                 // keys per attention item (8 warps x 16)
 constexpr int MK_MAXCH = 128;                  // attention chunks (contexts up to 16384)
 constexpr int MK_ROWS = 4;                     // query rows per KV head (GQA group) at most
 constexpr int MK_TB = 8;                       // tiles of one stage per batched epilogue
-constexpr int MK_MAXKS = 3;                    // K splits of the o / down projections
+constexpr int MK_MAXKS = 4;                    // K splits of the o / down projections
 constexpr int MK_MAXTP = 8;
 constexpr int MK_MAXL = 128;                   // layers                    // tensor-parallel ranks
 constexpr int MK_MAXD = 4096;                  // hidden size: at most two staged words per thread
@@ -101,26 +116,51 @@ struct MkArgs {
   unsigned long long wait_ns;
   // phase trace (null = off): per CTA mk_trace_stride(n_layers) %globaltimer stamps, see trace_ev
   unsigned long long* trace;
+  // ring slots in use (<= MK_NSLOT): fewer slots bound how far the weight stream runs ahead of the
+  // consumers, and with it the traffic queued ahead of a stage transition's latency-bound loads
+  int nslot;
+  // how a norm learns that the o / down partial sums of every CTA (and rank) are complete:
+  // 0 = every thread polls its words' layer-parity tags; 1 = one thread per CTA waits on the
+  // row-split arrival counter (sync[7]) and the words are then loaded once
+  int split_sync;
 };
 
-// Trace events of a CTA: per layer l, 10 l + {0: q|k|v x staged, 1: q|k|v done, 2: attention start,
-// 3: attention done, 4: o x staged, 5: o done, 6: gate|up x staged, 7: gate|up done, 8: down x
-// staged, 9: down done}; then 10 L + {0: lm_head x staged, 1: lm_head done, 2: consumers start}.
+// Trace events of a CTA: per layer l and stage s (0 q|k|v, 1 attention, 2 o, 3 gate|up, 4 down),
+// 15 l + 3 s + {0: inputs ready (barrier passed / partial sums loaded), 1: x staged, 2: done}; then
+// 15 L + {0: lm_head inputs ready, 1: staged, 2: done, 3: consumers start}.
 __device__ __forceinline__ void trace_ev(const MkArgs& a, int e) {
-  if (a.trace && threadIdx.x == 32) a.trace[(size_t)blockIdx.x * mk_trace_stride(a.n_layers) + e] = globaltimer_ns();
+  if (a.trace && e >= 0 && threadIdx.x == 32)
+    a.trace[(size_t)blockIdx.x * mk_trace_stride(a.n_layers) + e] = globaltimer_ns();
 }
 
+// Attention scratch of one item; shares shared memory with the staged x, which is free between the
+// q|k|v projection (its last reads end before the stage arrival) and the o projection's staging.
+struct MkAttn {
+  float q[MK_HD];
+  float o[MK_CW][MK_HD];
+  float m[MK_CW], l[MK_CW], cs[MK_CW];
+};
+struct MkX {
+  uint4 hi[MK_XROW];  // word w of x as fp16 hi / lo pairs at xswz(w)
+  uint4 lo[MK_XROW];
+};
+// int8 form of a normed x (gate|up, lm_head: K = D): three terms as {even, odd} byte words per 8-k
+// word, rows 2 words (16 B = 4 banks) longer than D / 8 so the terms' rows fall on different banks
+constexpr int MK_QSTRIDE = MK_MAXD / 8 + 2;
+struct MkXq {
+  uint2 q[3 * MK_QSTRIDE];  // term m of word w at q[m * MK_QSTRIDE + w]
+  int4 g[MK_MAXD / 128];    // per 128-k group: {X_a, X_b, X_c, sx bits}
+};
+
 struct MkSmem {
-  uint8_t ring[MK_NSLOT][MK_SLOT];
-  uint4 xs_hi[MK_XROW];
-  uint4 xs_lo[MK_XROW];
-  float red[MK_TB][MK_CW][16];  // per-warp partial sums of up to MK_TB tiles of one stage
+  union {
+    MkX x;
+    MkXq xq;
+    MkAttn att;
+  } u;
+  float red[MK_TB][MK_CW][MK_SROWS];  // per-warp partial sums of up to MK_TB items of one stage
   float scratch[64];
   float rope_c[MK_HD], rope_s[MK_HD];  // RoPE rows of this step's position
-  float att_q[MK_ROWS][MK_HD];
-  float att_o[MK_CW][MK_ROWS][MK_HD];
-  float att_m[MK_CW][MK_ROWS], att_l[MK_CW][MK_ROWS];
-  float att_cs[MK_CW][MK_ROWS];
   unsigned long long best[MK_CW];
   // per layer: KV cache and norm weight pointers (read once at kernel start, not chased through
   // the layer table in global memory at every use)
@@ -133,7 +173,16 @@ struct MkSmem {
   unsigned tagbase;  // epoch * n_layers: partial sums of layer l carry parity (tagbase + l) & 1
   int last;
   int att_last;
+  // last: a launch allocates only the slots it uses (MkArgs::nslot), leaving the rest of the SM's
+  // 256 KB of L1 + shared memory to the L1 cache
+  alignas(1024) uint8_t ring[MK_NSLOT][MK_SLOT];
 };
+// dynamic shared memory of a launch with `nslot` ring slots (+1 KB for the 1024-byte alignment)
+static size_t mk_smem_bytes(int nslot) { return offsetof(MkSmem, ring) + (size_t)nslot * MK_SLOT + 1024; }
+
+// dynamic shared memory of the kernel (+1 KB for the 1024-byte alignment) within the 227 KB an SM
+// gives one CTA
+static_assert(sizeof(MkSmem) + 1024 <= 227 * 1024, "persistent decode: shared memory over 227 KB");
 
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
@@ -192,6 +241,21 @@ __device__ bool stage_wait(const MkArgs& a, MkSmem& sm, unsigned target) {
   consumer_sync();
   return !sm.abort_flag;
 }
+// Row-split completion (split_sync 1): this CTA's o / down partial sums, stored to every rank, happen
+// before one release add on every rank's counter sync[7] (never reset: targets grow by the step epoch).
+__device__ void split_arrive(const MkArgs& a) {
+  if (a.split_sync != 1) return;
+  consumer_sync();
+  if (threadIdx.x == 32) {
+    if (a.tp > 1) {
+      for (int r = 0; r < a.tp; ++r)
+        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(a.peer_sync[r] + 7) : "memory");
+    } else {
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync + 7) : "memory");
+    }
+  }
+}
+
 // Stage-end arrival: all consumer writes of this stage happen before the gpu-scope release.
 __device__ void stage_arrive(const MkArgs& a) {
   consumer_sync();
@@ -228,38 +292,41 @@ __device__ __forceinline__ float4 ld_fresh4(const float* p, bool sys) {
   return v;
 }
 
-// Projection of a stage: rows per tile pairing and geometry.
+// Projection of a stage: item geometry. An item is a run of rows (16 or 32) over a range of 1024-k
+// units; each unit of an item is one ring slot.
 struct ProjGeo {
-  int K, RT, NU;  // reduction dim, row tiles, 1024-k units per tile
-  bool paired;    // two runs of 8 rows per tile (SwiGLU gate/up, RoPE element halves)
-  int KS;         // K splits: work items are (row tile, unit range); partial sums go to psum
+  int K, RT, NU;  // reduction dim, row items, 1024-k units per item
+  bool paired;    // two runs of rows per item (SwiGLU gate | up, RoPE element halves)
+  int KS;         // K splits: work items are (row item, unit range); partial sums go to psum
+  int rows;       // weight rows per item: 16 (one MMA tile) or 32 (two)
 };
 __host__ __device__ __forceinline__ int k_splits(int nu) {
   for (int k = MK_MAXKS; k > 1; --k)
     if (nu % k == 0) return k;
   return 1;
 }
-// The o / down projections have D / 16 row tiles (192 for the 3B shape), too few to balance over
-// the SMs (one or two per CTA); splitting their K gives several smaller items per CTA. Their
-// partial sums are added to the residual stream in fixed order by the next stage's x staging.
+// The o / down projections have D / 32 row items (96 for the 3B shape), too few to balance over
+// the SMs; splitting their K gives several smaller items per CTA. Their partial sums are added to
+// the residual stream in fixed order by the next stage's x staging.
 __device__ __forceinline__ ProjGeo geo(const MkArgs& a, int st) {
   switch (st) {
-    case ST_QKV: return {a.D, (a.H + 2 * a.Hkv) * a.hd / 16, a.D / MK_UK, true, 1};
+    case ST_QKV: return {a.D, (a.H + 2 * a.Hkv) * a.hd / 16, a.D / MK_UK, true, 1, 16};
     case ST_WO: {
       const int nu = (a.H * a.hd + MK_UK - 1) / MK_UK;  // a TP shard may end inside a unit: zero-filled
-      return {a.H * a.hd, a.D / 16, nu, false, k_splits(nu)};
+      return {a.H * a.hd, a.D / 32, nu, false, k_splits(nu), 32};
     }
-    case ST_WGU: return {a.D, a.I / 8, a.D / MK_UK, true, 1};
+    case ST_WGU: return {a.D, a.I / 16, a.D / MK_UK, true, 1, 32};
     case ST_WDOWN: {
       const int nu = (a.I + MK_UK - 1) / MK_UK;
-      return {a.I, a.D / 16, nu, false, k_splits(nu)};
+      return {a.I, a.D / 32, nu, false, k_splits(nu), 32};
     }
-    default: return {a.D, a.V / 16, a.D / MK_UK, false, 1};  // lm_head
+    default: return {a.D, a.V / 32, a.D / MK_UK, false, 1, 32};  // lm_head
   }
 }
-// first weight row of run b (0 / 1) of a paired tile
+// first weight row of run b (0 / 1) of a paired item: gate | up rows [16 rt, 16 rt + 16) (slot rows
+// 0..15 / 16..31), or the RoPE halves e = 8 j .. 8 j + 7 and e + hd / 2 of a head (slot rows 0..7 / 8..15)
 __device__ __forceinline__ int pair_row(const MkArgs& a, int st, int rt, int b) {
-  if (st == ST_WGU) return (b ? a.I : 0) + rt * 8;
+  if (st == ST_WGU) return (b ? a.I : 0) + rt * 16;
   const int per = a.hd / 16, head = rt / per, j = rt - head * per;  // RoPE
   return head * a.hd + b * (a.hd / 2) + 8 * j;
 }
@@ -271,24 +338,25 @@ __device__ bool produce_stage(const MkArgs& a, MkSmem& sm, const MkProj& pj, int
   tma_prefetch_map(&pj.w);
   tma_prefetch_map(&pj.s);
   const int upi = gp.NU / gp.KS;  // units per item
+  const int half = gp.rows / 2;   // rows of one run of a paired item
   const uint64_t pol = l2_policy_evict_first();  // weights are read once per token
   for (int it = blockIdx.x; it < gp.RT * gp.KS; it += gridDim.x) {
     const int rt = it / gp.KS, ks = it - rt * gp.KS;
     for (int u = ks * upi; u < (ks + 1) * upi; ++u, ++seq) {
-      const int slot = seq % MK_NSLOT, round = seq / MK_NSLOT;
+      const int slot = seq % a.nslot, round = seq / a.nslot;
       if (round > 0 && !mbar_wait_bounded(&sm.empty[slot], (round - 1) & 1, a.wait_ns)) return false;
       if (sm.abort_flag) return false;
       uint8_t* dst = sm.ring[slot];
-      mbar_arrive_expect_tx(&sm.full[slot], MK_SLOT);
+      mbar_arrive_expect_tx(&sm.full[slot], gp.rows * (MK_UK / 2 + 16));
       if (gp.paired) {
         const int r0 = pair_row(a, st, rt, 0), r1 = pair_row(a, st, rt, 1);
         tma_load_2d_hint(dst, &pj.w, u * (MK_UK / 8), r0, &sm.full[slot], pol);
-        tma_load_2d_hint(dst + MK_WBYTES / 2, &pj.w, u * (MK_UK / 8), r1, &sm.full[slot], pol);
+        tma_load_2d_hint(dst + half * (MK_UK / 2), &pj.w, u * (MK_UK / 8), r1, &sm.full[slot], pol);
         tma_load_2d_hint(dst + MK_WBYTES, &pj.s, u * 4, r0, &sm.full[slot], pol);
-        tma_load_2d_hint(dst + MK_WBYTES + 128, &pj.s, u * 4, r1, &sm.full[slot], pol);
+        tma_load_2d_hint(dst + MK_WBYTES + half * 16, &pj.s, u * 4, r1, &sm.full[slot], pol);
       } else {
-        tma_load_2d_hint(dst, &pj.w, u * (MK_UK / 8), rt * 16, &sm.full[slot], pol);
-        tma_load_2d_hint(dst + MK_WBYTES, &pj.s, u * 4, rt * 16, &sm.full[slot], pol);
+        tma_load_2d_hint(dst, &pj.w, u * (MK_UK / 8), rt * gp.rows, &sm.full[slot], pol);
+        tma_load_2d_hint(dst + MK_WBYTES, &pj.s, u * 4, rt * gp.rows, &sm.full[slot], pol);
       }
     }
   }
@@ -311,20 +379,71 @@ __device__ bool producer_gate(const MkArgs& a, MkSmem& sm, unsigned target) {
 
 // ---- consumers: x staging --------------------------------------------------------------------
 
-// x[k] (fp32, k < K) -> hi / lo fp16 pairs in the permuted order of dequant_word
+// x[8 w .. 8 w + 7] (fp32) -> hi / lo fp16 pairs of word w in the permuted order of dequant_word
+// (x = hi + lo to ~22 bits; mma_tile_hl takes hi and lo as two columns of one MMA)
 __device__ __forceinline__ void stage_word(MkSmem& sm, int w, const float (&v)[8]) {
   uint4 hi, lo;
   split_pair(v[0], v[4], hi.x, lo.x);
   split_pair(v[1], v[5], hi.y, lo.y);
   split_pair(v[2], v[6], hi.z, lo.z);
   split_pair(v[3], v[7], hi.w, lo.w);
-  sm.xs_hi[xswz(w)] = hi;
-  sm.xs_lo[xswz(w)] = lo;
+  sm.u.x.hi[xswz(w)] = hi;
+  sm.u.x.lo[xswz(w)] = lo;
 }
 
-// The residual stream before a norm: the first layer's h is the embedding row of the token
+// Rounding to the nearest integer (ties to even) by adding 1.5 * 2^23: for |u| < 2^22 the sum's low
+// mantissa bits hold round(u) in two's complement, so its low byte is the int8 byte of round(u) and
+// (sum bits - 0x4B400000) is round(u) as an int; sum - 1.5 * 2^23 is round(u) as a float.
+constexpr float kRoundMagic = 12582912.0f;
+constexpr uint32_t kRoundBits = 0x4B400000u;
+
+// x[8 w .. 8 w + 7] (fp32) -> word w of the int8 form (MkXq): x ~= sx (a + b / 254 + c / 254^2) per
+// 128-k group with sx = max |x| / 127, the form of q4dev.cuh's mma_tile_i8. A group is 16 words held
+// by the 16 lanes of a half warp (the whole warp calls this together), whose shuffles give the
+// group's max |x| and term sums X. Byte i of the even word is k = 8 w + 2 i, of the odd word
+// k = 8 w + 2 i + 1 (the nibble order of the weights' byte masks).
+__device__ __forceinline__ void stage_word_i8(MkSmem& sm, int w, const float (&v)[8]) {
+  float am = 0.0f;
+#pragma unroll
+  for (int b = 0; b < 8; ++b) am = fmaxf(am, fabsf(v[b]));
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+  const float sx = am > 0.0f ? am / 127.0f : 1.0f;
+  const float inv = am > 0.0f ? 127.0f / am : 1.0f;
+  uint32_t f[3][8];              // bit patterns of round(.) + magic: low byte = the int8 term
+  uint32_t pab = 0u, pc = 0u;    // this word's term sums: a + 65536 b (fields recovered below), c
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float u = fminf(fmaxf(v[i] * inv, -127.0f), 127.0f);
+    const float ra = __fadd_rn(u, kRoundMagic);
+    const float r = (u - __fsub_rn(ra, kRoundMagic)) * 254.0f;
+    const float rb = __fadd_rn(r, kRoundMagic);
+    const float rc = __fadd_rn((r - __fsub_rn(rb, kRoundMagic)) * 254.0f, kRoundMagic);
+    f[0][i] = __float_as_uint(ra), f[1][i] = __float_as_uint(rb), f[2][i] = __float_as_uint(rc);
+    pab += (f[0][i] - kRoundBits) + (f[1][i] - kRoundBits) * 65536u;  // mod 2^32
+    pc += f[2][i] - kRoundBits;
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) {
+    pab += __shfl_xor_sync(0xffffffffu, pab, o);
+    pc += __shfl_xor_sync(0xffffffffu, pc, o);
+  }
+  // |group sums| <= 128 * 127 < 2^15: the low field of the packed a | b sum is exact as int16
+  const int Xa = (int)(short)(pab & 0xFFFFu);
+  const int Xb = ((int)pab - Xa) >> 16;
+#pragma unroll
+  for (int m = 0; m < 3; ++m) {
+    const uint32_t ev = __byte_perm(__byte_perm(f[m][0], f[m][2], 0x0040), __byte_perm(f[m][4], f[m][6], 0x0040), 0x5410);
+    const uint32_t od = __byte_perm(__byte_perm(f[m][1], f[m][3], 0x0040), __byte_perm(f[m][5], f[m][7], 0x0040), 0x5410);
+    sm.u.xq.q[m * MK_QSTRIDE + w] = make_uint2(ev, od);
+  }
+  if ((threadIdx.x & 15) == 0) sm.u.xq.g[w >> 4] = make_int4(Xa, Xb, (int)pc, __float_as_int(sx));
+}
+
+// The residual stream before a norm at word w: the first layer's h is the embedding row of the token
 // (QEmbedding.lookup, llama_q4.py:106-119); later it is h + the K-split partial sums of the o / down
-// projection (added in split order).
+// projection of every rank (added in rank, then split order). Returns whether every partial carries
+// the expected layer-parity tag.
 __device__ __forceinline__ bool norm_src(const MkArgs& a, int w, bool embed, int token, const float* hsrc,
                                          const float* psrc, int nparts, unsigned tag, float (&v)[8]) {
   if (embed) {
@@ -384,14 +503,35 @@ __device__ __forceinline__ void norm_weights(const MkArgs& a, const float* lnw, 
 
 // x = rmsnorm(h + partials) * w (rms_norm, llama_q4.py:141-142). With hdst the updated residual
 // stream is also written (each word by one CTA) to the other ping-pong buffer. Each thread reloads
-// its words until their partial sums carry the expected tag (bounded; a timeout aborts the step).
+// its words until their partial sums carry the expected tag (bounded; a timeout aborts the step), or
+// with split_sync 1 loads them once after the row-split counter reached split_target.
 __device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float (&lw)[2][8], bool embed, int token,
-                           const float* hsrc, const float* psrc, int nparts, unsigned tag, float* hdst) {
+                           const float* hsrc, const float* psrc, int nparts, unsigned tag, float* hdst,
+                           unsigned split_target, int ev_ready, bool i8) {
   const int ct = threadIdx.x - 32;
   const int words = a.D / 8;
   float v[2][8];
   float ss = 0.0f;
   uint64_t t0 = 0;
+  const bool counted = a.split_sync == 1 && !embed;
+  if (counted) {  // every CTA of every rank has stored its partial sums: then one round of loads
+    if (threadIdx.x == 32) {
+      t0 = globaltimer_ns();
+      for (;;) {
+        unsigned c;
+        if (a.tp > 1)
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(c) : "l"(a.sync + 7) : "memory");
+        else
+          asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(c) : "l"(a.sync + 7) : "memory");
+        if ((int)(c - split_target) >= 0) break;
+        if (globaltimer_ns() - t0 > a.wait_ns || *(volatile unsigned*)&a.sync[1]) {
+          raise_abort(a, sm);
+          break;
+        }
+      }
+    }
+    consumer_sync();
+  }
   for (int tries = 0;; ++tries) {
     bool fresh = true;
 #pragma unroll
@@ -399,13 +539,14 @@ __device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float (&lw)[2][8],
       const int w = ct + i * (MK_CW * 32);
       if (w < words) fresh = norm_src(a, w, embed, token, hsrc, psrc, nparts, tag, v[i]) && fresh;
     }
-    if (fresh) break;
+    if (fresh || counted) break;
     if (tries == 0) t0 = globaltimer_ns();
     if (globaltimer_ns() - t0 > a.wait_ns || *(volatile unsigned*)&a.sync[1]) {
       raise_abort(a, sm);
       break;
     }
   }
+  trace_ev(a, ev_ready);
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     const int w = ct + i * (MK_CW * 32);
@@ -428,27 +569,46 @@ __device__ void stage_norm(const MkArgs& a, MkSmem& sm, const float (&lw)[2][8],
       float x[8];
 #pragma unroll
       for (int b = 0; b < 8; ++b) x[b] = v[i][b] * rs * lw[i][b];
-      stage_word(sm, w, x);
+      if (i8)  // (w < words is uniform over each warp: D / 8 is a multiple of 32)
+        stage_word_i8(sm, w, x);
+      else
+        stage_word(sm, w, x);
     }
   }
 }
 
-// x = a (the SwiGLU output), plain
+// x = src[0, K) plain (the attention output, the SwiGLU output), zeros up to the next 1024-k unit (a
+// tensor-parallel shard may end inside one; its weights and scales there are zero-filled).
 __device__ void stage_plain(const MkArgs& a, MkSmem& sm, const float* src, int K) {
+  constexpr int kPer = MK_MAXK / 8 / (MK_CW * 32);  // words per thread at most
   const int ct = threadIdx.x - 32;
-  for (int w = ct; w < K / 8; w += MK_CW * 32) {
-    const float4 p0 = __ldcg(reinterpret_cast<const float4*>(src + 8 * w));
-    const float4 p1 = __ldcg(reinterpret_cast<const float4*>(src + 8 * w) + 1);
-    const float v[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-    stage_word(sm, w, v);
+  const int words = K / 8, padded = (K + MK_UK - 1) / MK_UK * (MK_UK / 8);
+  float4 p[kPer][2];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {  // one round: every load before any conversion
+    const int w = ct + i * (MK_CW * 32);
+    p[i][0] = p[i][1] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (w < words) {
+      p[i][0] = __ldcg(reinterpret_cast<const float4*>(src + 8 * w));
+      p[i][1] = __ldcg(reinterpret_cast<const float4*>(src + 8 * w) + 1);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int w = ct + i * (MK_CW * 32);
+    if (w < padded) {
+      const float v[8] = {p[i][0].x, p[i][0].y, p[i][0].z, p[i][0].w, p[i][1].x, p[i][1].y, p[i][1].z, p[i][1].w};
+      stage_word(sm, w, v);
+    }
   }
 }
 
 
 // ---- consumers: projections ------------------------------------------------------------------
 
-// Epilogue of slot pair (s, s + 8) of a 16-row tile: v0 / v1 are their dot products.
-__device__ void pair_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, int rt, int ks, int s, float v0,
+// Epilogue of output s of an item. q|k|v (16 rows): v0 / v1 = rows s / s + 8 (RoPE halves e, e + hd/2);
+// gate|up (32 rows): v0 / v1 = rows s / s + 16 (gate, up); o / down: v0 = row s of the item's 32.
+__device__ void item_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, int rt, int ks, int s, float v0,
                               float v1, int pos) {
   if (st == ST_QKV) {
     const int per = a.hd / 16, head = rt / per, jj = rt - head * per;
@@ -471,117 +631,128 @@ __device__ void pair_epilogue(const MkArgs& a, MkSmem& sm, int st, int layer, in
       vc[e2] = __float2half_rn(v1);
     }
   } else if (st == ST_WGU) {
-    a.a[rt * 8 + s] = silu(v0) * v1;
+    a.a[rt * 16 + s] = silu(v0) * v1;
   } else {  // WO / WDOWN: this rank's K-split partial sums, pushed to every rank (added to h there by
             // the next norm's staging, in rank and split order)
-    const size_t off = ((size_t)(st == ST_WDOWN) * a.tp * MK_MAXKS + (size_t)a.rank * MK_MAXKS + ks) * a.D + rt * 16;
-    const unsigned tag = (sm.tagbase + (unsigned)layer) & 1u;
-    for (int r = 0; r < a.tp; ++r) {
-      float* p = a.peer_psum[r] + off;
-      p[s] = tag_value(v0, tag);
-      p[s + 8] = tag_value(v1, tag);
-    }
+    const size_t off = ((size_t)(st == ST_WDOWN) * a.tp * MK_MAXKS + (size_t)a.rank * MK_MAXKS + ks) * a.D + rt * 32;
+    const float tv = tag_value(v0, (sm.tagbase + (unsigned)layer) & 1u);
+    for (int r = 0; r < a.tp; ++r) a.peer_psum[r][off + s] = tv;
   }
 }
 
 // K split across the consumer warps: warp w takes the 128-k group w of every 1024-k unit of an item
-// (a row tile and a range of its units). The per-warp sums of up to MK_TB items are reduced and
-// finished together (one barrier pair per batch).
-__device__ bool consume_stage(const MkArgs& a, MkSmem& sm, int st, int layer, unsigned& seq, int pos) {
-  const ProjGeo gp = geo(a, st);
+// (a run of 16 or 32 rows and a range of its units); per slot it loads its share of the NT 16-row
+// tiles into registers, releases the slot and runs NT independent MMA chains. The per-warp sums of
+// up to MK_TB items are reduced and finished together (one barrier pair per batch); `fin(j, it, s, v0,
+// v1)` finishes output s of the batch's item j (item index it).
+template <int NT, bool I8, typename Fin>
+__device__ bool consume_items(const MkArgs& a, MkSmem& sm, const ProjGeo& gp, unsigned& seq, Fin fin) {
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
   const int g = lane >> 2, t = lane & 3;
   const int upi = gp.NU / gp.KS;
   const int nitems = gp.RT * gp.KS;
   const int nmine = nitems > (int)blockIdx.x ? (nitems - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  // outputs per item and the row distance of a paired output's second value
+  const int nout = gp.paired ? gp.rows / 2 : gp.rows, pair = gp.rows / 2;
+  unsigned slot = seq % a.nslot, round = seq / a.nslot;  // advanced with seq (no division per slot)
   for (int b0 = 0; b0 < nmine; b0 += MK_TB) {
     const int nb = min(MK_TB, nmine - b0);
     for (int j = 0; j < nb; ++j) {
       const int it = blockIdx.x + (b0 + j) * gridDim.x;
       const int ks = it % gp.KS;
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      float acc[NT][4];
+#pragma unroll
+      for (int jj = 0; jj < NT; ++jj) acc[jj][0] = acc[jj][1] = acc[jj][2] = acc[jj][3] = 0.0f;
       for (int u = ks * upi; u < (ks + 1) * upi; ++u, ++seq) {
-        const int slot = seq % MK_NSLOT;
-        if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, a.wait_ns)) {
+        if (!mbar_wait_bounded(&sm.full[slot], round & 1, a.wait_ns)) {
           sm.abort_flag = 1;
           return false;
         }
         const uint8_t* sl = sm.ring[slot];
-        const uint4 wa = *reinterpret_cast<const uint4*>(sl + g * 512 + w * 64 + t * 16);
-        const uint4 wb = *reinterpret_cast<const uint4*>(sl + (g + 8) * 512 + w * 64 + t * 16);
         const __half* sc = reinterpret_cast<const __half*>(sl + MK_WBYTES);
-        const float sa = __half2float(sc[g * 8 + w]), sb = __half2float(sc[(g + 8) * 8 + w]);
+        uint4 wa[NT], wb[NT];
+        float sa[NT], sb[NT];
+#pragma unroll
+        for (int jj = 0; jj < NT; ++jj) {
+          wa[jj] = *reinterpret_cast<const uint4*>(sl + (16 * jj + g) * 512 + w * 64 + t * 16);
+          wb[jj] = *reinterpret_cast<const uint4*>(sl + (16 * jj + g + 8) * 512 + w * 64 + t * 16);
+          sa[jj] = __half2float(sc[(16 * jj + g) * 8 + w]);
+          sb[jj] = __half2float(sc[(16 * jj + g + 8) * 8 + w]);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive_cnt(&sm.empty[slot], 1);
-        mma_tile_hl(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, g, u * 128 + w * 16 + 4 * t, acc);
+        if constexpr (I8) {
+          const int ktile = u * 8 + w;  // 128-k group = scale group
+          uint2 xv[4];
+          if (g < 3) {
+            const uint4* src = reinterpret_cast<const uint4*>(sm.u.xq.q + g * MK_QSTRIDE + ktile * 16 + 4 * t);
+            const uint4 lo = src[0], hi = src[1];
+            xv[0] = make_uint2(lo.x, lo.y), xv[1] = make_uint2(lo.z, lo.w);
+            xv[2] = make_uint2(hi.x, hi.y), xv[3] = make_uint2(hi.z, hi.w);
+          } else {
+            xv[0] = xv[1] = xv[2] = xv[3] = make_uint2(0u, 0u);
+          }
+          const int4 xg = sm.u.xq.g[ktile];
+#pragma unroll
+          for (int jj = 0; jj < NT; ++jj) {
+            float hl[2] = {0.0f, 0.0f};
+            mma_tile_i8(wa[jj], wb[jj], sa[jj], sb[jj], xv, xg, hl);
+            acc[jj][0] += hl[0];  // rows g / g + 8 (lanes t == 0); columns 1 / 3 stay zero
+            acc[jj][2] += hl[1];
+          }
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < NT; ++jj)
+            mma_tile_hl(wa[jj], wb[jj], sa[jj], sb[jj], sm.u.x.hi, sm.u.x.lo, g, u * 128 + w * 16 + 4 * t, acc[jj]);
+        }
+        if (++slot == (unsigned)a.nslot) slot = 0, ++round;
       }
-      if (t == 0) {  // columns 0 / 1: the x_hi / x_lo products of rows g and g + 8
-        sm.red[j][w][g] = acc[0] + acc[1];
-        sm.red[j][w][g + 8] = acc[2] + acc[3];
+      if (t == 0) {  // columns 0 / 1: the x_hi / x_lo products of rows g and g + 8 of each tile
+#pragma unroll
+        for (int jj = 0; jj < NT; ++jj) {
+          sm.red[j][w][16 * jj + g] = acc[jj][0] + acc[jj][1];
+          sm.red[j][w][16 * jj + g + 8] = acc[jj][2] + acc[jj][3];
+        }
       }
     }
     consumer_sync();
-    for (int i = ct; i < nb * 8; i += MK_CW * 32) {
-      const int j = i >> 3, sl = i & 7;
+    for (int i = ct; i < nb * nout; i += MK_CW * 32) {
+      const int j = i / nout, sl = i - j * nout;
       float v0 = 0.0f, v1 = 0.0f;
 #pragma unroll
       for (int k = 0; k < MK_CW; ++k) {
         v0 += sm.red[j][k][sl];
-        v1 += sm.red[j][k][sl + 8];
+        if (gp.paired) v1 += sm.red[j][k][sl + pair];
       }
-      const int it = blockIdx.x + (b0 + j) * gridDim.x;
-      pair_epilogue(a, sm, st, layer, it / gp.KS, it % gp.KS, sl, v0, v1, pos);
+      fin(j, blockIdx.x + (b0 + j) * gridDim.x, sl, v0, v1);
     }
     consumer_sync();
   }
   return true;
 }
 
-// lm_head: the same split of K over the warps as consume_stage, each batch of tiles finished with
-// logits (optional) and greedy argmax keys; the CTA's best key goes to the step state, the last CTA
-// publishes the token (first maximum on ties, like torch.argmax).
+__device__ bool consume_stage(const MkArgs& a, MkSmem& sm, int st, int layer, unsigned& seq, int pos) {
+  const ProjGeo gp = geo(a, st);
+  const auto fin = [&](int, int it, int s, float v0, float v1) {
+    item_epilogue(a, sm, st, layer, it / gp.KS, it % gp.KS, s, v0, v1, pos);
+  };
+  // gate|up reads the int8 form of its normed x; the other projections fp16 hi / lo
+  if (st == ST_WGU) return consume_items<2, true>(a, sm, gp, seq, fin);
+  return gp.rows == 16 ? consume_items<1, false>(a, sm, gp, seq, fin) : consume_items<2, false>(a, sm, gp, seq, fin);
+}
+
+// lm_head: 32-row items finished with logits (optional) and greedy argmax keys; the CTA's best key
+// goes to the step state, the last CTA publishes the token (first maximum on ties, like torch.argmax).
 __device__ bool consume_lm(const MkArgs& a, MkSmem& sm, unsigned& seq, unsigned epoch) {
   const ProjGeo gp = geo(a, ST_PER_LAYER);
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
-  const int g = lane >> 2, t = lane & 3;
   unsigned long long best = 0ull;
-  const int ntile = gp.RT > (int)blockIdx.x ? (gp.RT - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-  for (int b0 = 0; b0 < ntile; b0 += MK_TB) {
-    const int nb = min(MK_TB, ntile - b0);
-    for (int j = 0; j < nb; ++j) {
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (int u = 0; u < gp.NU; ++u, ++seq) {
-        const int slot = seq % MK_NSLOT;
-        if (!mbar_wait_bounded(&sm.full[slot], (seq / MK_NSLOT) & 1, a.wait_ns)) {
-          sm.abort_flag = 1;
-          return false;
-        }
-        const uint8_t* sl = sm.ring[slot];
-        const uint4 wa = *reinterpret_cast<const uint4*>(sl + g * 512 + w * 64 + t * 16);
-        const uint4 wb = *reinterpret_cast<const uint4*>(sl + (g + 8) * 512 + w * 64 + t * 16);
-        const __half* sc = reinterpret_cast<const __half*>(sl + MK_WBYTES);
-        const float sa = __half2float(sc[g * 8 + w]), sb = __half2float(sc[(g + 8) * 8 + w]);
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cnt(&sm.empty[slot], 1);
-        mma_tile_hl(wa, wb, sa, sb, sm.xs_hi, sm.xs_lo, g, u * 128 + w * 16 + 4 * t, acc);
-      }
-      if (t == 0) {  // columns 0 / 1: the x_hi / x_lo products of rows g and g + 8
-        sm.red[j][w][g] = acc[0] + acc[1];
-        sm.red[j][w][g + 8] = acc[2] + acc[3];
-      }
-    }
-    consumer_sync();
-    for (int i = ct; i < nb * 16; i += MK_CW * 32) {
-      const int j = i >> 4, sl = i & 15;
-      float v = 0.0f;
-#pragma unroll
-      for (int k = 0; k < MK_CW; ++k) v += sm.red[j][k][sl];
-      const int row = (blockIdx.x + (b0 + j) * gridDim.x) * 16 + sl;
-      if (a.logits) a.logits[row] = v;
-      best = max(best, argmax_key(v, (unsigned)(a.rank * a.V + row)));
-    }
-    consumer_sync();
-  }
+  const auto fin = [&](int, int it, int s, float v, float) {
+    const int row = it * 32 + s;
+    if (a.logits) a.logits[row] = v;
+    best = max(best, argmax_key(v, (unsigned)(a.rank * a.V + row)));
+  };
+  if (!consume_items<2, true>(a, sm, gp, seq, fin)) return false;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
   if (lane == 0) sm.best[w] = best;
@@ -652,13 +823,13 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
   uint4 kr[HD / 16];
 #pragma unroll
   for (int i = 0; i < HD / 16; ++i) kr[i] = __ldcg(kp + 2 * i + hh);
-  if (ct < HD) sm.att_q[0][ct] = qv;
+  if (ct < HD) sm.u.att.q[ct] = qv;
   consumer_sync();
   float d0 = 0.0f, d1 = 0.0f;
 #pragma unroll
   for (int i = 0; i < HD / 16; ++i) {
     const __half2* h2 = reinterpret_cast<const __half2*>(&kr[i]);
-    const float* qp = &sm.att_q[0][8 * (2 * i + hh)];
+    const float* qp = &sm.u.att.q[8 * (2 * i + hh)];
 #pragma unroll
     for (int tt = 0; tt < 4; ++tt) {
       const float2 f = __half22float2(h2[tt]);
@@ -687,21 +858,21 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
     }
   }
   if (lane == 0) {
-    sm.att_m[w][0] = m;
-    sm.att_l[w][0] = lw;
+    sm.u.att.m[w] = m;
+    sm.u.att.l[w] = lw;
   }
-  *reinterpret_cast<float4*>(&sm.att_o[w][0][lane * EPL]) = make_float4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<float4*>(&sm.u.att.o[w][lane * EPL]) = make_float4(o[0], o[1], o[2], o[3]);
   consumer_sync();
   // merge the warps into this chunk's partial for row r
   float* part = a.part + (((size_t)kvh * MK_MAXCH + ch) * MK_ROWS + r) * (HD + MK_PAD);
   if (ct == 0) {
     float M = -INFINITY;
-    for (int i = 0; i < MK_CW; ++i) M = fmaxf(M, sm.att_m[i][0]);
+    for (int i = 0; i < MK_CW; ++i) M = fmaxf(M, sm.u.att.m[i]);
     float l = 0.0f;
     for (int i = 0; i < MK_CW; ++i) {
-      const float cs = sm.att_m[i][0] == -INFINITY ? 0.0f : expf(sm.att_m[i][0] - M);
-      sm.att_cs[i][0] = cs;
-      l += sm.att_l[i][0] * cs;
+      const float cs = sm.u.att.m[i] == -INFINITY ? 0.0f : expf(sm.u.att.m[i] - M);
+      sm.u.att.cs[i] = cs;
+      l += sm.u.att.l[i] * cs;
     }
     part[0] = M;
     part[1] = l;
@@ -709,7 +880,7 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
   consumer_sync();
   for (int e = ct; e < HD; e += MK_CW * 32) {
     float v = 0.0f;
-    for (int k = 0; k < MK_CW; ++k) v += sm.att_o[k][0][e] * sm.att_cs[k][0];
+    for (int k = 0; k < MK_CW; ++k) v += sm.u.att.o[k][e] * sm.u.att.cs[k];
     part[MK_PAD + e] = v;
   }
   // the CTA that completes a query row's chunks merges them (max, sum, weighted V, online over the
@@ -757,6 +928,8 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
   if (ct == 0) a.rowcnt[hq] = 0u;  // the next layer's items start after the next stage barrier
 }
 
+// One CTA of 9 warps per SM: a sub-partition holds 3 of the warps (16,384 registers each), so a
+// thread gets at most 168 registers.
 __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   MkSmem& sm = *reinterpret_cast<MkSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -815,11 +988,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     }
     if (blockIdx.x == 0)  // row counters of the attention merge (left non-zero only by an aborted launch)
       for (int i = ct; i < a.H; i += MK_CW * 32) a.rowcnt[i] = 0u;
-    // x past a shard's K meets zero-filled weights and scales: keep it finite
-    for (int e = ct; e < MK_XROW; e += MK_CW * 32) sm.xs_hi[e] = sm.xs_lo[e] = make_uint4(0, 0, 0, 0);
     consumer_sync();
   }
-  trace_ev(a, 10 * a.n_layers + 2);
+  trace_ev(a, 15 * a.n_layers + 3);
   unsigned seq = 0;
   unsigned stage = 0;
   const unsigned n = gridDim.x;
@@ -828,62 +999,74 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
   const float* pwd = a.psum + (size_t)a.tp * MK_MAXKS * a.D;      // down partials of every rank
   bool ok = !sm.abort_flag;  // a poisoned model (an earlier step timed out) does no work
   float lw[2][8];  // the next norm's weights
+  // row-split arrival counter: this step's c-th completion (layer c / 2; o for odd c, down for even
+  // c > 0) is reached at split0 + c * per
+  const unsigned per = n * (unsigned)a.tp;
+  const unsigned split0 = epoch * 2u * (unsigned)a.n_layers * per;
   for (int l = 0; l < a.n_layers && ok; ++l) {
     // QKV (x from the previous layer's down partials of every rank, tagged with that layer's parity)
     norm_weights(a, sm.ln_in[l], lw);
-    stage_norm(a, sm, lw, l == 0, token, a.hb, pwd, nwd, (sm.tagbase + l + 1) & 1u, a.hb + a.D);
+    stage_norm(a, sm, lw, l == 0, token, a.hb, pwd, nwd, (sm.tagbase + l + 1) & 1u, a.hb + a.D,
+               split0 + 2u * (unsigned)l * per, 15 * l + 0, false);
     consumer_sync();
-    trace_ev(a, 10 * l + 0);
+    trace_ev(a, 15 * l + 1);
     ok = consume_stage(a, sm, ST_QKV, l, seq, pos);
-    trace_ev(a, 10 * l + 1);
+    trace_ev(a, 15 * l + 2);
     stage_arrive(a);
     ++stage;
     if (!ok) break;
     // attention
     if (!(ok = stage_wait(a, sm, stage * n))) break;
-    trace_ev(a, 10 * l + 2);
+    trace_ev(a, 15 * l + 3);
+    trace_ev(a, 15 * l + 4);
     const int g = a.H / a.Hkv;
     for (int it = blockIdx.x; it < a.H * nch; it += gridDim.x) {  // (query row, chunk) items
       const int hq = it / nch, ch = it - hq * nch;
       attn_item(a, sm, l, hq / g, ch, hq % g, ctx, nch);
       consumer_sync();
     }
-    trace_ev(a, 10 * l + 3);
+    trace_ev(a, 15 * l + 5);
     stage_arrive(a);
     ++stage;
     // WO
     if (!(ok = stage_wait(a, sm, stage * n))) break;
+    trace_ev(a, 15 * l + 6);
     stage_plain(a, sm, a.attn_out, a.H * a.hd);
     consumer_sync();
-    trace_ev(a, 10 * l + 4);
+    trace_ev(a, 15 * l + 7);
     ok = consume_stage(a, sm, ST_WO, l, seq, pos);
-    trace_ev(a, 10 * l + 5);
+    trace_ev(a, 15 * l + 8);
     if (!ok || sm.abort_flag) break;
+    split_arrive(a);
     // WGU (x from every rank's o partials of this layer)
     norm_weights(a, sm.ln_post[l], lw);
-    stage_norm(a, sm, lw, false, token, a.hb + a.D, pwo, nwo, (sm.tagbase + l) & 1u, a.hb);
+    stage_norm(a, sm, lw, false, token, a.hb + a.D, pwo, nwo, (sm.tagbase + l) & 1u, a.hb,
+               split0 + (2u * (unsigned)l + 1u) * per, 15 * l + 9, true);
     consumer_sync();
-    trace_ev(a, 10 * l + 6);
+    trace_ev(a, 15 * l + 10);
     ok = consume_stage(a, sm, ST_WGU, l, seq, pos);
-    trace_ev(a, 10 * l + 7);
+    trace_ev(a, 15 * l + 11);
     stage_arrive(a);
     ++stage;
     if (!ok) break;
     // WDOWN
     if (!(ok = stage_wait(a, sm, stage * n))) break;
+    trace_ev(a, 15 * l + 12);
     stage_plain(a, sm, a.a, a.I);
     consumer_sync();
-    trace_ev(a, 10 * l + 8);
+    trace_ev(a, 15 * l + 13);
     ok = consume_stage(a, sm, ST_WDOWN, l, seq, pos) && !sm.abort_flag;
-    trace_ev(a, 10 * l + 9);
+    trace_ev(a, 15 * l + 14);
+    if (ok) split_arrive(a);
   }
   if (ok) {
     norm_weights(a, a.ln_f, lw);
-    stage_norm(a, sm, lw, false, token, a.hb, pwd, nwd, (sm.tagbase + a.n_layers + 1) & 1u, nullptr);
+    stage_norm(a, sm, lw, false, token, a.hb, pwd, nwd, (sm.tagbase + a.n_layers + 1) & 1u, nullptr,
+               split0 + 2u * (unsigned)a.n_layers * per, 15 * a.n_layers + 0, true);
     consumer_sync();
-    trace_ev(a, 10 * a.n_layers + 0);
+    trace_ev(a, 15 * a.n_layers + 1);
     ok = !sm.abort_flag && consume_lm(a, sm, seq, epoch);
-    trace_ev(a, 10 * a.n_layers + 1);
+    trace_ev(a, 15 * a.n_layers + 2);
   }
   if (!ok && threadIdx.x == 32) raise_abort(a, sm);
 }
@@ -897,7 +1080,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
 static bool mk_shapes_ok(const Model& m) {
   return m.cfg.tp_size <= MK_MAXTP && (int)m.layers.size() <= MK_MAXL && (m.cfg.tp_size == 1 || m.comm) && m.hd == MK_HD && m.H % m.Hkv == 0 &&
          m.H / m.Hkv <= MK_ROWS && m.H <= 32 && m.D <= MK_MAXD && m.D % MK_UK == 0 && (m.H * m.hd) % 128 == 0 &&
-         m.I % 128 == 0 && m.I <= MK_MAXK && m.H * m.hd <= MK_MAXK && m.V % 16 == 0 &&
+         m.I % 128 == 0 && m.I <= MK_MAXK && m.H * m.hd <= MK_MAXK && m.V % 32 == 0 &&
          m.cfg.max_ctx <= MK_MAXCH * MK_KCHUNK;
 }
 
@@ -925,30 +1108,31 @@ int Model::mk_prepare() {
   // is 8 groups = 4 pairs = 16 bytes). A tensor map's row stride is a multiple of 16 bytes, so a
   // shard whose scale rows are not (a tensor-parallel o / down shard: k/G = 12 or 6 or 3) is read
   // from a copy with rows padded by zero scales to a multiple of 8 groups.
-  auto mk = [&](size_t i, const q4b_qmat& w, bool paired) {
+  // box rows: one run of a paired item (8 for the RoPE halves, 16 for gate | up) or a whole 32-row item
+  auto mk = [&](size_t i, const q4b_qmat& w, int box_rows) {
     MkProj& p = proj[i];
-    int r = make_tmap_i32(&p.w, w.qweight, w.k / 8, w.n, w.k / 8, MK_UK / 8, paired ? 8 : 16);
+    int r = make_tmap_i32(&p.w, w.qweight, w.k / 8, w.n, w.k / 8, MK_UK / 8, box_rows);
     if (r) return r;
     const int groups = w.k / w.group;
-    if (groups % 8 == 0) return make_tmap_i32(&p.s, w.scales, groups / 2, w.n, groups / 2, 4, paired ? 8 : 16);
+    if (groups % 8 == 0) return make_tmap_i32(&p.s, w.scales, groups / 2, w.n, groups / 2, 4, box_rows);
     const int padded = (groups + 7) / 8 * 8;
     if (!mk_scale_pad[i] && (r = alloc(&mk_scale_pad[i], sizeof(__half) * (size_t)w.n * padded, true))) return r;
     cudaError_t e = cudaMemcpy2D(mk_scale_pad[i], sizeof(__half) * padded, w.scales, sizeof(__half) * groups,
                                  sizeof(__half) * groups, w.n, cudaMemcpyDeviceToDevice);
     if (e != cudaSuccess) return set_error(Q4B_ECUDA, "persistent decode: scale copy: %s", cudaGetErrorString(e));
-    return make_tmap_i32(&p.s, mk_scale_pad[i], (groups + 1) / 2, w.n, padded / 2, 4, paired ? 8 : 16);
+    return make_tmap_i32(&p.s, mk_scale_pad[i], (groups + 1) / 2, w.n, padded / 2, 4, box_rows);
   };
   for (size_t l = 0; l < layers.size(); ++l) {
-    if ((rc = mk(4 * l + 0, layers[l].wqkv, true))) return rc;
-    if ((rc = mk(4 * l + 1, layers[l].wo, false))) return rc;
-    if ((rc = mk(4 * l + 2, layers[l].wgu, true))) return rc;
-    if ((rc = mk(4 * l + 3, layers[l].wdown, false))) return rc;
+    if ((rc = mk(4 * l + 0, layers[l].wqkv, 8))) return rc;
+    if ((rc = mk(4 * l + 1, layers[l].wo, 32))) return rc;
+    if ((rc = mk(4 * l + 2, layers[l].wgu, 16))) return rc;
+    if ((rc = mk(4 * l + 3, layers[l].wdown, 32))) return rc;
   }
   q4b_qmat head = embed;  // this rank's vocab rows of the tied table
   head.qweight = embed.qweight + (size_t)cfg.tp_rank * V * (D / 8);
   head.scales = embed.scales + (size_t)cfg.tp_rank * V * (D / embed.group);
   head.n = V;
-  if ((rc = mk(4 * layers.size(), head, false))) return rc;
+  if ((rc = mk(4 * layers.size(), head, 32))) return rc;
   if (!mk_proj && (rc = alloc(&mk_proj, sizeof(MkProj) * proj.size(), false))) return rc;
   if (!mk_layers && (rc = alloc(&mk_layers, sizeof(q4b_layer_weights) * layers.size(), false))) return rc;
   if (!mk_part && (rc = alloc((void**)&mk_part, sizeof(float) * Hkv * MK_MAXCH * MK_ROWS * (hd + MK_PAD), true))) return rc;
@@ -967,10 +1151,9 @@ int Model::mk_prepare() {
     unsigned w[8];
     if (cudaMemcpy(w, mk_sync, sizeof(w), cudaMemcpyDeviceToHost) != cudaSuccess)
       return set_error(Q4B_ECUDA, "persistent decode: state read");
-    if (w[6]) {
-      const int p0 = (int)((w[5] * (unsigned)layers.size()) & 1u);
-      if (cudaMemset(mk_h + 2 * D, p0 ? 0x00 : 0x01, psum_bytes) != cudaSuccess ||
-          cudaMemset(mk_sync + 6, 0, sizeof(unsigned)) != cudaSuccess)
+    if (w[6]) {  // back to the state of a new model: epoch 0, tags of parity 1, no row-split arrivals
+      if (cudaMemset(mk_h + 2 * D, 0x01, psum_bytes) != cudaSuccess ||
+          cudaMemset(mk_sync + 5, 0, 3 * sizeof(unsigned)) != cudaSuccess)
         return set_error(Q4B_ECUDA, "persistent decode: reset");
     }
   }
@@ -995,12 +1178,19 @@ int Model::mk_prepare() {
   int dev = 0, sms = 0, per = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const size_t smem = sizeof(MkSmem) + 1024;
+  // 6 of the 10 slots by default: a deeper ring keeps more weight traffic queued ahead of each stage
+  // transition's latency-bound loads (measured: 40.4 us per 3B layer with 6 slots, 42.2 with 10)
+  mk_nslot = kMkDefaultSlots;
+  if (const char* v = std::getenv("Q4B_MK_SLOTS")) mk_nslot = std::max(2, std::min(MK_NSLOT, std::atoi(v)));
+  const size_t smem = mk_smem_bytes(mk_nslot);
   e = cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, decode_step_kernel, MK_THREADS, smem);
   if (e != cudaSuccess || per < 1)
     return set_error(Q4B_EUNSUPPORTED, "persistent decode: kernel does not fit an SM (%s)", cudaGetErrorString(e));
   mk_ctas = sms;
+  // ring depth (above) and row-split synchronisation: tuning knobs Q4B_MK_SLOTS, Q4B_MK_SPLIT_SYNC
+  mk_split_sync = 0;
+  if (const char* e = std::getenv("Q4B_MK_SPLIT_SYNC")) mk_split_sync = std::atoi(e) == 1 ? 1 : 0;
   mk_ready = true;
   return Q4B_OK;
 }
@@ -1074,10 +1264,12 @@ int Model::mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_
   a.attn_out = mk_attn;
   a.sync = mk_sync;
   a.trace = mk_trace_cap >= (size_t)mk_ctas * mk_trace_stride(a.n_layers) ? mk_trace : nullptr;
+  a.nslot = mk_nslot;
+  a.split_sync = mk_split_sync;
   cudaLaunchConfig_t cfgl = {};
   cfgl.gridDim = dim3(mk_ctas);
   cfgl.blockDim = dim3(MK_THREADS);
-  cfgl.dynamicSmemBytes = sizeof(MkSmem) + 1024;
+  cfgl.dynamicSmemBytes = mk_smem_bytes(mk_nslot);
   cfgl.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;

@@ -9,8 +9,8 @@ struct ncclComm;
 
 namespace q4b {
 
-// Stamps per CTA of the persistent decode step's phase trace (10 per layer, then 4).
-__host__ __device__ inline int mk_trace_stride(int n_layers) { return 10 * n_layers + 4; }
+// Stamps per CTA of the persistent decode step's phase trace (15 per layer, then 4).
+__host__ __device__ inline int mk_trace_stride(int n_layers) { return 15 * n_layers + 4; }
 
 struct Model {
   q4b_model_cfg cfg{};
@@ -43,6 +43,8 @@ struct Model {
   std::vector<void*> mk_scale_pad;      // per projection: scale rows padded to 16 bytes (or null)
   int tp_map_peers(void* local, void** peers);
   int mk_ctas = 0;
+  int mk_nslot = 0;        // ring slots the persistent step uses
+  int mk_split_sync = 0;   // 0: tag-polled partial sums, 1: row-split arrival counter
   unsigned long long* mk_trace = nullptr;  // caller's phase-trace buffer (q4b_model_set_trace) or null
   size_t mk_trace_cap = 0;
   bool mk_ready = false;

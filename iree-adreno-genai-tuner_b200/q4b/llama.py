@@ -283,7 +283,7 @@ class LlamaQ4(nn.Module):
 
     def decode_trace(self, on: bool = True):
         """Turn the persistent decode step's phase trace on (returns the int64 device buffer the
-        steps fill: [CTAs, 10 * n_layers + 4] %globaltimer stamps, layout of q4b_model_set_trace) or
+        steps fill: [CTAs, 15 * n_layers + 4] %globaltimer stamps, layout of q4b_model_set_trace) or
         off (returns None)."""
         L = _lib.lib()
         h = self.native()
@@ -293,7 +293,7 @@ class LlamaQ4(nn.Module):
             return None
         with torch.cuda.device(self.device):
             n = int(L.q4b_model_trace_events(h))
-        stride = 10 * self.n_layers + 4
+        stride = 15 * self.n_layers + 4
         buf = torch.zeros(n // stride, stride, dtype=torch.int64, device=self.device)
         _lib.check(L.q4b_model_set_trace(h, buf.data_ptr(), n), "model_set_trace")
         self._trace = buf  # held while the native model may write it
