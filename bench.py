@@ -725,6 +725,141 @@ def run_sweep(args, rank, world, local, dist_mod):
             "rows": rows, "gpu_launches": sum(r["weight_copies"] for r in rows) * args.steps}
 
 
+def shard_measure(dev, n, k, m, split, rank, world, dist_mod, comm, steps, warmup, seed=99):
+    """Seconds per sharded q4_linear call on this rank (the max over ranks is taken by the caller):
+    col = this rank's n/t output rows; row = its k/t slice, then an NCCL all-reduce (sum) of the fp32
+    partial y. Every rank holds distinct weight copies of its shard (together > 2x L2), all calls of
+    one pass captured in one CUDA graph (the all-reduces too). Returns (seconds, copies, max relative
+    error of one assembled y against the unsharded call on this GPU)."""
+    import math
+
+    import torch
+
+    import q4b
+    from q4b import ops
+    from q4b.shard import shard_q4, shard_x
+    wbytes = (n * k // 2 + 2 * n * (k // 128)) // world
+    copies = max(1, math.ceil(2 * L2_BYTES / wbytes))
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)  # the same full weights on every rank; each keeps its shard
+    x = torch.randn(m, k, device=dev, generator=g).half()
+    xr = shard_x(x, rank, world, split)
+    qws, scs = [], []
+    err = None
+    for c in range(copies):
+        qw = torch.randint(-2**31, 2**31 - 1, (n, k // 8), dtype=torch.int32, device=dev, generator=g)
+        sc = (torch.randn(n, k // 128, device=dev, generator=g) * 0.02).abs().half()
+        a, b = shard_q4(qw, sc, 128, rank, world, split)
+        qws.append(a)
+        scs.append(b)
+        if c == 0:  # parity of the assembled result against the unsharded call
+            full = ops.q4_linear(x.float(), qw, sc, 128).float()
+            part = ops.q4_linear(xr.float(), a, b, 128).float()
+            if split == "col":
+                parts = [torch.empty_like(part) for _ in range(world)]
+                dist_mod.all_gather(parts, part)
+                got = torch.cat(parts, 1)
+            else:
+                dist_mod.all_reduce(part)
+                got = part
+            err = float((got - full).abs().max() / full.abs().max().clamp_min(1e-30))
+        del qw, sc
+    ys = [torch.empty(m, qws[0].shape[0], dtype=torch.float16 if split == "col" else torch.float32, device=dev)
+          for _ in range(copies)]
+    stream = torch.cuda.Stream(device=dev)
+    comm = comm if split == "row" else None  # the library's NCCL communicator (capturable)
+
+    def one_pass():
+        for i in range(copies):
+            ops.q4_linear(xr, qws[i], scs[i], 128, out=ys[i])
+            if comm:
+                comm.allreduce(ys[i])
+
+    with torch.cuda.stream(stream):
+        one_pass()  # workspace and communicator set up outside the capture
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        graph.capture_begin()
+        one_pass()
+        graph.capture_end()
+        for _ in range(warmup):
+            graph.replay()
+    stream.synchronize()
+    dist_mod.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    dist_mod.barrier()
+    if q4b.lib().q4b_device_status(1) != 0:
+        raise RuntimeError("q4b: a bounded device wait gave up during the measurement")
+    per_call = e0.elapsed_time(e1) / 1e3 / (steps * copies)
+    del graph  # graphs holding NCCL calls go before the communicator and the process group
+    torch.cuda.synchronize()
+    return per_call, copies, err
+
+
+def run_shard(args, rank, world, local, dist_mod):
+    """Row e3: the config-5 projections sharded over the N GPUs, column split (no collective) and row
+    split (NCCL all-reduce of y), timed per call as the max over ranks; value = every rank's weight
+    bytes / that time (aggregate GB/s)."""
+    import torch
+
+    from q4b.shard import shard_ok
+    from q4b.tp import TpComm
+    if world < 2:
+        raise SystemExit("--workload shard needs torchrun with 2 or more ranks")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pk = peaks()
+    rows, tot_b, tot_s = [], 0, 0.0
+    shapes = args.shapes or list(SWEEP_SHAPES)
+    comm = TpComm(rank, world, dist_mod) if "row" in args.splits else None
+    for name in shapes:
+        n, k = SWEEP_SHAPES[name]
+        for m in args.m:
+            for split in args.splits:
+                if not shard_ok(n, k, 128, world, split):
+                    continue
+                per_call, copies, err = shard_measure(dev, n, k, m, split, rank, world, dist_mod, comm,
+                                                      args.steps, args.warmup)
+                t = torch.tensor([per_call, err], dtype=torch.float64, device=dev)
+                dist_mod.all_reduce(t, op=dist_mod.ReduceOp.MAX)
+                per_call, err = float(t[0]), float(t[1])
+                b = linear_bytes(n, k, m)
+                gbs = b / per_call / 1e9
+                rows.append({"shape": name, "N": n, "K": k, "M": m, "split": split, "bytes": b,
+                             "us_per_call": round(per_call * 1e6, 3), "GB_s": round(gbs, 1),
+                             "frac_of_world_hbm": round(gbs / (world * pk["hbm_gbs"]), 4), "weight_copies": copies,
+                             "max_rel_err_vs_unsharded": err})
+                tot_b += b
+                tot_s += per_call
+                torch.cuda.empty_cache()
+    if comm:
+        comm.close()
+    if rank != 0:
+        return None
+    worst = max(r["max_rel_err_vs_unsharded"] for r in rows)
+    return {"metric": "sharded int4 projection sweep GB/s (3B shapes x M, column / row split)",
+            "value": round(tot_b / tot_s / 1e9, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int4 weights, fp16 x, fp32 accumulate", "data": "synthetic",
+            "config": {"workload": "BASELINE config 5 sharded over GPUs (row e3)", "splits": args.splits,
+                       "parallelism": f"tp{world}", "l2": "each rank: distinct shard copies > 2x L2",
+                       "collective": "row split: NCCL all-reduce (sum) of fp32 y [M, N], inside the timed call"},
+            "roofline": {"bound": "hbm", "peak": round(world * pk["hbm_gbs"], 1), "unit": "GB/s",
+                         "peak_source": pk["source"] + f" x {world} GPUs",
+                         "achieved": round(tot_b / tot_s / 1e9, 1),
+                         "frac": round(tot_b / tot_s / 1e9 / (world * pk["hbm_gbs"]), 4), "traffic": None},
+            "parity": {"max_rel_err_vs_unsharded": worst, "bar": 1e-3, "ok": worst <= 1e-3},
+            "rows": rows, "gpu_launches": sum(r["weight_copies"] for r in rows) * args.steps}
+
+
 def run_profile(args, rank, world, local, dist_mod):
     """A short fixed launch sequence for profilers: a 3B-shaped model with --layers layers, an optional
     --prefill C chunk at position 0, then --steps single-token decode steps at position --pos."""
@@ -831,7 +966,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="decode: tokens (255); gemv: graph replays (200)")
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "sweep", "profile", "ctx", "gemm"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "sweep", "shard", "profile", "ctx", "gemm"])
+    ap.add_argument("--splits", nargs="*", default=["col", "row"], help="shard: column and / or row split")
     ap.add_argument("--ctx", type=int, nargs="*", default=[256, 512, 1024, 2048, 4096], help="ctx: context lengths")
     ap.add_argument("--new", type=int, default=64, help="ctx: generated tokens per run")
     ap.add_argument("--prompts", type=int, default=3, help="ctx: prompts per context length")
@@ -853,7 +989,8 @@ def main():
     if args.warmup < 3 and args.workload != "profile":
         args.warmup = 3
     if args.steps is None:
-        args.steps = {"decode": 255, "gemv": 200, "sweep": 20, "profile": 3, "ctx": 0, "gemm": 20}[args.workload]
+        args.steps = {"decode": 255, "gemv": 200, "sweep": 20, "shard": 20, "profile": 3, "ctx": 0,
+                      "gemm": 20}[args.workload]
     rank, world, local = dist_env()
     if args.impl == "reference":
         line = run_reference(args, rank, world)
@@ -862,8 +999,8 @@ def main():
         return
     dist_mod = init_dist(world, local)
     try:
-        run = {"decode": run_decode, "gemv": run_gemv, "sweep": run_sweep, "profile": run_profile,
-               "ctx": run_ctx, "gemm": run_gemm}[args.workload]
+        run = {"decode": run_decode, "gemv": run_gemv, "sweep": run_sweep, "shard": run_shard,
+               "profile": run_profile, "ctx": run_ctx, "gemm": run_gemm}[args.workload]
         line = run(args, rank, world, local, dist_mod)
     finally:
         if dist_mod:
