@@ -139,6 +139,10 @@ long long q4b_gemm_f16_workspace(int m, int n, int k, char la, char lb, const q4
  * [m][k], 'T' = stored [k][m]; lb 'N' = B stored [k][n], 'T' = stored [n][k]. C is row-major [m][n].
  * The tcgen05 kernel needs 16-byte aligned A / B and row pitches (k or m for A, n or k for B) that
  * are multiples of 8; the default falls back to kernel 2 otherwise. */
+/* The schedule q4b_gemm_f16 runs for this problem and cfg (NULL = the default: for the config-2
+ * shapes the schedule a search on a B200 measured fastest, q4b/gemm/tuned_b200.json; otherwise the
+ * built-in plan), written to *out (kernel 1 or 2, bn, stages, split). No reference counterpart. */
+int q4b_gemm_f16_plan(int m, int n, int k, char la, char lb, const q4b_gemm_cfg* cfg, q4b_gemm_cfg* out);
 int q4b_gemm_f16(const void* a, const void* b, void* c, int m, int n, int k, char la, char lb,
                  const q4b_gemm_cfg* cfg, void* workspace, size_t workspace_bytes, q4b_stream_t stream);
 

@@ -285,6 +285,24 @@ bool tma_ok(int M, int N, int K, char la, char lb) {
   return lda % 8 == 0 && ldb % 8 == 0;
 }
 
+// The schedules the search (q4b.gemm.search on a B200, q4b/gemm/tuned_b200.json) measured fastest for
+// the config-2 problems: the default plan of exactly these shapes and layouts.
+struct TunedSchedule {
+  int M, N, K;
+  char la, lb;
+  int bn, stages, split;
+};
+constexpr TunedSchedule kTuned[] = {
+    {128, 5120, 3072, 'N', 'N', 64, 3, 3},  // B1 qkv_m128: 184 TFLOP/s
+    {128, 3072, 3072, 'N', 'N', 64, 2, 3},  // B2 o_m128: 146 TFLOP/s
+    {128, 16384, 3072, 'N', 'N', 128, 5, 1},  // B3 gate_up_m128: 529 TFLOP/s
+    {128, 3072, 8192, 'N', 'N', 64, 5, 3},  // B4 down_m128: 230 TFLOP/s
+    {2048, 5120, 3072, 'N', 'N', 256, 2, 1},  // B5 qkv_m2048: 881 TFLOP/s
+    {2048, 3072, 3072, 'N', 'N', 256, 2, 1},  // B6 o_m2048: 943 TFLOP/s
+    {2048, 16384, 3072, 'N', 'N', 256, 2, 1},  // B7 gate_up_m2048: 1009 TFLOP/s
+    {2048, 3072, 8192, 'N', 'N', 256, 2, 1},  // B8 down_m2048: 922 TFLOP/s
+};
+
 int plan_gemm(int M, int N, int K, char la, char lb, const q4b_gemm_cfg* cfg, GemmPlan& pl) {
   if (M <= 0 || N <= 0 || K <= 0) return set_error(Q4B_EINVAL, "gemm_f16: sizes must be positive");
   if ((la != 'N' && la != 'T') || (lb != 'N' && lb != 'T'))
@@ -304,6 +322,14 @@ int plan_gemm(int M, int N, int K, char la, char lb, const q4b_gemm_cfg* cfg, Ge
   pl.kernel = 1;
   const int kt = (K + kBK - 1) / kBK;
   const int tm = (M + kBM - 1) / kBM;
+  q4b_gemm_cfg tuned = {};
+  if (!cfg || (!cfg->kernel && !cfg->bn && !cfg->stages && !cfg->split)) {
+    for (const TunedSchedule& t : kTuned)
+      if (t.M == M && t.N == N && t.K == K && t.la == la && t.lb == lb) {
+        tuned = {1, t.bn, t.stages, t.split};
+        cfg = &tuned;
+      }
+  }
   int bn = cfg && cfg->bn ? cfg->bn : 0;
   if (bn && bn != 64 && bn != 128 && bn != 256) return set_error(Q4B_EINVAL, "gemm_f16: bn is 64, 128 or 256");
   if (!bn) {
@@ -321,7 +347,10 @@ int plan_gemm(int M, int N, int K, char la, char lb, const q4b_gemm_cfg* cfg, Ge
   }
   const int stage = (kBM + bn) * kBK * 2;
   const int max_stages = kGemmSmemBudget / stage;
-  int stages = cfg && cfg->stages ? cfg->stages : max_stages;
+  // 256-wide tiles over many row tiles: 2 stages (96 KB) leave room for two CTAs per SM, one's
+  // epilogue beside the other's main loop (the search's fastest schedule for every M = 2048 shape)
+  const int def_stages = (bn == 256 && tm >= 8 && max_stages >= 2) ? 2 : max_stages;
+  int stages = cfg && cfg->stages ? cfg->stages : def_stages;
   if (stages < 2 || stages > max_stages)
     return set_error(Q4B_EINVAL, "gemm_f16: stages must be in [2, %d] for bn %d", max_stages, bn);
   const long long tiles = (long long)tm * tn;
@@ -422,6 +451,15 @@ extern "C" long long q4b_gemm_f16_workspace(int M, int N, int K, char la, char l
   GemmPlan pl;
   if (plan_gemm(M, N, K, la, lb, cfg, pl)) return -1;
   return (long long)pl.ws;
+}
+
+extern "C" int q4b_gemm_f16_plan(int M, int N, int K, char la, char lb, const q4b_gemm_cfg* cfg, q4b_gemm_cfg* out) {
+  if (!out) return set_error(Q4B_EINVAL, "gemm_f16_plan: null output");
+  GemmPlan pl;
+  const int rc = plan_gemm(M, N, K, la, lb, cfg, pl);
+  if (rc) return rc;
+  *out = {pl.kernel, pl.kernel == 1 ? pl.bn : 0, pl.kernel == 1 ? pl.stages : 0, pl.split};
+  return Q4B_OK;
 }
 
 extern "C" int q4b_gemm_f16(const void* A, const void* B, void* C, int M, int N, int K, char la, char lb,

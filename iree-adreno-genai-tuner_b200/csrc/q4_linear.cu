@@ -1079,14 +1079,19 @@ __global__ void __launch_bounds__(256) q4_linear_simt(LinArgs p) {
 //
 // One CTA per (128 x rows, BN weight rows = BN/16 row tiles, k split). A pre-pass writes x as two
 // fp16 matrices hi / lo (x = hi + lo, ~22 bits) in the nibble-permuted k order of dequant_word;
-// the TMA engine streams their 128 x 64 tiles into a 128-byte-swizzled ring. Raw int4 rows arrive
+// the TMA engine streams their 128 x 64 tiles into a 128-byte-swizzled ring, hi and lo of a stage
+// back to back. Raw int4 rows arrive
 // by bulk copies (32 bytes per row and 64-k stage, rows picked by tile_row, so SwiGLU and RoPE
 // tiles keep their row pairs); four dequant warps turn them into exact fp16 (nib - 8) tiles in the
-// same swizzled K-major layout. One thread issues tcgen05.mma (M=128, N=BN, K=16; hi and lo into
-// one TMEM accumulator) per stage, alternating between two TMEM accumulators by scale group;
-// eight epilogue warps read each finished group from TMEM, scale it by the group's fp16 scales
-// and add it to fp32 registers -- the same arithmetic as kernels 1 and 3 (per-group fp32 sum of
-// exact products, then one fmaf with the scale). Split-K partials go through the workspace as in
+// same swizzled K-major layout. One thread issues tcgen05.mma per stage, alternating between two TMEM
+// accumulators by scale group. BN = 128: the weights are the A operand (M = 128 weight rows) and the
+// stage's hi and lo x tiles together the B operand (N = 256: tokens' hi then lo), so a 64-k stage is
+// 4 MMAs of N = 256 (measured: 8 MMAs of N = 128 issue at about half the tensor core's rate); the
+// accumulator's TMEM lane is a weight row, its columns the tokens' hi and lo partial sums. BN = 64:
+// x is A (M = 128 tokens), the weights B (N = 64), hi and lo into one accumulator. Eight epilogue
+// warps read each finished group from TMEM, scale it by the group's fp16 scale and add it to fp32
+// registers -- the same arithmetic as kernels 1 and 3 (per-group fp32 sum of exact products, then
+// one fmaf with the scale). Split-K partials go through the workspace as in
 // the other kernels; the shared epilogue_tile then handles store / accumulate / SwiGLU / RoPE+KV.
 constexpr int K5_BM = 128, K5_BK = 64;
 constexpr int K5_RAW = 8, K5_XS = 3, K5_DS = 3;
@@ -1221,7 +1226,11 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
     s_raw_n = s_x_n = s_mma_n = 0;
     fence_mbar_init();
   }
-  if (warp == 13) tmem_alloc(&s_tmem, 2 * BN);
+  // BN = 128: weights as A, x hi | lo as B (see above); BN = 64: x as A
+  constexpr bool SWAP = BN == 128;
+  constexpr int XN = XF32 ? 2 * K5_BM : K5_BM;  // B rows when swapped: tokens' hi, then lo
+  constexpr int ACOLS = SWAP ? XN : BN;         // TMEM columns of one group accumulator
+  if (warp == 13) tmem_alloc(&s_tmem, 2 * ACOLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -1306,7 +1315,7 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
     }
   } else if (warp == 13) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(K5_BM, BN, false, false);
+      constexpr uint32_t idesc = SWAP ? idesc_f16_f32(BN, XN, false, false) : idesc_f16_f32(K5_BM, BN, false, false);
       for (int i = 0; i < NS; ++i) {
         const int xs = i % K5_XS, ds = i % K5_DS;
         const int gl = i / SPG, kg = i - gl * SPG, b = gl & 1;
@@ -1321,12 +1330,16 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
         tc_fence_after();
         const uint32_t xa = smem_u32(smem + L::X_OFF + xs * L::XSTAGE);
         const uint32_t wb = smem_u32(smem + L::W_OFF + ds * L::W_BYTES);
-        const uint32_t d = tmem + b * BN;
+        const uint32_t d = tmem + b * ACOLS;
 #pragma unroll
         for (int kk = 0; kk < K5_BK / 16; ++kk) {
-          const uint64_t bd = sw128_desc(wb + kk * 32, 16, 1024);
-          tc_mma_f16(d, sw128_desc(xa + kk * 32, 16, 1024), bd, idesc, (kg | kk) != 0);
-          if constexpr (XF32) tc_mma_f16(d, sw128_desc(xa + L::X_BYTES + kk * 32, 16, 1024), bd, idesc, 1u);
+          const uint64_t wd = sw128_desc(wb + kk * 32, 16, 1024);
+          if constexpr (SWAP) {  // B spans the hi tile and the lo tile right after it (rows 128..255)
+            tc_mma_f16(d, wd, sw128_desc(xa + kk * 32, 16, 1024), idesc, (kg | kk) != 0);
+          } else {
+            tc_mma_f16(d, sw128_desc(xa + kk * 32, 16, 1024), wd, idesc, (kg | kk) != 0);
+            if constexpr (XF32) tc_mma_f16(d, sw128_desc(xa + L::X_BYTES + kk * 32, 16, 1024), wd, idesc, 1u);
+          }
         }
         tc_commit(&x_empty[xs]);
         tc_commit(&deq_empty[ds]);
@@ -1337,8 +1350,10 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
     __syncwarp();
   }
 
-  // epilogue warps: scale each finished group and accumulate in registers
-  constexpr int HC = BN / 2;  // columns per epilogue thread
+  // epilogue warps: scale each finished group and accumulate in registers. Swapped: thread (warp q,
+  // lane) holds weight row q * 32 + lane (its TMEM lane) for tokens [h * 64, h * 64 + 64); otherwise
+  // token row q * 32 + lane for weight columns [h * BN / 2, (h + 1) * BN / 2).
+  constexpr int HC = SWAP ? K5_BM / 2 : BN / 2;  // values per epilogue thread
   float acc[HC];
 #pragma unroll
   for (int c = 0; c < HC; ++c) acc[c] = 0.0f;
@@ -1352,13 +1367,33 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
         break;
       }
       tc_fence_after();
-      const __half* sc = s_sc + gl * BN + h * HC;
+      const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + b * ACOLS;
+      if constexpr (SWAP) {
+        const float sv = __half2float(s_sc[gl * BN + q * 32 + lane]);  // this weight row's group scale
 #pragma unroll
-      for (int cc = 0; cc < HC; cc += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32(tmem + ((uint32_t)(q * 32) << 16) + b * BN + h * HC + cc, r);
+        for (int cc = 0; cc < HC; cc += 16) {  // 16 columns of hi and of lo at a time (registers)
+          uint32_t rh[16];
+          tmem_ld_32x16(lane_base + h * HC + cc, rh);
+          if constexpr (XF32) {
+            uint32_t rl[16];
+            tmem_ld_32x16(lane_base + K5_BM + h * HC + cc, rl);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) acc[cc + e] = fmaf(__half2float(sc[cc + e]), __uint_as_float(r[e]), acc[cc + e]);
+            for (int e = 0; e < 16; ++e)
+              acc[cc + e] = fmaf(sv, __uint_as_float(rh[e]) + __uint_as_float(rl[e]), acc[cc + e]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) acc[cc + e] = fmaf(sv, __uint_as_float(rh[e]), acc[cc + e]);
+          }
+        }
+      } else {
+        const __half* sc = s_sc + gl * BN + h * HC;
+#pragma unroll
+        for (int cc = 0; cc < HC; cc += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32(lane_base + h * HC + cc, r);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) acc[cc + e] = fmaf(__half2float(sc[cc + e]), __uint_as_float(r[e]), acc[cc + e]);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -1384,7 +1419,7 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
   }
   if (warp == 13) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * BN);
+    tmem_dealloc(tmem, 2 * ACOLS);
   }
   if (s_fail) {
     if (threadIdx.x == 0) {
@@ -1407,11 +1442,18 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
   const int n_tiles = gridDim.y;
   if (p.nsplit == 1) {
     if (warp < 8) {
-#pragma unroll
-      for (int c = 0; c < HC; ++c) {
+      if constexpr (SWAP) {
         int rtl, sl;
-        k5_col(p, RTS, h * HC + c, rtl, sl);
-        fin[(rtl * K5_BM + m) * K5_FS + sl] = acc[c];
+        k5_col(p, RTS, m, rtl, sl);  // m = this thread's weight row
+#pragma unroll
+        for (int j = 0; j < HC; ++j) fin[(rtl * K5_BM + h * HC + j) * K5_FS + sl] = acc[j];
+      } else {
+#pragma unroll
+        for (int c = 0; c < HC; ++c) {
+          int rtl, sl;
+          k5_col(p, RTS, h * HC + c, rtl, sl);
+          fin[(rtl * K5_BM + m) * K5_FS + sl] = acc[c];
+        }
       }
     }
     __syncthreads();
@@ -1420,9 +1462,16 @@ __global__ void __launch_bounds__(K5_THREADS, 1)
     const size_t tile = (size_t)blockIdx.x * n_tiles + blockIdx.y;
     const size_t tiles = (size_t)gridDim.x * n_tiles;
     if (warp < 8) {
-      float* dst = p.ws + ((size_t)z * tiles + tile) * (K5_BM * BN) + (size_t)m * BN + h * HC;
+      if constexpr (SWAP) {  // [token][weight row]: a warp writes 32 consecutive rows per token
+        float* dst = p.ws + ((size_t)z * tiles + tile) * (K5_BM * BN) + (size_t)(h * HC) * BN + m;
 #pragma unroll
-      for (int c = 0; c < HC; c += 4) *reinterpret_cast<float4*>(dst + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+        for (int j = 0; j < HC; ++j) dst[(size_t)j * BN] = acc[j];
+      } else {
+        float* dst = p.ws + ((size_t)z * tiles + tile) * (K5_BM * BN) + (size_t)m * BN + h * HC;
+#pragma unroll
+        for (int c = 0; c < HC; c += 4)
+          *reinterpret_cast<float4*>(dst + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+      }
     }
     __threadfence();
     __syncthreads();

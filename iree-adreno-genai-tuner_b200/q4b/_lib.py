@@ -85,6 +85,7 @@ SIGNATURES = {
     "q4b_q4_linear_noalloc": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int,
                                       c_int, c_int, c_void_p]),
     "q4b_gemm_f16_workspace": (ctypes.c_longlong, [c_int, c_int, c_int, ctypes.c_char, ctypes.c_char, c_void_p]),
+    "q4b_gemm_f16_plan": (c_int, [c_int, c_int, c_int, ctypes.c_char, ctypes.c_char, c_void_p, c_void_p]),
     "q4b_gemm_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, ctypes.c_char, ctypes.c_char, c_void_p,
                              c_void_p, c_size_t, c_void_p]),
     "q4b_embed_q4_lookup": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),

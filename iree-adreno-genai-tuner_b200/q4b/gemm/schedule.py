@@ -121,11 +121,32 @@ def domains(s):
     }
 
 
+def tuned_schedules() -> dict:
+    """{(M, N, K, layout): Schedule} from tuned_b200.json: the schedules a search on a B200 measured
+    fastest for the config-2 shapes, which plan_gemm takes as its default for exactly those problems."""
+    import json
+    import pathlib
+
+    from .shapes import BY_ID
+    out = {}
+    for sid, rec in json.loads((pathlib.Path(__file__).with_name("tuned_b200.json")).read_text()).items():
+        sh = BY_ID[sid]
+        kv = dict(p.split("=") for p in rec["candidate"].split(":", 1)[1].split(","))
+        out[(sh.M, sh.N, sh.K, sh.layout)] = Schedule(kernel=1, bn=int(kv["bn"]), stages=int(kv["stages"]),
+                                                       split=int(kv["split"]))
+    return out
+
+
 def default_schedule(s) -> Schedule:
-    """The library's built-in choice (plan_gemm in csrc/gemm_f16.cu): the widest tile that still
-    gives 148 tiles, then split-K while that fills more SMs and each split keeps >= 4 k steps."""
+    """The library's built-in choice (plan_gemm in csrc/gemm_f16.cu): the searched schedule for the
+    config-2 problems (tuned_b200.json); otherwise the widest tile that still gives 148 tiles, then
+    split-K while that fills more SMs and each split keeps >= 4 k steps (stages: as many as fit, or
+    2 for 256-wide tiles over 8 or more row tiles)."""
     if s.la == "N" and s.K % 8 or s.la == "T" and s.M % 8 or s.lb == "N" and s.N % 8 or s.lb == "T" and s.K % 8:
         return Schedule(kernel=2)
+    tuned = tuned_schedules().get((s.M, s.N, s.K, s.layout))
+    if tuned is not None:
+        return tuned
     tm = -(-s.M // BM)
     bn = 256
     while bn > 64 and tm * -(-s.N // bn) < 148:

@@ -109,6 +109,26 @@ def test_default_schedule_matches_the_library():
         assert L.q4b_gemm_f16_workspace(s.M, s.N, s.K, s.la.encode(), s.lb.encode(), ctypes.byref(c)) == ws
 
 
+def test_tuned_schedules_are_the_library_default():
+    """For the config-2 shapes the library's default plan is the schedule the B200 search measured
+    fastest (q4b/gemm/tuned_b200.json, compiled into plan_gemm's table)."""
+    import ctypes
+
+    from q4b import _lib
+    from q4b.gemm.schedule import tuned_schedules
+    L = _lib.lib()
+    t = tuned_schedules()
+    assert len(t) == 8
+    for (m, n, k, lay), sc in t.items():
+        out = _lib.GemmCfg()
+        assert L.q4b_gemm_f16_plan(m, n, k, lay[0].encode(), lay[1].encode(), None, ctypes.byref(out)) == 0
+        assert (out.kernel, out.bn, out.stages, out.split) == (1, sc.bn, sc.stages, sc.split), (m, n, k)
+    # a problem outside the table keeps the built-in plan: 256-wide tiles over many rows -> 2 stages
+    out = _lib.GemmCfg()
+    assert L.q4b_gemm_f16_plan(4096, 4096, 4096, b"N", b"N", None, ctypes.byref(out)) == 0
+    assert (out.bn, out.stages) == (256, 2)
+
+
 def test_cost_model_sanity():
     g = _gemm()
     from q4b.gemm import cost_model
