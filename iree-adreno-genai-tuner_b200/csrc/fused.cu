@@ -48,6 +48,42 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   griddep_wait();
   const int r = blockIdx.x;
   const float* xr = x + (size_t)((row_sel ? *row_sel : 0) + r) * dim;
+  constexpr int kV = 4;  // float4 per thread held in registers (rows up to 4096 with 256 threads)
+  if (dim % 4 == 0 && dim <= kV * 4 * (int)blockDim.x &&
+      (reinterpret_cast<uintptr_t>(xr) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) % 16 == 0) {
+    // one pass: every load of the row issued before the reduction, the row kept in registers
+    const float4* x4 = reinterpret_cast<const float4*>(xr);
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    float4* o4 = reinterpret_cast<float4*>(out + (size_t)r * dim);
+    const int n4 = dim / 4;
+    float4 v[kV];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const int j = threadIdx.x + i * blockDim.x;
+      v[i] = j < n4 ? x4[j] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+      t = warp_sum(t);
+      if (threadIdx.x == 0) red[0] = 1.0f / sqrtf(t / (float)dim + eps);
+    }
+    __syncthreads();
+    const float rs = red[0];
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const int j = threadIdx.x + i * blockDim.x;
+      if (j < n4) {
+        const float4 g = w4[j];
+        o4[j] = make_float4(v[i].x * rs * g.x, v[i].y * rs * g.y, v[i].z * rs * g.z, v[i].w * rs * g.w);
+      }
+    }
+    return;
+  }
   float ss = 0.0f;
   for (int k = threadIdx.x; k < dim; k += blockDim.x) ss += xr[k] * xr[k];
   ss = warp_sum(ss);
@@ -268,21 +304,23 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(AttnArgs a) {
 // P.V with lanes owning head elements (hd / 32 each) over the block's V rows, loaded together.
 template <int EPL>
 __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
-  constexpr int HD = EPL * 32, KU4 = HD / 8;
-  __shared__ float s_q[4][HD];
-  const int h = blockIdx.x;
+  // one CTA per (head, query row): the row's visible keys go to the 4 warps by 32-key blocks (warp
+  // w takes blocks w, w + 4, ...), each an online softmax; the warps' (max, sum, weighted V) merge
+  // in shared memory. A row's loads are a few rounds in parallel instead of nk / 32 in sequence.
+  constexpr int HD = EPL * 32, KU4 = HD / 8, NW = 4;
+  __shared__ float s_q[HD];
+  __shared__ float s_o[NW][HD];
+  __shared__ float s_m[NW], s_l[NW];
+  const int h = blockIdx.x, c = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c = blockIdx.y * 4 + warp;
   griddep_launch_dependents();
   griddep_wait();
-  if (c >= a.C) return;  // whole warp; no block-wide barrier below
   const int g = a.H / a.Hkv, kvh = h / g;
   const int start = *a.pos0;
   const int nk = min(a.L, start + c + 1);
   const float* qp = a.q + ((size_t)c * a.H + h) * HD;
-#pragma unroll
-  for (int e = 0; e < EPL; ++e) s_q[warp][lane * EPL + e] = qp[lane * EPL + e];
-  __syncwarp();
+  for (int e = threadIdx.x; e < HD; e += blockDim.x) s_q[e] = qp[e];
+  __syncthreads();
   float o[EPL];
 #pragma unroll
   for (int e = 0; e < EPL; ++e) o[e] = 0.0f;
@@ -290,7 +328,7 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
   const size_t kv_stride = (size_t)a.Hkv * HD;
   const __half* kbase = a.k_cache + (size_t)kvh * HD;
   const __half* vbase = a.v_cache + (size_t)kvh * HD + lane * EPL;
-  for (int kb = 0; kb < nk; kb += 32) {
+  for (int kb = 32 * warp; kb < nk; kb += 32 * NW) {
     const int j = kb + lane;
     const bool valid = j < nk;
     // this lane's key row and the block's V slices of this lane's elements, in one round
@@ -319,12 +357,12 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         const float2 f = __half22float2(h2[t]);
-        d = fmaf(s_q[warp][8 * u + 2 * t], f.x, d);
-        d = fmaf(s_q[warp][8 * u + 2 * t + 1], f.y, d);
+        d = fmaf(s_q[8 * u + 2 * t], f.x, d);
+        d = fmaf(s_q[8 * u + 2 * t + 1], f.y, d);
       }
     }
     const float sc = valid ? d * a.scale : -INFINITY;
-    const float mn = fmaxf(m, warp_max(sc));  // lane 0's key is always visible: mn is finite
+    const float mn = fmaxf(m, warp_max(sc));  // the block's lane 0 key is always visible: mn is finite
     const float p = valid ? expf(sc - mn) : 0.0f;
     const float cs = m == -INFINITY ? 0.0f : expf(m - mn);
     l = l * cs + warp_sum(p);
@@ -338,9 +376,32 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
     }
     m = mn;
   }
-  float* op = a.out + ((size_t)c * a.H + h) * HD + lane * EPL;
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_l[warp] = l;
+  }
 #pragma unroll
-  for (int e = 0; e < EPL; ++e) op[e] = o[e] / l;
+  for (int e = 0; e < EPL; ++e) s_o[warp][lane * EPL + e] = o[e];
+  __syncthreads();
+  if (warp == 0) {  // merge the warps (a warp without keys has max -inf and is skipped)
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, s_m[w]);
+    float L = 0.0f, acc[EPL];
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) acc[e] = 0.0f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      if (s_m[w] == -INFINITY) continue;
+      const float cs = expf(s_m[w] - M);
+      L += s_l[w] * cs;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) acc[e] = fmaf(s_o[w][lane * EPL + e], cs, acc[e]);
+    }
+    float* op = a.out + ((size_t)c * a.H + h) * HD + lane * EPL;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) op[e] = acc[e] / L;
+  }
 }
 
 int attn_decode_chunks(int L) { return (L + kChunk - 1) / kChunk; }
@@ -388,7 +449,7 @@ int attention_run(const AttnArgs& in, cudaStream_t st) {
     const int R = a.C * g;
     e = R <= 4 ? launch_decode<4>(a, grid, st) : R <= 8 ? launch_decode<8>(a, grid, st) : launch_decode<16>(a, grid, st);
   } else {
-    const dim3 grid(a.H, (a.C + 3) / 4);
+    const dim3 grid(a.H, a.C);
     switch (a.head_dim) {
       case 32: e = launch_pdl(attn_prefill_kernel<1>, grid, dim3(128), 0, st, a); break;
       case 64: e = launch_pdl(attn_prefill_kernel<2>, grid, dim3(128), 0, st, a); break;
