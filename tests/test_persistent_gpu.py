@@ -97,23 +97,37 @@ def test_persistent_matches_per_projection_path(model):
 
 
 def test_persistent_matches_oracle(model):
+    """Every decode step from the oracle's own KV cache and token (teacher forcing): logits within
+    1e-3 of max|logit| and the same greedy token; and the free-running greedy stream identical.
+    (Free-running logits are not compared: the fp16 KV cache rounds a value one ulp apart wherever
+    the two fp32 paths differ in the last bit, and this deliberately large-weight model amplifies
+    that over steps -- measured: the same 2.8e-2 deviation at step 5 with either prefill kernel and
+    either decode path.)"""
     m, sd = model
-    t_on, l_on = _decode(m, True)
+    t_on, _ = _decode(m, True)
     ref_sd = {k: sd[k].float().cpu().numpy() for k in _state_keys()}
     om = O.OracleModel.from_state_dict(CFG, ref_sd, MAX_CTX, group=128)
-    caches = om.new_caches()
-    p = _prompt()
-    nxt, _ = om.step(p, 0, PROMPT - 1, caches, 64)
-    toks, logits = [int(nxt)], []
-    for i in range(STEPS):
-        pos = PROMPT + i
-        L = 64 if pos < 64 else 128 if pos < 128 else 256
-        nxt, lg = om.step(np.array([nxt]), pos, 0, caches, L)
-        toks.append(int(nxt))
-        logits.append(np.asarray(lg).reshape(-1))
-    ref = np.stack(logits)
+    oc = om.new_caches()
+    nxt, _ = om.step(_prompt(), 0, PROMPT - 1, oc, 64)
+    caches = m.new_caches()
+    toks = [int(nxt)]
+    with _Persistent(True):
+        for i in range(STEPS):
+            pos = PROMPT + i
+            L = 64 if pos < 64 else 128 if pos < 128 else 256
+            for c, o in zip(caches, oc):
+                c.copy_(torch.from_numpy(o))
+            got_nxt, got_lg = m.step(torch.tensor([[int(nxt)]], dtype=torch.int32), torch.tensor([pos]),
+                                     torch.tensor([0]), caches, L)
+            nxt, lg = om.step(np.array([nxt]), pos, 0, oc, L)
+            lg = np.asarray(lg).reshape(-1)
+            err = float(np.abs(got_lg.cpu().numpy()[0] - lg).max())
+            assert err <= 1e-3 * max(1.0, float(np.abs(lg).max())), (i, err)
+            assert int(got_nxt) == int(nxt), i
+            toks.append(int(nxt))
     assert t_on == toks
-    assert np.abs(l_on - ref).max() <= 1e-3 * max(1.0, np.abs(ref).max())
+    from q4b import _lib
+    assert _lib.lib().q4b_device_status(1) == 0
 
 
 def test_persistent_through_runner_graphs(model):
