@@ -688,6 +688,39 @@ def cpu_gemm_baseline(budget_s=10.0):
                       f"(median {med * 1e3:.1f} ms)"}
 
 
+def cpu_sweep_baseline(ms, budget_s=12.0):
+    """BASELINE config 5 on the host cores, the reference's two QLinear forms on the q|k|v shape
+    (5120 x 3072, g128): M = 1 the fused GEMV (the C restatement, one thread per CPU), M > 1
+    dequantize_q4 of the whole weight on every call then a float32 matmul (llama_q4.py:72, numpy).
+    GB/s = algorithmic bytes of the timed calls / their time (the sweep's metric)."""
+    import numpy as np
+
+    from oracle import q4_cpu as C
+    from oracle import q4_oracle as O
+    n, k = SWEEP_SHAPES["qkv"]
+    rng = np.random.default_rng(5)
+    qw = rng.integers(-2**31, 2**31 - 1, size=(n, k // 8), dtype=np.int64).astype(np.int32)
+    sc = (np.abs(rng.standard_normal((n, k // 128))) * 0.02).astype(np.float16)
+    tot_b, tot_s, done = 0, 0.0, []
+    per = budget_s / max(1, len(ms))
+    for m in ms:
+        x = rng.standard_normal((m, k)).astype(np.float32)
+        t_end, calls, t = time.perf_counter() + per, 0, 0.0
+        while calls < 2 or (time.perf_counter() < t_end and calls < 200):
+            t0 = time.perf_counter()
+            if m == 1:
+                C.gemv(qw, sc, 128, x[0])
+            else:
+                x @ O.dequantize_q4(qw, sc, 128).T
+            t += time.perf_counter() - t0
+            calls += 1
+        tot_b += calls * linear_bytes(n, k, m)
+        tot_s += t
+        done.append(f"M={m}: {calls} calls, {t / calls * 1e3:.2f} ms/call")
+    return {"value": round(tot_b / tot_s / 1e9, 3), "unit": "GB/s", "cores": C.threads(), "kind": "port",
+            "sample": "q|k|v 5120x3072 g128, " + "; ".join(done)}
+
+
 def run_sweep(args, rank, world, local, dist_mod):
     """every 3B projection (and the lm_head) at M in {1, 4, 16, 64}, each timed as
     a chain over distinct weight copies, against the HBM roofline; one GPU per rank (replicas)."""
@@ -722,7 +755,8 @@ def run_sweep(args, rank, world, local, dist_mod):
             "roofline": {"bound": "hbm", "peak": pk["hbm_gbs"], "unit": "GB/s", "peak_source": pk["source"],
                          "achieved": round(tot_b / tot_s / 1e9, 1),
                          "frac": round(tot_b / tot_s / 1e9 / pk["hbm_gbs"], 4), "traffic": None},
-            "rows": rows, "gpu_launches": sum(r["weight_copies"] for r in rows) * args.steps}
+            "rows": rows, "gpu_launches": sum(r["weight_copies"] for r in rows) * args.steps,
+            **({} if args.no_cpu_baseline else {"cpu_baseline": cpu_sweep_baseline(args.m)})}
 
 
 def shard_measure(dev, n, k, m, split, rank, world, dist_mod, comm, steps, warmup, seed=99):
@@ -860,6 +894,81 @@ def run_shard(args, rank, world, local, dist_mod):
             "rows": rows, "gpu_launches": sum(r["weight_copies"] for r in rows) * args.steps}
 
 
+def run_tiny(args, rank, world, local, dist_mod):
+    """the tiny LlamaQ4 (4 layers, hidden 256, 8 / 2 heads, head_dim 32, inter 688,
+    vocab 1024) with the reference's own quantised weights and greedy stream
+    (tests/golden/model_tiny_baseline.npz, written by tests/golden/make_golden.py from the unmodified
+    reference): 64-token prompt, chunk 32, KV buckets {128, 256}, 64 new tokens through the runner
+    (bucketed schedule, CUDA graphs). value = decode tokens/s (median over --steps generate calls);
+    e2e = the same with the per-step host read; the tokens must equal the reference's; cpu_baseline =
+    the oracle's step (numpy) on the same request's decode steps."""
+    import statistics
+    import sys
+    import time
+
+    import numpy as np
+    import torch
+
+    import q4b
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import golden_inputs as gi
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    spec = gi.MODEL_SPECS["tiny_baseline"]
+    z = dict(np.load(ROOT / "tests" / "golden" / "model_tiny_baseline.npz"))
+    model = q4b.LlamaQ4.from_packed(spec["cfg"], z, spec["max_ctx"], vocab_chunk=spec["vocab_chunk"],
+                                    max_chunk=spec["chunk"], device=dev)
+    prompt, want = z["prompt"].tolist(), z["bucketed_tokens"].tolist()
+    runner = q4b.Runner(model, spec["chunk"], spec["buckets"], "bucketed", graphs=True)
+    for _ in range(args.warmup):
+        runner.generate(prompt, spec["max_new"])
+    reps = []
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            toks, rep = runner.generate(prompt, spec["max_new"])
+            reps.append(rep)
+    same = toks == want
+    sync = q4b.Runner(model, spec["chunk"], spec["buckets"], "bucketed", graphs=True, sync_every_step=True)
+    sync.generate(prompt, spec["max_new"])
+    e2e = [sync.generate(prompt, spec["max_new"])[1]["decode_tok_s"] for _ in range(3)]
+    value = statistics.median(r["decode_tok_s"] for r in reps)
+    line = {"metric": "tiny LlamaQ4 decode tokens/s (BASELINE config 3)", "value": round(value, 1),
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, fp32 activations, fp16 KV cache",
+            "data": "the reference's own quantised random-init weights (seed 0) and prompt",
+            "config": {"workload": "tiny LlamaQ4 (BASELINE config 3)", "prompt": len(prompt),
+                       "new_tokens": spec["max_new"], "chunk": spec["chunk"], "buckets": spec["buckets"],
+                       "schedule": "bucketed", "graphs": True,
+                       "decode_kernel": "per projection (the tiny shape is below the persistent step's)"},
+            "tokens_match_reference": same, "ttft_ms": statistics.median(r["ttft_ms"] for r in reps),
+            "e2e": {"value": round(statistics.median(e2e), 1), "unit": "tokens/s", "h2d_bytes_per_step": 104,
+                    "d2h_bytes_per_step": 4, "path": "q4b.Runner(sync_every_step=True).generate"},
+            "clocks": clk.summary(), "gpu_launches": None}
+    if not args.no_cpu_baseline:
+        from oracle import q4_oracle as O
+        layers = [dict(wqkv=(z[f"l{i}_wqkv_qweight"], z[f"l{i}_wqkv_scales"], int(z[f"l{i}_wqkv_group"])),
+                       wo=(z[f"l{i}_wo_qweight"], z[f"l{i}_wo_scales"], int(z[f"l{i}_wo_group"])),
+                       wgu=(z[f"l{i}_wgu_qweight"], z[f"l{i}_wgu_scales"], int(z[f"l{i}_wgu_group"])),
+                       wdown=(z[f"l{i}_wdown_qweight"], z[f"l{i}_wdown_scales"], int(z[f"l{i}_wdown_group"])),
+                       ln_in=z[f"l{i}_ln_in"], ln_post=z[f"l{i}_ln_post"]) for i in range(spec["cfg"]["num_hidden_layers"])]
+        om = O.OracleModel(spec["cfg"], layers, (z["embed_qweight"], z["embed_scales"], int(z["embed_group"])),
+                           z["ln_f"], spec["max_ctx"])
+        caches = om.new_caches()
+        nxt = None
+        for s0 in range(0, len(prompt), spec["chunk"]):
+            chunk = np.array(prompt[s0:s0 + spec["chunk"]])
+            nxt, _ = om.step(chunk, s0, len(chunk) - 1, caches, 128)
+        t0, n, pos = time.perf_counter(), 0, len(prompt)
+        while n < spec["max_new"] - 1 and time.perf_counter() - t0 < 20.0:
+            nxt, _ = om.step(np.array([nxt]), pos, 0, caches, 128 if pos < 128 else 256)
+            pos += 1
+            n += 1
+        line["cpu_baseline"] = {"value": round(n / (time.perf_counter() - t0), 3), "unit": "tokens/s",
+                                "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"{n} decode steps of the same request (numpy restatement)"}
+    return line
+
+
 def run_profile(args, rank, world, local, dist_mod):
     """A short fixed launch sequence for profilers: a 3B-shaped model with --layers layers, an optional
     --prefill C chunk at position 0, then --steps single-token decode steps at position --pos."""
@@ -966,7 +1075,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="decode: tokens (255); gemv: graph replays (200)")
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="decode", choices=["decode", "gemv", "sweep", "shard", "profile", "ctx", "gemm"])
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "gemv", "sweep", "shard", "tiny", "profile", "ctx", "gemm"])
     ap.add_argument("--splits", nargs="*", default=["col", "row"], help="shard: column and / or row split")
     ap.add_argument("--ctx", type=int, nargs="*", default=[256, 512, 1024, 2048, 4096], help="ctx: context lengths")
     ap.add_argument("--new", type=int, default=64, help="ctx: generated tokens per run")
@@ -989,7 +1099,7 @@ def main():
     if args.warmup < 3 and args.workload != "profile":
         args.warmup = 3
     if args.steps is None:
-        args.steps = {"decode": 255, "gemv": 200, "sweep": 20, "shard": 20, "profile": 3, "ctx": 0,
+        args.steps = {"decode": 255, "gemv": 200, "sweep": 20, "shard": 20, "tiny": 10, "profile": 3, "ctx": 0,
                       "gemm": 20}[args.workload]
     rank, world, local = dist_env()
     if args.impl == "reference":
@@ -999,7 +1109,7 @@ def main():
         return
     dist_mod = init_dist(world, local)
     try:
-        run = {"decode": run_decode, "gemv": run_gemv, "sweep": run_sweep, "shard": run_shard,
+        run = {"decode": run_decode, "gemv": run_gemv, "sweep": run_sweep, "shard": run_shard, "tiny": run_tiny,
                "profile": run_profile, "ctx": run_ctx, "gemm": run_gemm}[args.workload]
         line = run(args, rank, world, local, dist_mod)
     finally:

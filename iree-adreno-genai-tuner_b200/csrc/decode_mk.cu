@@ -123,6 +123,9 @@ struct MkArgs {
   // 0 = every thread polls its words' layer-parity tags; 1 = one thread per CTA waits on the
   // row-split arrival counter (sync[7]) and the words are then loaded once
   int split_sync;
+  // 1: the o projection's weights are requested only once the layer's attention is over (see
+  // producer_gate); 0: right after the q|k|v weights, during attention
+  int gate_o;
 };
 
 // Trace events of a CTA: per layer l and stage s (0 q|k|v, 1 attention, 2 o, 3 gate|up, 4 down),
@@ -965,7 +968,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
       };
       for (int i = 0; i < nproj && ok; ++i) {
         // local stage arrivals: q|k|v, attention, gate|up per layer (n CTAs each)
-        if (kind(i) == ST_WO) ok = producer_gate(a, sm, (3u * (i >> 2) + 2u) * gridDim.x);
+        if (kind(i) == ST_WO && a.gate_o) ok = producer_gate(a, sm, (3u * (i >> 2) + 2u) * gridDim.x);
         ok = ok && produce_stage(a, sm, a.proj[i], kind(i), seq);
       }
       if (!ok) raise_abort(a, sm);
@@ -1189,6 +1192,8 @@ int Model::mk_prepare() {
     return set_error(Q4B_EUNSUPPORTED, "persistent decode: kernel does not fit an SM (%s)", cudaGetErrorString(e));
   mk_ctas = sms;
   // ring depth (above) and row-split synchronisation: tuning knobs Q4B_MK_SLOTS, Q4B_MK_SPLIT_SYNC
+  mk_gate_o = 1;
+  if (const char* e = std::getenv("Q4B_MK_GATE_O")) mk_gate_o = std::atoi(e) != 0;
   mk_split_sync = 0;
   if (const char* e = std::getenv("Q4B_MK_SPLIT_SYNC")) mk_split_sync = std::atoi(e) == 1 ? 1 : 0;
   mk_ready = true;
@@ -1266,6 +1271,7 @@ int Model::mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_
   a.trace = mk_trace_cap >= (size_t)mk_ctas * mk_trace_stride(a.n_layers) ? mk_trace : nullptr;
   a.nslot = mk_nslot;
   a.split_sync = mk_split_sync;
+  a.gate_o = mk_gate_o;
   cudaLaunchConfig_t cfgl = {};
   cfgl.gridDim = dim3(mk_ctas);
   cfgl.blockDim = dim3(MK_THREADS);

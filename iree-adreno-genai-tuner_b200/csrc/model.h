@@ -45,6 +45,7 @@ struct Model {
   int mk_ctas = 0;
   int mk_nslot = 0;        // ring slots the persistent step uses
   int mk_split_sync = 0;   // 0: tag-polled partial sums, 1: row-split arrival counter
+  int mk_gate_o = 1;       // o weights requested after the layer's attention (Q4B_MK_GATE_O)
   unsigned long long* mk_trace = nullptr;  // caller's phase-trace buffer (q4b_model_set_trace) or null
   size_t mk_trace_cap = 0;
   bool mk_ready = false;

@@ -34,3 +34,28 @@ def test_profile_traffic_lines():
     assert t is not None and abs(t / bench.decode_bytes_per_token(q4b.SYNTHETIC["3b"], 640) - 1) < 0.01
     g = bench.profile_traffic("q4_gemv_mma_5120x3072")
     assert g is not None and abs(g / bench.GEMV_BYTES - 1) < 0.01
+
+
+def test_trace_summary_reads_the_stamp_layout():
+    """bench.trace_summary on a synthetic trace (q4b_model_set_trace layout: 15 stamps per layer,
+    then lm_head ready / staged / done and the consumers' start): every stage takes 1 us to become
+    ready, 1 us to stage and 1 us to run."""
+    import numpy as np
+
+    import bench
+    L, ctas = 3, 4
+    ev = np.zeros((ctas, 15 * L + 4), np.int64)
+    for c in range(ctas):
+        ev[c, 15 * L + 3] = 1000
+        for i in range(15 * L + 3):
+            ev[c, i] = 1000 + (i + 1) * 1000
+    t = bench.trace_summary(ev, L)
+    for stage in bench.TRACE_PHASES:
+        assert t[stage]["stage"] == 1.0 and t[stage]["busy"] == 1.0 and t[stage]["wait"] == 1.0
+    assert t["layer_us"] == 15.0 and t["ctas"] == ctas
+
+
+def test_cpu_sweep_baseline_is_bounded():
+    import bench
+    cb = bench.cpu_sweep_baseline([1], budget_s=0.5)
+    assert cb["value"] > 0 and cb["kind"] == "port" and "M=1" in cb["sample"]
