@@ -82,3 +82,17 @@ def test_tp_collectives(world):
     assert out["f32_err"] <= 1e-5 * world
     assert out["f16_err"] <= 2e-2 * world
     assert out["token"] == out["want_token"]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_3b_matches_reference_stream():
+    """BASELINE config 4 over 2 GPUs: the 28-layer 3B shape, the bench's 512-token request through the
+    runner with the persistent step on both ranks, gives the unmodified reference's 256 greedy tokens
+    (tests/golden/model_3b_ref.npz; its smallest top-2 margin is 1.04e-3, so all of them must match)."""
+    out = _run(2, Q4B_TP_MODE="ref3b")
+    z = np.load(HERE / "golden" / "model_3b_ref.npz")
+    want = z["tokens"].tolist()
+    bad = next((i for i, (a, b) in enumerate(zip(out["tokens"], want)) if a != b), None)
+    assert out["tokens"] == want, f"first mismatch at step {bad}"
+    assert out["chunks"] == z["chunk_buckets"].tolist()
+    assert out["decode_path"] == 1 and out["status"] == 0

@@ -1,7 +1,8 @@
 """One rank of the tensor-parallel GPU parity checks (launched by tests/test_tp_gpu.py under
 torch.distributed.run). Default: builds the reference's tiny KAT model (HF random init, seed 0)
 sharded over the ranks, runs the llm_runner.c schedule, and rank 0 prints the tokens as JSON.
-Q4B_TP_MODE=persistent: the persistent decode step sharded over the ranks (see persistent_main)."""
+Q4B_TP_MODE=persistent: the persistent decode step sharded over the ranks (see persistent_main);
+collectives: the standalone TP collectives; ref3b: the 3B shape against the reference's stream."""
 
 import json
 import os
@@ -132,6 +133,26 @@ def collectives_main(rank, world, dev):
     return out
 
 
+def ref3b_main(rank, world, dev):
+    """BASELINE config 4 at full depth over the ranks: the 3B-shape model (SyntheticStateDict seed 0,
+    the weights tests/golden/model_3b_ref.npz was made from) sharded over the ranks, the bench's
+    request through the runner (persistent decode step on every rank); rank 0 reports the tokens."""
+    import q4b
+    z = np.load(HERE / "golden" / "model_3b_ref.npz")
+    cfg = q4b.SYNTHETIC["3b"]
+    model = q4b.LlamaQ4(None, group=128, max_ctx=4096, vocab_chunk=32064,
+                        sd=q4b.SyntheticStateDict(cfg, seed=0, device=dev), cfg=cfg, max_chunk=128,
+                        tp_rank=rank, tp_size=world, device=dev)
+    model.attach_tp()
+    r = q4b.Runner(model, 128, [256, 512, 1024, 2048, 4096], "bucketed", graphs=True)
+    toks, rep = r.generate(z["prompt"].tolist(), len(z["tokens"]))
+    out = dict(tokens=toks, chunks=[c[0] for c in rep["chunks"]],
+               decode_path=int(q4b.lib().q4b_model_decode_path(model.native())),
+               status=int(q4b.lib().q4b_device_status(1)))
+    del r  # graphs holding NCCL calls go before the process group
+    return out
+
+
 def _one_step_kernels(model):
     from torch.profiler import ProfilerActivity, profile
     os.environ["Q4B_PERSISTENT"] = "1"
@@ -150,8 +171,8 @@ def main():
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     mode = os.environ.get("Q4B_TP_MODE")
-    if mode in ("persistent", "collectives"):
-        out = (persistent_main if mode == "persistent" else collectives_main)(rank, world, dev)
+    if mode in ("persistent", "collectives", "ref3b"):
+        out = {"persistent": persistent_main, "collectives": collectives_main, "ref3b": ref3b_main}[mode](rank, world, dev)
         torch.cuda.synchronize()
         dist.barrier()
         if rank == 0:
