@@ -139,9 +139,9 @@ __device__ __forceinline__ void trace_ev(const MkArgs& a, int e) {
 // Attention scratch of one item; shares shared memory with the staged x, which is free between the
 // q|k|v projection (its last reads end before the stage arrival) and the o projection's staging.
 struct MkAttn {
-  float q[MK_HD];
-  float o[MK_CW][MK_HD];
-  float m[MK_CW], l[MK_CW], cs[MK_CW];
+  float q[MK_ROWS][MK_HD];
+  float o[MK_CW][MK_ROWS][MK_HD];
+  float m[MK_CW][MK_ROWS], l[MK_CW][MK_ROWS], cs[MK_CW][MK_ROWS];
 };
 struct MkX {
   uint4 hi[MK_XROW];  // word w of x as fp16 hi / lo pairs at xswz(w)
@@ -826,13 +826,13 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
   uint4 kr[HD / 16];
 #pragma unroll
   for (int i = 0; i < HD / 16; ++i) kr[i] = __ldcg(kp + 2 * i + hh);
-  if (ct < HD) sm.u.att.q[ct] = qv;
+  if (ct < HD) sm.u.att.q[0][ct] = qv;
   consumer_sync();
   float d0 = 0.0f, d1 = 0.0f;
 #pragma unroll
   for (int i = 0; i < HD / 16; ++i) {
     const __half2* h2 = reinterpret_cast<const __half2*>(&kr[i]);
-    const float* qp = &sm.u.att.q[8 * (2 * i + hh)];
+    const float* qp = &sm.u.att.q[0][8 * (2 * i + hh)];
 #pragma unroll
     for (int tt = 0; tt < 4; ++tt) {
       const float2 f = __half22float2(h2[tt]);
@@ -861,21 +861,21 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
     }
   }
   if (lane == 0) {
-    sm.u.att.m[w] = m;
-    sm.u.att.l[w] = lw;
+    sm.u.att.m[w][0] = m;
+    sm.u.att.l[w][0] = lw;
   }
-  *reinterpret_cast<float4*>(&sm.u.att.o[w][lane * EPL]) = make_float4(o[0], o[1], o[2], o[3]);
+  *reinterpret_cast<float4*>(&sm.u.att.o[w][0][lane * EPL]) = make_float4(o[0], o[1], o[2], o[3]);
   consumer_sync();
   // merge the warps into this chunk's partial for row r
   float* part = a.part + (((size_t)kvh * MK_MAXCH + ch) * MK_ROWS + r) * (HD + MK_PAD);
   if (ct == 0) {
     float M = -INFINITY;
-    for (int i = 0; i < MK_CW; ++i) M = fmaxf(M, sm.u.att.m[i]);
+    for (int i = 0; i < MK_CW; ++i) M = fmaxf(M, sm.u.att.m[i][0]);
     float l = 0.0f;
     for (int i = 0; i < MK_CW; ++i) {
-      const float cs = sm.u.att.m[i] == -INFINITY ? 0.0f : expf(sm.u.att.m[i] - M);
-      sm.u.att.cs[i] = cs;
-      l += sm.u.att.l[i] * cs;
+      const float cs = sm.u.att.m[i][0] == -INFINITY ? 0.0f : expf(sm.u.att.m[i][0] - M);
+      sm.u.att.cs[i][0] = cs;
+      l += sm.u.att.l[i][0] * cs;
     }
     part[0] = M;
     part[1] = l;
@@ -883,7 +883,7 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
   consumer_sync();
   for (int e = ct; e < HD; e += MK_CW * 32) {
     float v = 0.0f;
-    for (int k = 0; k < MK_CW; ++k) v += sm.u.att.o[k][e] * sm.u.att.cs[k];
+    for (int k = 0; k < MK_CW; ++k) v += sm.u.att.o[k][0][e] * sm.u.att.cs[k][0];
     part[MK_PAD + e] = v;
   }
   // the CTA that completes a query row's chunks merges them (max, sum, weighted V, online over the
@@ -931,8 +931,152 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
   if (ct == 0) a.rowcnt[hq] = 0u;  // the next layer's items start after the next stage barrier
 }
 
+// Long-context attention item (many chunks): all nr = g query rows of KV head kvh's group against
+// keys [128 ch, 128 ch + 128), sharing one round of K and V loads; the rows' chunk partials as in
+// attn_item, and the CTA completing the group's chunks (a counter on the group's first row) merges
+// all its rows. Only the long-bucket instantiation of the step kernel contains it, so the registers
+// it needs stay out of the short-bucket kernel.
+__device__ void attn_group_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int ch, int r0, int nr,
+                                             int ctx, int nch) {
+  constexpr int HD = MK_HD, EPL = HD / 32, KW = MK_KCHUNK / MK_CW;  // KW keys per warp (16)
+  const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
+  const int kk = lane >> 1, hh = lane & 1;  // scores: two lanes per key, alternate 16-byte pieces
+  const int g = a.H / a.Hkv;
+  const __half* kc = sm.kcache[layer];
+  const __half* vc = sm.vcache[layer];
+  const size_t row_stride = (size_t)a.Hkv * HD;
+  const int k0 = ch * MK_KCHUNK, k1 = min(k0 + MK_KCHUNK, ctx);
+  const int jbase = k0 + KW * w, j = jbase + kk;
+  // one round of loads: the query rows (one element per thread and row, to shared memory), this
+  // lane's 4 elements of every V row of the warp's keys (8 bytes per key) and its half of its key's K
+  // row (pieces 2i + hh of 16 bytes, so a load instruction reads 32 contiguous bytes of 16 rows)
+  if (ct < HD) {
+#pragma unroll 1
+    for (int rr = 0; rr < nr; ++rr) sm.u.att.q[rr][ct] = __ldcg(a.q + ((size_t)kvh * g + r0 + rr) * HD + ct);
+  }
+  uint2 vv[KW];
+#pragma unroll
+  for (int jj = 0; jj < KW; ++jj) {
+    const int key = min(jbase + jj, k1 - 1);
+    vv[jj] = __ldcg(reinterpret_cast<const uint2*>(vc + (size_t)key * row_stride + (size_t)kvh * HD + lane * EPL));
+  }
+  const uint4* kp = reinterpret_cast<const uint4*>(kc + (size_t)min(j, k1 - 1) * row_stride + (size_t)kvh * HD);
+  uint4 kr[HD / 16];
+#pragma unroll
+  for (int i = 0; i < HD / 16; ++i) kr[i] = __ldcg(kp + 2 * i + hh);
+  consumer_sync();
+#pragma unroll 1
+  for (int rr = 0; rr < nr; ++rr) {  // uniform over the CTA
+    float d0 = 0.0f, d1 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < HD / 16; ++i) {
+      const __half2* h2 = reinterpret_cast<const __half2*>(&kr[i]);
+      const float* qp = &sm.u.att.q[rr][8 * (2 * i + hh)];
+#pragma unroll
+      for (int tt = 0; tt < 4; ++tt) {
+        const float2 f = __half22float2(h2[tt]);
+        d0 = fmaf(qp[2 * tt], f.x, d0);
+        d1 = fmaf(qp[2 * tt + 1], f.y, d1);
+      }
+    }
+    float d = d0 + d1;
+    d += __shfl_xor_sync(0xffffffffu, d, 1);
+    const float sc = j < k1 ? d * a.scale : -INFINITY;
+    const float m = warp_max(sc);  // each key twice: the maximum is the same
+    float o[EPL] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float lw = 0.0f;
+    if (m != -INFINITY) {
+      const float p = expf(sc - m);  // 0 for keys past the chunk: their V slices are never used
+      lw = warp_sum(hh == 0 ? p : 0.0f);
+#pragma unroll
+      for (int jj = 0; jj < KW; ++jj) {
+        const float pj = __shfl_sync(0xffffffffu, p, 2 * jj);
+        const float2 v0 = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj].x));
+        const float2 v1 = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj].y));
+        o[0] = fmaf(pj, v0.x, o[0]);
+        o[1] = fmaf(pj, v0.y, o[1]);
+        o[2] = fmaf(pj, v1.x, o[2]);
+        o[3] = fmaf(pj, v1.y, o[3]);
+      }
+    }
+    if (lane == 0) {
+      sm.u.att.m[w][rr] = m;
+      sm.u.att.l[w][rr] = lw;
+    }
+    *reinterpret_cast<float4*>(&sm.u.att.o[w][rr][lane * EPL]) = make_float4(o[0], o[1], o[2], o[3]);
+  }
+  consumer_sync();
+  // merge the warps into this chunk's partial for each row
+  if (ct < nr) {
+    const int rr = ct;
+    float* part = a.part + (((size_t)kvh * MK_MAXCH + ch) * MK_ROWS + r0 + rr) * (HD + MK_PAD);
+    float M = -INFINITY;
+    for (int i = 0; i < MK_CW; ++i) M = fmaxf(M, sm.u.att.m[i][rr]);
+    float l = 0.0f;
+    for (int i = 0; i < MK_CW; ++i) {
+      const float cs = sm.u.att.m[i][rr] == -INFINITY ? 0.0f : expf(sm.u.att.m[i][rr] - M);
+      sm.u.att.cs[i][rr] = cs;
+      l += sm.u.att.l[i][rr] * cs;
+    }
+    part[0] = M;
+    part[1] = l;
+  }
+  consumer_sync();
+  for (int idx = ct; idx < nr * HD; idx += MK_CW * 32) {
+    const int rr = idx / HD, e = idx - rr * HD;
+    float v = 0.0f;
+    for (int k = 0; k < MK_CW; ++k) v += sm.u.att.o[k][rr][e] * sm.u.att.cs[k][rr];
+    a.part[(((size_t)kvh * MK_MAXCH + ch) * MK_ROWS + r0 + rr) * (HD + MK_PAD) + MK_PAD + e] = v;
+  }
+  // the CTA that completes the rows' chunks merges them (max, sum, weighted V, online over the
+  // chunks) into the attention output, so the o projection stages x with one plain round of loads
+  const int cnt = kvh * g + r0;
+  consumer_sync();
+  if (ct == 0) {
+    __threadfence();
+    sm.att_last = atomicAdd(&a.rowcnt[cnt], 1u) == (unsigned)(nch - 1);
+  }
+  consumer_sync();
+  if (!sm.att_last) return;
+  __threadfence();
+  for (int idx = ct; idx < nr * HD; idx += MK_CW * 32) {
+    const int rr = idx / HD, e = idx - rr * HD;
+    const float* base = a.part + ((size_t)kvh * MK_MAXCH * MK_ROWS + r0 + rr) * (HD + MK_PAD);
+    float M = -INFINITY, L = 0.0f, v = 0.0f;
+    for (int c0 = 0; c0 < nch; c0 += 4) {
+      float2 ml[4];
+      float ov[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {  // one round of loads per four chunks
+        if (c0 + k < nch) {
+          const float* pc = base + (size_t)(c0 + k) * MK_ROWS * (HD + MK_PAD);
+          ml[k] = __ldcg(reinterpret_cast<const float2*>(pc));
+          ov[k] = __ldcg(pc + MK_PAD + e);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (c0 + k < nch && ml[k].x != -INFINITY) {
+          if (ml[k].x > M) {  // rescale what was merged so far to the new maximum
+            const float rs = M == -INFINITY ? 0.0f : expf(M - ml[k].x);
+            L *= rs;
+            v *= rs;
+            M = ml[k].x;
+          }
+          const float cs = expf(ml[k].x - M);
+          L += ml[k].y * cs;
+          v += cs * ov[k];
+        }
+      }
+    }
+    a.attn_out[(size_t)(kvh * g + r0 + rr) * HD + e] = v / L;
+  }
+  if (ct == 0) a.rowcnt[cnt] = 0u;  // the next layer's items start after the next stage barrier
+}
+
 // One CTA of 9 warps per SM: a sub-partition holds 3 of the warps (16,384 registers each), so a
 // thread gets at most 168 registers.
+template <bool GROUPED>
 __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   MkSmem& sm = *reinterpret_cast<MkSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1023,10 +1167,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) decode_step_kernel(MkArgs a) {
     trace_ev(a, 15 * l + 3);
     trace_ev(a, 15 * l + 4);
     const int g = a.H / a.Hkv;
-    for (int it = blockIdx.x; it < a.H * nch; it += gridDim.x) {  // (query row, chunk) items
-      const int hq = it / nch, ch = it - hq * nch;
-      attn_item(a, sm, l, hq / g, ch, hq % g, ctx, nch);
-      consumer_sync();
+    if (GROUPED && a.H * nch > 2 * (int)gridDim.x) {  // long context: (KV head, chunk) items of g rows
+      for (int it = blockIdx.x; it < a.Hkv * nch; it += gridDim.x) {
+        const int kvh = it / nch, ch = it - kvh * nch;
+        attn_group_item(a, sm, l, kvh, ch, 0, g, ctx, nch);
+        consumer_sync();
+      }
+    } else {
+      for (int it = blockIdx.x; it < a.H * nch; it += gridDim.x) {  // (query row, chunk) items
+        const int hq = it / nch, ch = it - hq * nch;
+        attn_item(a, sm, l, hq / g, ch, hq % g, ctx, nch);
+        consumer_sync();
+      }
     }
     trace_ev(a, 15 * l + 5);
     stage_arrive(a);
@@ -1186,8 +1338,12 @@ int Model::mk_prepare() {
   mk_nslot = kMkDefaultSlots;
   if (const char* v = std::getenv("Q4B_MK_SLOTS")) mk_nslot = std::max(2, std::min(MK_NSLOT, std::atoi(v)));
   const size_t smem = mk_smem_bytes(mk_nslot);
-  e = cudaFuncSetAttribute(decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, decode_step_kernel, MK_THREADS, smem);
+  for (int grouped = 0; grouped < 2 && e == cudaSuccess; ++grouped) {
+    auto kern = grouped ? decode_step_kernel<true> : decode_step_kernel<false>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, MK_THREADS, smem);
+    if (per < 1) break;
+  }
   if (e != cudaSuccess || per < 1)
     return set_error(Q4B_EUNSUPPORTED, "persistent decode: kernel does not fit an SM (%s)", cudaGetErrorString(e));
   mk_ctas = sms;
@@ -1282,7 +1438,10 @@ int Model::mk_forward(const int32_t* toks, int L, float* logits, int32_t* token_
   attr[0].val.cooperative = 1;
   cfgl.attrs = attr;
   cfgl.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfgl, decode_step_kernel, a);
+  // grouped (KV head, chunk) attention items only where the bucket reaches them: a step of this
+  // bucket attends over at most L keys, so H * ceil(L / 128) > 2 * CTAs for some position
+  const bool grouped = (long long)a.H * ((L + MK_KCHUNK - 1) / MK_KCHUNK) > 2LL * mk_ctas;
+  e = grouped ? cudaLaunchKernelEx(&cfgl, decode_step_kernel<true>, a) : cudaLaunchKernelEx(&cfgl, decode_step_kernel<false>, a);
   if (e != cudaSuccess) return set_error(Q4B_ELAUNCH, "persistent decode: launch: %s", cudaGetErrorString(e));
   return check_launch("persistent decode");
 }

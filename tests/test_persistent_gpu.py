@@ -199,3 +199,30 @@ def test_persistent_3b_shape_two_layers():
     assert res[True][0] == res[False][0]
     ref = res[False][1]
     assert np.abs(res[True][1] - ref).max() <= 1e-3 * max(1.0, np.abs(ref).max())
+
+
+def test_persistent_3b_shape_long_context():
+    """The 3B shape with two layers in the 4096 bucket, caches filled with seeded random K and V:
+    short contexts take one attention item per (query row, chunk), long ones (24 heads x more than
+    12 chunks exceed two items per CTA) one per (KV head, chunk) of four rows; tokens and logits
+    of the persistent step equal the per-projection path's at both."""
+    import q4b
+    cfg = dict(q4b.SYNTHETIC["3b"], num_hidden_layers=2)
+    m = q4b.LlamaQ4(None, group=128, max_ctx=4096, vocab_chunk=cfg["vocab_size"], sd=q4b.SyntheticStateDict(cfg),
+                    cfg=cfg, max_chunk=8)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    fill = [torch.randn(c.shape, generator=g, device="cuda").to(torch.float16) for c in m.new_caches()]
+    res = {}
+    for on in (True, False):
+        caches = [c.clone() for c in fill]
+        tok = torch.tensor([[17]], dtype=torch.int32)
+        toks, lgs = [], []
+        with _Persistent(on):
+            for pos in (300, 1700, 2600, 4095):
+                tok, lg = m.step(tok.reshape(1, 1), torch.tensor([pos]), torch.tensor([0]), caches, 4096)
+                toks.append(int(tok))
+                lgs.append(lg.cpu().numpy()[0])
+        res[on] = (toks, np.stack(lgs))
+    assert res[True][0] == res[False][0]
+    ref = res[False][1]
+    assert np.abs(res[True][1] - ref).max() <= 1e-3 * max(1.0, np.abs(ref).max())
