@@ -611,7 +611,10 @@ def run_gemm(args, rank, world, local, dist_mod):
     rows = []
     g = torch.Generator(device=dev)
     g.manual_seed(0)
+    gcfg = json.loads(args.gemm_cfg) if args.gemm_cfg else None
     for s in SHAPES + EXTRA:
+        # the cfg applies to the tcgen05 shapes; the M = 1 rows keep their default plan
+        cfg = gcfg if (gcfg and s.M > 1) else None
         copies = max(1, math.ceil(2 * L2_BYTES / s.min_bytes)) if s.min_bytes < 2 * L2_BYTES else 1
         A = [(torch.rand(s.M, s.K, device=dev, generator=g) * 2 - 1).half() for _ in range(copies)]
         B = [(torch.rand(s.K, s.N, device=dev, generator=g) * 2 - 1).half() for _ in range(copies)]
@@ -619,11 +622,11 @@ def run_gemm(args, rank, world, local, dist_mod):
         stream = torch.cuda.Stream(device=dev)
         with torch.cuda.stream(stream):
             for i in range(copies):
-                ops.gemm_f16(A[i], B[i], out=C[i])
+                ops.gemm_f16(A[i], B[i], out=C[i], cfg=cfg)
             graph = torch.cuda.CUDAGraph()
             graph.capture_begin()
             for i in range(copies):
-                ops.gemm_f16(A[i], B[i], out=C[i])
+                ops.gemm_f16(A[i], B[i], out=C[i], cfg=cfg)
             graph.capture_end()
             for _ in range(args.warmup):
                 graph.replay()
@@ -641,7 +644,8 @@ def run_gemm(args, rank, world, local, dist_mod):
         err = float((C[0].float() - ref).abs().max() / ref.abs().max())
         tf = s.flops / t / 1e12
         attainable = min(pk["bf16_tflops"], s.flops / s.min_bytes * pk["hbm_gbs"] / 1e3)
-        rows.append({"id": s.id, "shape": s.name, "M": s.M, "N": s.N, "K": s.K, "us": round(t * 1e6, 2),
+        rows.append({"id": s.id, "shape": s.name, "M": s.M, "N": s.N, "K": s.K, "plan": gemm_plan(s.M, s.N, s.K, cfg),
+                     "us": round(t * 1e6, 2),
                      "TFLOP_s": round(tf, 1), "attainable_TFLOP_s": round(attainable, 1),
                      "frac_attainable": round(tf / attainable, 4), "bound": "tensor" if attainable >= pk["bf16_tflops"]
                      else "hbm", "rel_err": err, "copies": copies})
@@ -655,7 +659,7 @@ def run_gemm(args, rank, world, local, dist_mod):
             "unit": "fraction", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16 in/out, fp32 accumulate",
             "data": "synthetic U(-1, 1)",
-            "config": {"workload": "fp16 GEMM sweep (BASELINE config 2) + M=1 rows", "layout": "NN",
+            "config": {"workload": "fp16 GEMM sweep (BASELINE config 2) + M=1 rows", "layout": "NN", "cfg": gcfg,
                        "parallelism": f"replicas x{world}", "l2": "operand copies > 2x L2 per shape where needed"},
             "roofline": {"bound": "tensor", "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "peak_source": pk["source"],
                          "achieved": max(r["TFLOP_s"] for r in main),
@@ -664,6 +668,18 @@ def run_gemm(args, rank, world, local, dist_mod):
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_gemm_baseline()
     return line
+
+
+def gemm_plan(M, N, K, cfg=None):
+    """The schedule q4b_gemm_f16 runs for an NN problem (q4b_gemm_f16_plan), as a candidate string."""
+    import ctypes
+
+    from q4b._lib import GemmCfg, lib
+    out = GemmCfg()
+    cp = ctypes.byref(GemmCfg(**cfg)) if cfg else None
+    if lib().q4b_gemm_f16_plan(M, N, K, b"N", b"N", cp, ctypes.byref(out)) != 0:
+        return None
+    return f"{out.kernel}:bn={out.bn},stages={out.stages},split={out.split}"
 
 
 def cpu_gemm_baseline(budget_s=10.0):
@@ -1094,6 +1110,7 @@ def main():
     ap.add_argument("--no-gemv", action="store_true", help="decode: skip the config-1 GEMV sub-measurement")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gemv-cfg", default=None, help='JSON q4b_linear_cfg, e.g. {"warps":4,"tiles":2}')
+    ap.add_argument("--gemm-cfg", default=None, help='gemm: JSON q4b_gemm_cfg for every shape, e.g. {"kernel":3}')
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3 and args.workload != "profile":

@@ -124,10 +124,13 @@ int q4b_q4_linear_noalloc(const int32_t* qweight, const uint16_t* scales, int gr
 /* Kernel choice and schedule of q4b_gemm_f16 (the CUDA counterpart of gemm/schedule.py:43-103's
  * Schedule; all zero = the built-in default for the shape). */
 typedef struct q4b_gemm_cfg {
-  int kernel; /* 0 = default, 1 = tcgen05 (TMA + TMEM accumulator), 2 = CUDA-core 64x64 tiles */
-  int bn;     /* kernel 1: output tile width 64 | 128 | 256 (tile height is 128); 0 = auto */
-  int stages; /* kernel 1: shared-memory ring depth, 2 .. as many as fit in 200 KB; 0 = max */
-  int split;  /* kernel 1: k splits (fp32 partials in the workspace); 0 = auto, 1 = none */
+  int kernel; /* 0 = default, 1 = tcgen05 (TMA + TMEM accumulator), 2 = CUDA-core 64x64 tiles,
+                 3 = tcgen05 persistent stream-K (one CTA run of equal (tile, 64-k) units per SM
+                 slot, two TMEM accumulators, part-tiles added in k order by the last contributor) */
+  int bn;     /* kernels 1, 3: output tile width 64 | 128 | 256 (tile height is 128); 0 = auto */
+  int stages; /* kernels 1, 3: shared-memory ring depth, 2 .. as many as fit in 200 KB; 0 = max */
+  int split;  /* kernel 1: k splits (fp32 partials in the workspace); 0 = auto, 1 = none.
+                 kernel 3: 0 or 1 (it balances k itself) */
 } q4b_gemm_cfg;
 
 /* Bytes of workspace q4b_gemm_f16 needs (0 if none; -1 if the problem or cfg is invalid, with

@@ -11,6 +11,8 @@
 // then read TMEM (32 lanes each) and store fp16. Split-K (grid.z) writes fp32 partials to the
 // workspace and the last CTA of a tile adds them in split order (deterministic) before storing.
 // Kernel 2 (CUDA cores): 64 x 64 tiles for any size or alignment TMA cannot describe.
+// Kernel 3 (tcgen05, persistent stream-K; opt-in): described at the kernel. Measured slower than
+// kernel 1's searched schedules on every config-2 shape (one CTA's MMA stream per SM against two).
 #include <mutex>
 
 #include "tc.cuh"
@@ -29,6 +31,7 @@ struct GemmArgs {
   int M, N, K;
   int kt;      // number of 64-wide k steps
   int split;   // k splits (grid.z)
+  int tm, tn;  // kernel 3: output tiles along M and N
   int vec;     // C rows keep 16-byte alignment (n % 8 == 0, aligned base): vector stores
   __half* C;
   float* partial;       // split > 1: [split][tiles][128][BN] fp32
@@ -223,6 +226,265 @@ __global__ void __launch_bounds__(128, 1)
   griddep_launch_dependents();
 }
 
+// ---- kernel 3: tcgen05, persistent stream-K ---------------------------------------------------
+//
+// T = tiles_m x tiles_n output tiles of 128 x BN make U = T x kt units (one 64-wide k step of one
+// tile). CTA c of G takes the units [c U / G, (c + 1) U / G) in tile-major order, so every CTA
+// streams the same number of operand tiles whatever T is: no partly filled last wave, and no k
+// split chosen by hand. A CTA's run cuts into segments, one per tile it touches: the middle ones
+// are whole tiles, stored from TMEM directly; only the first and the last can cover part of a
+// tile. Warp 0 (one thread) keeps the TMA ring full across segment boundaries; warp 1 (one thread)
+// issues segment s's MMAs into TMEM accumulator s % 2 and commits it; warps 2-5 (TMEM lane
+// quadrants 2, 3, 0, 1) drain the other accumulator meanwhile, so one tile's epilogue runs under
+// the next tile's main loop. A part-tile goes to the CTA's partial slot (2c for its first segment,
+// 2c + 1 for its last) in the workspace; the last of a tile's contributors to arrive (arrival
+// counter) adds the slots in k order and stores the tile, so results are deterministic.
+constexpr int kSkThreads = 192;
+
+// the CTA whose run of units [c U / G, (c + 1) U / G) contains unit u (G <= U: no run is empty)
+__device__ __forceinline__ int sk_cta_of(long long u, long long U, int G) {
+  return (int)(((u + 1) * G + U - 1) / U) - 1;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kSkThreads, 1)
+    gemm_f16_sk(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, GemmArgs p,
+                int stages) {
+  using T = GemmTile<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full[T::MAX_STAGES], empty[T::MAX_STAGES], acc_full[2], acc_empty[2], mma_done;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_last, s_issued, s_consumed;
+  __shared__ volatile int s_fail;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const long long U = (long long)p.tm * p.tn * p.kt;
+  const long long u0 = U * blockIdx.x / G, u1 = U * (blockIdx.x + 1) / G;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(&mma_done, 1);
+    s_fail = 0;
+    s_issued = 0;
+    s_consumed = 0;
+    fence_mbar_init();
+    tma_prefetch_map(&ta);
+    tma_prefetch_map(&tb);
+  }
+  if (warp == 1) tmem_alloc(&s_tmem, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
+
+  griddep_wait();  // A / B may be written by the previous kernel on the stream
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer: the run's operand tiles, in unit order, through the ring (tile, k step, ring
+      // slot and round advance by increments: no divisions on this thread's per-unit path)
+      const int t0 = (int)(u0 / p.kt);
+      int k = (int)(u0 - (long long)t0 * p.kt), im = t0 % p.tm, in = t0 / p.tm;
+      int s = 0, r = 0;
+      for (long long u = u0; u < u1; ++u) {
+        if (s_fail || (r > 0 && !mbar_wait_bounded(&empty[s], (r - 1) & 1, kWaitLimitNs))) {
+          s_fail = 1;
+          break;
+        }
+        const int m0 = im * kBM, n0 = in * BN;
+        mbar_arrive_expect_tx(&full[s], T::STAGE);
+        uint8_t* a = smem + s * T::STAGE;
+        uint8_t* b = a + T::A_BYTES;
+        const int kx = k * kBK;
+        if constexpr (!A_MN) {
+          tma_load_2d(a, &ta, kx, m0, &full[s]);
+        } else {
+          tma_load_2d(a, &ta, m0, kx, &full[s]);
+          tma_load_2d(a + 8192, &ta, m0 + 64, kx, &full[s]);
+        }
+        if constexpr (!B_MN) {
+          tma_load_2d(b, &tb, kx, n0, &full[s]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 8192, &tb, n0 + 64 * j, kx, &full[s]);
+        }
+        s_issued = (int)(u - u0) + 1;
+        if (++k == p.kt) {
+          k = 0;
+          if (++im == p.tm) im = 0, ++in;
+        }
+        if (++s == stages) s = 0, ++r;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issue: segment seg accumulates in TMEM columns [BN (seg % 2), BN (seg % 2 + 1))
+      constexpr uint32_t idesc = idesc_f16_f32(kBM, BN, A_MN, B_MN);
+      int i = 0, seg = 0, s = 0, r = 0;
+      bool ok = true;
+      for (long long u = u0; u < u1 && ok; ++seg) {
+        const int t = (int)(u / p.kt), k0 = (int)(u - (long long)t * p.kt);
+        const int k1 = (int)min((long long)p.kt, (long long)k0 + (u1 - u));
+        const int b = seg & 1;
+        if (seg >= 2 && !mbar_wait_bounded(&acc_empty[b], ((seg >> 1) - 1) & 1, kWaitLimitNs)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * BN);
+        for (int k = k0; k < k1; ++k, ++i) {
+          if (s_fail || !mbar_wait_bounded(&full[s], r & 1, kWaitLimitNs)) {
+            ok = false;
+            break;
+          }
+          s_consumed = i + 1;
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * T::STAGE), bb = a + T::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = A_MN ? sw128_desc(a + kk * 2048, 8192, 1024) : sw128_desc(a + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sw128_desc(bb + kk * 2048, 8192, 1024) : sw128_desc(bb + kk * 32, 16, 1024);
+            tc_mma_f16(d, ad, bd, idesc, (k != k0 || kk != 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[s]);  // the slot is free once these MMAs have read it
+          if (++s == stages) s = 0, ++r;
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[b]);
+        u += k1 - k0;
+      }
+      if (!ok) s_fail = 1;
+      tc_commit(&mma_done);  // every MMA issued above has completed
+    }
+    __syncwarp();
+  } else {
+    // epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31, one output row per thread
+    const int q = warp & 3;
+    const int rloc = q * 32 + lane;
+    const bool vec = p.vec != 0;
+    int seg = 0;
+    for (long long u = u0; u < u1; ++seg) {
+      const int t = (int)(u / p.kt), k0 = (int)(u - (long long)t * p.kt);
+      const int k1 = (int)min((long long)p.kt, (long long)k0 + (u1 - u));
+      const bool whole = k0 == 0 && k1 == p.kt;
+      const int b = seg & 1;
+      // lane 0 waits; the warp takes one decision (tcgen05.ld below is warp-collective)
+      int okw = 0;
+      if (lane == 0) {
+        okw = !s_fail && mbar_wait_bounded(&acc_full[b], (seg >> 1) & 1, kWaitLimitNs);
+        if (!okw) s_fail = 1;
+      }
+      const bool ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+      tc_fence_after();
+      const int m0 = (t % p.tm) * kBM, n0 = (t / p.tm) * BN;
+      const int row = m0 + rloc;
+      const uint32_t trow = tmem + (uint32_t)(b * BN) + ((uint32_t)(q * 32) << 16);
+      if (ok) {
+        if (whole) {
+          __half* crow = p.C + (size_t)row * p.N;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32(trow + c * 32, r);
+            if (row < p.M && n0 + c * 32 < p.N)
+              store_row_f16(crow, n0 + c * 32, 32, p.N, reinterpret_cast<float*>(r), vec);
+          }
+        } else {
+          const int slot = 2 * (int)blockIdx.x + (u == u0 ? 0 : 1);
+          float* mine = p.partial + ((size_t)slot * kBM + rloc) * BN;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32(trow + c * 32, r);
+            float4* dst = reinterpret_cast<float4*>(mine + c * 32);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              dst[e] = make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
+                                   __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);  // the MMA thread may refill this accumulator
+      if (!whole) {
+        // arrive on the tile's counter (after a failure too, so that it ends at zero); the last
+        // contributor adds every contributor's slot in k order
+        const int c0 = sk_cta_of((long long)t * p.kt, U, G), c1 = sk_cta_of((long long)(t + 1) * p.kt - 1, U, G);
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (warp == 2 && lane == 0) s_last = atomicAdd(&p.counters[t], 1u) == (unsigned)(c1 - c0);
+        named_bar_sync(1, 128);
+        if (s_last) {
+          __threadfence();
+          if (!s_fail) {
+            __half* crow = p.C + (size_t)row * p.N;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+              float v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+              for (int cb = c0; cb <= c1; cb += 4) {  // four contributors' loads in flight, then their sums
+                float4 x[4][8];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const int cc = min(cb + j, c1);
+                  const int first_tile = (int)((U * cc / G) / p.kt);
+                  const int slot = 2 * cc + (t == first_tile ? 0 : 1);
+                  const float4* src =
+                      reinterpret_cast<const float4*>(p.partial + ((size_t)slot * kBM + rloc) * BN + c * 32);
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) x[j][e] = __ldcg(src + e);
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  if (cb + j > c1) break;
+#pragma unroll
+                  for (int e = 0; e < 8; ++e) {
+                    v[4 * e] += x[j][e].x;
+                    v[4 * e + 1] += x[j][e].y;
+                    v[4 * e + 2] += x[j][e].z;
+                    v[4 * e + 3] += x[j][e].w;
+                  }
+                }
+              }
+              if (row < p.M && n0 + c * 32 < p.N) store_row_f16(crow, n0 + c * 32, 32, p.N, v, vec);
+            }
+          }
+          if (warp == 2 && lane == 0) p.counters[t] = 0u;  // ready for the next call (graph replays)
+        }
+      }
+      u += k1 - k0;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (s_fail && threadIdx.x == 0) {
+    // a wait gave up: the copies still in flight land before the CTA exits (bounded)
+    for (int i = s_consumed; i < s_issued; ++i)
+      mbar_wait_bounded(&full[i % stages], (uint32_t)((i / stages) & 1), kWaitLimitNs);
+    atomicOr(&g_gemm_status, kStatusTimeout);
+  }
+  if (warp == 1) {
+    if (lane == 0) mbar_wait_bounded(&mma_done, 0, kWaitLimitNs);
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 2 * BN);
+  }
+  griddep_launch_dependents();
+}
+
 // ---- kernel 2: CUDA-core tiles, any layout and alignment ----------------------------------------
 
 template <bool A_T, bool B_T>
@@ -277,8 +539,20 @@ __global__ void __launch_bounds__(256) gemm_f16_simt(const __half* __restrict__ 
 struct GemmPlan {
   int kernel = 1, bn = 128, stages = 4, split = 1;
   int tiles_m = 0, tiles_n = 0;
+  int ctas = 0;  // kernel 3: persistent CTAs
   size_t smem = 0, ws = 0;
 };
+
+// SMs of the current device (148 on a B200; also the planning answer without a device)
+int device_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      sms <= 0) {
+    cudaGetLastError();
+    return 148;
+  }
+  return sms;
+}
 
 bool tma_ok(int M, int N, int K, char la, char lb) {
   const long long lda = la == 'N' ? K : M, ldb = lb == 'N' ? N : K;
@@ -303,15 +577,44 @@ constexpr TunedSchedule kTuned[] = {
     {2048, 3072, 8192, 'N', 'N', 256, 2, 1},  // B8 down_m2048: 922 TFLOP/s
 };
 
+// kernel 3: tile width (cfg or 256 once there are 8 row tiles, else 128), the deepest ring that fits,
+// and one CTA per SM times the CTAs an SM holds (shared memory; 2 BN TMEM columns each, of 512).
+// Workspace: the per-tile counters and two partial slots [128][BN] fp32 per CTA.
+int plan_sk(int M, int N, int kt, int tm, const q4b_gemm_cfg* cfg, GemmPlan& pl) {
+  (void)M;
+  int bn = cfg->bn ? cfg->bn : (tm >= 8 ? 256 : 128);
+  if (bn != 64 && bn != 128 && bn != 256) return set_error(Q4B_EINVAL, "gemm_f16: bn is 64, 128 or 256");
+  if (cfg->split > 1) return set_error(Q4B_EINVAL, "gemm_f16: kernel 3 balances k itself (split 0 or 1)");
+  const int stage = (kBM + bn) * kBK * 2;
+  const int max_stages = kGemmSmemBudget / stage;
+  const int stages = cfg->stages ? cfg->stages : max_stages;
+  if (stages < 2 || stages > max_stages)
+    return set_error(Q4B_EINVAL, "gemm_f16: stages must be in [2, %d] for bn %d", max_stages, bn);
+  const int tn = (N + bn - 1) / bn;
+  const long long tiles = (long long)tm * tn;
+  if (tiles * 4 > (long long)kGemmCounterBytes) return set_error(Q4B_EUNSUPPORTED, "gemm_f16: too many tiles");
+  pl.kernel = 3;
+  pl.bn = bn;
+  pl.stages = stages;
+  pl.split = 1;
+  pl.tiles_m = tm;
+  pl.tiles_n = tn;
+  pl.smem = (size_t)stages * stage + 1024;
+  const int occ = std::max(1, std::min(512 / (2 * bn), (int)(233472 / (pl.smem + 2048))));
+  pl.ctas = (int)std::min<long long>(tiles * kt, (long long)device_sms() * occ);
+  pl.ws = kGemmCounterBytes + (size_t)2 * pl.ctas * kBM * bn * 4;
+  return Q4B_OK;
+}
+
 int plan_gemm(int M, int N, int K, char la, char lb, const q4b_gemm_cfg* cfg, GemmPlan& pl) {
   if (M <= 0 || N <= 0 || K <= 0) return set_error(Q4B_EINVAL, "gemm_f16: sizes must be positive");
   if ((la != 'N' && la != 'T') || (lb != 'N' && lb != 'T'))
     return set_error(Q4B_EINVAL, "gemm_f16: layouts are 'N' or 'T'");
   const int want = cfg ? cfg->kernel : 0;
-  if (want != 0 && want != 1 && want != 2) return set_error(Q4B_EINVAL, "gemm_f16: kernel is 0, 1 or 2");
+  if (want < 0 || want > 3) return set_error(Q4B_EINVAL, "gemm_f16: kernel is 0, 1, 2 or 3");
   const bool tma = tma_ok(M, N, K, la, lb);
-  if (want == 1 && !tma)
-    return set_error(Q4B_EUNSUPPORTED, "gemm_f16: the tcgen05 kernel needs row pitches that are multiples of 8");
+  if ((want == 1 || want == 3) && !tma)
+    return set_error(Q4B_EUNSUPPORTED, "gemm_f16: the tcgen05 kernels need row pitches that are multiples of 8");
   if (want == 2 || !tma) {
     pl.kernel = 2;
     pl.split = 1;
@@ -319,9 +622,10 @@ int plan_gemm(int M, int N, int K, char la, char lb, const q4b_gemm_cfg* cfg, Ge
     pl.ws = 0;
     return Q4B_OK;
   }
-  pl.kernel = 1;
   const int kt = (K + kBK - 1) / kBK;
   const int tm = (M + kBM - 1) / kBM;
+  if (want == 3) return plan_sk(M, N, kt, tm, cfg, pl);
+  pl.kernel = 1;
   q4b_gemm_cfg tuned = {};
   if (!cfg || (!cfg->kernel && !cfg->bn && !cfg->stages && !cfg->split)) {
     for (const TunedSchedule& t : kTuned)
@@ -393,6 +697,25 @@ cudaError_t launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
   return launch_pdl(kern, dim3(pl.tiles_m, pl.tiles_n, pl.split), dim3(128), pl.smem, st, ta, tb, a, pl.stages);
 }
 
+template <int BN, bool A_MN, bool B_MN>
+cudaError_t launch_sk(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, const GemmPlan& pl,
+                      cudaStream_t st) {
+  auto kern = gemm_f16_sk<BN, A_MN, B_MN>;
+  static std::atomic<unsigned long long> done;  // per device: the smem attribute is set once
+  const cudaError_t e = set_max_dynamic_smem(kern, kGemmSmemBudget + 1024, done);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(kern, dim3(pl.ctas), dim3(kSkThreads), pl.smem, st, ta, tb, a, pl.stages);
+}
+
+template <int BN>
+cudaError_t launch_sk_bn(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                         const GemmPlan& pl, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_sk<BN, false, false>(ta, tb, a, pl, st);
+  if (!a_mn && b_mn) return launch_sk<BN, false, true>(ta, tb, a, pl, st);
+  if (a_mn && !b_mn) return launch_sk<BN, true, false>(ta, tb, a, pl, st);
+  return launch_sk<BN, true, true>(ta, tb, a, pl, st);
+}
+
 template <int BN>
 cudaError_t launch_tc_bn(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                          const GemmPlan& pl, cudaStream_t st) {
@@ -458,7 +781,8 @@ extern "C" int q4b_gemm_f16_plan(int M, int N, int K, char la, char lb, const q4
   GemmPlan pl;
   const int rc = plan_gemm(M, N, K, la, lb, cfg, pl);
   if (rc) return rc;
-  *out = {pl.kernel, pl.kernel == 1 ? pl.bn : 0, pl.kernel == 1 ? pl.stages : 0, pl.split};
+  const bool tc = pl.kernel == 1 || pl.kernel == 3;
+  *out = {pl.kernel, tc ? pl.bn : 0, tc ? pl.stages : 0, pl.split};
   return Q4B_OK;
 }
 
@@ -496,13 +820,21 @@ extern "C" int q4b_gemm_f16(const void* A, const void* B, void* C, int M, int N,
   a.K = K;
   a.kt = (K + kBK - 1) / kBK;
   a.split = pl.split;
+  a.tm = pl.tiles_m;
+  a.tn = pl.tiles_n;
   a.vec = (N % 8 == 0) && aligned(C, 16);
   a.C = static_cast<__half*>(C);
   a.counters = pl.ws ? static_cast<unsigned*>(workspace) : nullptr;
   a.partial = pl.ws ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kGemmCounterBytes) : nullptr;
-  cudaError_t e = pl.bn == 256 ? launch_tc_bn<256>(a_mn, b_mn, ta, tb, a, pl, st)
-                  : pl.bn == 128 ? launch_tc_bn<128>(a_mn, b_mn, ta, tb, a, pl, st)
-                                 : launch_tc_bn<64>(a_mn, b_mn, ta, tb, a, pl, st);
+  cudaError_t e;
+  if (pl.kernel == 3)
+    e = pl.bn == 256 ? launch_sk_bn<256>(a_mn, b_mn, ta, tb, a, pl, st)
+        : pl.bn == 128 ? launch_sk_bn<128>(a_mn, b_mn, ta, tb, a, pl, st)
+                       : launch_sk_bn<64>(a_mn, b_mn, ta, tb, a, pl, st);
+  else
+    e = pl.bn == 256 ? launch_tc_bn<256>(a_mn, b_mn, ta, tb, a, pl, st)
+        : pl.bn == 128 ? launch_tc_bn<128>(a_mn, b_mn, ta, tb, a, pl, st)
+                       : launch_tc_bn<64>(a_mn, b_mn, ta, tb, a, pl, st);
   if (e != cudaSuccess) return set_error(Q4B_ELAUNCH, "gemm_f16 (tcgen05): %s", cudaGetErrorString(e));
   return Q4B_OK;
 }

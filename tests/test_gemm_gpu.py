@@ -85,7 +85,8 @@ def test_ragged(M, N, K, layout):
 # the same product)
 CFGS = [dict(kernel=2), dict(kernel=1, bn=64), dict(kernel=1, bn=128), dict(kernel=1, bn=256),
         dict(kernel=1, bn=64, stages=2), dict(kernel=1, bn=256, stages=2), dict(kernel=1, bn=128, split=3),
-        dict(kernel=1, bn=64, split=16), dict(kernel=1, bn=256, split=2, stages=3), dict(kernel=1, bn=128, stages=5)]
+        dict(kernel=1, bn=64, split=16), dict(kernel=1, bn=256, split=2, stages=3), dict(kernel=1, bn=128, stages=5),
+        dict(kernel=3), dict(kernel=3, bn=64), dict(kernel=3, bn=256), dict(kernel=3, bn=128, stages=3)]
 
 
 @pytest.mark.parametrize("cfg", CFGS, ids=[str(c) for c in CFGS])
@@ -105,6 +106,23 @@ def test_split_k_is_deterministic():
     assert torch.equal(c1, c2)
 
 
+# kernel 3 (stream-K): runs of units that cover whole tiles in the middle and part-tiles at both ends
+# (4096 x 4096 x 128: ~7 units of 2-step tiles per CTA), every tile split over several CTAs (the
+# M = 128 projection), and long K (8192)
+SK_SHAPES = [(4096, 4096, 128), (128, 5120, 3072), (2048, 3072, 8192), (136, 200, 4160)]
+
+
+@pytest.mark.parametrize("M,N,K", SK_SHAPES, ids=[f"{m}x{n}x{k}" for m, n, k in SK_SHAPES])
+def test_stream_k(M, N, K):
+    import q4b
+    a, b, ref = _device_ref(M, N, K, "N", "N", seed=M + 11 * N + K)
+    c1 = q4b.gemm_f16(a, b, cfg=dict(kernel=3))
+    c2 = q4b.gemm_f16(a, b, cfg=dict(kernel=3))
+    torch.cuda.synchronize()
+    assert _rel(c1, ref) <= TOL
+    assert torch.equal(c1, c2)  # the part-tiles are added in k order: deterministic
+
+
 def test_rejects_bad_config():
     import q4b
     a = torch.zeros(128, 128, dtype=torch.float16, device="cuda:0")
@@ -114,6 +132,8 @@ def test_rejects_bad_config():
         q4b.gemm_f16(a, a, cfg=dict(kernel=1, stages=1))
     with pytest.raises(q4b.Q4BError):
         q4b.gemm_f16(a, a, cfg=dict(kernel=1, split=3))  # K = 128 has two 64-wide steps
+    with pytest.raises(q4b.Q4BError):
+        q4b.gemm_f16(a, a, cfg=dict(kernel=3, split=2))  # kernel 3 balances k itself
 
 
 def test_no_timeouts():
