@@ -247,9 +247,9 @@ __device__ __forceinline__ int sk_cta_of(long long u, long long U, int G) {
 }
 
 template <int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kSkThreads, 1)
+__global__ void __launch_bounds__(kSkThreads, 2)
     gemm_f16_sk(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb, GemmArgs p,
-                int stages) {
+                int stages, int nacc) {
   using T = GemmTile<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     tma_prefetch_map(&ta);
     tma_prefetch_map(&tb);
   }
-  if (warp == 1) tmem_alloc(&s_tmem, 2 * BN);
+  if (warp == 1) tmem_alloc(&s_tmem, nacc * BN);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -335,8 +335,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       for (long long u = u0; u < u1 && ok; ++seg) {
         const int t = (int)(u / p.kt), k0 = (int)(u - (long long)t * p.kt);
         const int k1 = (int)min((long long)p.kt, (long long)k0 + (u1 - u));
-        const int b = seg & 1;
-        if (seg >= 2 && !mbar_wait_bounded(&acc_empty[b], ((seg >> 1) - 1) & 1, kWaitLimitNs)) {
+        const int b = nacc == 2 ? seg & 1 : 0, use = nacc == 2 ? seg >> 1 : seg;
+        if (use > 0 && !mbar_wait_bounded(&acc_empty[b], (use - 1) & 1, kWaitLimitNs)) {
           ok = false;
           break;
         }
@@ -377,11 +377,11 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       const int t = (int)(u / p.kt), k0 = (int)(u - (long long)t * p.kt);
       const int k1 = (int)min((long long)p.kt, (long long)k0 + (u1 - u));
       const bool whole = k0 == 0 && k1 == p.kt;
-      const int b = seg & 1;
+      const int b = nacc == 2 ? seg & 1 : 0, use = nacc == 2 ? seg >> 1 : seg;
       // lane 0 waits; the warp takes one decision (tcgen05.ld below is warp-collective)
       int okw = 0;
       if (lane == 0) {
-        okw = !s_fail && mbar_wait_bounded(&acc_full[b], (seg >> 1) & 1, kWaitLimitNs);
+        okw = !s_fail && mbar_wait_bounded(&acc_full[b], use & 1, kWaitLimitNs);
         if (!okw) s_fail = 1;
       }
       const bool ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
@@ -480,7 +480,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     if (lane == 0) mbar_wait_bounded(&mma_done, 0, kWaitLimitNs);
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * BN);
+    tmem_dealloc(tmem, nacc * BN);
   }
   griddep_launch_dependents();
 }
@@ -540,6 +540,7 @@ struct GemmPlan {
   int kernel = 1, bn = 128, stages = 4, split = 1;
   int tiles_m = 0, tiles_n = 0;
   int ctas = 0;  // kernel 3: persistent CTAs
+  int nacc = 2;  // kernel 3: TMEM accumulators per CTA
   size_t smem = 0, ws = 0;
 };
 
@@ -577,9 +578,11 @@ constexpr TunedSchedule kTuned[] = {
     {2048, 3072, 8192, 'N', 'N', 256, 2, 1},  // B8 down_m2048: 922 TFLOP/s
 };
 
-// kernel 3: tile width (cfg or 256 once there are 8 row tiles, else 128), the deepest ring that fits,
-// and one CTA per SM times the CTAs an SM holds (shared memory; 2 BN TMEM columns each, of 512).
-// Workspace: the per-tile counters and two partial slots [128][BN] fp32 per CTA.
+// kernel 3: tile width (cfg or 256 once there are 8 row tiles, else 128) and ring depth (cfg, or the
+// deepest that fits: one CTA per SM alternating two TMEM accumulators). A ring shallow enough for two
+// CTAs on an SM (register cap 170 per thread) gives each one accumulator, the other CTA supplying the
+// overlap (measured slower: B5 142 us against 95 us alone). Grid: SMs x CTAs per SM, at most one CTA
+// per unit. Workspace: the per-tile counters and two partial slots [128][BN] fp32 per CTA.
 int plan_sk(int M, int N, int kt, int tm, const q4b_gemm_cfg* cfg, GemmPlan& pl) {
   (void)M;
   int bn = cfg->bn ? cfg->bn : (tm >= 8 ? 256 : 128);
@@ -587,6 +590,7 @@ int plan_sk(int M, int N, int kt, int tm, const q4b_gemm_cfg* cfg, GemmPlan& pl)
   if (cfg->split > 1) return set_error(Q4B_EINVAL, "gemm_f16: kernel 3 balances k itself (split 0 or 1)");
   const int stage = (kBM + bn) * kBK * 2;
   const int max_stages = kGemmSmemBudget / stage;
+  const auto per_sm = [](size_t smem) { return (int)(233472 / (smem + 2048)); };  // 228 KB an SM, 1 KB reserved per CTA
   const int stages = cfg->stages ? cfg->stages : max_stages;
   if (stages < 2 || stages > max_stages)
     return set_error(Q4B_EINVAL, "gemm_f16: stages must be in [2, %d] for bn %d", max_stages, bn);
@@ -600,7 +604,8 @@ int plan_sk(int M, int N, int kt, int tm, const q4b_gemm_cfg* cfg, GemmPlan& pl)
   pl.tiles_m = tm;
   pl.tiles_n = tn;
   pl.smem = (size_t)stages * stage + 1024;
-  const int occ = std::max(1, std::min(512 / (2 * bn), (int)(233472 / (pl.smem + 2048))));
+  const int occ = std::max(1, std::min(2, per_sm(pl.smem)));
+  pl.nacc = occ >= 2 ? 1 : 2;
   pl.ctas = (int)std::min<long long>(tiles * kt, (long long)device_sms() * occ);
   pl.ws = kGemmCounterBytes + (size_t)2 * pl.ctas * kBM * bn * 4;
   return Q4B_OK;
@@ -704,7 +709,7 @@ cudaError_t launch_sk(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
   static std::atomic<unsigned long long> done;  // per device: the smem attribute is set once
   const cudaError_t e = set_max_dynamic_smem(kern, kGemmSmemBudget + 1024, done);
   if (e != cudaSuccess) return e;
-  return launch_pdl(kern, dim3(pl.ctas), dim3(kSkThreads), pl.smem, st, ta, tb, a, pl.stages);
+  return launch_pdl(kern, dim3(pl.ctas), dim3(kSkThreads), pl.smem, st, ta, tb, a, pl.stages, pl.nacc);
 }
 
 template <int BN>
