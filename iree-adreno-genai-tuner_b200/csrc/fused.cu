@@ -404,6 +404,138 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
   }
 }
 
+// Tiled prefill form: one CTA per (KV head, block of kPfRows query rows) takes all g heads of the
+// group, NQW = g kPfRows / 4 query vectors per warp. Each 32-key tile of K and V is staged once per
+// CTA in shared memory and serves every query vector of the block (the one-row form re-reads a KV
+// head's keys once per query row and head: g C times per chunk). Per tile lane j holds key kb + j:
+// its K row is read from shared memory (rows padded by one word, so the 32 lanes hit 32 banks) and
+// scored against the warp's query vectors in the same dimension order as the one-row form; then an
+// online softmax per query vector and P V with lane l owning dimensions EPL l .. EPL l + EPL - 1.
+// fp32 throughout, fp16 K / V as stored.
+constexpr int kPfRows = 4;
+
+template <int EPL, int NQW>
+__global__ void __launch_bounds__(128) attn_prefill_tiled_kernel(AttnArgs a) {
+  constexpr int HD = EPL * 32, HW = HD / 2 + 1, NQ = 4 * NQW;  // HW: 32-bit words per staged K row
+  __shared__ __align__(16) float s_q[NQ][HD];
+  __shared__ uint32_t s_k[32 * HW];
+  __shared__ __align__(16) __half s_v[32][HD];
+  const int kvh = blockIdx.x, c0 = blockIdx.y * kPfRows;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  griddep_launch_dependents();
+  griddep_wait();
+  const int g = a.H / a.Hkv;  // NQ / kPfRows
+  const int start = *a.pos0;
+  // query vector qi: row c0 + qi / g of the chunk, head kvh g + qi % g
+  for (int i = threadIdx.x; i < NQ * HD; i += blockDim.x) {
+    const int qi = i / HD, e = i - qi * HD, c = c0 + qi / g;
+    s_q[qi][e] = c < a.C ? a.q[((size_t)c * a.H + kvh * g + qi % g) * HD + e] : 0.0f;
+  }
+  // this warp's query vectors qi = warp + 4 t and the keys each sees (0 for rows past the chunk)
+  int lim[NQW];
+#pragma unroll
+  for (int t = 0; t < NQW; ++t) {
+    const int c = c0 + (warp + 4 * t) / g;
+    lim[t] = c < a.C ? min(a.L, start + c + 1) : 0;
+  }
+  const int nk = min(a.L, start + min(c0 + kPfRows, a.C));  // keys any row of the block sees
+  float o[NQW][EPL], m[NQW], l[NQW];
+#pragma unroll
+  for (int t = 0; t < NQW; ++t) {
+    m[t] = -INFINITY;
+    l[t] = 0.0f;
+#pragma unroll
+    for (int e = 0; e < EPL; ++e) o[t][e] = 0.0f;
+  }
+  const size_t kv_stride = (size_t)a.Hkv * HD;
+  const __half* kbase = a.k_cache + (size_t)kvh * HD;
+  const __half* vbase = a.v_cache + (size_t)kvh * HD;
+  for (int kb = 0; kb < nk; kb += 32) {
+    __syncthreads();  // the previous tile is consumed (the first time: s_q is written)
+    // stage K / V rows kb .. kb + 31 (rows past nk repeat row nk - 1: finite, weighted 0)
+    for (int i = threadIdx.x; i < 32 * (HD / 8); i += blockDim.x) {
+      const int r = i / (HD / 8), u = i - r * (HD / 8);
+      const size_t row = (size_t)min(kb + r, nk - 1) * kv_stride + u * 8;
+      const uint4 kv = *reinterpret_cast<const uint4*>(kbase + row);
+      const uint4 vv = *reinterpret_cast<const uint4*>(vbase + row);
+      uint32_t* kw = s_k + r * HW + u * 4;
+      kw[0] = kv.x, kw[1] = kv.y, kw[2] = kv.z, kw[3] = kv.w;
+      *reinterpret_cast<uint4*>(&s_v[r][u * 8]) = vv;
+    }
+    __syncthreads();
+    float s[NQW];
+#pragma unroll
+    for (int t = 0; t < NQW; ++t) s[t] = 0.0f;
+    const uint32_t* kr = s_k + lane * HW;
+#pragma unroll 8
+    for (int u = 0; u < HD / 4; ++u) {  // dimensions 4u .. 4u + 3 of key kb + lane
+      const uint32_t w0 = kr[2 * u], w1 = kr[2 * u + 1];
+      const float2 k01 = __half22float2(*reinterpret_cast<const __half2*>(&w0));
+      const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&w1));
+#pragma unroll
+      for (int t = 0; t < NQW; ++t) {
+        const float4 qv = *reinterpret_cast<const float4*>(&s_q[warp + 4 * t][4 * u]);
+        s[t] = fmaf(qv.x, k01.x, s[t]);
+        s[t] = fmaf(qv.y, k01.y, s[t]);
+        s[t] = fmaf(qv.z, k23.x, s[t]);
+        s[t] = fmaf(qv.w, k23.y, s[t]);
+      }
+    }
+    float p[NQW];
+    const int j = kb + lane;
+#pragma unroll
+    for (int t = 0; t < NQW; ++t) {
+      const float sc = j < lim[t] ? s[t] * a.scale : -INFINITY;
+      const float mn = fmaxf(m[t], warp_max(sc));  // -inf only while the vector has seen no key
+      p[t] = j < lim[t] ? expf(sc - mn) : 0.0f;
+      const float cs = m[t] == -INFINITY ? 0.0f : expf(m[t] - mn);
+      l[t] = l[t] * cs + warp_sum(p[t]);
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) o[t][e] *= cs;
+      m[t] = mn;
+    }
+#pragma unroll 4
+    for (int jj = 0; jj < 32; ++jj) {
+      float vf[EPL];
+      if constexpr (EPL == 4) {
+        const uint2 vw = *reinterpret_cast<const uint2*>(&s_v[jj][lane * 4]);
+        const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vw.x));
+        const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vw.y));
+        vf[0] = v01.x, vf[1] = v01.y, vf[2] = v23.x, vf[3] = v23.y;
+      } else {
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) vf[e] = __half2float(s_v[jj][lane * EPL + e]);
+      }
+#pragma unroll
+      for (int t = 0; t < NQW; ++t) {
+        const float pj = __shfl_sync(0xffffffffu, p[t], jj);  // 0 for keys this vector does not see
+#pragma unroll
+        for (int e = 0; e < EPL; ++e) o[t][e] = fmaf(pj, vf[e], o[t][e]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < NQW; ++t) {
+    const int qi = warp + 4 * t, c = c0 + qi / g;
+    if (c < a.C) {
+      float* op = a.out + ((size_t)c * a.H + kvh * g + qi % g) * HD + lane * EPL;
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) op[e] = o[t][e] / l[t];
+    }
+  }
+}
+
+template <int EPL>
+static cudaError_t launch_prefill_tiled(const AttnArgs& a, int g, cudaStream_t st) {
+  const dim3 grid(a.Hkv, (a.C + kPfRows - 1) / kPfRows);
+  switch (g) {  // g kPfRows / 4 query vectors per warp
+    case 1: return launch_pdl(attn_prefill_tiled_kernel<EPL, 1>, grid, dim3(128), 0, st, a);
+    case 2: return launch_pdl(attn_prefill_tiled_kernel<EPL, 2>, grid, dim3(128), 0, st, a);
+    case 3: return launch_pdl(attn_prefill_tiled_kernel<EPL, 3>, grid, dim3(128), 0, st, a);
+    default: return launch_pdl(attn_prefill_tiled_kernel<EPL, 4>, grid, dim3(128), 0, st, a);
+  }
+}
+
 int attn_decode_chunks(int L) { return (L + kChunk - 1) / kChunk; }
 
 template <int HD, int ROWS>
@@ -448,6 +580,10 @@ int attention_run(const AttnArgs& in, cudaStream_t st) {
     const dim3 grid(a.Hkv, attn_decode_chunks(a.L));
     const int R = a.C * g;
     e = R <= 4 ? launch_decode<4>(a, grid, st) : R <= 8 ? launch_decode<8>(a, grid, st) : launch_decode<16>(a, grid, st);
+  } else if (g <= 4) {  // groups of up to 4 heads: the tiled form
+    e = a.head_dim == 32   ? launch_prefill_tiled<1>(a, g, st)
+        : a.head_dim == 64 ? launch_prefill_tiled<2>(a, g, st)
+                           : launch_prefill_tiled<4>(a, g, st);
   } else {
     const dim3 grid(a.H, a.C);
     switch (a.head_dim) {

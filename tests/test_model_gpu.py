@@ -41,9 +41,13 @@ def test_rmsnorm(dev, golden_ops):
 @pytest.mark.parametrize("C,H,Hkv,hd,start,L", [(1, 8, 2, 32, 40, 128), (1, 24, 8, 128, 700, 1024),
                                                 (3, 8, 2, 32, 5, 16), (32, 8, 2, 32, 32, 128),
                                                 (17, 24, 8, 128, 300, 512), (1, 4, 4, 64, 0, 64),
-                                                (2, 8, 2, 32, 60, 32)])
+                                                (2, 8, 2, 32, 60, 32), (128, 24, 8, 128, 384, 512),
+                                                (13, 24, 8, 128, 100, 256), (20, 8, 8, 64, 10, 64),
+                                                (9, 8, 4, 32, 3, 32), (40, 16, 2, 64, 0, 64)])
 def test_attention_vs_oracle(dev, C, H, Hkv, hd, start, L):
-    """Decode (split-key) and prefill forms against the reference's masked softmax over cache[:L]."""
+    """Decode (split-key) and prefill forms against the reference's masked softmax over cache[:L]:
+    the tiled prefill form for groups of 1-4 heads (the 3B shape's 4th prompt chunk, ragged row
+    blocks, keys past the bucket), the one-row form for larger groups (16 / 2)."""
     import q4b
     rng = np.random.default_rng(C * 1000 + start)
     max_ctx = max(L, start + C) + 8
