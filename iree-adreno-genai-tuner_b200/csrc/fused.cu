@@ -7,7 +7,9 @@
 //     decode form   (few query rows): split over key chunks; each CTA keeps an online softmax
 //                   (max, sum, weighted V) per query row; the last CTA of a KV head (arrival
 //                   counter) merges the chunks in chunk order.
-//     prefill form  one warp per (query row, head), online softmax over the row's keys.
+//     prefill form  tiled: one CTA per (KV head, 4 query rows) for all heads of a group of up to 4,
+//                   K / V tiles staged once in shared memory; larger groups: one CTA per (head,
+//                   query row), its keys split over 4 warps. Online softmax over the row's keys.
 #include "fused.h"
 
 namespace q4b {
@@ -405,23 +407,26 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(AttnArgs a) {
 }
 
 // Tiled prefill form: one CTA per (KV head, block of kPfRows query rows) takes all g heads of the
-// group, NQW = g kPfRows / 4 query vectors per warp. Each 32-key tile of K and V is staged once per
-// CTA in shared memory and serves every query vector of the block (the one-row form re-reads a KV
-// head's keys once per query row and head: g C times per chunk). Per tile lane j holds key kb + j:
-// its K row is read from shared memory (rows padded by one word, so the 32 lanes hit 32 banks) and
-// scored against the warp's query vectors in the same dimension order as the one-row form; then an
-// online softmax per query vector and P V with lane l owning dimensions EPL l .. EPL l + EPL - 1.
-// fp32 throughout, fp16 K / V as stored.
-constexpr int kPfRows = 4;
+// group, NQW = g kPfRows / 4 query vectors per query set; 8 warps: warp w takes query set w % 4 and
+// the even (w < 4) or odd (w >= 4) 32-key tiles. Each round stages 64 keys of K and V once per CTA in
+// shared memory, serving every query vector of the block (the one-row form re-reads a KV head's keys
+// once per query row and head: g C times per chunk). Per tile lane j holds key kb + j: its K row is
+// read from shared memory (rows padded by one word, so the 32 lanes hit 32 banks) and scored against
+// the warp's query vectors in the same dimension order as the one-row form; then an online softmax
+// per query vector and P V with lane l owning dimensions EPL l .. EPL l + EPL - 1. The odd-tile
+// warps' (max, sum, weighted V) merge into the even ones' at the end. fp32 throughout, fp16 K / V as
+// stored.
+constexpr int kPfRows = 4, kPfWarps = 8;
 
 template <int EPL, int NQW>
-__global__ void __launch_bounds__(128) attn_prefill_tiled_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kPfWarps * 32) attn_prefill_tiled_kernel(AttnArgs a) {
   constexpr int HD = EPL * 32, HW = HD / 2 + 1, NQ = 4 * NQW;  // HW: 32-bit words per staged K row
   __shared__ __align__(16) float s_q[NQ][HD];
-  __shared__ uint32_t s_k[32 * HW];
-  __shared__ __align__(16) __half s_v[32][HD];
+  __shared__ uint32_t s_k[2][32 * HW];
+  __shared__ __align__(16) __half s_v[2][32][HD];
   const int kvh = blockIdx.x, c0 = blockIdx.y * kPfRows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qs = warp & 3, half = warp >> 2;  // query set, tile parity
   griddep_launch_dependents();
   griddep_wait();
   const int g = a.H / a.Hkv;  // NQ / kPfRows
@@ -431,11 +436,11 @@ __global__ void __launch_bounds__(128) attn_prefill_tiled_kernel(AttnArgs a) {
     const int qi = i / HD, e = i - qi * HD, c = c0 + qi / g;
     s_q[qi][e] = c < a.C ? a.q[((size_t)c * a.H + kvh * g + qi % g) * HD + e] : 0.0f;
   }
-  // this warp's query vectors qi = warp + 4 t and the keys each sees (0 for rows past the chunk)
+  // this warp's query vectors qi = qs + 4 t and the keys each sees (0 for rows past the chunk)
   int lim[NQW];
 #pragma unroll
   for (int t = 0; t < NQW; ++t) {
-    const int c = c0 + (warp + 4 * t) / g;
+    const int c = c0 + (qs + 4 * t) / g;
     lim[t] = c < a.C ? min(a.L, start + c + 1) : 0;
   }
   const int nk = min(a.L, start + min(c0 + kPfRows, a.C));  // keys any row of the block sees
@@ -450,23 +455,25 @@ __global__ void __launch_bounds__(128) attn_prefill_tiled_kernel(AttnArgs a) {
   const size_t kv_stride = (size_t)a.Hkv * HD;
   const __half* kbase = a.k_cache + (size_t)kvh * HD;
   const __half* vbase = a.v_cache + (size_t)kvh * HD;
-  for (int kb = 0; kb < nk; kb += 32) {
-    __syncthreads();  // the previous tile is consumed (the first time: s_q is written)
-    // stage K / V rows kb .. kb + 31 (rows past nk repeat row nk - 1: finite, weighted 0)
-    for (int i = threadIdx.x; i < 32 * (HD / 8); i += blockDim.x) {
-      const int r = i / (HD / 8), u = i - r * (HD / 8);
-      const size_t row = (size_t)min(kb + r, nk - 1) * kv_stride + u * 8;
+  for (int k0 = 0; k0 < nk; k0 += 64) {
+    __syncthreads();  // the previous round is consumed (the first time: s_q is written)
+    // stage K / V rows k0 .. k0 + 63 (rows past nk repeat row nk - 1: finite, weighted 0)
+    for (int i = threadIdx.x; i < 64 * (HD / 8); i += blockDim.x) {
+      const int r = i / (HD / 8), u = i - r * (HD / 8), tb = r >> 5, rr = r & 31;
+      const size_t row = (size_t)min(k0 + r, nk - 1) * kv_stride + u * 8;
       const uint4 kv = *reinterpret_cast<const uint4*>(kbase + row);
       const uint4 vv = *reinterpret_cast<const uint4*>(vbase + row);
-      uint32_t* kw = s_k + r * HW + u * 4;
+      uint32_t* kw = s_k[tb] + rr * HW + u * 4;
       kw[0] = kv.x, kw[1] = kv.y, kw[2] = kv.z, kw[3] = kv.w;
-      *reinterpret_cast<uint4*>(&s_v[r][u * 8]) = vv;
+      *reinterpret_cast<uint4*>(&s_v[tb][rr][u * 8]) = vv;
     }
     __syncthreads();
+    const int kb = k0 + 32 * half;
+    if (kb >= nk) continue;  // (uniform per warp; the barriers above are outside this branch)
     float s[NQW];
 #pragma unroll
     for (int t = 0; t < NQW; ++t) s[t] = 0.0f;
-    const uint32_t* kr = s_k + lane * HW;
+    const uint32_t* kr = s_k[half] + lane * HW;
 #pragma unroll 8
     for (int u = 0; u < HD / 4; ++u) {  // dimensions 4u .. 4u + 3 of key kb + lane
       const uint32_t w0 = kr[2 * u], w1 = kr[2 * u + 1];
@@ -474,7 +481,7 @@ __global__ void __launch_bounds__(128) attn_prefill_tiled_kernel(AttnArgs a) {
       const float2 k23 = __half22float2(*reinterpret_cast<const __half2*>(&w1));
 #pragma unroll
       for (int t = 0; t < NQW; ++t) {
-        const float4 qv = *reinterpret_cast<const float4*>(&s_q[warp + 4 * t][4 * u]);
+        const float4 qv = *reinterpret_cast<const float4*>(&s_q[qs + 4 * t][4 * u]);
         s[t] = fmaf(qv.x, k01.x, s[t]);
         s[t] = fmaf(qv.y, k01.y, s[t]);
         s[t] = fmaf(qv.z, k23.x, s[t]);
@@ -498,13 +505,13 @@ __global__ void __launch_bounds__(128) attn_prefill_tiled_kernel(AttnArgs a) {
     for (int jj = 0; jj < 32; ++jj) {
       float vf[EPL];
       if constexpr (EPL == 4) {
-        const uint2 vw = *reinterpret_cast<const uint2*>(&s_v[jj][lane * 4]);
+        const uint2 vw = *reinterpret_cast<const uint2*>(&s_v[half][jj][lane * 4]);
         const float2 v01 = __half22float2(*reinterpret_cast<const __half2*>(&vw.x));
         const float2 v23 = __half22float2(*reinterpret_cast<const __half2*>(&vw.y));
         vf[0] = v01.x, vf[1] = v01.y, vf[2] = v23.x, vf[3] = v23.y;
       } else {
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) vf[e] = __half2float(s_v[jj][lane * EPL + e]);
+        for (int e = 0; e < EPL; ++e) vf[e] = __half2float(s_v[half][jj][lane * EPL + e]);
       }
 #pragma unroll
       for (int t = 0; t < NQW; ++t) {
@@ -514,14 +521,31 @@ __global__ void __launch_bounds__(128) attn_prefill_tiled_kernel(AttnArgs a) {
       }
     }
   }
+  // the odd-tile warps hand (max, sum, weighted V) over through the K / V staging area
+  __syncthreads();
+  float* xo = reinterpret_cast<float*>(&s_v[0][0][0]);  // [4 sets][NQW][HD] (<= 2 * 32 * HD halves)
+  float* xm = reinterpret_cast<float*>(s_k[0]);          // [4 sets][NQW][2]
+  if (half == 1) {
+#pragma unroll
+    for (int t = 0; t < NQW; ++t) {
+#pragma unroll
+      for (int e = 0; e < EPL; ++e) xo[(qs * NQW + t) * HD + lane * EPL + e] = o[t][e];
+      if (lane == 0) xm[(qs * NQW + t) * 2] = m[t], xm[(qs * NQW + t) * 2 + 1] = l[t];
+    }
+  }
+  __syncthreads();
+  if (half == 1) return;
 #pragma unroll
   for (int t = 0; t < NQW; ++t) {
-    const int qi = warp + 4 * t, c = c0 + qi / g;
-    if (c < a.C) {
-      float* op = a.out + ((size_t)c * a.H + kvh * g + qi % g) * HD + lane * EPL;
+    const int qi = qs + 4 * t, c = c0 + qi / g;
+    if (c >= a.C) continue;
+    const float m1 = xm[(qs * NQW + t) * 2], l1 = xm[(qs * NQW + t) * 2 + 1];
+    const float M = fmaxf(m[t], m1);  // finite: key 0 is in the even tiles and visible to every row
+    const float c_0 = expf(m[t] - M), c_1 = m1 == -INFINITY ? 0.0f : expf(m1 - M);
+    const float L = l[t] * c_0 + l1 * c_1;
+    float* op = a.out + ((size_t)c * a.H + kvh * g + qi % g) * HD + lane * EPL;
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) op[e] = o[t][e] / l[t];
-    }
+    for (int e = 0; e < EPL; ++e) op[e] = (o[t][e] * c_0 + xo[(qs * NQW + t) * HD + lane * EPL + e] * c_1) / L;
   }
 }
 
@@ -529,10 +553,10 @@ template <int EPL>
 static cudaError_t launch_prefill_tiled(const AttnArgs& a, int g, cudaStream_t st) {
   const dim3 grid(a.Hkv, (a.C + kPfRows - 1) / kPfRows);
   switch (g) {  // g kPfRows / 4 query vectors per warp
-    case 1: return launch_pdl(attn_prefill_tiled_kernel<EPL, 1>, grid, dim3(128), 0, st, a);
-    case 2: return launch_pdl(attn_prefill_tiled_kernel<EPL, 2>, grid, dim3(128), 0, st, a);
-    case 3: return launch_pdl(attn_prefill_tiled_kernel<EPL, 3>, grid, dim3(128), 0, st, a);
-    default: return launch_pdl(attn_prefill_tiled_kernel<EPL, 4>, grid, dim3(128), 0, st, a);
+    case 1: return launch_pdl(attn_prefill_tiled_kernel<EPL, 1>, grid, dim3(kPfWarps * 32), 0, st, a);
+    case 2: return launch_pdl(attn_prefill_tiled_kernel<EPL, 2>, grid, dim3(kPfWarps * 32), 0, st, a);
+    case 3: return launch_pdl(attn_prefill_tiled_kernel<EPL, 3>, grid, dim3(kPfWarps * 32), 0, st, a);
+    default: return launch_pdl(attn_prefill_tiled_kernel<EPL, 4>, grid, dim3(kPfWarps * 32), 0, st, a);
   }
 }
 
