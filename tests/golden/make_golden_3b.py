@@ -23,6 +23,7 @@ formulation its export compiles for M == 1; prefill chunks use dequantise + F.li
 from __future__ import annotations
 
 import argparse
+import os
 import pathlib
 import sys
 import time
@@ -45,7 +46,7 @@ def kept_indices(logits: np.ndarray) -> np.ndarray:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", type=pathlib.Path, default=pathlib.Path("/root/reference"))
+    ap.add_argument("--ref", type=pathlib.Path, default=pathlib.Path(os.environ.get("Q4B_REFERENCE", "reference")))
     ap.add_argument("--new", type=int, default=256)
     ap.add_argument("--keep", type=int, default=8)
     ap.add_argument("--layers", type=int, default=None, help="fewer layers, for a timing probe only")
