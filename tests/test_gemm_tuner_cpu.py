@@ -208,3 +208,41 @@ def test_search_runs_end_to_end_on_a_fake_harness(tmp_path, monkeypatch):
     assert all(r["status"] == "ok" for r in meas)
     rounds = [r for r in log if r["event"] == "round"]
     assert [r["round"] for r in rounds if r["strategy"] == "ranked"] == [0, 1, 2]
+
+
+def test_stream_k_plan_and_workspace():
+    """Kernel 3 (persistent stream-K): tile width 256 once there are 8 row tiles (else 128), the
+    deepest ring that fits (one CTA per SM, two TMEM accumulators), a shallower ring on request; the
+    workspace is the per-tile counters plus two [128][bn] fp32 part-tile slots per CTA (148 CTAs on
+    a B200, or one per unit when there are fewer units); split > 1 is rejected."""
+    import ctypes
+
+    from q4b import _lib
+    L = _lib.lib()
+
+    def plan(m, n, k, **cfg):
+        out = _lib.GemmCfg()
+        rc = L.q4b_gemm_f16_plan(m, n, k, b"N", b"N", ctypes.byref(_lib.GemmCfg(kernel=3, **cfg)), ctypes.byref(out))
+        return rc, (out.kernel, out.bn, out.stages, out.split)
+
+    def ws(m, n, k, **cfg):
+        return L.q4b_gemm_f16_workspace(m, n, k, b"N", b"N", ctypes.byref(_lib.GemmCfg(kernel=3, **cfg)))
+
+    assert plan(2048, 5120, 3072) == (0, (3, 256, 4, 1))
+    assert plan(128, 5120, 3072) == (0, (3, 128, 6, 1))
+    assert plan(128, 5120, 3072, bn=64) == (0, (3, 64, 8, 1))
+    assert plan(128, 5120, 3072, stages=3) == (0, (3, 128, 3, 1))
+    counters = 64 * 1024
+    assert ws(2048, 5120, 3072) == counters + 2 * 148 * 128 * 256 * 4
+    # 2 tiles x 2 k steps = 4 units: four CTAs
+    assert ws(128, 256, 128) == counters + 2 * 4 * 128 * 128 * 4
+    assert plan(128, 5120, 3072, split=2)[0] != 0
+    assert plan(128, 5120, 3072, bn=96)[0] != 0
+
+
+def test_bench_reports_the_plan():
+    """bench.py's gemm rows name the schedule each shape ran (the default or --gemm-cfg)."""
+    import bench
+    assert bench.gemm_plan(128, 16384, 3072) == "1:bn=128,stages=5,split=1"
+    assert bench.gemm_plan(2048, 5120, 3072, {"kernel": 3}) == "3:bn=256,stages=4,split=1"
+    assert bench.gemm_plan(8, 8, 8, {"kernel": 2}) == "2:bn=0,stages=0,split=1"
