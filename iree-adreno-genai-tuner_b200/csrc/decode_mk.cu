@@ -136,8 +136,9 @@ __device__ __forceinline__ void trace_ev(const MkArgs& a, int e) {
     a.trace[(size_t)blockIdx.x * mk_trace_stride(a.n_layers) + e] = globaltimer_ns();
 }
 
-// Attention scratch of one item; shares shared memory with the staged x, which is free between the
-// q|k|v projection (its last reads end before the stage arrival) and the o projection's staging.
+// Attention scratch of one item (row 0 for a one-row item, rows 0 .. g - 1 for a long-context item
+// of a KV head's group); shares shared memory with the staged x, which is free between the q|k|v
+// projection (its last reads end before the stage arrival) and the o projection's staging.
 struct MkAttn {
   float q[MK_ROWS][MK_HD];
   float o[MK_CW][MK_ROWS][MK_HD];
@@ -936,8 +937,8 @@ __device__ void attn_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int c
 // attn_item, and the CTA completing the group's chunks (a counter on the group's first row) merges
 // all its rows. Only the long-bucket instantiation of the step kernel contains it, so the registers
 // it needs stay out of the short-bucket kernel.
-__device__ void attn_group_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int ch, int r0, int nr,
-                                             int ctx, int nch) {
+__device__ void attn_group_item(const MkArgs& a, MkSmem& sm, int layer, int kvh, int ch, int r0, int nr, int ctx,
+                                int nch) {
   constexpr int HD = MK_HD, EPL = HD / 32, KW = MK_KCHUNK / MK_CW;  // KW keys per warp (16)
   const int ct = threadIdx.x - 32, w = ct >> 5, lane = ct & 31;
   const int kk = lane >> 1, hh = lane & 1;  // scores: two lanes per key, alternate 16-byte pieces
