@@ -67,6 +67,9 @@ struct LinearOp {
 };
 
 int linear_run(const LinearOp& op, cudaStream_t st);
+// Whether the default plan of an m-row call applies an RMSNorm of fp32 x itself (op.ln_w): up to 8
+// rows in the GEMV's prologue, or the tcgen05 path's x split (head_dim: the RoPE epilogue's heads).
+bool linear_fuses_norm(int m, int k, int group, int epi, int head_dim);
 // Greedy argmax of one row (first maximum): the key (orderable value, index) and / or the index
 // (idx_offset added: a vocabulary shard's first row). One CTA.
 int argmax_run(const float* v, int n, int idx_offset, unsigned long long* key_out, int32_t* index_out,

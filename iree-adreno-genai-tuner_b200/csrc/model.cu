@@ -129,7 +129,6 @@ int Model::forward(const int32_t* toks, int C, int L, float* logits, int32_t* to
   if ((rc = check_ready())) return rc;
   if (mk_usable(C, st)) return mk_forward(toks, L, logits, token_log, st);
   if ((rc = embed_run(toks, C, embed.qweight, embed.scales, cfg.vocab, D, embed.group, h, st))) return rc;
-  const bool fuse_norm = C <= 8;
   const int* start = &state->start;
   for (size_t li = 0; li < layers.size(); ++li) {
     const q4b_layer_weights& Lw = layers[li];
@@ -137,6 +136,10 @@ int Model::forward(const int32_t* toks, int C, int L, float* logits, int32_t* to
     for (int r0 = 0; r0 < C; r0 += row_block(C)) {
       const int m = std::min(row_block(C), C - r0);
       const float* xin = h + (size_t)r0 * D;
+      // RMSNorm inside the projection's own launch where its plan has one (the GEMV prologue up to
+      // 8 rows, the tcgen05 path's x split), else a separate launch
+      const bool fuse_norm = linear_fuses_norm(m, Lw.wqkv.k, Lw.wqkv.group, EPI_ROPE_KV, hd) && aligned(Lw.ln_in, 16) &&
+                             aligned(xin, 16);
       if (!fuse_norm) {
         if ((rc = rmsnorm_run(h + (size_t)r0 * D, Lw.ln_in, cfg.rms_eps, m, D, nullptr, xn, st))) return rc;
         xin = xn;
@@ -182,6 +185,8 @@ int Model::forward(const int32_t* toks, int C, int L, float* logits, int32_t* to
     for (int r0 = 0; r0 < C; r0 += row_block(C)) {
       const int m = std::min(row_block(C), C - r0);
       const float* xin = h + (size_t)r0 * D;
+      const bool fuse_norm =
+          linear_fuses_norm(m, Lw.wgu.k, Lw.wgu.group, EPI_SWIGLU, hd) && aligned(Lw.ln_post, 16) && aligned(xin, 16);
       if (!fuse_norm) {
         if ((rc = rmsnorm_run(h + (size_t)r0 * D, Lw.ln_post, cfg.rms_eps, m, D, nullptr, xn, st))) return rc;
         xin = xn;

@@ -1113,10 +1113,59 @@ struct K5 {
   static_assert(BN * K5_BM * 4 / 16 * K5_FS <= K5_XS * XSTAGE, "final tile must fit in the x ring");
 };
 
-// x [M, K] (fp32 or fp16, rows from x_row) -> hi / lo fp16 [M, K] in the permuted k order
+// Row blockIdx.x of x, RMS-normalised and scaled by ln_w, -> hi / lo fp16 in the permuted k order.
+// The sum of squares runs in the order of rmsnorm_kernel's one-pass form (thread t adds float4s
+// t, t + 256, ... in turn, then the warps' sums in warp order) and each value is (x rs) w as there,
+// so the split sees the same fp32 values as a separate RMSNorm launch would write.
+__device__ void xsplit_norm_row(const LinArgs& p, __half* xh, __half* xl) {
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  const float* xr = reinterpret_cast<const float*>(p.x) + (size_t)x_row(p, m) * p.K;
+  const float4* x4 = reinterpret_cast<const float4*>(xr);
+  const int n4 = p.K / 4;
+  float ss = 0.0f;
+  for (int j = threadIdx.x; j < n4; j += blockDim.x) {
+    const float4 v = x4[j];
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = 1.0f / sqrtf(t / (float)p.K + p.eps);
+  }
+  __syncthreads();
+  const float rs = red[0];
+  const float4* w4 = reinterpret_cast<const float4*>(p.ln_w);
+  for (int w = threadIdx.x; w < p.K / 8; w += blockDim.x) {
+    float4 a = x4[2 * w], b = x4[2 * w + 1];
+    const float4 ga = w4[2 * w], gb = w4[2 * w + 1];
+    a = make_float4(a.x * rs * ga.x, a.y * rs * ga.y, a.z * rs * ga.z, a.w * rs * ga.w);
+    b = make_float4(b.x * rs * gb.x, b.y * rs * gb.y, b.z * rs * gb.z, b.w * rs * gb.w);
+    uint4 hi, lo;
+    split_pair(a.x, b.x, hi.x, lo.x);
+    split_pair(a.y, b.y, hi.y, lo.y);
+    split_pair(a.z, b.z, hi.z, lo.z);
+    split_pair(a.w, b.w, hi.w, lo.w);
+    *reinterpret_cast<uint4*>(xh + (size_t)m * p.K + 8 * w) = hi;
+    *reinterpret_cast<uint4*>(xl + (size_t)m * p.K + 8 * w) = lo;
+  }
+}
+
+// x [M, K] (fp32 or fp16, rows from x_row) -> hi / lo fp16 [M, K] in the permuted k order (fp32 x
+// with ln_w: the fused RMSNorm form above)
 template <bool XF32>
 __global__ void __launch_bounds__(256) q4_xsplit(LinArgs p, __half* xh, __half* xl) {
   griddep_wait();
+  if constexpr (XF32) {
+    if (p.ln_w) {  // fused RMSNorm (rms_norm, llama_q4.py:141-142): one CTA per row, grid = M
+      xsplit_norm_row(p, xh, xl);
+      griddep_launch_dependents();
+      return;
+    }
+  }
   const int kw = p.K / 8;
   const int n = p.M * kw;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
@@ -1681,7 +1730,8 @@ static int plan_stream(int M, int K, bool xf32, const q4b_linear_cfg* cfg, Plan&
 // kernel 5: weight rows per CTA from cfg->tiles (row tiles of 16: 4 or 8), k split at scale-group
 // granularity; workspace = counters | x hi | x lo | split partials
 static bool tc_ok(int M, int K, int G, int epi, bool norm) {
-  return M > 32 && G % 128 == 0 && !norm && epi != EPI_ARGMAX && K / G <= 64 * 64;
+  (void)norm;  // the x split applies a fused RMSNorm (fp32 x, checked by validate)
+  return M > 32 && G % 128 == 0 && epi != EPI_ARGMAX && K / G <= 64 * 64;
 }
 // RoPE tiles map onto TMA boxes of whole half-heads (row tiles per head and per CTA nest)
 static bool tc_rope_ok(int epi, int hd, int bn) {
@@ -1808,8 +1858,8 @@ static int plan_linear(int M, int N, int K, int G, int epi, bool xf32, bool norm
   pl.RT = row_tiles(N, n_out, epi);
   pl.MT = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8;
   if (want == 5) {
-    if (!tc_ok(M, K, G, epi, norm) && !(M >= 1 && G % 128 == 0 && !norm && epi != EPI_ARGMAX))
-      return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 5 needs group %% 128 == 0, no fused norm, no argmax");
+    if (!tc_ok(M, K, G, epi, norm) && !(M >= 1 && G % 128 == 0 && epi != EPI_ARGMAX))
+      return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 5 needs group %% 128 == 0, no argmax");
     return plan_tc(M, K, G, xf32, cfg, pl);
   }
   if (want == 0 && tc_ok(M, K, G, epi, norm)) return plan_tc(M, K, G, xf32, cfg, pl);
@@ -1931,8 +1981,8 @@ static int validate(const LinearOp& op) {
     return set_error(Q4B_EINVAL, "q4_linear: bad dtype");
   if (op.epi < EPI_STORE || op.epi > EPI_ARGMAX) return set_error(Q4B_EINVAL, "q4_linear: bad epilogue %d", op.epi);
   if (op.epi == EPI_SWIGLU && op.n % 2) return set_error(Q4B_EINVAL, "q4_linear: SwiGLU needs an even row count");
-  if (op.ln_w && (op.x_dtype != Q4B_F32 || op.m > 8 || op.k % 4))
-    return set_error(Q4B_EINVAL, "q4_linear: fused RMSNorm needs fp32 x, m <= 8 and k %% 4 == 0");
+  if (op.ln_w && (op.x_dtype != Q4B_F32 || op.k % 4))
+    return set_error(Q4B_EINVAL, "q4_linear: fused RMSNorm needs fp32 x and k %% 4 == 0");
   if (op.epi == EPI_ROPE_KV &&
       (!op.rope_cos || !op.rope_sin || !op.pos0 || !op.q_out || !op.k_cache || !op.v_cache || op.head_dim % 16 ||
        op.n != (op.n_heads + 2 * op.n_kv) * op.head_dim))
@@ -1940,6 +1990,10 @@ static int validate(const LinearOp& op) {
   if (op.epi == EPI_ARGMAX && (!op.state || op.m != 1))
     return set_error(Q4B_EINVAL, "q4_linear: argmax epilogue needs a state and m == 1");
   return Q4B_OK;
+}
+
+bool linear_fuses_norm(int m, int k, int group, int epi, int head_dim) {
+  return m <= 8 || (tc_ok(m, k, group, epi, true) && tc_rope_ok(epi, head_dim, 128) && tc_rope_ok(epi, head_dim, 64));
 }
 
 static int plan_op(const LinearOp& op, Plan& pl) {
@@ -1973,9 +2027,15 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
   Plan pl;
   if ((rc = plan_op(op, pl))) return rc;
   const bool forced = op.cfg && op.cfg->kernel;
+  // a fused RMSNorm over more than 8 rows runs in kernel 5's x split only (the other kernels' norm
+  // prologue holds 8 rows): no fallback to another kernel for it
+  const bool wide_norm = op.ln_w && op.m > 8;
+  if (wide_norm && pl.kernel != 5)
+    return set_error(Q4B_EINVAL, "q4_linear: fused RMSNorm over %d rows needs the tcgen05 path (group %% 128 == 0, "
+                                 "m > 32)", op.m);
   if (pl.kernel != 2 && (!aligned(op.qw, 16) || !aligned(op.x, 16) || (op.ln_w && !aligned(op.ln_w, 16)) ||
                          (pl.kernel == 4 && !aligned(op.scales, 16)))) {
-    if (forced) return set_error(Q4B_EINVAL, "q4_linear: qweight, x and ln_w must be 16-byte aligned");
+    if (forced || wide_norm) return set_error(Q4B_EINVAL, "q4_linear: qweight, x and ln_w must be 16-byte aligned");
     simt_plan(op, pl);
   }
   if (pl.kernel == 6 && !aligned(op.scales, 16)) {  // scale rows arrive by bulk copies
@@ -1992,12 +2052,13 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
     pl.ws_bytes = 0;
   }
   if (pl.kernel == 5 && !tc_rope_ok(op.epi, op.head_dim, pl.bn)) {
-    if (forced) return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 5 RoPE tiles need head_dim / 16 and the tile to nest");
+    if (forced || wide_norm)
+      return set_error(Q4B_EUNSUPPORTED, "q4_linear: kernel 5 RoPE tiles need head_dim / 16 and the tile to nest");
     simt_plan(op, pl);
   }
   if (pl.kernel == 5 && (pl.ws_bytes > op.ws_bytes || !op.ws || !aligned(op.ws, 256))) {
-    if (forced) return set_error(Q4B_EINVAL, "q4_linear: workspace of %zu bytes needed, %zu given", pl.ws_bytes,
-                                 op.ws_bytes);
+    if (forced || wide_norm)
+      return set_error(Q4B_EINVAL, "q4_linear: workspace of %zu bytes needed, %zu given", pl.ws_bytes, op.ws_bytes);
     simt_plan(op, pl);  // the x conversion and split partials need the workspace
   }
   if (pl.kernel != 2 && pl.kernel != 5 && pl.nsplit > 1 &&
@@ -2080,7 +2141,7 @@ int linear_run(const LinearOp& op, cudaStream_t st) {
     if (!rc2) rc2 = make_tmap_i32(&tw, op.qw, op.k / 8, op.n, op.k / 8, 8, pl.bn / nb);
     if (rc2) return rc2;
     const int chunks = op.m * (op.k / 8);
-    const int pgrid = std::min((chunks + 255) / 256, 148 * 8);
+    const int pgrid = op.ln_w ? op.m : std::min((chunks + 255) / 256, 148 * 8);  // fused norm: a CTA per row
     e = xf32 ? launch_pdl(q4_xsplit<true>, dim3(pgrid), dim3(256), 0, st, a, xh, xl)
              : launch_pdl(q4_xsplit<false>, dim3(pgrid), dim3(256), 0, st, a, xh, xl);
     if (e == cudaSuccess) {
