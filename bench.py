@@ -90,13 +90,11 @@ def profile_traffic(name, key="traffic_bytes_per_launch"):
 
 
 def decode_traffic(bytes_tok, world):
-    """roofline.traffic of the decode line: the 1-GPU capture's dram bytes per launch; at tp > 1 (no
-    capture per rank) the capture's traffic / algorithmic ratio times this GPU's algorithmic bytes."""
-    t = profile_traffic("decode_step_3b")
-    if t is None or world == 1:
-        return t
-    alg = profile_traffic("decode_step_3b", "algorithmic_bytes_per_launch")
-    return round(t / alg * bytes_tok) if alg else None
+    """roofline.traffic of the decode line: the dram bytes per launch of the committed 1-GPU ncu
+    capture (profiles/decode_step_3b.txt); null at tp > 1, where no capture of a rank's launch exists
+    (a multi-rank command is never run under ncu)."""
+    del bytes_tok
+    return profile_traffic("decode_step_3b") if world == 1 else None
 
 
 class ClockSampler:
@@ -264,7 +262,7 @@ def run_gemv(args, rank, world, local, dist_mod):
         "clocks": clk.summary(),
         "parity_rel_err": check,
     }
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_gemv_baseline()
     return line
 
@@ -365,8 +363,8 @@ def run_decode(args, rank, world, local, dist_mod):
                    else "per projection"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": decode_traffic(bytes_tok, world),
-                     **({"traffic_note": "per GPU: the 1-GPU capture's traffic/algorithmic ratio x this GPU's "
-                                         "algorithmic bytes"} if world > 1 else {}),
+                     **({"traffic_note": "null: no ncu capture of a tensor-parallel rank's launch (the "
+                                         "1-GPU capture reads 1.007x the algorithmic bytes)"} if world > 1 else {}),
                      "peak_source": pk["source"], "kernel": "decode_step_kernel" if persistent else "decode step (q4_gemv_* dominant)",
                      "algorithmic_bytes_per_token_per_gpu": round(bytes_tok)},
         "e2e": {"value": round(steps / (e2e_ms / 1e3), 2), "unit": "tokens/s",
@@ -383,7 +381,7 @@ def run_decode(args, rank, world, local, dist_mod):
         line["gemv_5120x3072"] = gemv
     if lm:
         line["gemv_lm_head_128256x3072"] = lm
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:  # the host baseline belongs to the N = 1 line
         line["cpu_baseline"] = cpu_decode_baseline(steps=5, warmup=1)
     return line
 
@@ -665,7 +663,7 @@ def run_gemm(args, rank, world, local, dist_mod):
                          "achieved": max(r["TFLOP_s"] for r in main),
                          "frac": round(max(r["TFLOP_s"] for r in main) / pk["bf16_tflops"], 4), "traffic": None},
             "rows": rows}
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_gemm_baseline()
     return line
 
@@ -772,7 +770,7 @@ def run_sweep(args, rank, world, local, dist_mod):
                          "achieved": round(tot_b / tot_s / 1e9, 1),
                          "frac": round(tot_b / tot_s / 1e9 / pk["hbm_gbs"], 4), "traffic": None},
             "rows": rows, "gpu_launches": sum(r["weight_copies"] for r in rows) * args.steps,
-            **({} if args.no_cpu_baseline else {"cpu_baseline": cpu_sweep_baseline(args.m)})}
+            **({} if args.no_cpu_baseline or world > 1 else {"cpu_baseline": cpu_sweep_baseline(args.m)})}
 
 
 def shard_measure(dev, n, k, m, split, rank, world, dist_mod, comm, steps, warmup, seed=99):
@@ -960,7 +958,7 @@ def run_tiny(args, rank, world, local, dist_mod):
             "e2e": {"value": round(statistics.median(e2e), 1), "unit": "tokens/s", "h2d_bytes_per_step": 104,
                     "d2h_bytes_per_step": 4, "path": "q4b.Runner(sync_every_step=True).generate"},
             "clocks": clk.summary(), "gpu_launches": None}
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         from oracle import q4_oracle as O
         layers = [dict(wqkv=(z[f"l{i}_wqkv_qweight"], z[f"l{i}_wqkv_scales"], int(z[f"l{i}_wqkv_group"])),
                        wo=(z[f"l{i}_wo_qweight"], z[f"l{i}_wo_scales"], int(z[f"l{i}_wo_group"])),
