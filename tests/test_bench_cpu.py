@@ -34,6 +34,9 @@ def test_profile_traffic_lines():
     assert t is not None and abs(t / bench.decode_bytes_per_token(q4b.SYNTHETIC["3b"], 640) - 1) < 0.01
     g = bench.profile_traffic("q4_gemv_mma_5120x3072")
     assert g is not None and abs(g / bench.GEMV_BYTES - 1) < 0.01
+    # the decode line: the 1-GPU capture at N = 1, null at N > 1 (no capture of a rank's launch)
+    assert bench.decode_traffic(1.73e9, 1) == t
+    assert bench.decode_traffic(0.87e9, 2) is None
 
 
 def test_trace_summary_reads_the_stamp_layout():
