@@ -21,7 +21,7 @@ import pathlib
 
 import numpy as np
 
-from .schedule import BK, BM, Schedule, eff_stages, grid, k_steps, smem_bytes
+from .schedule import BK, BM, Schedule, eff_stages, grid, k_steps, sk_occupancy, sk_units, smem_bytes
 
 
 def _peaks():
@@ -47,6 +47,8 @@ EPI_US_PER_KB = 0.004  # TMEM -> registers -> global per KB of output tile
 def ctas_per_sm(sc: Schedule) -> int:
     if sc.kernel == 2:
         return 8
+    if sc.kernel == 3:
+        return sk_occupancy(sc)
     by_smem = max(1, 233472 // (smem_bytes(sc) + 1024))
     return max(1, min(by_smem, 512 // sc.bn))
 
@@ -61,6 +63,10 @@ def analytic_us(s, sc: Schedule) -> float:
     per_sm = ctas_per_sm(sc)
     waves = math.ceil(ctas / (SMS * per_sm))
     nk = k_steps(s) / sc.split
+    fixup = 0.0
+    if sc.kernel == 3:  # one wave of equal runs; part-tiles written and added back by the last CTA
+        waves, nk = 1, sk_units(s, sc) / ctas
+        fixup = 2.0 * BM * sc.bn * 4 * 2 / (L2_GBS * 1e3 / SMS) + 2 * FILL_US
     step_flops = 2.0 * BM * sc.bn * BK
     t_mma = step_flops / (TENSOR_TFLOPS * 1e6 / SMS)                    # us per k step
     step_bytes = (BM + sc.bn) * BK * 2.0
@@ -69,7 +75,7 @@ def analytic_us(s, sc: Schedule) -> float:
     # a shallow ring exposes part of the DRAM latency on every k step
     depth = eff_stages(sc)
     t_step = max(t_mma * per_sm, t_load) * (1.0 + 0.6 / depth)
-    t_cta = nk * t_step + FILL_US + EPI_US_PER_KB * BM * sc.bn * 2 / 1024
+    t_cta = nk * t_step + FILL_US + EPI_US_PER_KB * BM * sc.bn * 2 / 1024 + fixup
     t_waves = waves * t_cta
     part = 2.0 * sc.split * gx * gy * BM * sc.bn * 4 if sc.split > 1 else 0.0
     t_dram = (s.min_bytes + part) / (HBM_GBS * 1e3)

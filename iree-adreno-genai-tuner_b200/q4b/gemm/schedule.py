@@ -4,9 +4,13 @@ and the index algebra of its kernels, restated here so the verifier can replay i
 Kernel 1 (tcgen05): a CTA computes one 128 x bn tile of C over the k steps [k_begin, k_end) of its
 split z (64 wide each); grid = (ceil(M/128), ceil(N/bn), split); a shared-memory ring of `stages`
 slots, each holding A's 128 x 64 tile (16 KB) and B's bn x 64 tile; a TMEM accumulator of bn
-columns. Kernel 2 (CUDA cores): 64 x 64 tiles, no options.
+columns. Kernel 2 (CUDA cores): 64 x 64 tiles, no options. Kernel 3 (tcgen05, persistent stream-K):
+the U = tiles x k-steps units split into G equal runs [c U / G, (c + 1) U / G), G = min(U, 148 x
+CTAs per SM); the same ring and TMA boxes per unit as kernel 1; a CTA's run cuts into one segment per
+tile, only its first and last possibly part of a tile, written to partial slots 2c and 2c + 1.
 
-A schedule's candidate string is what the harness manifest carries: "1:bn=128,stages=6,split=2".
+A schedule's candidate string is what the harness manifest carries: "1:bn=128,stages=6,split=2",
+"3:bn=256,stages=4".
 """
 
 from __future__ import annotations
@@ -17,11 +21,12 @@ import math
 BM, BK = 128, 64
 SMEM_BUDGET = 200 * 1024  # ring bytes the kernel may use (csrc/gemm_f16.cu kGemmSmemBudget)
 COUNTER_TILES = 16384     # split-K arrival counters in the workspace (64 KB of u32)
+SMS = 148                 # the B200's SMs (kernel 3's persistent grid)
 
 
 @dataclasses.dataclass(frozen=True)
 class Schedule:
-    kernel: int = 1   # 1 = tcgen05 + TMA + TMEM, 2 = CUDA-core tiles
+    kernel: int = 1   # 1 = tcgen05 + TMA + TMEM, 2 = CUDA-core tiles, 3 = tcgen05 persistent stream-K
     bn: int = 128     # output tile width (64 | 128 | 256)
     stages: int = 0   # ring depth (0 = as many as fit)
     split: int = 1    # k splits
@@ -29,19 +34,29 @@ class Schedule:
     def key(self):
         # stages 0 means "as many as fit": the same kernel as naming that depth
         st = self.stages or SMEM_BUDGET // ((BM + self.bn) * BK * 2)
-        return (self.kernel, self.bn, st, self.split) if self.kernel == 1 else (2,)
+        if self.kernel == 2:
+            return (2,)
+        return (3, self.bn, st) if self.kernel == 3 else (self.kernel, self.bn, st, self.split)
 
     def candidate(self) -> str:
         if self.kernel == 2:
             return "2:"
+        if self.kernel == 3:
+            return f"3:bn={self.bn},stages={self.stages}"
         return f"1:bn={self.bn},stages={self.stages},split={self.split}"
 
     def short(self) -> str:
-        return "simt" if self.kernel == 2 else f"tc bn{self.bn} st{self.stages or 'max'} sk{self.split}"
+        if self.kernel == 2:
+            return "simt"
+        if self.kernel == 3:
+            return f"streamk bn{self.bn} st{self.stages or 'max'}"
+        return f"tc bn{self.bn} st{self.stages or 'max'} sk{self.split}"
 
     def cfg(self) -> dict:
         if self.kernel == 2:
             return dict(kernel=2)
+        if self.kernel == 3:
+            return dict(kernel=3, bn=self.bn, stages=self.stages)
         return dict(kernel=1, bn=self.bn, stages=self.stages, split=self.split)
 
     @staticmethod
@@ -80,7 +95,67 @@ def k_steps(s) -> int:
 def grid(s, sc: Schedule):
     if sc.kernel == 2:
         return (-(-s.N // 64), -(-s.M // 64), 1)
+    if sc.kernel == 3:
+        return (sk_ctas(s, sc), 1, 1)
     return (-(-s.M // BM), -(-s.N // sc.bn), sc.split)
+
+
+# ---- kernel 3 (stream-K): the index algebra of gemm_f16_sk and plan_sk ----------------------------
+
+def sk_occupancy(sc: Schedule) -> int:
+    """CTAs per SM: by shared memory (228 KB an SM, 1 KB reserved per CTA), at most 2 (register cap)."""
+    return max(1, min(2, 233472 // (smem_bytes(sc) + 2048)))
+
+
+def sk_accumulators(sc: Schedule) -> int:
+    """TMEM accumulators per CTA: one when two CTAs share an SM, else two."""
+    return 1 if sk_occupancy(sc) >= 2 else 2
+
+
+def sk_tiles(s, sc: Schedule):
+    return -(-s.M // BM), -(-s.N // sc.bn)
+
+
+def sk_units(s, sc: Schedule) -> int:
+    tm, tn = sk_tiles(s, sc)
+    return tm * tn * k_steps(s)
+
+
+def sk_ctas(s, sc: Schedule, sms: int = SMS) -> int:
+    return min(sk_units(s, sc), sms * sk_occupancy(sc))
+
+
+def sk_run(U: int, G: int, c: int):
+    """Units [u0, u1) of CTA c."""
+    return U * c // G, U * (c + 1) // G
+
+
+def sk_cta_of(u: int, U: int, G: int) -> int:
+    """The CTA whose run contains unit u (G <= U: no run is empty)."""
+    return ((u + 1) * G + U - 1) // U - 1
+
+
+def sk_segments(s, sc: Schedule, c: int, G: int):
+    """CTA c's segments in order: (tile, k0, k1, slot) with slot None for a whole tile, else the
+    partial slot 2c (its first segment) or 2c + 1."""
+    U, kt = sk_units(s, sc), k_steps(s)
+    u0, u1 = sk_run(U, G, c)
+    out, u = [], u0
+    while u < u1:
+        t, k0 = divmod(u, kt)
+        k1 = min(kt, k0 + (u1 - u))
+        whole = k0 == 0 and k1 == kt
+        out.append((t, k0, k1, None if whole else 2 * c + (0 if u == u0 else 1)))
+        u += k1 - k0
+    return out
+
+
+def sk_fixup_slots(s, sc: Schedule, t: int, G: int):
+    """The contributors of tile t and the slot the last of them reads for each, in k order (the
+    kernel's fix-up: slot 2cc if t is cc's first tile, else 2cc + 1)."""
+    U, kt = sk_units(s, sc), k_steps(s)
+    c0, c1 = sk_cta_of(t * kt, U, G), sk_cta_of((t + 1) * kt - 1, U, G)
+    return [(cc, 2 * cc + (0 if t == (U * cc // G) // kt else 1)) for cc in range(c0, c1 + 1)]
 
 
 def k_range(s, sc: Schedule, z: int):
@@ -106,6 +181,8 @@ def tma_loads(s, sc: Schedule, m_tile: int, n_tile: int, k_step: int):
 
 
 def workspace_bytes(s, sc: Schedule) -> int:
+    if sc.kernel == 3:
+        return 64 * 1024 + 2 * sk_ctas(s, sc) * BM * sc.bn * 4
     if sc.kernel == 2 or sc.split == 1:
         return 0
     gx, gy, _ = grid(s, sc)

@@ -39,11 +39,14 @@ from .verifier import library_accepts, verify
 
 
 def space(s):
-    """Every tcgen05 schedule the domains of shape s name (unverified), one per distinct kernel."""
+    """Every tcgen05 schedule the domains of shape s name (unverified), one per distinct kernel:
+    kernel 1 over tile width x ring depth x k split, kernel 3 (stream-K) over tile width x ring depth."""
     d = domains(s)
     out, keys = [], set()
-    for bn, st, sp in itertools.product(d["bn"], d["stages"], d["split"]):
-        sc = Schedule(kernel=1, bn=bn, stages=st, split=sp)
+    cands = [Schedule(kernel=1, bn=bn, stages=st, split=sp)
+             for bn, st, sp in itertools.product(d["bn"], d["stages"], d["split"])]
+    cands += [Schedule(kernel=3, bn=bn, stages=st) for bn, st in itertools.product(d["bn"], d["stages"])]
+    for sc in cands:
         if sc.key() not in keys:
             keys.add(sc.key())
             out.append(sc)

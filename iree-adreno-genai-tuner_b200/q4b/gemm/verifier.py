@@ -22,7 +22,8 @@ import collections
 import dataclasses
 
 from .schedule import (BK, BM, COUNTER_TILES, SMEM_BUDGET, Schedule, eff_stages, grid, k_range, k_steps, max_stages,
-                       smem_bytes, stage_bytes, tma_loads, workspace_bytes)
+                       sk_accumulators, sk_cta_of, sk_fixup_slots, sk_occupancy, sk_run, sk_segments, sk_tiles,
+                       sk_units, smem_bytes, stage_bytes, tma_loads, workspace_bytes)
 
 DEVICES = {
     # B200 (sm_100a): 148 SMs, 227 KB shared memory per CTA (228 KB per SM), 512 TMEM columns per SM
@@ -34,10 +35,12 @@ DEVICES = {
 def static_check(s, sc: Schedule, device="b200"):
     d = DEVICES[device]
     v = []
-    if sc.kernel not in (1, 2):
+    if sc.kernel not in (1, 2, 3):
         return ["kernel-id"]
     if sc.kernel == 2:
         return v  # any size and alignment
+    if sc.kernel == 3:
+        return static_check_sk(s, sc, d)
     if sc.bn not in (64, 128, 256):
         return ["tile-width"]
     # TMA: row pitches must be multiples of 16 bytes (8 fp16) for both stored operands
@@ -76,9 +79,93 @@ def static_check(s, sc: Schedule, device="b200"):
     return v
 
 
+def static_check_sk(s, sc: Schedule, d):
+    """Kernel 3's static rules: the kernel-1 tile / TMA / ring rules, no k split (it balances k
+    itself), TMEM for its accumulators on every CTA an SM holds, one counter per tile."""
+    v = []
+    if sc.bn not in (64, 128, 256):
+        return ["tile-width"]
+    lda = s.K if s.la == "N" else s.M
+    ldb = s.N if s.lb == "N" else s.K
+    if lda % 8:
+        v.append("tma-pitch-A")
+    if ldb % 8:
+        v.append("tma-pitch-B")
+    if sc.stages and not 2 <= sc.stages <= max_stages(sc):
+        v.append("ring-depth")
+    if eff_stages(sc) * stage_bytes(sc) > SMEM_BUDGET or smem_bytes(sc) > d["smem_per_cta"]:
+        v.append("shared-memory")
+    if sk_occupancy(sc) * sk_accumulators(sc) * sc.bn > d["tmem_cols"]:
+        v.append("tmem-columns")
+    if sc.split != 1:
+        v.append("split-range")
+    tm, tn = sk_tiles(s, sc)
+    if tm * tn > COUNTER_TILES:
+        v.append("split-counters")
+    if workspace_bytes(s, sc) > d["max_ws_bytes"]:
+        v.append("workspace-size")
+    if sc.bn > 64 and sc.bn >= 2 * s.N:
+        v.append("tile-exceeds-problem")
+    return v
+
+
+def mapping_check_sk(s, sc: Schedule):
+    """Replay kernel 3's run / segment / part-tile algebra: the runs partition the units with none
+    empty; sk_cta_of finds each run's owner; a CTA's segments cover its run in order, whole tiles
+    except possibly the first and the last; every tile's units are covered once, by one whole
+    segment or by the contiguous CTAs the fix-up finds, whose partial slots are the ones they write."""
+    v = []
+    U, kt = sk_units(s, sc), k_steps(s)
+    G = grid(s, sc)[0]
+    if G < 1 or G > U:
+        return ["empty-run"]
+    prev = 0
+    written = {}  # tile -> [(cta, slot, k0, k1)] from the CTAs' own segments
+    whole = collections.Counter()
+    for c in range(G):
+        u0, u1 = sk_run(U, G, c)
+        if u0 != prev or u1 <= u0:
+            v.append("run-partition")
+        prev = u1
+        if sk_cta_of(u0, U, G) != c or sk_cta_of(u1 - 1, U, G) != c:
+            v.append("run-owner")
+        segs = sk_segments(s, sc, c, G)
+        if sum(k1 - k0 for _, k0, k1, _ in segs) != u1 - u0:
+            v.append("segment-coverage")
+        for i, (t, k0, k1, slot) in enumerate(segs):
+            if slot is None:
+                whole[t] += 1
+            else:
+                if 0 < i < len(segs) - 1:
+                    v.append("partial-middle-segment")
+                written.setdefault(t, []).append((c, slot, k0, k1))
+    if prev != U:
+        v.append("run-partition")
+    tm, tn = sk_tiles(s, sc)
+    for t in range(tm * tn):
+        parts = written.get(t, [])
+        if whole[t] + (1 if parts else 0) != 1 or whole[t] > 1:
+            v.append("tile-ownership")
+            continue
+        if not parts:
+            continue
+        if [(c, slot) for c, slot, _, _ in parts] != sk_fixup_slots(s, sc, t, G):
+            v.append("fixup-slots")
+        ks = [(k0, k1) for _, _, k0, k1 in parts]
+        if ks[0][0] != 0 or ks[-1][1] != kt or any(a[1] != b[0] for a, b in zip(ks, ks[1:])):
+            v.append("reduction-coverage")
+    return sorted(set(v))
+
+
 def mapping_check(s, sc: Schedule):
     """Replay the kernel's index algebra for the first, an interior and the last tile."""
     v = []
+    if sc.kernel == 3:
+        v = mapping_check_sk(s, sc)
+        tm, tn = sk_tiles(s, sc)
+        sc = Schedule(kernel=1, bn=sc.bn, stages=sc.stages, split=1)  # the same TMA boxes per unit
+        gx, gy = tm, tn
+        return sorted(set(v + tma_check(s, sc, gx, gy)))
     if sc.kernel == 2:
         gx, gy, _ = grid(s, sc)
         if gx * 64 < s.N or gy * 64 < s.M:
@@ -98,9 +185,15 @@ def mapping_check(s, sc: Schedule):
         kcount.update(range(lo, hi))
     if sorted(kcount) != list(range(k_steps(s))) or any(c != 1 for c in kcount.values()):
         v.append("reduction-coverage")
-    # ring slots: the boxes of one slot deliver exactly stage_bytes (the expect_tx count); the
-    # innermost coordinate of every box is a multiple of 16 bytes; boxes of one operand tile the
-    # operand's shared-memory region without overlap
+    v += tma_check(s, sc, gx, gy)
+    return sorted(set(v))
+
+
+def tma_check(s, sc: Schedule, gx: int, gy: int):
+    """Ring slots: the boxes of one slot deliver exactly stage_bytes (the expect_tx count); the
+    innermost coordinate of every box is a multiple of 16 bytes; boxes of one operand tile the
+    operand's shared-memory region without overlap (first, an interior and the last tile)."""
+    v = []
     tiles = {(0, 0), (gx // 2, gy // 2), (gx - 1, gy - 1)}
     for (mt, nt) in tiles:
         for ks in {0, k_steps(s) - 1}:

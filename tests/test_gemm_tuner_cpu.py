@@ -246,3 +246,50 @@ def test_bench_reports_the_plan():
     assert bench.gemm_plan(128, 16384, 3072) == "1:bn=128,stages=5,split=1"
     assert bench.gemm_plan(2048, 5120, 3072, {"kernel": 3}) == "3:bn=256,stages=4,split=1"
     assert bench.gemm_plan(8, 8, 8, {"kernel": 2}) == "2:bn=0,stages=0,split=1"
+
+
+def test_stream_k_schedules_in_the_space():
+    """Kernel 3 (stream-K) schedules: candidate strings round-trip, the verifier's replay of the
+    run / segment / part-tile algebra is clean on the config-2 and ragged shapes, and its workspace
+    restatement equals the library's."""
+    import ctypes
+
+    from q4b import _lib
+    from q4b.gemm import schedule, search
+    g = _gemm()
+    sc = schedule.Schedule.parse("3:bn=256,stages=4")
+    assert (sc.kernel, sc.bn, sc.stages, sc.split) == (3, 256, 4, 1) and sc.candidate() == "3:bn=256,stages=4"
+    assert sc.cfg() == dict(kernel=3, bn=256, stages=4)
+    L = _lib.lib()
+    shapes = g.SHAPES + [g.Shape("R1", "r", 100, 200, 136, "NN"), g.Shape("R5", "r", 4096, 4096, 128, "NN"),
+                         g.Shape("R6", "r", 136, 200, 4160, "TT")]
+    n3 = 0
+    for s in shapes:
+        for sc in (x for x in search.space(s) if x.kernel == 3):
+            v = g.verify(s, sc)
+            if not v.ok:
+                assert set(v.reasons) <= {"ring-depth", "shared-memory", "tile-exceeds-problem"}, (s, sc, v)
+                continue
+            n3 += 1
+            ws = L.q4b_gemm_f16_workspace(s.M, s.N, s.K, s.la.encode(), s.lb.encode(),
+                                          ctypes.byref(_lib.GemmCfg(**sc.cfg())))
+            assert ws == schedule.workspace_bytes(s, sc), (s, sc)
+    assert n3 > 50
+
+
+def test_stream_k_mapping_catches_planted_errors(monkeypatch):
+    """Plant mistakes in kernel 3's replayed algebra (CPU only): an owner search one CTA off, a
+    fix-up reading the other slot of a contributor, runs that overlap."""
+    from q4b.gemm import schedule, verifier
+    g = _gemm()
+    s, sc = g.BY_ID["B5"], g.Schedule(kernel=3, bn=256)
+    assert g.verify(s, sc).ok
+    monkeypatch.setattr(verifier, "sk_cta_of", lambda u, U, G: min(G - 1, schedule.sk_cta_of(u, U, G) + 1))
+    assert "run-owner" in g.verify(s, sc).reasons
+    monkeypatch.undo()
+    real = schedule.sk_fixup_slots
+    monkeypatch.setattr(verifier, "sk_fixup_slots", lambda *a: [(c, slot ^ 1) for c, slot in real(*a)])
+    assert "fixup-slots" in g.verify(s, sc).reasons
+    monkeypatch.undo()
+    monkeypatch.setattr(verifier, "sk_run", lambda U, G, c: (max(0, U * c // G - 1), U * (c + 1) // G))
+    assert "run-partition" in g.verify(s, sc).reasons
