@@ -98,18 +98,58 @@ def decode_traffic(bytes_tok, world):
 
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region (median SM clock, throttle reasons seen)."""
+    """SM clock and throttle reasons during the timed region: NVML polled every 5 ms on a thread
+    (read-only queries), else nvidia-smi at its 100 ms minimum; summary = median SM MHz under load,
+    max SM MHz, the reasons seen and the sample count."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits (nvml.h): the ones the timing rules name
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
+    PERIOD_S = 0.005
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.nvml = None  # (module, handle) while NVML samples
+        self.samples = []  # NVML: (sm_mhz, max_mhz, reason bits)
+        self.stop = threading.Event()
+
+    def _nvml_handle(self, nv):
+        try:  # the NVML device of this process's CUDA device, by PCI address (CUDA and NVML orders can differ)
+            import torch
+            p = torch.cuda.get_device_properties(self.gpu)
+            return nv.nvmlDeviceGetHandleByPciBusId(f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0")
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.gpu)
+
+    def _nvml_sample(self):
+        nv, h = self.nvml
+        self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                             nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM),
+                             nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+
+    def _poll(self):
+        while not self.stop.wait(self.PERIOD_S):
+            try:
+                self._nvml_sample()
+            except Exception:
+                return
 
     def __enter__(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nvml = (nv, self._nvml_handle(nv))
+            self._nvml_sample()  # one sample as the region starts
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nvml = None
+            self.samples = []
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-lms", "100", "-i", str(self.gpu)], stdout=subprocess.PIPE,
@@ -125,6 +165,14 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *a):
+        if self.nvml:
+            self.stop.set()
+            self.t.join(timeout=2)
+            try:
+                self._nvml_sample()  # and one as it ends
+                self.nvml[0].nvmlShutdown()
+            except Exception:
+                pass
         if self.proc:
             self.proc.terminate()
             try:
@@ -133,6 +181,11 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        if self.samples:
+            sm = [float(x[0]) for x in self.samples]
+            reasons = {nm for _, _, bits in self.samples for nm, bit in self.REASON_BITS.items() if bits & bit}
+            return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(self.samples[-1][1]),
+                    "reasons": sorted(reasons), "samples": len(sm), "source": "nvml"}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
@@ -148,7 +201,7 @@ class ClockSampler:
                 if v.lower().startswith("active"):
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi"}
 
 
 def dist_env():

@@ -62,3 +62,36 @@ def test_cpu_sweep_baseline_is_bounded():
     import bench
     cb = bench.cpu_sweep_baseline([1], budget_s=0.5)
     assert cb["value"] > 0 and cb["kind"] == "port" and "M=1" in cb["sample"]
+
+
+def test_clock_sampler_with_a_fake_nvml(monkeypatch):
+    """The clock record of a timed region comes from NVML polled on a thread (read-only queries):
+    samples at the start, every few ms and at the end; the timing rules' throttle reasons from the
+    clocks-event bits; no NVML -> the nvidia-smi form (here: none available, no samples)."""
+    import time
+    import types
+
+    import bench
+    calls = {"n": 0}
+    fake = types.SimpleNamespace(
+        NVML_CLOCK_SM=1, nvmlInit=lambda: None, nvmlShutdown=lambda: None,
+        nvmlDeviceGetHandleByPciBusId=lambda b: "h", nvmlDeviceGetHandleByIndex=lambda i: "h",
+        nvmlDeviceGetClockInfo=lambda h, c: 1965 if calls["n"] % 2 else 1900,
+        nvmlDeviceGetMaxClockInfo=lambda h, c: 1965)
+
+    def reasons(h):
+        calls["n"] += 1
+        return 0x4 if calls["n"] == 3 else 0  # sw_power_cap once
+    fake.nvmlDeviceGetCurrentClocksEventReasons = reasons
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    with bench.ClockSampler(0) as c:
+        time.sleep(0.05)
+    s = c.summary()
+    assert s["source"] == "nvml" and s["samples"] >= 3 and s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["sw_power_cap"] and 1900 <= s["sm_mhz"] <= 1965
+    broken = types.SimpleNamespace(nvmlInit=lambda: (_ for _ in ()).throw(RuntimeError("no NVML")))
+    monkeypatch.setitem(sys.modules, "pynvml", broken)
+    monkeypatch.setattr(bench.subprocess, "Popen", lambda *a, **k: (_ for _ in ()).throw(OSError("no nvidia-smi")))
+    with bench.ClockSampler(0) as c:
+        pass
+    assert c.summary()["samples"] == 0 and c.summary()["source"] == "nvidia-smi"
