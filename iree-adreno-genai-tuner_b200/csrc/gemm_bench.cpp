@@ -2,8 +2,9 @@
 // (gemm/harness/vk_gemm_bench.c:1-13, 389-492). Same files, same protocol, same output:
 //
 //   manifest line   <name> <shape_dir> <candidate>          ('#' starts a comment)
-//   candidate       <kernel>:<key=value,...>, kernel 1 = tcgen05, 2 = CUDA cores, e.g.
-//                   1:bn=128,stages=6,split=2   or   2:   (keys: bn, stages, split; 0 / absent = auto)
+//   candidate       <kernel>:<key=value,...>, kernel 1 = tcgen05, 2 = CUDA cores, 3 = tcgen05
+//                   persistent stream-K, e.g. 1:bn=128,stages=6,split=2   or   3:bn=256,stages=4   or   2:
+//                   (keys: bn, stages, split; 0 / absent = auto)
 //   shape_dir       meta.txt "M N K LA LB TOL" (TOL < 0: no check); A.bin, B.bin fp16 in the stored
 //                   layout of the BLAS letters; Cref.bin fp32 row-major M x N (absent if TOL < 0)
 //   per candidate   poison C with 0xFF bytes (fp16 NaN), run once, max|C - Cref| / max|Cref| against
@@ -127,7 +128,7 @@ bool parse_candidate(const std::string& text, q4b_gemm_cfg& cfg) {
     else if (k == "split") cfg.split = v;
     else return false;
   }
-  return cfg.kernel == 1 || cfg.kernel == 2;
+  return cfg.kernel >= 1 && cfg.kernel <= 3;
 }
 
 struct Runner {
